@@ -1,0 +1,640 @@
+"""Benchmark of simtgo's hot path on B200: prints ONE JSON line.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...        (N > 1)
+
+Headline (value): FIR throughput in Gsamples/s over the whole job. Each GPU
+owns 2^28 consecutive outputs of one long signal with 127 taps -- 2^31
+samples at 8 GPUs -- and receives its input slice with the 126 preceding
+samples duplicated (the halo), so there is no data-path collective
+("scaling": "weak"). One step = one simtgo_FIR_shard launch per GPU over
+its resident shard. The inputs (1 GiB per buffer) exceed the 126 MB L2, so
+no flush is needed between steps.
+
+e2e: the same metric through the C ABI with HOST buffers: every step copies
+the shard in from pinned memory, runs the FIR and copies the outputs back.
+
+Also reported: the roofline of the FIR kernel (FP32 FMA-bound at 127 taps),
+clocks sampled during the timed region, a CPU baseline (the oracle port on
+the host cores, bounded sample), and at N=1 every kernel's achieved HBM
+GB/s at its workload size ("kernels"), plus, at every N, the sharded
+histogram (with the bins all-reduced) and the sharded tile graph.
+
+--impl reference times the reference's CPU path (the oracle port of
+gpu.RunCPU's FIR; the reference's own generated FIR.cu stages a 320-sample
+tile and cannot hold 127 taps) on the same metric, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import datetime
+import json
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = pathlib.Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = ("achieved HBM GB/s (% of B200 peak) per kernel; FIR Gsamples/s at 1/2/4/8 GPU")
+TAPS = 127
+FIR_LOG2 = 28            # outputs per GPU
+HALO = 128               # >= TAPS-1, a multiple of 4 so shard inputs stay 16-byte aligned
+P = C.c_void_p
+
+
+def env_rank():
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)),
+            int(os.environ.get("LOCAL_RANK", 0)))
+
+
+def fir_taps():
+    """127 taps uniform[-1,1], normalised to sum 1 (redrawn while the sum is
+    below 0.1 in magnitude)."""
+    import numpy as np
+
+    seed = 3
+    while True:
+        h = np.random.default_rng(seed).uniform(-1, 1, TAPS)
+        if abs(h.sum()) >= 0.1:
+            return (h / h.sum()).astype(np.float32)
+        seed += 1000
+
+
+def signal(torch, g0, n, device):
+    """Samples g0 .. g0+n-1 of one long uniform[-1,1) signal, as a function
+    of the global index, so every shard sees the same halo values."""
+    g = torch.arange(g0, g0 + n, dtype=torch.int64, device=device)
+    h = (g * 0x9E3779B1 + 0x7F4A7C15) & 0xFFFFFFFF
+    h = (h ^ (h >> 15)) * 0x2C1B3C6D & 0xFFFFFFFF
+    h = h ^ (h >> 12)
+    out = ((h & 0xFFFFFF).to(torch.float32) * (2.0 / 16777216.0) - 1.0)
+    out[g < 0] = 0.0
+    return out
+
+
+class Clocks:
+    """nvidia-smi sampled every 200 ms while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f,
+                stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        self.f.close()
+
+    def summary(self):
+        rows = []
+        try:
+            for line in open(self.path):
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9 and parts[1].replace(".", "").isdigit():
+                    rows.append(parts)
+        finally:
+            os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm = [float(r[1]) for r in rows]
+        loaded = [float(r[1]) for r in rows if float(r[3]) > 300] or sm
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for name, v in zip(names, r[5:9]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": float(rows[0][2]),
+                "samples": len(rows), "power_w_max": max(float(r[3]) for r in rows),
+                "reasons": sorted(reasons)}
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return json.loads(p.read_text()), "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
+
+
+def ncu_traffic(name):
+    """Per-unit DRAM bytes from a committed ncu summary, or None."""
+    p = ROOT / "profiles" / "ncu_traffic.json"
+    if not p.exists():
+        return None
+    try:
+        return json.loads(p.read_text()).get(name)
+    except (ValueError, OSError):
+        return None
+
+
+# ---------------------------------------------------------------------------
+def run_ours(args):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from simtgo_b200 import _lib
+
+    rank, world, local = env_rank()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
+    L = _lib.load()
+    stream = torch.cuda.current_stream()
+    sp = P(stream.cuda_stream)
+    sms = C.c_int32()
+    _lib.check(L.simtgo_device_info(C.byref(sms), None, None))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def events():
+        return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    # ---- the FIR shard -----------------------------------------------------
+    n = 1 << args.fir_log2
+    g0 = rank * n
+    halo = min(HALO, g0)
+    h = torch.from_numpy(fir_taps()).to(dev)
+    x = signal(torch, g0 - halo, n + halo, dev)
+    y = torch.empty(n, dtype=torch.float32, device=dev)
+
+    def fir_step(yb=y, xb=x):
+        rc = L.simtgo_FIR_shard(P(yb.data_ptr()), n, P(xb.data_ptr()), xb.numel(), halo,
+                                P(h.data_ptr()), TAPS, sp)
+        if rc:
+            _lib.check(rc)
+
+    for _ in range(args.warmup):
+        fir_step()
+    barrier()
+    e0, e1 = events()
+    with Clocks(local) as clk:
+        barrier()
+        e0.record(stream)
+        for _ in range(args.steps):
+            fir_step()
+        e1.record(stream)
+        e1.synchronize()
+        barrier()
+    ms = e0.elapsed_time(e1)
+    ms_max = max_over_ranks(ms)
+    clocks = clk.summary()
+    _lib.check(L.simtgo_stream_sync(sp))
+    value = world * n * args.steps / (ms_max * 1e-3) / 1e9
+    launch_ms = ms / args.steps
+
+    # Parity spot check of this rank's shard against the oracle (512 outputs).
+    spot = spot_check(np, x[: halo + 512].cpu().numpy() if rank == 0 else None, y, h, halo)
+
+    # ---- e2e: host buffers through the C ABI ----------------------------------
+    xh = torch.empty(n + halo, dtype=torch.float32, pin_memory=True)
+    xh.copy_(x)
+    yh = torch.empty(n, dtype=torch.float32, pin_memory=True)
+    xd = torch.empty_like(x)
+    e2e_steps = max(3, min(args.steps, args.e2e_steps))
+
+    def e2e_step():
+        xd.copy_(xh, non_blocking=True)
+        fir_step(y, xd)
+        yh.copy_(y, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    barrier()
+    e0, e1 = events()
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    e1.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+    e2e_value = world * n * e2e_steps / (e2e_ms * 1e-3) / 1e9
+    del xh, yh, xd
+
+    # ---- roofline of the FIR kernel ---------------------------------------------
+    peaks, peak_src = measured_peaks()
+    flops = 2.0 * TAPS * n
+    achieved_tflops = flops / (launch_ms * 1e-3) / 1e12
+    sm_mhz = clocks.get("sm_mhz") or peaks.get("clocks_under_load", {}).get("sm_mhz_median", 1965)
+    fp32_peak = sms.value * 128 * 2 * sm_mhz * 1e6 / 1e12
+    hbm_gbs = (8.0 * n + 4.0 * halo) / (launch_ms * 1e-3) / 1e9
+    traffic = ncu_traffic("FIR_shard_127")
+    roofline = {
+        "bound": "fp32",
+        "achieved": round(achieved_tflops, 2), "peak": round(fp32_peak, 2), "unit": "TFLOP/s",
+        "frac": round(achieved_tflops / fp32_peak, 4),
+        "peak_basis": f"{sms.value} SMs x 128 FP32 lanes x 2 FLOP x {sm_mhz:.0f} MHz "
+                      "(the SM clock sampled during the timed region); FIR at 127 taps is "
+                      "bound by FMA issue, not HBM or tensor cores",
+        "traffic": None if traffic is None else int(traffic * n),
+        "hbm_achieved_gbs": round(hbm_gbs, 1),
+        "hbm_frac": round(hbm_gbs / peaks["hbm_gbs"], 4),
+        "hbm_peak_gbs": peaks["hbm_gbs"], "hbm_peak_source": peak_src,
+        "kernel_ms": round(launch_ms, 4),
+    }
+
+    # ---- sharded histogram (bins all-reduced) and sharded tile graph ------------
+    sharded = {}
+    del x, y
+    torch.cuda.empty_cache()
+    sharded["histogram_allreduce"] = bench_histogram(args, torch, L, dev, sp, rank, world,
+                                                     barrier, max_over_ranks, events)
+    sharded["tile_graph"] = bench_tile(args, torch, np, L, dev, sp, rank, world, barrier,
+                                       max_over_ranks, events)
+
+    kernels = None
+    cpu = None
+    if world == 1 and not args.skip_kernels:
+        kernels = bench_kernels(args, torch, np, L, dev, sp, events, peaks)
+    if rank == 0 and world == 1 and not args.skip_cpu:
+        cpu = cpu_baseline(args, np, seconds=args.cpu_seconds)
+
+    line = {
+        "metric": METRIC, "value": round(value, 3), "unit": "Gsamples/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (uniform[-1,1) signal from a counter hash; seeded taps)",
+        "config": {
+            "workload": f"FIR, 2^{args.fir_log2} outputs per GPU ({world}x2^{args.fir_log2} "
+                        f"of one signal), {TAPS} taps normalised to sum 1",
+            "taps": TAPS, "samples_per_gpu": n, "total_samples": world * n,
+            "halo": "126 preceding samples duplicated into each shard's input (128 staged)",
+            "parallelism": f"{world} shards, no data-path collective",
+            "l2": "inputs larger than L2 (1 GiB per buffer), no flush",
+        },
+        "e2e": {"value": round(e2e_value, 3), "unit": "Gsamples/s",
+                "h2d_bytes_per_step": world * (n + HALO) * 4,
+                "d2h_bytes_per_step": world * n * 4,
+                "steps": e2e_steps,
+                "path": "pinned host -> device copy, simtgo_FIR_shard, device -> pinned host, "
+                        "one stream; bytes summed over ranks"},
+        "gpu_launches": args.steps,
+        "gpu_launches_note": "simtgo_FIR_shard kernels per rank inside the timed region",
+        "roofline": roofline,
+        "clocks": clocks,
+        "cpu_baseline": cpu,
+        "parity_spot_check": spot,
+        "sharded": sharded,
+        "kernels": kernels,
+    }
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def spot_check(np, x_host, y, h, halo):
+    """512 outputs of rank 0's shard against the oracle's fma order."""
+    if x_host is None:
+        return None
+    sys.path.insert(0, str(ROOT / "tests"))
+    import oracle_lib as O
+
+    yh = y[:512].cpu().numpy()
+    rc, want = O.fir_shard(np.ascontiguousarray(x_host[: halo + 512]), halo,
+                           h.cpu().numpy(), 512)
+    return {"outputs": 512, "bit_exact": bool(rc == 0 and np.array_equal(
+        yh.view(np.uint32), want.view(np.uint32)))}
+
+
+def timed(fn, steps, warmup, stream, events):
+    for _ in range(warmup):
+        fn()
+    import torch
+
+    torch.cuda.synchronize()
+    e0, e1 = events()
+    e0.record(stream)
+    for _ in range(steps):
+        fn()
+    e1.record(stream)
+    e1.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def bench_histogram(args, torch, L, dev, sp, rank, world, barrier, max_over_ranks, events):
+    """2^28 samples in total, uniform over [0,255], split over the ranks;
+    each rank counts its part and the bins are all-reduced (NCCL)."""
+    from simtgo_b200 import _lib
+
+    total = 1 << 28
+    n = total // world
+    gen = torch.Generator(device=dev).manual_seed(4 + rank)
+    x = torch.randint(0, 256, (n,), dtype=torch.int32, device=dev, generator=gen)
+    bins = torch.zeros(256, dtype=torch.int32, device=dev)
+    comm = P()
+    uid = C.create_string_buffer(128)
+    if world > 1:
+        import torch.distributed as dist
+
+        buf = torch.zeros(128, dtype=torch.uint8, device=dev)
+        if rank == 0:
+            _lib.check(L.simtgo_comm_unique_id(uid))
+            buf.copy_(torch.frombuffer(bytearray(uid.raw), dtype=torch.uint8))
+        dist.broadcast(buf, 0)
+        uid = C.create_string_buffer(bytes(buf.cpu().numpy().tobytes()), 128)
+    else:
+        _lib.check(L.simtgo_comm_unique_id(uid))
+    _lib.check(L.simtgo_comm_init(C.byref(comm), uid, world, rank))
+
+    def step():
+        bins.zero_()
+        rc = L.simtgo_Histogram_allreduce(comm, P(bins.data_ptr()), 256, P(x.data_ptr()), n, sp)
+        if rc:
+            _lib.check(rc)
+
+    barrier()
+    ms = timed(step, args.steps, args.warmup, torch.cuda.current_stream(), events)
+    ms = max_over_ranks(ms)
+    ok = int(bins.sum().item()) == total
+    _lib.check(L.simtgo_comm_destroy(comm))
+    return {"samples_total": total, "ms_per_step": round(ms, 4),
+            "gbs": round(4.0 * total / (ms * 1e-3) / 1e9, 1),
+            "gsamples_per_s": round(total / (ms * 1e-3) / 1e9, 2),
+            "scaling": "strong", "bins_sum_ok": ok,
+            "step": "zero bins; local privatised histogram; NCCL all-reduce of 256 int32"}
+
+
+def twelve(tile, g, a, b, c, h):
+    s = tile.Scale(a, 0.5)
+    ab = tile.Abs(b)
+    q = tile.Sqrt(ab)
+    m = tile.Mul(s, q)
+    d = tile.Add(m, c)
+    f = tile.FIR(s, h)
+    y = tile.Hypot(d, f)
+    return tile.Mul(y, ab)
+
+
+def bench_tile(args, torch, np, L, dev, sp, rank, world, barrier, max_over_ranks, events):
+    """3 x 2^28 inputs uniform[-4,4] through the 12-node graph, split over
+    the ranks (a 32-element halo for the FIR node)."""
+    from simtgo_b200 import tile
+
+    total = 1 << 28
+    n = total // world
+    halo = 32 if rank > 0 else 0
+    gen = torch.Generator(device=dev).manual_seed(6 + rank)
+    ins = [torch.rand(n + halo, device=dev, generator=gen) * 8 - 4 for _ in range(3)]
+    g = tile.New()
+    a, b, c = (g.InputDevice(t[halo:]) for t in ins)
+    root = twelve(tile, g, a, b, c, np.full(31, 1 / 31, np.float32))
+    out = torch.empty(n, device=dev)
+    stream = torch.cuda.current_stream()
+
+    def step():
+        root.Run(out, stream, halo=halo)
+
+    barrier()
+    ms = timed(step, args.steps, args.warmup, stream, events)
+    ms = max_over_ranks(ms)
+    return {"elements_total": total, "ms_per_step": round(ms, 4),
+            "gbs": round(16.0 * total / (ms * 1e-3) / 1e9, 1),
+            "gelements_per_s": round(total / (ms * 1e-3) / 1e9, 2),
+            "scaling": "strong", "bytes_per_element": 16}
+
+
+def bench_kernels(args, torch, np, L, dev, sp, events, peaks):
+    """Each kernel at its workload size, inputs resident and larger than L2,
+    timed with CUDA events; GB/s from the algorithmic bytes per unit."""
+    stream = torch.cuda.current_stream()
+    steps, warm = max(5, min(args.steps, 20)), 3
+    hbm = peaks["hbm_gbs"]
+    out = {}
+    N = 1 << 28
+    gen = torch.Generator(device=dev).manual_seed(11)
+
+    def rec(name, ms, nbytes, units, unit_name):
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        out[name] = {"ms": round(ms, 4), "gbs": round(gbs, 1), "frac_hbm": round(gbs / hbm, 4),
+                     "size": units, "unit": unit_name,
+                     "bytes_per_unit": round(nbytes / units, 3)}
+
+    def grid(n, block=256):
+        return (n + block - 1) // block
+
+    a = torch.randn(N, device=dev, generator=gen)
+    b = torch.randn(N, device=dev, generator=gen)
+    c = torch.empty(N, device=dev)
+    pa, pb, pc = P(a.data_ptr()), P(b.data_ptr()), P(c.data_ptr())
+    G = grid(N)
+    rec("VecAdd", timed(lambda: L.simtgo_VecAdd(pc, N, pa, N, pb, N, G, 256, sp), steps, warm,
+                        stream, events), 12.0 * N, N, "elements")
+    rec("Scale", timed(lambda: L.simtgo_Scale(pc, N, pa, N, 0.75, G, 256, sp), steps, warm,
+                       stream, events), 8.0 * N, N, "elements")
+    rec("Magnitude", timed(lambda: L.simtgo_Magnitude(pc, N, pa, N, pb, N, G, 256, sp), steps,
+                           warm, stream, events), 12.0 * N, N, "elements")
+    rec("MagnitudeFast", timed(lambda: L.simtgo_MagnitudeFast(pc, N, pa, N, pb, N, 3.0, G, 256,
+                                                              sp), steps, warm, stream, events),
+        12.0 * N, N, "elements")
+    rec("Softclip", timed(lambda: L.simtgo_Softclip(pc, N, pa, N, 0.5, G, 256, sp), steps, warm,
+                          stream, events), 8.0 * N, N, "elements")
+    edges = torch.tensor([0.1, 0.25, 0.5, 0.8, 1.2, 1.8, 2.5], device=dev)
+    rec("Classify", timed(lambda: L.simtgo_Classify(pc, N, pa, N, P(edges.data_ptr()), 7, G, 256,
+                                                    sp), steps, warm, stream, events),
+        8.0 * N, N, "elements")
+    from simtgo_b200._lib import Shape
+
+    bands = torch.tensor([-0.5, 0.25, 0.0, 0.5, 0.5, 1.0, 1.0, 2.0], device=dev)
+    cfg = Shape(0.125, 3, 0.001)
+    rec("BandGain", timed(lambda: L.simtgo_BandGain(pc, N, pa, N, P(bands.data_ptr()), 4,
+                                                    C.byref(cfg), G, 256, sp), steps, warm,
+                          stream, events), 8.0 * N, N, "elements")
+    WN = N // 32
+    rec("WarpReduceSum", timed(lambda: L.simtgo_WarpReduceSum(pc, WN, pa, N, grid(N, 128), 128,
+                                                              sp), steps, warm, stream, events),
+        4.125 * N, N, "elements")
+    del b
+    torch.cuda.empty_cache()
+    # Signal chain: interleaved complex -> MagnitudeFast -> Softclip -> Quantize.
+    z = torch.randn(2 * N, device=dev, generator=gen)
+    rec("MagnitudeFast_interleaved",
+        timed(lambda: L.simtgo_MagnitudeFast_interleaved(pc, N, P(z.data_ptr()), 2 * N, 3.0, G,
+                                                         256, sp), steps, warm, stream, events),
+        12.0 * N, N, "complex samples")
+    del z
+    torch.cuda.empty_cache()
+    code = torch.empty(N, dtype=torch.int32, device=dev)
+    energy = torch.empty(N, dtype=torch.int64, device=dev)
+    clipped = torch.empty(N, dtype=torch.uint8, device=dev)
+    rec("Quantize", timed(lambda: L.simtgo_Quantize(P(code.data_ptr()), N, P(energy.data_ptr()),
+                                                    N, P(clipped.data_ptr()), N, pa, N, 0.25,
+                                                    0x9E3779B9, G, 256, sp), steps, warm,
+                          stream, events), 17.0 * N, N, "elements")
+    del code, energy, clipped
+    xi = torch.randint(0, 256, (N,), dtype=torch.int32, device=dev, generator=gen)
+    bins = torch.zeros(256, dtype=torch.int32, device=dev)
+    rec("Histogram", timed(lambda: L.simtgo_Histogram(P(bins.data_ptr()), 256, P(xi.data_ptr()), N,
+                                                      G, 256, sp), steps, warm, stream, events),
+        4.0 * N, N, "samples (uniform)")
+    p = (torch.arange(256, device=dev, dtype=torch.float64) + 1) ** -1.2
+    cdf = torch.cumsum(p / p.sum(), 0)
+    u = torch.rand(N, device=dev, generator=gen, dtype=torch.float64)
+    xi = torch.searchsorted(cdf, u).clamp_(max=255).to(torch.int32)
+    del u
+    rec("Histogram_zipf", timed(lambda: L.simtgo_Histogram(P(bins.data_ptr()), 256,
+                                                           P(xi.data_ptr()), N, G, 256, sp),
+                                steps, warm, stream, events), 4.0 * N, N, "samples (Zipf 1.2)")
+    del xi
+    torch.cuda.empty_cache()
+    # Gray 7680x4320.
+    npx = 7680 * 4320
+    rgb = torch.randint(0, 256, (3 * npx,), dtype=torch.uint8, device=dev, generator=gen)
+    luma = torch.empty(npx, dtype=torch.uint8, device=dev)
+    rec("Gray", timed(lambda: L.simtgo_Gray(P(luma.data_ptr()), npx, P(rgb.data_ptr()), 3 * npx,
+                                            grid(npx), 256, sp), steps, warm, stream, events),
+        4.0 * npx, npx, "pixels")
+    del rgb, luma
+    # Transpose 16384^2.
+    T = 16384
+    rec("Transpose", timed(lambda: L.simtgo_Transpose(pc, T * T, pa, T * T, T, T, T // 16,
+                                                      T // 16, 16, 16, sp), steps, warm, stream,
+                           events), 8.0 * T * T, T * T, "elements")
+    # FIR of the 2^20-sample, 31-tap case (L2-resident, launch-bound).
+    n20 = 1 << 20
+    h31 = torch.rand(31, device=dev, generator=gen)
+    h31 /= h31.sum()
+    rec("FIR_31taps_2^20", timed(lambda: L.simtgo_FIR(pc, n20, pa, n20, P(h31.data_ptr()), 31,
+                                                      n20 // 256, 256, sp), steps, warm, stream,
+                                 events), 8.0 * n20, n20, "outputs (L2-resident)")
+    return out
+
+
+def cpu_baseline(args, np, seconds):
+    """The oracle's FIR in gpu.RunCPU's order (fir_shard_runcpu) on every
+    host core, over a bounded leading sample of rank 0's shard."""
+    sys.path.insert(0, str(ROOT / "tests"))
+    import oracle_lib as O
+
+    threads = os.cpu_count() or 1
+    O.set_threads(threads)
+    h = fir_taps()
+    sample = 1 << 18
+    x = np.random.default_rng(0).uniform(-1, 1, (1 << 24) + TAPS).astype(np.float32)
+    t0 = time.perf_counter()
+    O.fir_shard(x[: sample + TAPS], 0, h, sample, fused=False)
+    dt = time.perf_counter() - t0
+    sample = int(min(1 << 24, max(sample, sample * seconds / max(dt, 1e-6))))
+    t0 = time.perf_counter()
+    O.fir_shard(x[: sample + TAPS], 0, h, sample, fused=False)
+    dt = time.perf_counter() - t0
+    return {"value": round(sample / dt / 1e9, 4), "unit": "Gsamples/s", "cores": threads,
+            "kind": "port", "seconds": round(dt, 2),
+            "sample": f"{sample} outputs x {TAPS} taps of the FIR workload (oracle port of "
+                      "gpu.RunCPU's FIR, -O3 -ffp-contract=off, block-parallel pthreads)"}
+
+
+def run_reference(args):
+    """The reference arm: the oracle port of gpu.RunCPU's FIR on the host
+    cores, rank 0 only (no GPU work)."""
+    import numpy as np
+
+    rank, world, _ = env_rank()
+    if rank != 0:
+        return
+    sys.path.insert(0, str(ROOT / "tests"))
+    import oracle_lib as O
+
+    threads = os.cpu_count() or 1
+    O.set_threads(threads)
+    h = fir_taps()
+    x = np.random.default_rng(0).uniform(-1, 1, (1 << 22) + TAPS).astype(np.float32)
+    probe = 1 << 16
+    t0 = time.perf_counter()
+    O.fir_shard(x[: probe + TAPS], 0, h, probe, fused=False)
+    dt = time.perf_counter() - t0
+    per_step_s = min(2.0, 150.0 / max(1, args.steps + args.warmup))
+    sample = int(min(1 << 22, max(probe, probe * per_step_s / max(dt, 1e-6))))
+    for _ in range(args.warmup):
+        O.fir_shard(x[: sample + TAPS], 0, h, sample, fused=False)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        O.fir_shard(x[: sample + TAPS], 0, h, sample, fused=False)
+    dt = time.perf_counter() - t0
+    value = sample * args.steps / dt / 1e9
+    kind = "port"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "Gsamples/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(dt / args.steps * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"FIR, 2^{args.fir_log2} outputs per GPU, {TAPS} taps "
+                               f"(bounded CPU sample of {sample} outputs per step)",
+                   "taps": TAPS},
+        "cpu_baseline": {"value": round(value, 4), "unit": "Gsamples/s", "cores": threads,
+                         "kind": kind,
+                         "sample": f"{sample} outputs x {TAPS} taps per step; the reference's "
+                                   "generated FIR.cu holds at most 65 taps in its 320-sample "
+                                   "tile, so its CPU path for 127 taps is the oracle port of "
+                                   "gpu.RunCPU's arithmetic"},
+        "e2e": {"value": round(value, 4), "unit": "Gsamples/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "gpu_launches": 0,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--fir-log2", type=int, default=FIR_LOG2)
+    ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--skip-kernels", action="store_true")
+    ap.add_argument("--skip-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

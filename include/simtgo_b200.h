@@ -1,0 +1,274 @@
+/*
+ * simtgo_b200.h -- C ABI of libsimtgo_b200.so, the B200 (sm_100a) kernels for
+ * simtgo's data-parallel hot path.
+ *
+ * The library replaces the device half of two call sites in simtgo:
+ *
+ *   simt:  Kernel.launch -> cuda.Function.LaunchSync / Launch
+ *          (simt/kernel.go:488-514, cuda/driver_cuda.go:546, cuda/stream_cuda.go:270)
+ *   tile:  Tensor.run -> jit.Load + LaunchSync   (tile/run.go:37-83)
+ *
+ * Every symbol is a plain C function over plain pointers, sizes and a stream
+ * handle, so it can be bound by purego (no cgo), ctypes, or a C/C++ caller.
+ *
+ * Conventions
+ * -----------
+ * - Slices travel as (pointer, int32 length) pairs, exactly as
+ *   cuda.Slice.KernelArgs flattens them (cuda/slice_cuda.go:94) and in the
+ *   parameter order of the generated kernel (kernels/prebuilt/<K>.cu).
+ *   Output and input pointers are DEVICE pointers in the current CUDA
+ *   context (simtgo's cuMemAlloc'd DevPtrs in the primary context qualify).
+ * - grid and block are the launch geometry the caller asked for. The kernels
+ *   here choose their own B200 geometry, but the covered extent grid*block
+ *   is honoured: a thread index the original launch did not cover writes
+ *   nothing, exactly as in gpu.RunCPU (gpu/gpu.go:270-306).
+ * - stream is a cudaStream_t (NULL = the legacy default stream). Every entry
+ *   point is asynchronous on that stream; simtgo_stream_sync() is the
+ *   synchronous tail simt.Kernel.Launch adds (LaunchSync) and reports
+ *   sticky device errors.
+ * - Return value: 0 on success; a negative SIMTGO_E* code for an argument
+ *   the host refused before anything was launched; a positive value is a
+ *   cudaError_t (or ncclResult_t + 1000 for the communicator calls) passed
+ *   through. simtgo_last_error() returns the calling thread's message for
+ *   the most recent failure.
+ * - Nothing here traps the device. Bounds that gpu.RunCPU would turn into an
+ *   index-out-of-range panic are refused on the host with SIMTGO_ELENGTH.
+ */
+#ifndef SIMTGO_B200_H
+#define SIMTGO_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+enum {
+    SIMTGO_OK = 0,
+    SIMTGO_ENULL = -1,     /* a null pointer where the extent needs memory   */
+    SIMTGO_ELENGTH = -2,   /* a slice too short for the covered extent: the
+                              access gpu.RunCPU would panic on               */
+    SIMTGO_EBLOCK = -3,    /* simt.BlockSizeError (simt/kernel.go:220-229)   */
+    SIMTGO_EALIAS = -4,    /* simt.AliasError / tile.AliasError
+                              (simt/kernel.go:251-264, tile/alias.go:17-23) */
+    SIMTGO_ELAUNCH = -5,   /* grid/block the driver would refuse             */
+    SIMTGO_ETAPS = -6,     /* FIR taps outside what the kernel can stage     */
+    SIMTGO_EGRAPH = -7,    /* a latched tile graph error (tile/tile.go:78)   */
+    SIMTGO_EDEVICE = -8,   /* no usable CUDA device / wrong architecture     */
+    SIMTGO_ECOMM = -9,     /* communicator misuse or NCCL not loadable       */
+    SIMTGO_ESIZE = -10,    /* a size beyond a documented library maximum     */
+    SIMTGO_EARG = -11      /* any other refused argument                     */
+};
+
+/* Message for the calling thread's most recent failure ("" if none). */
+const char* simtgo_last_error(void);
+/* Library version string. */
+const char* simtgo_version(void);
+/* Names the device the library would launch on and checks it is sm_100.
+ * Writes the SM count and the device's compute capability. */
+int simtgo_device_info(int32_t* sm_count, int32_t* cc_major, int32_t* cc_minor);
+/* cudaStreamSynchronize(stream); the synchronous tail of simt.Kernel.Launch. */
+int simtgo_stream_sync(void* stream);
+
+/* ---- the simt kernels (package kernels) -------------------------------- */
+
+/* kernels/kernels.go:12 VecAdd; generated kernels/prebuilt/VecAdd.cu.
+ * c[i] = a[i] + b[i] for i < min(c_len, grid*block). Bit-exact. */
+int simtgo_VecAdd(float* c, int32_t c_len, const float* a, int32_t a_len,
+                  const float* b, int32_t b_len,
+                  int32_t grid, int32_t block, void* stream);
+
+/* kernels/kernels.go:29 Scale; Scale.cu. y[i] = k*x[i]. Bit-exact. */
+int simtgo_Scale(float* y, int32_t y_len, const float* x, int32_t x_len, float k,
+                 int32_t grid, int32_t block, void* stream);
+
+/* kernels/kernels.go:21 Magnitude; Magnitude.cu. mag[i] = gpu.Hypot(re[i], im[i])
+ * with gpu.Hypot = float32(math.Hypot(float64, float64)) (gpu/math.go:17).
+ * Bit-exact with the emulator's definition. */
+int simtgo_Magnitude(float* mag, int32_t mag_len, const float* re, int32_t re_len,
+                     const float* im, int32_t im_len,
+                     int32_t grid, int32_t block, void* stream);
+
+/* kernels/magnitudefast.go:20 MagnitudeFast; MagnitudeFast.cu.
+ * mag[i] = Sqrt(re*re + im*im) / scale, each operation rounded to nearest
+ * (the gpu.RunCPU result, so bit-exact with it; the reference's
+ * --use_fast_math build is within its documented 1e-5 of this). */
+int simtgo_MagnitudeFast(float* mag, int32_t mag_len, const float* re, int32_t re_len,
+                         const float* im, int32_t im_len, float scale,
+                         int32_t grid, int32_t block, void* stream);
+
+/* MagnitudeFast over interleaved complex samples z = (re0, im0, re1, im1, ...).
+ * z_len counts floats; element i reads z[2i], z[2i+1]. Same arithmetic as
+ * simtgo_MagnitudeFast with re[i] = z[2i], im[i] = z[2i+1]. No counterpart
+ * signature in the reference (its MagnitudeFast is planar); the signal-chain
+ * workload stores complex values interleaved. */
+int simtgo_MagnitudeFast_interleaved(float* mag, int32_t mag_len, const float* z,
+                                     int32_t z_len, float scale,
+                                     int32_t grid, int32_t block, void* stream);
+
+/* kernels/softclip.go:11-30 Softclip; Softclip.cu. Bit-exact. */
+int simtgo_Softclip(float* y, int32_t y_len, const float* x, int32_t x_len,
+                    float threshold, int32_t grid, int32_t block, void* stream);
+
+/* kernels/classify.go:14-56 Classify; Classify.cu. edges is a device slice.
+ * Bit-exact with gpu.RunCPU (gain*v and bias*0.001 rounded separately). */
+int simtgo_Classify(float* out, int32_t out_len, const float* x, int32_t x_len,
+                    const float* edges, int32_t edges_len,
+                    int32_t grid, int32_t block, void* stream);
+
+/* kernels/bandgain.go:9-12 Band (8 bytes) and :26-30 Shape (16 bytes). */
+typedef struct simtgo_band { float upper; float gain; } simtgo_band;
+typedef struct simtgo_shape { float floor_gain; int32_t count; double bias; } simtgo_shape;
+
+/* kernels/bandgain.go:42-76 BandGain; BandGain.cu. bands is a device slice;
+ * cfg is a HOST pointer to the Shape the reference passes by value.
+ * Bit-exact with gpu.RunCPU (float64 steps rounded separately). */
+int simtgo_BandGain(float* y, int32_t y_len, const float* x, int32_t x_len,
+                    const simtgo_band* bands, int32_t bands_len, const simtgo_shape* cfg,
+                    int32_t grid, int32_t block, void* stream);
+
+/* kernels/quantize.go:16-45 Quantize; Quantize.cu. clipped is Go's []bool
+ * (one byte, 0 or 1). A float->int32 conversion out of range (or NaN) gives
+ * INT32_MIN, as amd64 CVTTSS2SL does under gpu.RunCPU. Bit-exact. */
+int simtgo_Quantize(int32_t* code, int32_t code_len, int64_t* energy, int32_t energy_len,
+                    uint8_t* clipped, int32_t clipped_len, const float* x, int32_t x_len,
+                    float step, uint32_t seed, int32_t grid, int32_t block, void* stream);
+
+/* kernels/gray.go:34-55 Gray; Gray.cu. Bit-exact. */
+int simtgo_Gray(uint8_t* out, int32_t out_len, const uint8_t* rgb, int32_t rgb_len,
+                int32_t grid, int32_t block, void* stream);
+
+/* kernels/histogram.go:23-50 Histogram; Histogram.cu. ADDS the counts of
+ * x[i] in [0,256) (i < min(x_len, grid*block)) into bins[k], k < bins_len;
+ * callers zero bins first, as the reference's test does. Exact. */
+int simtgo_Histogram(int32_t* bins, int32_t bins_len, const int32_t* x, int32_t x_len,
+                     int32_t grid, int32_t block, void* stream);
+
+/* kernels/transpose.go:15-38 Transpose; Transpose.cu. out[x*h+y] = in[y*w+x]
+ * for x < min(w, 16*grid_x), y < min(h, 16*grid_y). block_x*block_y must be
+ * 256 (AssumeBlockDim(TransposeTile*TransposeTile)). Exact. */
+int simtgo_Transpose(float* out, int32_t out_len, const float* in, int32_t in_len,
+                     int32_t w, int32_t h, int32_t grid_x, int32_t grid_y,
+                     int32_t block_x, int32_t block_y, void* stream);
+
+/* kernels/warpreduce.go:21-43 WarpReduceSum; WarpReduceSum.cu. block must be
+ * 128. out[w] = the shuffle-down tree sum of x[32w..32w+31] (missing samples
+ * are 0) for w < min(out_len, grid*4). Bit-exact (same addition tree). */
+int simtgo_WarpReduceSum(float* out, int32_t out_len, const float* x, int32_t x_len,
+                         int32_t grid, int32_t block, void* stream);
+
+/* kernels/fir.go:17-46 FIR; FIR.cu. block must be 256 (FIRBlock). y[n] =
+ * sum_k h[k]*x[n-k], x zero outside [0, x_len), for n < min(y_len, 256*grid).
+ * The accumulation is fma(h[k], x, acc) for k = 0..taps-1 in order: bit-exact
+ * with the reference's device code (nvcc contracts `acc += h*x`), within 1e-5
+ * of gpu.RunCPU (kernels' tolerance). taps = h_len may be 0..65 (the staged
+ * tile is FIRBlock+FIRMaxTaps samples); more is SIMTGO_ETAPS. */
+int simtgo_FIR(float* y, int32_t y_len, const float* x, int32_t x_len,
+               const float* h, int32_t h_len,
+               int32_t grid, int32_t block, void* stream);
+
+/* ---- sharded / large-extent forms -------------------------------------- */
+
+/* Maximum taps of simtgo_FIR_shard. */
+#define SIMTGO_FIR_SHARD_MAX_TAPS 1024
+
+/* One shard of a long FIR (the 2^31-sample, 127-tap workload): the FIR of
+ * kernels/fir.go:17 with 64-bit extents and up to SIMTGO_FIR_SHARD_MAX_TAPS
+ * taps. y[j], j < y_len, is output (g0 + j) of the whole signal; x holds the
+ * `halo` samples that precede the shard followed by the shard's own, so
+ * x[halo + j] is sample g0 + j. Samples before x[0] or at/after x[x_len] read
+ * as zero (shard 0 passes halo = 0). Same fma order as simtgo_FIR. h is a
+ * device pointer. No counterpart in the reference, which has no multi-GPU
+ * support; it generalises kernels/fir.go:17-46. */
+int simtgo_FIR_shard(float* y, int64_t y_len, const float* x, int64_t x_len, int64_t halo,
+                     const float* h, int32_t taps, void* stream);
+
+/* kernels/histogram.go:23 over a 64-bit extent: adds the counts of every
+ * x[i], i < x_len, into bins[k], k < bins_len. */
+int simtgo_Histogram_shard(int32_t* bins, int32_t bins_len, const int32_t* x, int64_t x_len,
+                           void* stream);
+
+/* ---- communicator (histogram partial bins -> one result on every rank) -- */
+
+typedef struct simtgo_comm simtgo_comm;
+/* 128-byte NCCL unique id, created on one rank and shared by the caller. */
+int simtgo_comm_unique_id(uint8_t out_id[128]);
+/* One rank of a communicator over the current device. NCCL is dlopen'ed
+ * (libnccl.so.2, the process's already-loaded copy if there is one). */
+int simtgo_comm_init(simtgo_comm** out, const uint8_t id[128], int32_t nranks, int32_t rank);
+int simtgo_comm_destroy(simtgo_comm* comm);
+/* In-place sum all-reduce of n int32 on stream. */
+int simtgo_comm_allreduce_i32(simtgo_comm* comm, int32_t* buf, int32_t n, void* stream);
+/* Histogram of this rank's shard added into bins, then the bins summed over
+ * all ranks, so every rank ends with the histogram of the whole input. */
+int simtgo_Histogram_allreduce(simtgo_comm* comm, int32_t* bins, int32_t bins_len,
+                               const int32_t* x, int64_t x_len, void* stream);
+
+/* ---- the tile track (package tile) -------------------------------------- */
+
+/* tile/tile.go:22 BlockSize and :25 MaxTaps. */
+#define SIMTGO_TILE_BLOCK_SIZE 256
+#define SIMTGO_TILE_MAX_TAPS 64
+
+typedef struct simtgo_tile_graph simtgo_tile_graph;
+/* A tensor handle is the node id within its graph (>= 0). */
+typedef int32_t simtgo_tensor;
+
+/* tile/tile.go:60 New. The graph records operations; nothing touches the
+ * device until a materialisation. */
+simtgo_tile_graph* simtgo_tile_new(void);
+void simtgo_tile_free(simtgo_tile_graph* g);
+/* tile/tile.go:86 Input: host data, uploaded on materialisation. The graph
+ * keeps the pointer, not a copy: the data must outlive the graph's use. */
+simtgo_tensor simtgo_tile_input(simtgo_tile_graph* g, const float* host, int32_t n);
+/* Device-resident input (the `dev` field of tile/tile.go:46): no upload. */
+simtgo_tensor simtgo_tile_input_device(simtgo_tile_graph* g, const float* dev, int32_t n);
+/* tile/tile.go:105-149. On a latched error each returns its first operand,
+ * as the reference does; simtgo_tile_err() reports the first error. */
+simtgo_tensor simtgo_tile_add(simtgo_tile_graph* g, simtgo_tensor a, simtgo_tensor b);
+simtgo_tensor simtgo_tile_mul(simtgo_tile_graph* g, simtgo_tensor a, simtgo_tensor b);
+simtgo_tensor simtgo_tile_hypot(simtgo_tile_graph* g, simtgo_tensor a, simtgo_tensor b);
+simtgo_tensor simtgo_tile_scale(simtgo_tile_graph* g, simtgo_tensor a, float k);
+simtgo_tensor simtgo_tile_sqrt(simtgo_tile_graph* g, simtgo_tensor a);
+simtgo_tensor simtgo_tile_abs(simtgo_tile_graph* g, simtgo_tensor a);
+/* tile/tile.go:135 FIR: h is HOST memory of `taps` floats (copied). */
+simtgo_tensor simtgo_tile_fir(simtgo_tile_graph* g, simtgo_tensor a, const float* h, int32_t taps);
+/* tile/tile.go:63 Tensor.Len. -1 for a handle that is not in the graph. */
+int32_t simtgo_tile_len(const simtgo_tile_graph* g, simtgo_tensor t);
+/* tile/tile.go:163 Err: SIMTGO_OK or SIMTGO_EGRAPH; the message is in
+ * simtgo_tile_err_string. */
+int simtgo_tile_err(const simtgo_tile_graph* g);
+const char* simtgo_tile_err_string(const simtgo_tile_graph* g);
+/* Number of device instructions the fused program for t has (the analogue of
+ * Tensor.Source, tile/run.go:10: it compiles without running). */
+int simtgo_tile_program_size(simtgo_tile_graph* g, simtgo_tensor t, int32_t* n_instructions,
+                             int32_t* n_inputs, int32_t* n_windows);
+
+/* tile/run.go:20 Materialize: upload host inputs, run the one fused kernel,
+ * download into host_out (out_len == Len(t)), free what the call allocated.
+ * Synchronous. */
+int simtgo_tile_materialize(simtgo_tile_graph* g, simtgo_tensor t, float* host_out,
+                            int32_t out_len);
+/* tile/run.go:89 MaterializeStepwise: one kernel per operation node with a
+ * device temporary between each; writes the launch count. Synchronous. */
+int simtgo_tile_materialize_stepwise(simtgo_tile_graph* g, simtgo_tensor t, float* host_out,
+                                     int32_t out_len, int32_t* launches);
+/* Device-resident run (tile/run.go:37 `run` without the uploads): every input
+ * must be a device input; out is a device buffer of Len(t) floats.
+ * Asynchronous on stream. The output may not overlap an input
+ * (tile/alias.go:42). */
+int simtgo_tile_run(simtgo_tile_graph* g, simtgo_tensor t, float* dev_out, int32_t out_len,
+                    void* stream);
+/* One shard of the graph's elementwise split: every device input holds the
+ * `halo` elements preceding the shard followed by out_len of its own
+ * (halo = 0 on the first shard); window (FIR) nodes read the halo instead of
+ * zeros. Without a FIR node, halo may be 0 on every shard. */
+int simtgo_tile_run_shard(simtgo_tile_graph* g, simtgo_tensor t, float* dev_out,
+                          int32_t out_len, int32_t halo, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SIMTGO_B200_H */

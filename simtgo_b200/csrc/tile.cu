@@ -1,0 +1,930 @@
+// tile.cu -- the tile track (package tile): graph recording (tile/tile.go),
+// lowering to one fused program (tile/codegen.go) and running it
+// (tile/run.go), with no run-time compiler.
+//
+// The reference renders each graph as CUDA C and compiles it with NVRTC per
+// distinct graph (tile/run.go:40). Here the graph is lowered on the host to a
+// short register program that travels in the kernel's parameter block (the
+// constant bank), and ONE precompiled sm_100a kernel interprets it:
+//  * a thread owns 4 consecutive elements; values live in 8 register slots
+//    of 4 floats each;
+//  * every instruction is warp-uniform, and each (operation, slot, slot)
+//    combination is its own case of one switch, so all slot indices are
+//    compile-time and values never leave registers;
+//  * inputs are read once with 16-byte streaming loads, hoisted to the start
+//    of the program so they are all in flight together, and the result is
+//    written once: 4 bytes per input and 4 bytes out per element, one pass
+//    over HBM;
+//  * a windowed (FIR) node is evaluated as in tile/codegen.go:80-108: its
+//    signal sub-expression is run by the same interpreter over the block's
+//    span plus a halo of taps-1 (zero outside the signal), staged in shared
+//    memory, then each thread forms fma(h[k], tile, acc) in k order for its
+//    4 outputs from two 16-byte shared loads per 4 taps.
+// Every operation is rounded on its own (Scale = k*x, Add, Mul, Sqrt
+// correctly rounded, Abs exact, Hypot = gpu.Hypot), so the fused program and
+// the stepwise one (one launch per node, tile/run.go:89) agree bit for bit.
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <algorithm>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "common.cuh"
+#include "exact.cuh"
+
+using namespace sgd;
+
+namespace tilek {
+
+constexpr int kSlots = 8;
+constexpr int kV = 4;  // elements per thread
+constexpr int kThreads = 256;
+constexpr int kChunk = kThreads * kV;  // elements per block iteration
+constexpr int kMaxCode = 1024;
+constexpr int kMaxIn = 32;
+constexpr int kMaxFir = 8;
+constexpr int kMaxTaps = SIMTGO_TILE_MAX_TAPS;
+constexpr int kTileF = kChunk + kMaxTaps + 8;  // staged floats per window node
+
+// Instruction codes: one per (operation, destination slot, source slot).
+enum : uint16_t {
+    OP_END = 0,
+    OP_LOAD = 1,      // + d            aux = input index
+    OP_STORE = 9,     // + s
+    OP_STAGE = 17,    // + s
+    OP_FIRACC = 25,   // + d            aux = window index
+    OP_SCALE = 33,    // + d (in place) imm = k
+    OP_SQRT = 41,     // + d
+    OP_ABS = 49,      // + d
+    OP_MOV = 57,      // + 8d + s
+    OP_ADD = 121,     // + 8d + s: r[d] = r[d] + r[s]
+    OP_MUL = 185,     // + 8d + s
+    OP_HYPOT = 249,   // + 8d + s
+    OP_COUNT = 313,
+};
+
+struct Insn {
+    uint16_t code;
+    uint16_t aux;
+    float imm;
+};
+
+struct FirDesc {
+    int32_t start;  // pc of the staging program
+    int32_t taps;
+    float h[kMaxTaps];  // the coefficients travel in the parameter block
+};
+
+struct Program {
+    int32_t main_start;
+    int32_t n_fir;
+    int32_t n_in;
+    int32_t n_code;
+    FirDesc fir[kMaxFir];
+    const float* in[kMaxIn];  // each already offset by the halo: in[k][i], i in [-halo, n)
+    Insn code[kMaxCode];
+};
+
+struct Exec {
+    int64_t p0;     // first of the thread's 4 positions
+    int64_t n;      // shard length
+    int64_t halo;   // positions [-halo, n) are valid
+    bool vec;       // all inputs (+halo) and out are 16-byte aligned
+    float* out;
+    float* stage;   // STAGE target (tile + offset of p0)
+    const float* taps_s;
+    const float* tiles;
+    int64_t cb;     // chunk base (for FIRACC)
+};
+
+__device__ __forceinline__ float4 load_pos(const float* base, const Exec& x) {
+    const int64_t p = x.p0;
+    if (x.vec && p >= -x.halo && p + 3 < x.n) return ld_stream_f4(base + p);
+    float4 v;
+    v.x = (p + 0 >= -x.halo && p + 0 < x.n) ? base[p + 0] : 0.0f;
+    v.y = (p + 1 >= -x.halo && p + 1 < x.n) ? base[p + 1] : 0.0f;
+    v.z = (p + 2 >= -x.halo && p + 2 < x.n) ? base[p + 2] : 0.0f;
+    v.w = (p + 3 >= -x.halo && p + 3 < x.n) ? base[p + 3] : 0.0f;
+    return v;
+}
+
+__device__ __forceinline__ void store_pos(const float4 v, const Exec& x) {
+    const int64_t p = x.p0;
+    if (x.vec && p + 3 < x.n) {
+        st_stream_f4(x.out + p, v);
+        return;
+    }
+    if (p + 0 < x.n) x.out[p + 0] = v.x;
+    if (p + 1 < x.n) x.out[p + 1] = v.y;
+    if (p + 2 < x.n) x.out[p + 2] = v.z;
+    if (p + 3 < x.n) x.out[p + 3] = v.w;
+}
+
+__device__ __forceinline__ void stage_pos(const float4 v, const Exec& x) {
+    const int64_t p = x.p0;
+    float4 s;
+    s.x = (p + 0 >= -x.halo && p + 0 < x.n) ? v.x : 0.0f;
+    s.y = (p + 1 >= -x.halo && p + 1 < x.n) ? v.y : 0.0f;
+    s.z = (p + 2 >= -x.halo && p + 2 < x.n) ? v.z : 0.0f;
+    s.w = (p + 3 >= -x.halo && p + 3 < x.n) ? v.w : 0.0f;
+    *reinterpret_cast<float4*>(x.stage) = s;
+}
+
+// Window start of node f for chunk cb: 16-byte aligned, 4 floats of slack
+// below the first halo sample.
+__device__ __forceinline__ int64_t tile_start(int64_t cb, int taps) {
+    return ((cb - (taps - 1)) & ~int64_t(3)) - 4;
+}
+
+__device__ __forceinline__ float4 fir_acc(const Program& P, int f, const Exec& x) {
+    const int taps = P.fir[f].taps;
+    const float* tile = x.tiles + f * kTileF;
+    const float* h = x.taps_s + f * kMaxTaps;
+    const int64_t q0 = x.p0 - tile_start(x.cb, taps);  // tile index of p0, = 0 mod 4
+    float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+    for (int k0 = 0; k0 < taps; k0 += 4) {
+        const float* w = tile + (q0 - k0 - 4);
+        const float4 lo = *reinterpret_cast<const float4*>(w);
+        const float4 hi = *reinterpret_cast<const float4*>(w + 4);
+        const float wv[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+        const float4 hk = *reinterpret_cast<const float4*>(h + k0);
+        const float hv[4] = {hk.x, hk.y, hk.z, hk.w};
+        const int nk = min(4, taps - k0);
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            if (u < nk) {
+                // output e at tap k0+u reads position p0 + e - k0 - u = wv[4 + e - u]
+                a0 = __fmaf_rn(hv[u], wv[4 - u], a0);
+                a1 = __fmaf_rn(hv[u], wv[5 - u], a1);
+                a2 = __fmaf_rn(hv[u], wv[6 - u], a2);
+                a3 = __fmaf_rn(hv[u], wv[7 - u], a3);
+            }
+        }
+    }
+    return make_float4(a0, a1, a2, a3);
+}
+
+__device__ __forceinline__ float4 f4_add(float4 a, float4 b) {
+    return make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z),
+                       __fadd_rn(a.w, b.w));
+}
+__device__ __forceinline__ float4 f4_mul(float4 a, float4 b) {
+    return make_float4(__fmul_rn(a.x, b.x), __fmul_rn(a.y, b.y), __fmul_rn(a.z, b.z),
+                       __fmul_rn(a.w, b.w));
+}
+__device__ __forceinline__ float4 f4_hypot(float4 a, float4 b) {
+    return make_float4(hypot_go(a.x, b.x), hypot_go(a.y, b.y), hypot_go(a.z, b.z),
+                       hypot_go(a.w, b.w));
+}
+__device__ __forceinline__ float4 f4_scale(float k, float4 a) {
+    return make_float4(__fmul_rn(k, a.x), __fmul_rn(k, a.y), __fmul_rn(k, a.z),
+                       __fmul_rn(k, a.w));
+}
+__device__ __forceinline__ float4 f4_sqrt(float4 a) {
+    return make_float4(__fsqrt_rn(a.x), __fsqrt_rn(a.y), __fsqrt_rn(a.z), __fsqrt_rn(a.w));
+}
+__device__ __forceinline__ float4 f4_abs(float4 a) {
+    return make_float4(fabsf(a.x), fabsf(a.y), fabsf(a.z), fabsf(a.w));
+}
+
+#define SG_C1(op, d, body) \
+    case (op) + (d): {     \
+        body;              \
+        break;             \
+    }
+#define SG_ROW1(op, M) M(op, 0) M(op, 1) M(op, 2) M(op, 3) M(op, 4) M(op, 5) M(op, 6) M(op, 7)
+#define SG_C2(op, d, s, body)     \
+    case (op) + 8 * (d) + (s): { \
+        body;                     \
+        break;                    \
+    }
+#define SG_ROW2(op, M, d) \
+    M(op, d, 0) M(op, d, 1) M(op, d, 2) M(op, d, 3) M(op, d, 4) M(op, d, 5) M(op, d, 6) M(op, d, 7)
+#define SG_ALL2(op, M)                                                                    \
+    SG_ROW2(op, M, 0) SG_ROW2(op, M, 1) SG_ROW2(op, M, 2) SG_ROW2(op, M, 3) SG_ROW2(op, M, 4) \
+        SG_ROW2(op, M, 5) SG_ROW2(op, M, 6) SG_ROW2(op, M, 7)
+
+#define M_LOAD(op, d) SG_C1(op, d, r[d] = load_pos(P.in[in.aux], x))
+#define M_STORE(op, s) SG_C1(op, s, store_pos(r[s], x))
+#define M_STAGE(op, s) SG_C1(op, s, stage_pos(r[s], x))
+#define M_FIRACC(op, d) SG_C1(op, d, r[d] = fir_acc(P, in.aux, x))
+#define M_SCALE(op, d) SG_C1(op, d, r[d] = f4_scale(in.imm, r[d]))
+#define M_SQRT(op, d) SG_C1(op, d, r[d] = f4_sqrt(r[d]))
+#define M_ABS(op, d) SG_C1(op, d, r[d] = f4_abs(r[d]))
+#define M_MOV(op, d, s) SG_C2(op, d, s, r[d] = r[s])
+#define M_ADD(op, d, s) SG_C2(op, d, s, r[d] = f4_add(r[d], r[s]))
+#define M_MUL(op, d, s) SG_C2(op, d, s, r[d] = f4_mul(r[d], r[s]))
+#define M_HYPOT(op, d, s) SG_C2(op, d, s, r[d] = f4_hypot(r[d], r[s]))
+
+// Runs the program from pc until OP_END for the thread's 4 positions.
+__device__ __noinline__ void interpret(const Program& P, int pc, const Exec& x) {
+    float4 r[kSlots];
+#pragma unroll
+    for (int i = 0; i < kSlots; i++) r[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (;; pc++) {
+        const Insn in = P.code[pc];
+        switch (in.code) {
+            case OP_END:
+                return;
+                SG_ROW1(OP_LOAD, M_LOAD)
+                SG_ROW1(OP_STORE, M_STORE)
+                SG_ROW1(OP_STAGE, M_STAGE)
+                SG_ROW1(OP_FIRACC, M_FIRACC)
+                SG_ROW1(OP_SCALE, M_SCALE)
+                SG_ROW1(OP_SQRT, M_SQRT)
+                SG_ROW1(OP_ABS, M_ABS)
+                SG_ALL2(OP_MOV, M_MOV)
+                SG_ALL2(OP_ADD, M_ADD)
+                SG_ALL2(OP_MUL, M_MUL)
+                SG_ALL2(OP_HYPOT, M_HYPOT)
+            default:
+                return;
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kThreads) k_tile(const __grid_constant__ Program P,
+                                                   float* __restrict__ out, int64_t n,
+                                                   int64_t halo, bool vec) {
+    extern __shared__ float4 sm4[];
+    float* sm = reinterpret_cast<float*>(sm4);
+    float* taps_s = sm;                       // n_fir x kMaxTaps
+    float* tiles = sm + P.n_fir * kMaxTaps;   // n_fir x kTileF
+    const int tid = threadIdx.x;
+    for (int f = 0; f < P.n_fir; f++)
+        for (int k = tid; k < kMaxTaps; k += kThreads)
+            taps_s[f * kMaxTaps + k] = P.fir[f].h[k];  // zero past taps
+    __syncthreads();
+
+    Exec x;
+    x.n = n;
+    x.halo = halo;
+    x.vec = vec;
+    x.out = out;
+    x.taps_s = taps_s;
+    x.tiles = tiles;
+    const int64_t nchunks = (n + kChunk - 1) / kChunk;
+    for (int64_t c = blockIdx.x; c < nchunks; c += gridDim.x) {
+        const int64_t cb = c * kChunk;
+        x.cb = cb;
+        if (P.n_fir > 0) {
+            for (int f = 0; f < P.n_fir; f++) {
+                const int64_t ts = tile_start(cb, P.fir[f].taps);
+                const int64_t span = cb + kChunk - ts;
+                for (int64_t off = 4 * tid; off < span; off += 4 * kThreads) {
+                    x.p0 = ts + off;
+                    x.stage = tiles + f * kTileF + off;
+                    interpret(P, P.fir[f].start, x);
+                }
+            }
+            __syncthreads();
+        }
+        x.p0 = cb + 4 * tid;
+        if (x.p0 < n) interpret(P, P.main_start, x);
+        if (P.n_fir > 0) __syncthreads();
+    }
+}
+
+}  // namespace tilek
+
+// ============================================================================
+// Host side: the recorded graph (tile/tile.go) and its lowering.
+// ============================================================================
+
+namespace {
+
+enum Kind { K_INPUT = 0, K_SCALE, K_ADD, K_MUL, K_SQRT, K_ABS, K_HYPOT, K_FIR };
+
+struct Node {
+    Kind kind;
+    int32_t n;
+    int a = -1, b = -1;
+    float scale = 0.0f;
+    const float* host = nullptr;  // K_INPUT with host data
+    const float* dev = nullptr;   // K_INPUT with device data
+    std::vector<float> taps;      // K_INPUT that holds a FIR's coefficients (copied)
+    bool is_taps = false;
+};
+
+}  // namespace
+
+struct simtgo_tile_graph {
+    std::vector<Node> nodes;
+    std::string err;
+};
+
+namespace {
+
+using tilek::Insn;
+using tilek::Program;
+
+void latch(simtgo_tile_graph* g, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+void latch(simtgo_tile_graph* g, const char* fmt, ...) {
+    if (!g->err.empty()) return;  // the first error is kept (tile/tile.go:78-82)
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g->err = std::string("tile: ") + buf;
+}
+
+bool valid(const simtgo_tile_graph* g, simtgo_tensor t) {
+    return g && t >= 0 && (size_t)t < g->nodes.size();
+}
+
+simtgo_tensor add_node(simtgo_tile_graph* g, Node nd) {
+    g->nodes.push_back(std::move(nd));
+    return (simtgo_tensor)(g->nodes.size() - 1);
+}
+
+bool contains_fir(const simtgo_tile_graph* g, int id) {
+    const Node& n = g->nodes[id];
+    if (n.kind == K_FIR) return true;
+    if (n.a >= 0 && contains_fir(g, n.a)) return true;
+    if (n.b >= 0 && contains_fir(g, n.b)) return true;
+    return false;
+}
+
+// postorder (tile/codegen.go:135-144): dependencies first, each node once.
+void postorder(const simtgo_tile_graph* g, int id, std::vector<int>& out, std::vector<char>& seen,
+               bool stop_at_fir) {
+    if (seen[id]) return;
+    seen[id] = 1;
+    const Node& n = g->nodes[id];
+    if (!(stop_at_fir && n.kind == K_FIR)) {
+        if (n.a >= 0) postorder(g, n.a, out, seen, stop_at_fir);
+        if (n.b >= 0) postorder(g, n.b, out, seen, stop_at_fir);
+    }
+    out.push_back(id);
+}
+
+struct Lowered {
+    Program prog;
+    std::vector<int> in_nodes;   // data input node ids, in prog.in order
+    std::vector<int> fir_nodes;  // window node ids, in prog.fir order
+    std::vector<int> param_of;   // reference parameter index pK of each data input
+};
+
+// Emits one program computing `root` (main: root's value, window nodes read
+// from their tiles; staging: a window's signal, stopped at nothing since a
+// signal contains no window). Register slots are assigned linearly over the
+// postorder; a slot is reused as soon as its value has no uses left.
+int emit_program(const simtgo_tile_graph* g, int root, bool main, Lowered& L, bool hoist,
+                 std::unordered_map<int, int>& input_index,
+                 std::unordered_map<int, int>& fir_index, std::vector<Insn>& code) {
+    std::vector<int> order;
+    std::vector<char> seen(g->nodes.size(), 0);
+    postorder(g, root, order, seen, main);
+    std::vector<int> uses(g->nodes.size(), 0);
+    for (int id : order) {
+        const Node& n = g->nodes[id];
+        if (main && n.kind == K_FIR) continue;
+        if (n.kind == K_INPUT) continue;
+        if (n.a >= 0) uses[n.a]++;
+        if (n.b >= 0) uses[n.b]++;
+    }
+    std::vector<int> slot(g->nodes.size(), -1);
+    bool free_slot[tilek::kSlots];
+    for (bool& f : free_slot) f = true;
+    auto alloc = [&]() -> int {
+        for (int s = 0; s < tilek::kSlots; s++)
+            if (free_slot[s]) {
+                free_slot[s] = false;
+                return s;
+            }
+        return -1;
+    };
+    auto push = [&](uint16_t c, uint16_t aux = 0, float imm = 0.0f) {
+        code.push_back(Insn{c, aux, imm});
+    };
+    auto load = [&](int id) -> int {
+        int s = alloc();
+        if (s < 0) return -1;
+        auto it = input_index.find(id);
+        int k;
+        if (it == input_index.end()) {
+            k = (int)L.in_nodes.size();
+            if (k >= tilek::kMaxIn) return -2;
+            input_index[id] = k;
+            L.in_nodes.push_back(id);
+        } else {
+            k = it->second;
+        }
+        push(tilek::OP_LOAD + s, (uint16_t)k);
+        slot[id] = s;
+        return s;
+    };
+    if (hoist)
+        for (int id : order)
+            if (g->nodes[id].kind == K_INPUT && slot[id] < 0)
+                if (load(id) < 0) return -1;
+    auto need = [&](int id) -> int {
+        if (slot[id] >= 0) return slot[id];
+        return load(id);  // not hoisted
+    };
+    auto release = [&](int id) {
+        if (--uses[id] == 0 && slot[id] >= 0) free_slot[slot[id]] = true;
+    };
+    for (int id : order) {
+        const Node& n = g->nodes[id];
+        if (n.kind == K_INPUT) {
+            if (id == root && need(id) < 0) return -1;
+            continue;
+        }
+        if (main && n.kind == K_FIR) {
+            int d = alloc();
+            if (d < 0) return -1;
+            auto it = fir_index.find(id);
+            if (it == fir_index.end()) return -3;
+            push(tilek::OP_FIRACC + d, (uint16_t)it->second);
+            slot[id] = d;
+            continue;
+        }
+        if (n.kind == K_FIR) return -3;  // a window inside a signal is refused at build
+        const bool unary = (n.kind == K_SCALE || n.kind == K_SQRT || n.kind == K_ABS);
+        const int sa = need(n.a);
+        if (sa < 0) return -1;
+        int d;
+        if (unary) {
+            if (uses[n.a] == 1) {
+                d = sa;
+                slot[n.a] = -1;
+                uses[n.a] = 0;
+            } else {
+                d = alloc();
+                if (d < 0) return -1;
+                push(tilek::OP_MOV + 8 * d + sa);
+                release(n.a);
+            }
+            if (n.kind == K_SCALE) push(tilek::OP_SCALE + d, 0, n.scale);
+            if (n.kind == K_SQRT) push(tilek::OP_SQRT + d);
+            if (n.kind == K_ABS) push(tilek::OP_ABS + d);
+        } else {
+            const int sb = need(n.b);
+            if (sb < 0) return -1;
+            const uint16_t base = n.kind == K_ADD ? tilek::OP_ADD
+                                  : n.kind == K_MUL ? tilek::OP_MUL
+                                                    : tilek::OP_HYPOT;
+            if (n.a == n.b) {
+                if (uses[n.a] == 2) {
+                    d = sa;
+                    slot[n.a] = -1;
+                    uses[n.a] = 0;
+                } else {
+                    d = alloc();
+                    if (d < 0) return -1;
+                    push(tilek::OP_MOV + 8 * d + sa);
+                    release(n.a);
+                    release(n.a);
+                }
+                push(base + 8 * d + d);
+            } else if (uses[n.a] == 1) {
+                d = sa;
+                slot[n.a] = -1;
+                uses[n.a] = 0;
+                push(base + 8 * d + sb);
+                release(n.b);
+            } else if (uses[n.b] == 1) {
+                // Add, Mul and Hypot are commutative bit for bit.
+                d = sb;
+                slot[n.b] = -1;
+                uses[n.b] = 0;
+                push(base + 8 * d + sa);
+                release(n.a);
+            } else {
+                d = alloc();
+                if (d < 0) return -1;
+                push(tilek::OP_MOV + 8 * d + sa);
+                push(base + 8 * d + sb);
+                release(n.a);
+                release(n.b);
+            }
+        }
+        slot[id] = d;
+    }
+    push((main ? tilek::OP_STORE : tilek::OP_STAGE) + slot[root]);
+    push(tilek::OP_END);
+    return 0;
+}
+
+// Lowers the graph rooted at t. Returns 0 or a status (message recorded).
+int lower(const simtgo_tile_graph* g, int root, Lowered& L) {
+    memset(&L.prog, 0, sizeof L.prog);
+    L.in_nodes.clear();
+    L.fir_nodes.clear();
+    L.param_of.clear();
+    // The reference's parameter numbering: every input node, taps included,
+    // in postorder (tile/codegen.go:24-35).
+    {
+        std::vector<int> order;
+        std::vector<char> seen(g->nodes.size(), 0);
+        postorder(g, root, order, seen, false);
+        int p = 0;
+        std::unordered_map<int, int> pidx;
+        for (int id : order)
+            if (g->nodes[id].kind == K_INPUT) pidx[id] = p++;
+        for (int id : order)
+            if (g->nodes[id].kind == K_FIR) L.fir_nodes.push_back(id);
+        L.param_of.resize(g->nodes.size(), -1);
+        for (auto& kv : pidx) L.param_of[kv.first] = kv.second;
+    }
+    if ((int)L.fir_nodes.size() > tilek::kMaxFir)
+        return sg::fail(SIMTGO_ESIZE, "tile: %zu windowed operations; the fused kernel stages at most %d",
+                        L.fir_nodes.size(), tilek::kMaxFir);
+    std::unordered_map<int, int> fir_index;
+    for (size_t i = 0; i < L.fir_nodes.size(); i++) fir_index[L.fir_nodes[i]] = (int)i;
+    for (int hoist = 1; hoist >= 0; hoist--) {
+        std::vector<Insn> code;
+        std::unordered_map<int, int> input_index;
+        L.in_nodes.clear();
+        int rc = 0;
+        for (size_t f = 0; f < L.fir_nodes.size() && rc == 0; f++) {
+            const Node& fn = g->nodes[L.fir_nodes[f]];
+            L.prog.fir[f].start = (int32_t)code.size();
+            const std::vector<float>& h = g->nodes[fn.b].taps;
+            L.prog.fir[f].taps = (int32_t)h.size();
+            for (size_t k = 0; k < h.size(); k++) L.prog.fir[f].h[k] = h[k];
+            rc = emit_program(g, fn.a, false, L, hoist, input_index, fir_index, code);
+        }
+        if (rc == 0) {
+            L.prog.main_start = (int32_t)code.size();
+            rc = emit_program(g, root, true, L, hoist, input_index, fir_index, code);
+        }
+        if (rc == -2)
+            return sg::fail(SIMTGO_ESIZE, "tile: more than %d distinct inputs", tilek::kMaxIn);
+        if (rc == -3) return sg::fail(SIMTGO_EGRAPH, "tile: a windowed operation inside a window");
+        if (rc == -1) continue;  // out of slots: retry without hoisting the loads
+        if (code.size() > (size_t)tilek::kMaxCode)
+            return sg::fail(SIMTGO_ESIZE, "tile: the program has %zu instructions (max %d)",
+                            code.size(), tilek::kMaxCode);
+        memcpy(L.prog.code, code.data(), code.size() * sizeof(Insn));
+        L.prog.n_code = (int32_t)code.size();
+        L.prog.n_fir = (int32_t)L.fir_nodes.size();
+        L.prog.n_in = (int32_t)L.in_nodes.size();
+        return 0;
+    }
+    return sg::fail(SIMTGO_ESIZE,
+                    "tile: the graph keeps more than %d values live at once; materialise part of it",
+                    tilek::kSlots);
+}
+
+// Launches a lowered program. dev_in[k] = device data of L.in_nodes[k] (halo
+// elements first).
+int launch_program(Lowered& L, const std::vector<const float*>& dev_in, float* out, int64_t n,
+                   int64_t halo, cudaStream_t s) {
+    const sg::DevInfo* d;
+    int rc;
+    if ((rc = sg::current_device(&d))) return rc;
+    if (n <= 0) return 0;
+    bool vec = sg::aligned16(out);
+    for (size_t k = 0; k < dev_in.size(); k++) {
+        L.prog.in[k] = dev_in[k] + halo;
+        vec = vec && sg::aligned16(L.prog.in[k]);
+    }
+    const size_t smem = (size_t)L.prog.n_fir * (tilek::kMaxTaps + tilek::kTileF) * sizeof(float);
+    if (smem > 48 * 1024) {
+        rc = sg::cuda_status(cudaFuncSetAttribute(tilek::k_tile,
+                                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                  (int)smem),
+                             "cudaFuncSetAttribute(tile)");
+        if (rc) return rc;
+    }
+    const int64_t chunks = sg::ceil_div(n, tilek::kChunk);
+    const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(chunks, (int64_t)d->sms * 4));
+    tilek::k_tile<<<blocks, tilek::kThreads, smem, s>>>(L.prog, out, n, halo, vec);
+    return sg::launch_status("tile");
+}
+
+struct DevBuf {
+    float* p = nullptr;
+    ~DevBuf() {
+        if (p) cudaFree(p);
+    }
+};
+
+int upload(const float* host, int64_t n, DevBuf& b) {
+    int rc = sg::cuda_status(cudaMalloc(&b.p, std::max<int64_t>(n, 1) * sizeof(float)),
+                             "cudaMalloc");
+    if (rc) return rc;
+    if (n > 0)
+        rc = sg::cuda_status(cudaMemcpy(b.p, host, n * sizeof(float), cudaMemcpyHostToDevice),
+                             "upload");
+    return rc;
+}
+
+// tile/alias.go:42-78: the output may not overlap an input it reads.
+int check_out_alias(const Lowered& L, const simtgo_tile_graph* g, const float* out, int64_t n,
+                    const std::vector<const float*>& dev_in, int64_t halo) {
+    const uintptr_t o0 = (uintptr_t)out, o1 = o0 + (uintptr_t)n * 4;
+    for (size_t k = 0; k < dev_in.size(); k++) {
+        const Node& nd = g->nodes[L.in_nodes[k]];
+        const uintptr_t i0 = (uintptr_t)dev_in[k], i1 = i0 + (uintptr_t)(nd.n + halo) * 4;
+        if (o0 >= i1 || i0 >= o1) continue;
+        return sg::fail(SIMTGO_EALIAS,
+                        "tile: the output buffer overlaps input p%d, which the kernel reads while "
+                        "it writes out; the generated kernel declares every pointer __restrict__, "
+                        "which promises that they do not overlap",
+                        L.param_of[L.in_nodes[k]]);
+    }
+    return 0;
+}
+
+// Runs the fused program for root with inputs resolved by `resolve`
+// (node id -> device pointer).
+template <class Resolve>
+int run_fused(const simtgo_tile_graph* g, int root, float* out, int64_t n, int64_t halo,
+              cudaStream_t s, Resolve resolve, bool check_alias) {
+    Lowered L;
+    int rc = lower(g, root, L);
+    if (rc) return rc;
+    std::vector<const float*> dev_in;
+    for (int id : L.in_nodes) {
+        const float* p = resolve(id);
+        if (!p) return sg::fail(SIMTGO_EARG, "tile: input node %d has no device data", id);
+        dev_in.push_back(p);
+    }
+    if (check_alias && (rc = check_out_alias(L, g, out, n, dev_in, halo))) return rc;
+    return launch_program(L, dev_in, out, n, halo, s);
+}
+
+}  // namespace
+
+extern "C" {
+
+simtgo_tile_graph* simtgo_tile_new(void) { return new simtgo_tile_graph(); }
+
+void simtgo_tile_free(simtgo_tile_graph* g) { delete g; }
+
+simtgo_tensor simtgo_tile_input(simtgo_tile_graph* g, const float* host, int32_t n) {
+    if (!g) return -1;
+    if (n < 0) latch(g, "Input: negative length %d", n);
+    if (n > 0 && !host) latch(g, "Input: null data for %d elements", n);
+    Node nd;
+    nd.kind = K_INPUT;
+    nd.n = std::max(n, 0);
+    nd.host = host;
+    return add_node(g, std::move(nd));
+}
+
+simtgo_tensor simtgo_tile_input_device(simtgo_tile_graph* g, const float* dev, int32_t n) {
+    if (!g) return -1;
+    if (n < 0) latch(g, "Input: negative length %d", n);
+    if (n > 0 && !dev) latch(g, "Input: null device data for %d elements", n);
+    Node nd;
+    nd.kind = K_INPUT;
+    nd.n = std::max(n, 0);
+    nd.dev = dev;
+    return add_node(g, std::move(nd));
+}
+
+static simtgo_tensor binary(simtgo_tile_graph* g, simtgo_tensor a, simtgo_tensor b, Kind k,
+                            const char* name) {
+    if (!g) return -1;
+    if (!valid(g, a) || !valid(g, b)) {
+        latch(g, "%s: operands come from different graphs", name);
+        return a;
+    }
+    if (g->nodes[a].n != g->nodes[b].n) {
+        latch(g, "%s: length %d does not match %d", name, g->nodes[a].n, g->nodes[b].n);
+        return a;
+    }
+    Node nd;
+    nd.kind = k;
+    nd.n = g->nodes[a].n;
+    nd.a = a;
+    nd.b = b;
+    return add_node(g, std::move(nd));
+}
+
+simtgo_tensor simtgo_tile_add(simtgo_tile_graph* g, simtgo_tensor a, simtgo_tensor b) {
+    return binary(g, a, b, K_ADD, "Add");
+}
+simtgo_tensor simtgo_tile_mul(simtgo_tile_graph* g, simtgo_tensor a, simtgo_tensor b) {
+    return binary(g, a, b, K_MUL, "Mul");
+}
+simtgo_tensor simtgo_tile_hypot(simtgo_tile_graph* g, simtgo_tensor a, simtgo_tensor b) {
+    return binary(g, a, b, K_HYPOT, "Hypot");
+}
+
+static simtgo_tensor unary(simtgo_tile_graph* g, simtgo_tensor a, Kind k, float scale,
+                           const char* name) {
+    if (!g) return -1;
+    if (!valid(g, a)) {
+        latch(g, "%s: the operand is not a tensor of this graph", name);
+        return a;
+    }
+    Node nd;
+    nd.kind = k;
+    nd.n = g->nodes[a].n;
+    nd.a = a;
+    nd.scale = scale;
+    return add_node(g, std::move(nd));
+}
+
+simtgo_tensor simtgo_tile_scale(simtgo_tile_graph* g, simtgo_tensor a, float k) {
+    return unary(g, a, K_SCALE, k, "Scale");
+}
+simtgo_tensor simtgo_tile_sqrt(simtgo_tile_graph* g, simtgo_tensor a) {
+    return unary(g, a, K_SQRT, 0, "Sqrt");
+}
+simtgo_tensor simtgo_tile_abs(simtgo_tile_graph* g, simtgo_tensor a) {
+    return unary(g, a, K_ABS, 0, "Abs");
+}
+
+simtgo_tensor simtgo_tile_fir(simtgo_tile_graph* g, simtgo_tensor a, const float* h,
+                              int32_t taps) {
+    if (!g) return -1;
+    if (!valid(g, a)) {
+        latch(g, "FIR: the operand is not a tensor of this graph");
+        return a;
+    }
+    if (taps <= 0 || taps > SIMTGO_TILE_MAX_TAPS) {
+        latch(g, "FIR: %d taps is outside 1..%d", taps, SIMTGO_TILE_MAX_TAPS);
+        return a;
+    }
+    if (!h) {
+        latch(g, "FIR: null coefficients");
+        return a;
+    }
+    if (contains_fir(g, a)) {
+        latch(g, "FIR: chaining windowed operations is not supported; materialise the first one");
+        return a;
+    }
+    Node t;
+    t.kind = K_INPUT;
+    t.n = taps;
+    t.taps.assign(h, h + taps);
+    t.is_taps = true;
+    const simtgo_tensor tid = add_node(g, std::move(t));
+    Node f;
+    f.kind = K_FIR;
+    f.n = g->nodes[a].n;
+    f.a = a;
+    f.b = tid;
+    return add_node(g, std::move(f));
+}
+
+int32_t simtgo_tile_len(const simtgo_tile_graph* g, simtgo_tensor t) {
+    return valid(g, t) ? g->nodes[t].n : -1;
+}
+
+int simtgo_tile_err(const simtgo_tile_graph* g) {
+    if (!g) return SIMTGO_ENULL;
+    return g->err.empty() ? SIMTGO_OK : SIMTGO_EGRAPH;
+}
+
+const char* simtgo_tile_err_string(const simtgo_tile_graph* g) {
+    return g ? g->err.c_str() : "tile: null graph";
+}
+
+int simtgo_tile_program_size(simtgo_tile_graph* g, simtgo_tensor t, int32_t* n_instructions,
+                             int32_t* n_inputs, int32_t* n_windows) {
+    sg::clear_error();
+    if (!g) return sg::fail(SIMTGO_ENULL, "tile: null graph");
+    if (!g->err.empty()) return sg::fail(SIMTGO_EGRAPH, "%s", g->err.c_str());
+    if (!valid(g, t)) return sg::fail(SIMTGO_EARG, "tile: unknown tensor %d", t);
+    Lowered L;
+    int rc = lower(g, t, L);
+    if (rc) return rc;
+    if (n_instructions) *n_instructions = L.prog.n_code;
+    if (n_inputs) *n_inputs = L.prog.n_in;
+    if (n_windows) *n_windows = L.prog.n_fir;
+    return 0;
+}
+
+static int check_run(simtgo_tile_graph* g, simtgo_tensor t, int32_t out_len) {
+    if (!g) return sg::fail(SIMTGO_ENULL, "tile: null graph");
+    if (!g->err.empty()) return sg::fail(SIMTGO_EGRAPH, "%s", g->err.c_str());
+    if (!valid(g, t)) return sg::fail(SIMTGO_EARG, "tile: unknown tensor %d", t);
+    if (out_len != g->nodes[t].n)
+        return sg::fail(SIMTGO_ELENGTH, "tile: the output holds %d elements, the tensor has %d",
+                        out_len, g->nodes[t].n);
+    return 0;
+}
+
+int simtgo_tile_materialize(simtgo_tile_graph* g, simtgo_tensor t, float* host_out,
+                            int32_t out_len) {
+    sg::clear_error();
+    int rc;
+    if ((rc = check_run(g, t, out_len))) return rc;
+    const int64_t n = out_len;
+    if (n == 0) return 0;
+    if (!host_out) return sg::fail(SIMTGO_ENULL, "tile: null output");
+    const sg::DevInfo* d;
+    if ((rc = sg::current_device(&d))) return rc;
+    std::vector<DevBuf> owned;
+    std::unordered_map<int, const float*> uploaded;
+    DevBuf out;
+    if ((rc = sg::cuda_status(cudaMalloc(&out.p, n * sizeof(float)), "cudaMalloc"))) return rc;
+    int err = 0;
+    auto resolve = [&](int id) -> const float* {
+        const Node& nd = g->nodes[id];
+        if (nd.dev) return nd.dev;
+        auto it = uploaded.find(id);
+        if (it != uploaded.end()) return it->second;
+        owned.emplace_back();
+        if (int r = upload(nd.host, nd.n, owned.back())) {
+            err = r;
+            return nullptr;
+        }
+        uploaded[id] = owned.back().p;
+        return owned.back().p;
+    };
+    rc = run_fused(g, t, out.p, n, 0, 0, resolve, true);
+    if (err) return err;
+    if (rc) return rc;
+    return sg::cuda_status(cudaMemcpy(host_out, out.p, n * sizeof(float), cudaMemcpyDeviceToHost),
+                           "download");
+}
+
+int simtgo_tile_materialize_stepwise(simtgo_tile_graph* g, simtgo_tensor t, float* host_out,
+                                     int32_t out_len, int32_t* launches) {
+    sg::clear_error();
+    int rc;
+    if (launches) *launches = 0;
+    if ((rc = check_run(g, t, out_len))) return rc;
+    const int64_t n = out_len;
+    if (n > 0 && !host_out) return sg::fail(SIMTGO_ENULL, "tile: null output");
+    const sg::DevInfo* d;
+    if ((rc = sg::current_device(&d))) return rc;
+    // tile/run.go:113 step: every node materialised into a device buffer of
+    // its own, through a one-operation graph over the buffers of its arguments.
+    std::vector<DevBuf> owned;
+    std::unordered_map<int, const float*> buf;
+    std::vector<int> order;
+    std::vector<char> seen(g->nodes.size(), 0);
+    postorder(g, t, order, seen, false);
+    int count = 0;
+    for (int id : order) {
+        const Node& nd = g->nodes[id];
+        if (nd.kind == K_INPUT) {
+            if (nd.is_taps) continue;
+            if (nd.dev) {
+                buf[id] = nd.dev;
+            } else {
+                owned.emplace_back();
+                if ((rc = upload(nd.host, nd.n, owned.back()))) return rc;
+                buf[id] = owned.back().p;
+            }
+            continue;
+        }
+        simtgo_tile_graph one;
+        const int a = simtgo_tile_input_device(&one, buf[nd.a], g->nodes[nd.a].n);
+        int r;
+        if (nd.kind == K_FIR) {
+            const Node& tp = g->nodes[nd.b];
+            r = simtgo_tile_fir(&one, a, tp.taps.data(), (int32_t)tp.taps.size());
+        } else if (nd.kind == K_SCALE) {
+            r = simtgo_tile_scale(&one, a, nd.scale);
+        } else if (nd.kind == K_SQRT) {
+            r = simtgo_tile_sqrt(&one, a);
+        } else if (nd.kind == K_ABS) {
+            r = simtgo_tile_abs(&one, a);
+        } else {
+            // A node feeding both operands is one buffer read twice (tile/run.go:122-127).
+            const int b = nd.b == nd.a ? a
+                                       : simtgo_tile_input_device(&one, buf[nd.b], g->nodes[nd.b].n);
+            r = nd.kind == K_ADD   ? simtgo_tile_add(&one, a, b)
+                : nd.kind == K_MUL ? simtgo_tile_mul(&one, a, b)
+                                   : simtgo_tile_hypot(&one, a, b);
+        }
+        owned.emplace_back();
+        if ((rc = sg::cuda_status(cudaMalloc(&owned.back().p, std::max<int64_t>(nd.n, 1) * 4),
+                                  "cudaMalloc")))
+            return rc;
+        float* outp = owned.back().p;
+        auto resolve = [&](int nid) -> const float* { return one.nodes[nid].dev; };
+        rc = run_fused(&one, r, outp, nd.n, 0, 0, resolve, true);
+        count++;
+        if (launches) *launches = count;
+        if (rc) return rc;
+        buf[id] = outp;
+    }
+    if (n == 0) return 0;
+    if ((rc = sg::cuda_status(cudaDeviceSynchronize(), "stepwise"))) return rc;
+    return sg::cuda_status(
+        cudaMemcpy(host_out, buf[t], n * sizeof(float), cudaMemcpyDeviceToHost), "download");
+}
+
+int simtgo_tile_run_shard(simtgo_tile_graph* g, simtgo_tensor t, float* dev_out,
+                          int32_t out_len, int32_t halo, void* stream) {
+    sg::clear_error();
+    int rc;
+    if ((rc = check_run(g, t, out_len))) return rc;
+    if (halo < 0) return sg::fail(SIMTGO_EARG, "tile: negative halo");
+    if (out_len == 0) return 0;
+    if (!dev_out) return sg::fail(SIMTGO_ENULL, "tile: null output");
+    auto resolve = [&](int id) -> const float* { return g->nodes[id].dev; };
+    return run_fused(g, t, dev_out, out_len, halo, (cudaStream_t)stream, resolve, true);
+}
+
+int simtgo_tile_run(simtgo_tile_graph* g, simtgo_tensor t, float* dev_out, int32_t out_len,
+                    void* stream) {
+    return simtgo_tile_run_shard(g, t, dev_out, out_len, 0, stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,143 @@
+"""The tile track (package tile, tile/tile.go and tile/run.go) over
+libsimtgo_b200.so. The graph is recorded and lowered in the library (C++);
+this module only keeps the host arrays alive and spells the Go API:
+
+    g = tile.New()
+    out = tile.Hypot(tile.FIR(tile.Scale(g.Input(re), 0.5), h), g.Input(im))
+    vals = out.Materialize()                 # tile/run.go:20
+    vals, launches = out.MaterializeStepwise()   # tile/run.go:89
+
+Device-resident values (the `dev` field of tile/tile.go:46):
+    a = g.InputDevice(tensor)               # a CUDA float32 tensor
+    out.Run(dev_out, stream)                 # no upload, no download
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+
+from . import _lib
+from ._lib import GraphError, check
+
+BlockSize = 256   # tile/tile.go:22
+MaxTaps = 64      # tile/tile.go:25
+
+
+class Graph:
+    """tile.Graph: records a pipeline; nothing runs until a materialisation."""
+
+    def __init__(self):
+        self._L = _lib.load()
+        self._h = self._L.simtgo_tile_new()
+        self._keep = []   # host arrays the library points at
+
+    def __del__(self):
+        h, self._h = getattr(self, "_h", None), None
+        if h:
+            self._L.simtgo_tile_free(h)
+
+    def _t(self, node):
+        return Tensor(self, node)
+
+    def Input(self, xs) -> "Tensor":
+        a = np.ascontiguousarray(xs, dtype=np.float32)
+        self._keep.append(a)
+        return self._t(self._L.simtgo_tile_input(self._h, a.ctypes.data_as(C.c_void_p), len(a)))
+
+    def InputDevice(self, t) -> "Tensor":
+        import torch
+
+        if not (isinstance(t, torch.Tensor) and t.is_cuda and t.dtype == torch.float32
+                and t.is_contiguous()):
+            raise TypeError("tile: InputDevice takes a contiguous CUDA float32 tensor")
+        self._keep.append(t)
+        return self._t(self._L.simtgo_tile_input_device(self._h, C.c_void_p(t.data_ptr()),
+                                                        t.numel()))
+
+    def Err(self):
+        """tile/tile.go:163: the first error recorded while building, or None."""
+        if self._L.simtgo_tile_err(self._h) == 0:
+            return None
+        return GraphError(_lib.EGRAPH, self._L.simtgo_tile_err_string(self._h).decode())
+
+
+class Tensor:
+    def __init__(self, g: Graph, node: int):
+        self.g = g
+        self.node = node
+
+    def Len(self) -> int:
+        return self.g._L.simtgo_tile_len(self.g._h, self.node)
+
+    def ProgramSize(self):
+        """(instructions, inputs, windows) of the fused program: the analogue
+        of Tensor.Source (tile/run.go:10), which compiles without running."""
+        a, b, c = C.c_int32(), C.c_int32(), C.c_int32()
+        check(self.g._L.simtgo_tile_program_size(self.g._h, self.node, C.byref(a), C.byref(b),
+                                                 C.byref(c)))
+        return a.value, b.value, c.value
+
+    def Materialize(self) -> np.ndarray:
+        out = np.empty(max(self.Len(), 0), np.float32)
+        check(self.g._L.simtgo_tile_materialize(self.g._h, self.node,
+                                                out.ctypes.data_as(C.c_void_p), len(out)))
+        return out
+
+    def MaterializeStepwise(self):
+        out = np.empty(max(self.Len(), 0), np.float32)
+        n = C.c_int32()
+        check(self.g._L.simtgo_tile_materialize_stepwise(
+            self.g._h, self.node, out.ctypes.data_as(C.c_void_p), len(out), C.byref(n)))
+        return out, n.value
+
+    def Run(self, dev_out, stream=None, halo: int = 0):
+        """Device-resident run into dev_out (CUDA float32 tensor of Len()
+        elements); asynchronous on stream. halo: see simtgo_tile_run_shard."""
+        sp = getattr(stream, "cuda_stream", stream)
+        check(self.g._L.simtgo_tile_run_shard(self.g._h, self.node,
+                                              C.c_void_p(dev_out.data_ptr()), dev_out.numel(),
+                                              int(halo), sp))
+
+
+def New() -> Graph:
+    return Graph()
+
+
+def Add(a: Tensor, b: Tensor) -> Tensor:
+    return a.g._t(a.g._L.simtgo_tile_add(a.g._h, a.node, _same(a, b)))
+
+
+def Mul(a: Tensor, b: Tensor) -> Tensor:
+    return a.g._t(a.g._L.simtgo_tile_mul(a.g._h, a.node, _same(a, b)))
+
+
+def Hypot(a: Tensor, b: Tensor) -> Tensor:
+    return a.g._t(a.g._L.simtgo_tile_hypot(a.g._h, a.node, _same(a, b)))
+
+
+def Scale(a: Tensor, k: float) -> Tensor:
+    return a.g._t(a.g._L.simtgo_tile_scale(a.g._h, a.node, float(k)))
+
+
+def Sqrt(a: Tensor) -> Tensor:
+    return a.g._t(a.g._L.simtgo_tile_sqrt(a.g._h, a.node))
+
+
+def Abs(a: Tensor) -> Tensor:
+    return a.g._t(a.g._L.simtgo_tile_abs(a.g._h, a.node))
+
+
+def FIR(a: Tensor, h) -> Tensor:
+    hh = np.ascontiguousarray(h, dtype=np.float32)
+    return a.g._t(a.g._L.simtgo_tile_fir(a.g._h, a.node, hh.ctypes.data_as(C.c_void_p), len(hh)))
+
+
+def _same(a: Tensor, b: Tensor) -> int:
+    # Operands from different graphs: the library sees an id it cannot
+    # trust, so pass one it will refuse ("operands come from different graphs").
+    return b.node if a.g is b.g else -1
+
+
+__all__ = ["New", "Graph", "Tensor", "Add", "Mul", "Hypot", "Scale", "Sqrt", "Abs", "FIR",
+           "BlockSize", "MaxTaps"]

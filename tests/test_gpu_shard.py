@@ -1,0 +1,117 @@
+"""GPU tests of the long / sharded forms: simtgo_FIR_shard (64-bit extents,
+up to 1024 taps, halos), simtgo_Histogram_shard and the single-rank
+communicator path of simtgo_Histogram_allreduce. Full-size cases are checked
+through properties that do not need the oracle at that size: shards
+concatenate to the whole, totals are conserved, sampled outputs match."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+import oracle_lib as O
+from tolerance import assert_agree, assert_equal
+
+torch = pytest.importorskip("torch")
+from simtgo_b200 import _lib  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+P = C.c_void_p
+
+
+def fir_shard(y, x, halo, h):
+    L = _lib.load()
+    _lib.check(L.simtgo_FIR_shard(P(y.data_ptr()), y.numel(), P(x.data_ptr()), x.numel(), halo,
+                                  P(h.data_ptr()), h.numel(), None))
+    _lib.check(L.simtgo_stream_sync(None))
+
+
+@pytest.mark.parametrize("n,taps,halo", [(1, 1, 0), (8192, 127, 0), (8193, 127, 126),
+                                         (100000, 127, 126), (50000, 1024, 1023),
+                                         (20000, 200, 50), (777, 9, 700), ((1 << 20) + 5, 31, 30)])
+def test_fir_shard_parity(n, taps, halo):
+    rng = np.random.default_rng(n + taps)
+    x = rng.uniform(-1, 1, n + halo).astype(np.float32)
+    h = rng.uniform(-1, 1, taps).astype(np.float32)
+    h /= np.float32(max(1.0, abs(float(h.sum()))))
+    rc, want = O.fir_shard(x, halo, h, n)
+    assert rc == 0
+    for off in (0, 1):
+        xb = torch.empty(n + halo + off, device="cuda")
+        xd = xb[off:]
+        xd.copy_(torch.from_numpy(x))
+        yd = torch.empty(n, device="cuda")
+        fir_shard(yd, xd, halo, torch.from_numpy(h).cuda())
+        assert_agree("fir_shard", yd.cpu().numpy(), want)
+
+
+def test_fir_shards_concatenate_to_whole():
+    """Eight shards of one signal, each with a 126-sample halo, equal the
+    unsharded FIR over the whole (127 taps): the 2^31-sample workload's
+    decomposition, at 2^24 samples."""
+    n, taps, G = 1 << 24, 127, 8
+    rng = np.random.default_rng(3)
+    x = torch.from_numpy(rng.uniform(-1, 1, n).astype(np.float32)).cuda()
+    h = torch.from_numpy((rng.uniform(-1, 1, taps) / 10).astype(np.float32)).cuda()
+    whole = torch.empty(n, device="cuda")
+    fir_shard(whole, x, 0, h)
+    per = n // G
+    for g in range(G):
+        lo = g * per
+        halo = min(lo, taps - 1)
+        y = torch.empty(per, device="cuda")
+        fir_shard(y, x[lo - halo: lo + per], halo, h)
+        assert torch.equal(y, whole[lo: lo + per]), f"shard {g}"
+    # sampled outputs against the oracle
+    xs, hs = x.cpu().numpy(), h.cpu().numpy()
+    idx = np.random.default_rng(4).integers(0, n, 2000)
+    ws = whole.cpu().numpy()
+    for i in idx:
+        lo = max(0, i - taps + 1)
+        rc, w = O.fir_shard(xs[lo:i + 1].copy(), i - lo, hs, 1)
+        assert_agree(f"sample {i}", ws[i:i + 1], w)
+
+
+@pytest.mark.parametrize("n", [0, 5, 1 << 20, (1 << 24) + 1])
+def test_histogram_shard(n):
+    rng = np.random.default_rng(n)
+    x = rng.integers(-10, 270, n, dtype=np.int32)
+    rc, want = O.histogram_shard(x)
+    bins = torch.zeros(256, dtype=torch.int32, device="cuda")
+    xd = torch.from_numpy(x).cuda()
+    L = _lib.load()
+    _lib.check(L.simtgo_Histogram_shard(P(bins.data_ptr()), 256, P(xd.data_ptr()) if n else None,
+                                        n, None))
+    _lib.check(L.simtgo_stream_sync(None))
+    assert_equal("bins", bins.cpu().numpy(), want)
+
+
+def test_histogram_full_size_conserves_counts():
+    """2^28 uniform int32 in [0,255] and a Zipf(1.2) draw: every sample is
+    counted once (the bins sum to 2^28) and the bins equal numpy's."""
+    n = 1 << 28
+    g = torch.Generator(device="cuda").manual_seed(4)
+    x = torch.randint(0, 256, (n,), dtype=torch.int32, device="cuda", generator=g)
+    bins = torch.zeros(256, dtype=torch.int32, device="cuda")
+    L = _lib.load()
+    _lib.check(L.simtgo_Histogram_shard(P(bins.data_ptr()), 256, P(x.data_ptr()), n, None))
+    _lib.check(L.simtgo_stream_sync(None))
+    want = torch.bincount(x.long(), minlength=256).to(torch.int32)
+    assert int(bins.sum()) == n
+    assert torch.equal(bins, want)
+
+
+def test_histogram_allreduce_single_rank():
+    L = _lib.load()
+    uid = C.create_string_buffer(128)
+    _lib.check(L.simtgo_comm_unique_id(uid))
+    comm = P()
+    _lib.check(L.simtgo_comm_init(C.byref(comm), uid, 1, 0))
+    try:
+        x = torch.randint(0, 256, (1 << 20,), dtype=torch.int32, device="cuda")
+        bins = torch.zeros(256, dtype=torch.int32, device="cuda")
+        _lib.check(L.simtgo_Histogram_allreduce(comm, P(bins.data_ptr()), 256, P(x.data_ptr()),
+                                                x.numel(), None))
+        _lib.check(L.simtgo_stream_sync(None))
+        assert torch.equal(bins, torch.bincount(x.long(), minlength=256).to(torch.int32))
+    finally:
+        _lib.check(L.simtgo_comm_destroy(comm))

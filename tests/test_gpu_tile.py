@@ -1,0 +1,223 @@
+"""GPU parity of the tile track (package tile): the fused interpreter against
+the oracle's node-by-node evaluation, the stepwise path against the fused
+one, and the reference's own pipeline test (tile/tile_test.go:53-99)."""
+import math
+
+import numpy as np
+import pytest
+
+import oracle_lib as O
+from test_abi import twelve_node_graph
+from tolerance import assert_agree, assert_close
+
+torch = pytest.importorskip("torch")
+from simtgo_b200 import tile  # noqa: E402
+from simtgo_b200._lib import AliasError  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+
+def normal(n, seed):
+    return np.random.default_rng(seed).standard_normal(n).astype(np.float32)
+
+
+class Recorder:
+    """Builds the same graph in the library and as an oracle node table."""
+
+    def __init__(self, device_inputs=False):
+        self.g = tile.New()
+        self.nodes = []
+        self.dev = device_inputs
+        self.keep = []
+
+    def input(self, xs):
+        xs = np.asarray(xs, np.float32)
+        if self.dev:
+            t = torch.from_numpy(xs).cuda()
+            self.keep.append(t)
+            r = self.g.InputDevice(t)
+        else:
+            r = self.g.Input(xs)
+        self.nodes.append({"kind": "input", "data": xs})
+        return r
+
+    def _add(self, r, **nd):
+        assert r.node == len(self.nodes), (r.node, len(self.nodes))
+        self.nodes.append(nd)
+        return r
+
+    def scale(self, a, k):
+        return self._add(tile.Scale(a, k), kind="scale", a=a.node, scale=k)
+
+    def add(self, a, b):
+        return self._add(tile.Add(a, b), kind="add", a=a.node, b=b.node)
+
+    def mul(self, a, b):
+        return self._add(tile.Mul(a, b), kind="mul", a=a.node, b=b.node)
+
+    def hypot(self, a, b):
+        return self._add(tile.Hypot(a, b), kind="hypot", a=a.node, b=b.node)
+
+    def sqrt(self, a):
+        return self._add(tile.Sqrt(a), kind="sqrt", a=a.node)
+
+    def abs(self, a):
+        return self._add(tile.Abs(a), kind="abs", a=a.node)
+
+    def fir(self, a, h):
+        h = np.asarray(h, np.float32)
+        r = tile.FIR(a, h)
+        self.nodes.append({"kind": "input", "data": h})   # the taps node
+        return self._add(r, kind="fir", a=a.node, taps=h)
+
+    def want(self, root, n, halo=0):
+        rc, out = O.tile_eval(self.nodes, root.node, n, halo)
+        assert rc == 0
+        return out
+
+
+def build_twelve(rec, n, seed=6):
+    rng = np.random.default_rng(seed)
+    a, b, c = (rec.input(rng.uniform(-4, 4, n).astype(np.float32)) for _ in range(3))
+    h = np.full(31, 1 / 31, np.float32)
+    s = rec.scale(a, 0.5)
+    ab = rec.abs(b)
+    q = rec.sqrt(ab)
+    m = rec.mul(s, q)
+    d = rec.add(m, c)
+    f = rec.fir(s, h)
+    y = rec.hypot(d, f)
+    return rec.mul(y, ab)
+
+
+@pytest.mark.parametrize("n", [1, 5, 255, 1024, 1025, 4099, 1 << 16, (1 << 20) + 3])
+def test_twelve_node_graph(n):
+    rec = Recorder()
+    out = build_twelve(rec, n)
+    assert rec.g.Err() is None
+    got = out.Materialize()
+    assert_agree("fused vs oracle", got, rec.want(out, n))
+    step, launches = out.MaterializeStepwise()
+    assert launches == 8  # scale, abs, sqrt, mul, add, fir, hypot, mul
+    assert_agree("stepwise vs fused", step, got)
+
+
+def test_reference_pipeline():
+    """tile/tile_test.go:53-99: Hypot(FIR(Scale(re, 0.5), h), im), 2^14
+    samples, 17 taps of 1/17; fused vs a float64 reference at 1e-5, stepwise
+    vs fused at 1e-6, 3 launches."""
+    n = 1 << 14
+    re, im = normal(n, 1), normal(n, 2)
+    h = np.full(17, 1 / 17, np.float32)
+    g = tile.New()
+    filtered = tile.FIR(tile.Scale(g.Input(re), 0.5), h)
+    out = tile.Hypot(filtered, g.Input(im))
+    got = out.Materialize()
+    want = np.zeros(n, np.float32)
+    for i in range(n):
+        acc = np.float32(0)
+        for k in range(17):
+            if i - k >= 0:
+                acc = np.float32(acc + np.float32(h[k] * np.float32(0.5)) * re[i - k])
+        want[i] = np.float32(math.hypot(float(acc), float(im[i])))
+    assert_close("fused vs reference", got, want, 1e-5)
+    step, launches = out.MaterializeStepwise()
+    assert launches == 3
+    assert_close("stepwise vs fused", step, got, 1e-6)
+
+
+@pytest.mark.parametrize("taps", [1, 2, 3, 4, 5, 31, 63, 64])
+def test_fir_node_taps(taps):
+    n = 5000
+    rec = Recorder()
+    x = rec.input(normal(n, 3))
+    h = normal(taps, 4) / taps
+    out = rec.fir(x, h)
+    assert_agree("fir node", out.Materialize(), rec.want(out, n))
+
+
+def test_two_windows_and_shared_nodes():
+    n = 20011
+    rec = Recorder()
+    a, b = rec.input(normal(n, 5)), rec.input(normal(n, 6))
+    s = rec.sqrt(rec.abs(a))
+    f1 = rec.fir(s, normal(7, 7))
+    f2 = rec.fir(rec.add(a, b), normal(40, 8))
+    m = rec.mul(f1, f2)
+    out = rec.hypot(rec.add(m, s), rec.mul(a, a))
+    assert_agree("two windows", out.Materialize(), rec.want(out, n))
+
+
+def test_device_resident_run_and_alias():
+    n = (1 << 18) + 7
+    rec = Recorder(device_inputs=True)
+    out = build_twelve(rec, n, seed=11)
+    dout = torch.empty(n, dtype=torch.float32, device="cuda")
+    out.Run(dout)
+    torch.cuda.synchronize()
+    assert_agree("device run", dout.cpu().numpy(), rec.want(out, n))
+    with pytest.raises(AliasError, match="overlaps input p"):
+        out.Run(rec.keep[0])
+
+
+@pytest.mark.parametrize("halo", [0, 30, 32, 40])
+def test_shard_with_halo(halo):
+    """A shard of the graph: inputs carry `halo` preceding elements; the FIR
+    reads them instead of zeros. Equal to the matching slice of the whole."""
+    n_total, start = 9000, 4000
+    n = 3000
+    rng = np.random.default_rng(12)
+    full = [rng.uniform(-4, 4, n_total).astype(np.float32) for _ in range(3)]
+    # whole-signal reference
+    whole = Recorder()
+    out_w = build_twelve_inputs(whole, full)
+    ref = whole.want(out_w, n_total)
+    # the shard
+    shard = Recorder(device_inputs=True)
+    lo = start - halo
+    out_s = build_twelve_inputs(shard, [x[lo:start + n] for x in full], n_override=n + halo)
+    # rebuild with shard length n and halo-offset device inputs
+    g = tile.New()
+    keep = [torch.from_numpy(x[lo:start + n].copy()).cuda() for x in full]
+    ins = [g.InputDevice(t[halo:]) for t in keep]
+    root = twelve_node_graph(g, *ins, np.full(31, 1 / 31, np.float32))
+    dout = torch.empty(n, dtype=torch.float32, device="cuda")
+    root.Run(dout, halo=halo)
+    torch.cuda.synchronize()
+    got = dout.cpu().numpy()
+    if halo >= 30:
+        assert_agree("shard == slice of whole", got, ref[start:start + n])
+    # and the oracle's own shard evaluation agrees in every case
+    rc, want = O.tile_eval(shard.nodes, out_s.node, n, halo)
+    assert rc == 0
+    assert_agree("shard vs oracle shard", got, want)
+    del out_s
+
+
+def build_twelve_inputs(rec, xs, n_override=None):
+    a, b, c = (rec.input(x) for x in xs)
+    h = np.full(31, 1 / 31, np.float32)
+    s = rec.scale(a, 0.5)
+    ab = rec.abs(b)
+    q = rec.sqrt(ab)
+    m = rec.mul(s, q)
+    d = rec.add(m, c)
+    f = rec.fir(s, h)
+    y = rec.hypot(d, f)
+    return rec.mul(y, ab)
+
+
+def test_input_only_and_unaligned():
+    n = 1001
+    x = normal(n + 1, 13)
+    rec = Recorder()
+    a = rec.input(x[1:])
+    assert_agree("identity", a.Materialize(), x[1:])
+    t = torch.from_numpy(x).cuda()
+    g = tile.New()
+    root = tile.Hypot(g.InputDevice(t[1:]), g.InputDevice(t[1:]))
+    out = torch.empty(n, dtype=torch.float32, device="cuda")
+    root.Run(out)
+    torch.cuda.synchronize()
+    want = np.array([O.oracle().oracle_hypot(float(v), float(v)) for v in x[1:]], np.float32)
+    assert_agree("unaligned device inputs", out.cpu().numpy(), want)
