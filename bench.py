@@ -190,11 +190,12 @@ def run_ours(args):
         return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
 
     # ---- the FIR shard -----------------------------------------------------
-    n = 1 << args.fir_log2
-    g0 = rank * n
-    halo = min(HALO, g0)
+    from simtgo_b200 import shard
+
+    plan = shard.fir_plan(world << args.fir_log2, world, rank, TAPS)
+    n, halo = plan.n, plan.halo
     h = torch.from_numpy(fir_taps()).to(dev)
-    x = signal(torch, g0 - halo, n + halo, dev)
+    x = signal(torch, plan.in_lo, plan.in_len, dev)
     y = torch.empty(n, dtype=torch.float32, device=dev)
 
     def fir_step(yb=y, xb=x):
@@ -357,10 +358,10 @@ def timed(fn, steps, warmup, stream, events):
 def bench_histogram(args, torch, L, dev, sp, rank, world, barrier, max_over_ranks, events):
     """2^28 samples in total, uniform over [0,255], split over the ranks;
     each rank counts its part and the bins are all-reduced (NCCL)."""
-    from simtgo_b200 import _lib
+    from simtgo_b200 import _lib, shard
 
     total = 1 << 28
-    n = total // world
+    n = shard.histogram_plan(total, world, rank).n
     gen = torch.Generator(device=dev).manual_seed(4 + rank)
     x = torch.randint(0, 256, (n,), dtype=torch.int32, device=dev, generator=gen)
     bins = torch.zeros(256, dtype=torch.int32, device=dev)
@@ -411,11 +412,11 @@ def twelve(tile, g, a, b, c, h):
 def bench_tile(args, torch, np, L, dev, sp, rank, world, barrier, max_over_ranks, events):
     """3 x 2^28 inputs uniform[-4,4] through the 12-node graph, split over
     the ranks (a 32-element halo for the FIR node)."""
-    from simtgo_b200 import tile
+    from simtgo_b200 import shard, tile
 
     total = 1 << 28
-    n = total // world
-    halo = 32 if rank > 0 else 0
+    plan = shard.tile_plan(total, world, rank, max_taps=31)
+    n, halo = plan.n, plan.halo
     gen = torch.Generator(device=dev).manual_seed(6 + rank)
     ins = [torch.rand(n + halo, device=dev, generator=gen) * 8 - 4 for _ in range(3)]
     g = tile.New()

@@ -246,6 +246,13 @@ const char* simtgo_tile_err_string(const simtgo_tile_graph* g);
 int simtgo_tile_program_size(simtgo_tile_graph* g, simtgo_tensor t, int32_t* n_instructions,
                              int32_t* n_inputs, int32_t* n_windows);
 
+/* tile/run.go:10 Tensor.Source: the program the tensor would be computed by,
+ * as text, without running anything -- here the listing of the lowered
+ * register program (one instruction per line). Writes at most cap bytes
+ * (NUL-terminated) and returns the size the whole listing needs, or a
+ * negative status. */
+int32_t simtgo_tile_source(simtgo_tile_graph* g, simtgo_tensor t, char* buf, int32_t cap);
+
 /* tile/run.go:20 Materialize: upload host inputs, run the one fused kernel,
  * download into host_out (out_len == Len(t)), free what the call allocated.
  * Synchronous. */
@@ -261,10 +268,11 @@ int simtgo_tile_materialize_stepwise(simtgo_tile_graph* g, simtgo_tensor t, floa
  * (tile/alias.go:42). */
 int simtgo_tile_run(simtgo_tile_graph* g, simtgo_tensor t, float* dev_out, int32_t out_len,
                     void* stream);
-/* One shard of the graph's elementwise split: every device input holds the
- * `halo` elements preceding the shard followed by out_len of its own
- * (halo = 0 on the first shard); window (FIR) nodes read the halo instead of
- * zeros. Without a FIR node, halo may be 0 on every shard. */
+/* One shard of the graph's elementwise split: every device input points at
+ * the shard's first own element and has `halo` valid elements in front of
+ * it (ptr[-halo .. -1], the samples preceding the shard; halo = 0 on the
+ * first shard); window (FIR) nodes read them instead of zeros. Without a FIR
+ * node, halo may be 0 on every shard. */
 int simtgo_tile_run_shard(simtgo_tile_graph* g, simtgo_tensor t, float* dev_out,
                           int32_t out_len, int32_t halo, void* stream);
 

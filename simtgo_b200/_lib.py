@@ -76,6 +76,7 @@ _SIGS = {
     "simtgo_tile_err": [_vp],
     "simtgo_tile_err_string": [_vp],
     "simtgo_tile_program_size": [_vp, _i32, C.POINTER(_i32), C.POINTER(_i32), C.POINTER(_i32)],
+    "simtgo_tile_source": [_vp, _i32, C.c_char_p, _i32],
     "simtgo_tile_materialize": [_vp, _i32, _vp, _i32],
     "simtgo_tile_materialize_stepwise": [_vp, _i32, _vp, _i32, C.POINTER(_i32)],
     "simtgo_tile_run": [_vp, _i32, _vp, _i32, _vp],

@@ -66,6 +66,10 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 
 inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
+// Discards an error left behind by some earlier runtime call of this
+// thread (someone else's), so launch_status reports only the launch that
+// follows. Sticky errors survive this and are reported all the same.
+inline void before_launch() { (void)cudaGetLastError(); }
 // Launch-error check after a <<<>>> launch.
 int launch_status(const char* kernel);
 

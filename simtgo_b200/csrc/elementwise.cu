@@ -61,6 +61,7 @@ int run_ew(const char* name, const Op& op, int64_t nvec, int64_t m, bool vec_ok,
     const int64_t units = vec_ok ? std::max<int64_t>(nvec, 1) : m;
     const int64_t want = sg::ceil_div(units, kThreads);
     const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(want, (int64_t)d->sms * 4));
+    sg::before_launch();
     if (vec_ok)
         k_vec<Op><<<blocks, kThreads, 0, s>>>(op, nvec, m);
     else
@@ -176,16 +177,28 @@ struct SoftclipOp : NoPrologue {
 };
 
 // ---- Classify ----------------------------------------------------------------------
-// The gain depends only on where the first edge with |x| <= edge falls among
-// edges[0..3] (classify.go:37-48: band 0 -> 0.25, 1-2 -> 0.5, 3 -> 0.75,
-// anything later or no match -> 1), so each thread keeps those four edges
-// in registers. The bias, the sequential float32 sum of every edge
-// (classify.go:50-53), is formed once per block by one thread.
+// The gain depends only on the band the search finds (classify.go:37-48:
+// band 0 -> 0.25, 1-2 -> 0.5, 3 -> 0.75, anything else -> 1). A match among
+// edges[0..3] decides it; otherwise the band is 4 or later, or -- with no
+// match at all -- len(edges), so the no-match gain is the switch applied to
+// min(len(edges), 4). Each thread keeps edges[0..3] in registers (a missing
+// edge is NaN, which never matches). The bias, the sequential float32 sum of
+// every edge (classify.go:50-53), is formed once per block by one thread.
+__host__ __device__ inline float classify_gain(int band) {
+    switch (band) {
+        case 0: return 0.25f;
+        case 1:
+        case 2: return 0.5f;
+        case 3: return 0.75f;
+        default: return 1.0f;
+    }
+}
 struct ClassifyOp {
     float* out;
     const float* x;
     const float* edges;
     int32_t n_edges;
+    float gain_none;  // classify_gain(len(edges)): the gain when nothing matches
     static constexpr int W = 4;
     using In = float4;
     // Filled by prologue().
@@ -208,13 +221,15 @@ struct ClassifyOp {
     }
     __device__ float one(float xv) const {
         const float v = fabsf(xv);
-        float gain = 1.0f;
+        float gain;
         if (v <= e0)
             gain = 0.25f;
         else if (v <= e1 || v <= e2)
             gain = 0.5f;
         else if (v <= e3)
             gain = 0.75f;
+        else
+            gain = gain_none;
         return __fadd_rn(__fmul_rn(gain, v), bias001);
     }
     __device__ In load(int64_t v) const { return ld_stream_f4(x + 4 * v); }
@@ -583,6 +598,7 @@ int simtgo_Classify(float* out, int32_t out_len, const float* x, int32_t x_len,
     op.x = x;
     op.edges = edges;
     op.n_edges = edges_len;
+    op.gain_none = classify_gain(edges_len);
     return run_ew(K, op, m / 4, m, sg::aligned16(out) && sg::aligned16(x), stream);
 }
 

@@ -206,6 +206,7 @@ int launch_fir(const char* K, float* y, int64_t y_len, const float* x, int64_t x
     if (rc) return rc;
     const int64_t blocks = sg::ceil_div(y_len, kTileOut);
     if (blocks > 0x7fffffffLL) return sg::fail(SIMTGO_ESIZE, "%s: y_len too large", K);
+    sg::before_launch();
     kern<<<(unsigned)blocks, kThreads, smem, (cudaStream_t)stream>>>(
         map, use_tma, y, x, h, g, sg::aligned16(y), sg::watchdog_device_ptr());
     return sg::launch_status(K);

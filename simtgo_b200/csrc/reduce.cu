@@ -170,6 +170,7 @@ int launch_histogram(const char* K, int32_t* bins, int32_t bins_len, const int32
     if (m <= 0 || bins_len <= 0) return 0;
     const int64_t want = sg::ceil_div(sg::ceil_div(m, 16), kHistThreads);
     const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(want, (int64_t)d->sms * 2));
+    sg::before_launch();
     k_histogram<<<blocks, kHistThreads, 0, (cudaStream_t)stream>>>(bins, bins_len, x, m,
                                                                    sg::aligned16(x));
     return sg::launch_status(K);
@@ -231,6 +232,7 @@ int simtgo_WarpReduceSum(float* out, int32_t out_len, const float* x, int32_t x_
         }
         const int64_t ntiles = sg::ceil_div(tma_rows, kWrRows);
         const int blocks = (int)std::min<int64_t>(ntiles, (int64_t)d->sms * 3);
+        sg::before_launch();
         k_warpreduce_tma<<<blocks, kWrRows, smem, s>>>(map, out, tma_rows,
                                                        sg::watchdog_device_ptr());
         if ((rc = sg::launch_status(K))) return rc;
@@ -239,6 +241,7 @@ int simtgo_WarpReduceSum(float* out, int32_t out_len, const float* x, int32_t x_
         const int64_t rows = m - tma_rows;
         const int blocks = (int)std::max<int64_t>(
             1, std::min<int64_t>(sg::ceil_div(rows, 256), (int64_t)d->sms * 4));
+        sg::before_launch();
         k_warpreduce_rows<<<blocks, 256, 0, s>>>(out, x, x_len, tma_rows, m);
         if ((rc = sg::launch_status(K))) return rc;
     }

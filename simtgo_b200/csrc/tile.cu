@@ -582,7 +582,7 @@ int launch_program(Lowered& L, const std::vector<const float*>& dev_in, float* o
     if (n <= 0) return 0;
     bool vec = sg::aligned16(out);
     for (size_t k = 0; k < dev_in.size(); k++) {
-        L.prog.in[k] = dev_in[k] + halo;
+        L.prog.in[k] = dev_in[k];  // element 0 of the shard; [-halo, 0) precede it
         vec = vec && sg::aligned16(L.prog.in[k]);
     }
     const size_t smem = (size_t)L.prog.n_fir * (tilek::kMaxTaps + tilek::kTileF) * sizeof(float);
@@ -595,12 +595,23 @@ int launch_program(Lowered& L, const std::vector<const float*>& dev_in, float* o
     }
     const int64_t chunks = sg::ceil_div(n, tilek::kChunk);
     const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(chunks, (int64_t)d->sms * 4));
+    sg::before_launch();
     tilek::k_tile<<<blocks, tilek::kThreads, smem, s>>>(L.prog, out, n, halo, vec);
     return sg::launch_status("tile");
 }
 
+// A device allocation owned by one materialisation. Move-only: a container
+// that relocates it must not free the memory it still refers to.
 struct DevBuf {
     float* p = nullptr;
+    DevBuf() = default;
+    DevBuf(const DevBuf&) = delete;
+    DevBuf& operator=(const DevBuf&) = delete;
+    DevBuf(DevBuf&& o) noexcept : p(o.p) { o.p = nullptr; }
+    DevBuf& operator=(DevBuf&& o) noexcept {
+        std::swap(p, o.p);
+        return *this;
+    }
     ~DevBuf() {
         if (p) cudaFree(p);
     }
@@ -622,7 +633,7 @@ int check_out_alias(const Lowered& L, const simtgo_tile_graph* g, const float* o
     const uintptr_t o0 = (uintptr_t)out, o1 = o0 + (uintptr_t)n * 4;
     for (size_t k = 0; k < dev_in.size(); k++) {
         const Node& nd = g->nodes[L.in_nodes[k]];
-        const uintptr_t i0 = (uintptr_t)dev_in[k], i1 = i0 + (uintptr_t)(nd.n + halo) * 4;
+        const uintptr_t i0 = (uintptr_t)(dev_in[k] - halo), i1 = (uintptr_t)(dev_in[k] + nd.n);
         if (o0 >= i1 || i0 >= o1) continue;
         return sg::fail(SIMTGO_EALIAS,
                         "tile: the output buffer overlaps input p%d, which the kernel reads while "
@@ -796,6 +807,60 @@ int simtgo_tile_program_size(simtgo_tile_graph* g, simtgo_tensor t, int32_t* n_i
     return 0;
 }
 
+// The listing of a lowered program, one instruction per line:
+//   "window <f> taps <T>" / "main" section headers, then
+//   "<pc> load r<d> in<k>", "scale r<d> <k as %a>", "sqrt r<d>", "abs r<d>",
+//   "mov r<d> r<s>", "add|mul|hypot r<d> r<s>", "firacc r<d> w<f>",
+//   "store r<s>", "stage r<s>", "end".
+static std::string listing(const simtgo_tile_graph* g, const Lowered& L) {
+    std::string s;
+    char line[160];
+    snprintf(line, sizeof line, "; simtgo_b200 tile program: %d instructions, %d inputs, %d windows\n",
+             L.prog.n_code, L.prog.n_in, L.prog.n_fir);
+    s += line;
+    for (int k = 0; k < L.prog.n_in; k++) {
+        snprintf(line, sizeof line, "; in%d = node %d (p%d)\n", k, L.in_nodes[k],
+                 L.param_of[L.in_nodes[k]]);
+        s += line;
+    }
+    for (int pc = 0; pc < L.prog.n_code; pc++) {
+        for (int f = 0; f < L.prog.n_fir; f++)
+            if (L.prog.fir[f].start == pc) {
+                snprintf(line, sizeof line, "window %d taps %d node %d\n", f, L.prog.fir[f].taps,
+                         L.fir_nodes[f]);
+                s += line;
+            }
+        if (pc == L.prog.main_start) s += "main\n";
+        const Insn& in = L.prog.code[pc];
+        const int c = in.code;
+        using namespace tilek;
+        if (c == OP_END)
+            snprintf(line, sizeof line, "%d end\n", pc);
+        else if (c < OP_STORE)
+            snprintf(line, sizeof line, "%d load r%d in%d\n", pc, c - OP_LOAD, in.aux);
+        else if (c < OP_STAGE)
+            snprintf(line, sizeof line, "%d store r%d\n", pc, c - OP_STORE);
+        else if (c < OP_FIRACC)
+            snprintf(line, sizeof line, "%d stage r%d\n", pc, c - OP_STAGE);
+        else if (c < OP_SCALE)
+            snprintf(line, sizeof line, "%d firacc r%d w%d\n", pc, c - OP_FIRACC, in.aux);
+        else if (c < OP_SQRT)
+            snprintf(line, sizeof line, "%d scale r%d %a\n", pc, c - OP_SCALE, (double)in.imm);
+        else if (c < OP_ABS)
+            snprintf(line, sizeof line, "%d sqrt r%d\n", pc, c - OP_SQRT);
+        else if (c < OP_MOV)
+            snprintf(line, sizeof line, "%d abs r%d\n", pc, c - OP_ABS);
+        else {
+            const char* name = c < OP_ADD ? "mov" : c < OP_MUL ? "add" : c < OP_HYPOT ? "mul" : "hypot";
+            const int base = c < OP_ADD ? OP_MOV : c < OP_MUL ? OP_ADD : c < OP_HYPOT ? OP_MUL : OP_HYPOT;
+            snprintf(line, sizeof line, "%d %s r%d r%d\n", pc, name, (c - base) / 8, (c - base) % 8);
+        }
+        s += line;
+    }
+    (void)g;
+    return s;
+}
+
 static int check_run(simtgo_tile_graph* g, simtgo_tensor t, int32_t out_len) {
     if (!g) return sg::fail(SIMTGO_ENULL, "tile: null graph");
     if (!g->err.empty()) return sg::fail(SIMTGO_EGRAPH, "%s", g->err.c_str());
@@ -804,6 +869,23 @@ static int check_run(simtgo_tile_graph* g, simtgo_tensor t, int32_t out_len) {
         return sg::fail(SIMTGO_ELENGTH, "tile: the output holds %d elements, the tensor has %d",
                         out_len, g->nodes[t].n);
     return 0;
+}
+
+int32_t simtgo_tile_source(simtgo_tile_graph* g, simtgo_tensor t, char* buf, int32_t cap) {
+    sg::clear_error();
+    if (!g) return sg::fail(SIMTGO_ENULL, "tile: null graph");
+    if (!g->err.empty()) return sg::fail(SIMTGO_EGRAPH, "%s", g->err.c_str());
+    if (!valid(g, t)) return sg::fail(SIMTGO_EARG, "tile: unknown tensor %d", t);
+    Lowered L;
+    int rc = lower(g, t, L);
+    if (rc) return rc;
+    const std::string s = listing(g, L);
+    if (buf && cap > 0) {
+        const size_t n = std::min<size_t>(s.size(), (size_t)cap - 1);
+        memcpy(buf, s.data(), n);
+        buf[n] = 0;
+    }
+    return (int32_t)s.size() + 1;
 }
 
 int simtgo_tile_materialize(simtgo_tile_graph* g, simtgo_tensor t, float* host_out,

@@ -129,6 +129,7 @@ extern "C" int simtgo_Transpose(float* out, int32_t out_len, const float* in, in
     if ((rc = sg::current_device(&d))) return rc;
     const bool vec_in = sg::aligned16(in) && (w % 4 == 0);
     const bool vec_out = sg::aligned16(out) && (h % 4 == 0);
+    sg::before_launch();
     k_transpose<<<(unsigned)tiles, kThreads, 0, (cudaStream_t)stream>>>(out, in, w, h, xcov, ycov,
                                                                        tiles_x, vec_in, vec_out);
     return sg::launch_status(K);

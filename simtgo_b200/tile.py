@@ -78,6 +78,16 @@ class Tensor:
                                                  C.byref(c)))
         return a.value, b.value, c.value
 
+    def Source(self) -> str:
+        """tile/run.go:10: the program this tensor would be computed by,
+        without running it (the listing of the lowered register program)."""
+        L, g = self.g._L, self.g._h
+        need = L.simtgo_tile_source(g, self.node, None, 0)
+        check(need if need < 0 else 0)
+        buf = C.create_string_buffer(need)
+        L.simtgo_tile_source(g, self.node, buf, need)
+        return buf.value.decode()
+
     def Materialize(self) -> np.ndarray:
         out = np.empty(max(self.Len(), 0), np.float32)
         check(self.g._L.simtgo_tile_materialize(self.g._h, self.node,
