@@ -60,7 +60,7 @@ inline int tile_rows(int taps) {
 
 template <int SH>
 __device__ __forceinline__ void fir_chunk(const uint8_t* tile, const float* hs, int k0, int nk,
-                                          int s4, float (&acc)[kPerThread]) {
+                                          int s4, float2 (&acc)[kPerThread / 2]) {
     // Window floats wv[i] = tile position s4 + i, i < 44.
     float wv[kWin];
 #pragma unroll
@@ -76,19 +76,19 @@ __device__ __forceinline__ void fir_chunk(const uint8_t* tile, const float* hs, 
     const float4 ha = *reinterpret_cast<const float4*>(hs + k0);
     const float4 hb = *reinterpret_cast<const float4*>(hs + k0 + 4);
     const float hv[kChunk] = {ha.x, ha.y, ha.z, ha.w, hb.x, hb.y, hb.z, hb.w};
-    if (nk == kChunk) {
+    // Outputs 2i and 2i+1 advance together through one packed FP32 FMA
+    // (fma.rn.f32x2): each lane is exactly fmaf, so every output keeps its
+    // own k-ordered chain while the FMA work takes half the issue slots.
 #pragma unroll
-        for (int u = 0; u < kChunk; u++)
+    for (int u = 0; u < kChunk; u++) {
+        if (nk == kChunk || u < nk) {
+            const float2 hh = make_float2(hv[u], hv[u]);
 #pragma unroll
-            for (int r = 0; r < kPerThread; r++)
-                acc[r] = __fmaf_rn(hv[u], wv[SH + 7 - u + r], acc[r]);
-    } else {
-#pragma unroll
-        for (int u = 0; u < kChunk; u++)
-            if (u < nk)
-#pragma unroll
-                for (int r = 0; r < kPerThread; r++)
-                    acc[r] = __fmaf_rn(hv[u], wv[SH + 7 - u + r], acc[r]);
+            for (int i = 0; i < kPerThread / 2; i++)
+                acc[i] = __ffma2_rn(hh,
+                                    make_float2(wv[SH + 7 - u + 2 * i], wv[SH + 8 - u + 2 * i]),
+                                    acc[i]);
+        }
     }
 }
 
@@ -146,9 +146,9 @@ __global__ void __launch_bounds__(kThreads, 2) k_fir(const __grid_constant__ CUt
     }
     __syncthreads();
 
-    float acc[kPerThread];
+    float2 acc[kPerThread / 2];  // acc[i] = outputs (2i, 2i+1) of this thread
 #pragma unroll
-    for (int r = 0; r < kPerThread; r++) acc[r] = 0.0f;
+    for (int i = 0; i < kPerThread / 2; i++) acc[i] = make_float2(0.0f, 0.0f);
     const int sbase = g.D + 32 * tid - 7 - SH;  // s4 at k0 = 0
     for (int k0 = 0; k0 < g.taps; k0 += kChunk)
         fir_chunk<SH>(tile, hs, k0, min(kChunk, g.taps - k0), sbase - k0, acc);
@@ -157,12 +157,12 @@ __global__ void __launch_bounds__(kThreads, 2) k_fir(const __grid_constant__ CUt
     if (vec_out && j0 + kPerThread <= g.y_len) {
 #pragma unroll
         for (int c = 0; c < kPerThread / 4; c++)
-            st_stream_f4(y + j0 + 4 * c,
-                         make_float4(acc[4 * c], acc[4 * c + 1], acc[4 * c + 2], acc[4 * c + 3]));
+            st_stream_f4(y + j0 + 4 * c, make_float4(acc[2 * c].x, acc[2 * c].y,
+                                                     acc[2 * c + 1].x, acc[2 * c + 1].y));
     } else {
 #pragma unroll
         for (int r = 0; r < kPerThread; r++)
-            if (j0 + r < g.y_len) y[j0 + r] = acc[r];
+            if (j0 + r < g.y_len) y[j0 + r] = (r & 1) ? acc[r / 2].y : acc[r / 2].x;
     }
 }
 

@@ -11,10 +11,13 @@
 //  * every instruction is warp-uniform, and each (operation, slot, slot)
 //    combination is its own case of one switch, so all slot indices are
 //    compile-time and values never leave registers;
-//  * inputs are read once with 16-byte streaming loads, hoisted to the start
-//    of the program so they are all in flight together, and the result is
-//    written once: 4 bytes per input and 4 bytes out per element, one pass
-//    over HBM;
+//  * every input is read from HBM once: a block's chunk of each input (plus
+//    the windows' halo) is brought into shared memory by cp.async.bulk,
+//    double-buffered so the next chunk streams in while this one is
+//    interpreted (inputs that are not 16-byte aligned are loaded directly,
+//    with the loads hoisted to the program's start); the result is written
+//    once with 16-byte streaming stores -- 4 bytes per input and 4 bytes out
+//    per element, one pass over HBM;
 //  * a windowed (FIR) node is evaluated as in tile/codegen.go:80-108: its
 //    signal sub-expression is run by the same interpreter over the block's
 //    span plus a halo of taps-1 (zero outside the signal), staged in shared
@@ -34,6 +37,7 @@
 
 #include "common.cuh"
 #include "exact.cuh"
+#include "tma.cuh"
 
 using namespace sgd;
 
@@ -84,7 +88,7 @@ struct Program {
     int32_t n_in;
     int32_t n_code;
     FirDesc fir[kMaxFir];
-    const float* in[kMaxIn];  // each already offset by the halo: in[k][i], i in [-halo, n)
+    const float* in[kMaxIn];  // element 0 of each input; in[k][i] is valid for i in [-halo, n)
     Insn code[kMaxCode];
 };
 
@@ -92,17 +96,34 @@ struct Exec {
     int64_t p0;     // first of the thread's 4 positions
     int64_t n;      // shard length
     int64_t halo;   // positions [-halo, n) are valid
-    bool vec;       // all inputs (+halo) and out are 16-byte aligned
+    bool vec;       // all inputs and out are 16-byte aligned
     float* out;
     float* stage;   // STAGE target (tile + offset of p0)
     const float* taps_s;
     const float* tiles;
     int64_t cb;     // chunk base (for FIRACC)
+    // Inputs staged in shared memory (bulk-copy mode), or null: position p
+    // of input k is sin[k * sstride + (p - sorg)].
+    const float* sin;
+    int64_t sorg;
+    int32_t sstride;
 };
 
-__device__ __forceinline__ float4 load_pos(const float* base, const Exec& x) {
+__device__ __forceinline__ float4 load_pos(const Program& P, int k, const Exec& x) {
     const int64_t p = x.p0;
-    if (x.vec && p >= -x.halo && p + 3 < x.n) return ld_stream_f4(base + p);
+    const bool inside = p >= -x.halo && p + 3 < x.n;
+    if (x.sin) {
+        // Shared memory: always one aligned 16-byte load; lanes outside the
+        // signal read whatever the buffer holds there and are zeroed.
+        const float4 v = *reinterpret_cast<const float4*>(x.sin + (int64_t)k * x.sstride + (p - x.sorg));
+        if (inside) return v;
+        return make_float4((p + 0 >= -x.halo && p + 0 < x.n) ? v.x : 0.0f,
+                           (p + 1 >= -x.halo && p + 1 < x.n) ? v.y : 0.0f,
+                           (p + 2 >= -x.halo && p + 2 < x.n) ? v.z : 0.0f,
+                           (p + 3 >= -x.halo && p + 3 < x.n) ? v.w : 0.0f);
+    }
+    const float* base = P.in[k];
+    if (x.vec && inside) return ld_stream_f4(base + p);
     float4 v;
     v.x = (p + 0 >= -x.halo && p + 0 < x.n) ? base[p + 0] : 0.0f;
     v.y = (p + 1 >= -x.halo && p + 1 < x.n) ? base[p + 1] : 0.0f;
@@ -144,7 +165,7 @@ __device__ __forceinline__ float4 fir_acc(const Program& P, int f, const Exec& x
     const float* tile = x.tiles + f * kTileF;
     const float* h = x.taps_s + f * kMaxTaps;
     const int64_t q0 = x.p0 - tile_start(x.cb, taps);  // tile index of p0, = 0 mod 4
-    float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+    float2 a01 = make_float2(0.0f, 0.0f), a23 = make_float2(0.0f, 0.0f);
     for (int k0 = 0; k0 < taps; k0 += 4) {
         const float* w = tile + (q0 - k0 - 4);
         const float4 lo = *reinterpret_cast<const float4*>(w);
@@ -156,15 +177,15 @@ __device__ __forceinline__ float4 fir_acc(const Program& P, int f, const Exec& x
 #pragma unroll
         for (int u = 0; u < 4; u++) {
             if (u < nk) {
-                // output e at tap k0+u reads position p0 + e - k0 - u = wv[4 + e - u]
-                a0 = __fmaf_rn(hv[u], wv[4 - u], a0);
-                a1 = __fmaf_rn(hv[u], wv[5 - u], a1);
-                a2 = __fmaf_rn(hv[u], wv[6 - u], a2);
-                a3 = __fmaf_rn(hv[u], wv[7 - u], a3);
+                // output e at tap k0+u reads position p0 + e - k0 - u = wv[4 + e - u];
+                // outputs (0,1) and (2,3) advance as packed pairs, each lane fmaf.
+                const float2 hh = make_float2(hv[u], hv[u]);
+                a01 = __ffma2_rn(hh, make_float2(wv[4 - u], wv[5 - u]), a01);
+                a23 = __ffma2_rn(hh, make_float2(wv[6 - u], wv[7 - u]), a23);
             }
         }
     }
-    return make_float4(a0, a1, a2, a3);
+    return make_float4(a01.x, a01.y, a23.x, a23.y);
 }
 
 __device__ __forceinline__ float4 f4_add(float4 a, float4 b) {
@@ -207,7 +228,7 @@ __device__ __forceinline__ float4 f4_abs(float4 a) {
     SG_ROW2(op, M, 0) SG_ROW2(op, M, 1) SG_ROW2(op, M, 2) SG_ROW2(op, M, 3) SG_ROW2(op, M, 4) \
         SG_ROW2(op, M, 5) SG_ROW2(op, M, 6) SG_ROW2(op, M, 7)
 
-#define M_LOAD(op, d) SG_C1(op, d, r[d] = load_pos(P.in[in.aux], x))
+#define M_LOAD(op, d) SG_C1(op, d, r[d] = load_pos(P, in.aux, x))
 #define M_STORE(op, s) SG_C1(op, s, store_pos(r[s], x))
 #define M_STAGE(op, s) SG_C1(op, s, stage_pos(r[s], x))
 #define M_FIRACC(op, d) SG_C1(op, d, r[d] = fir_acc(P, in.aux, x))
@@ -246,17 +267,74 @@ __device__ __noinline__ void interpret(const Program& P, int pc, const Exec& x) 
     }
 }
 
+// Bulk-copy mode: the chunk's inputs (positions [cb - hs, cb + kChunk),
+// clipped to the signal) travel HBM -> shared memory by cp.async.bulk, one
+// copy per input, double-buffered across chunks and completing on a
+// per-stage mbarrier, so the next chunk streams in while this one is
+// interpreted. Requires every input 16-byte aligned and halo = 0 mod 4.
+constexpr int kStages = 2;
+
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,
+                                         uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+struct ChunkSpan {
+    int64_t org, lo, len4, hi;  // buffer origin, copied [lo, lo+len4), valid [lo, hi)
+};
+
+__device__ __forceinline__ ChunkSpan chunk_span(int64_t cb, int hs, int64_t n, int64_t halo) {
+    ChunkSpan s;
+    s.org = cb - hs;
+    s.lo = max(s.org, -halo);
+    s.hi = min(cb + (int64_t)kChunk, n);
+    s.len4 = s.hi > s.lo ? ((s.hi - s.lo) & ~int64_t(3)) : 0;
+    return s;
+}
+
+template <bool BULK>
 __global__ void __launch_bounds__(kThreads) k_tile(const __grid_constant__ Program P,
                                                    float* __restrict__ out, int64_t n,
-                                                   int64_t halo, bool vec) {
+                                                   int64_t halo, bool vec, int32_t hs,
+                                                   uint32_t* wd) {
+    __shared__ __align__(8) uint64_t bars[kStages];
     extern __shared__ float4 sm4[];
     float* sm = reinterpret_cast<float*>(sm4);
     float* taps_s = sm;                       // n_fir x kMaxTaps
     float* tiles = sm + P.n_fir * kMaxTaps;   // n_fir x kTileF
+    float* stages = tiles + P.n_fir * kTileF; // kStages x n_in x sstride (bulk mode)
+    const int32_t sstride = kChunk + hs;
+    const int64_t stage_floats = (int64_t)P.n_in * sstride;
     const int tid = threadIdx.x;
+    const int64_t nchunks = (n + kChunk - 1) / kChunk;
     for (int f = 0; f < P.n_fir; f++)
         for (int k = tid; k < kMaxTaps; k += kThreads)
             taps_s[f * kMaxTaps + k] = P.fir[f].h[k];  // zero past taps
+
+    auto issue = [&](int64_t c, int s) {
+        const ChunkSpan sp = chunk_span(c * kChunk, hs, n, halo);
+        mbar_arrive_expect_tx(&bars[s], (uint32_t)(sp.len4 * 4 * P.n_in));
+        if (sp.len4 > 0)
+            for (int k = 0; k < P.n_in; k++)
+                bulk_g2s(stages + s * stage_floats + (int64_t)k * sstride + (sp.lo - sp.org),
+                         P.in[k] + sp.lo, (uint32_t)(sp.len4 * 4), &bars[s]);
+    };
+    if (BULK) {
+        if (tid == 0) {
+            for (int s = 0; s < kStages; s++) mbar_init(&bars[s], 1);
+            fence_mbar_init();
+        }
+        __syncthreads();
+        if (tid == 0)
+            for (int s = 0; s < kStages; s++) {
+                const int64_t c = blockIdx.x + (int64_t)s * gridDim.x;
+                if (c < nchunks) issue(c, s);
+            }
+    }
     __syncthreads();
 
     Exec x;
@@ -266,10 +344,29 @@ __global__ void __launch_bounds__(kThreads) k_tile(const __grid_constant__ Progr
     x.out = out;
     x.taps_s = taps_s;
     x.tiles = tiles;
-    const int64_t nchunks = (n + kChunk - 1) / kChunk;
-    for (int64_t c = blockIdx.x; c < nchunks; c += gridDim.x) {
+    x.sin = nullptr;
+    x.sstride = sstride;
+    int it = 0;
+    for (int64_t c = blockIdx.x; c < nchunks; c += gridDim.x, it++) {
         const int64_t cb = c * kChunk;
         x.cb = cb;
+        if (BULK) {
+            const int s = it % kStages;
+            if (!mbar_wait(&bars[s], (uint32_t)((it / kStages) & 1), wd)) return;
+            const ChunkSpan sp = chunk_span(cb, hs, n, halo);
+            float* buf = stages + s * stage_floats;
+            // The last 0-3 samples of a ragged signal are not a whole 16-byte
+            // unit: plain loads.
+            const int64_t tail = sp.hi - (sp.lo + sp.len4);
+            if (tail > 0 && tid < P.n_in * 4) {
+                const int k = tid / 4, e = tid % 4;
+                const int64_t pos = sp.lo + sp.len4 + e;
+                if (e < tail) buf[(int64_t)k * sstride + (pos - sp.org)] = P.in[k][pos];
+            }
+            __syncthreads();
+            x.sin = buf;
+            x.sorg = sp.org;
+        }
         if (P.n_fir > 0) {
             for (int f = 0; f < P.n_fir; f++) {
                 const int64_t ts = tile_start(cb, P.fir[f].taps);
@@ -284,7 +381,18 @@ __global__ void __launch_bounds__(kThreads) k_tile(const __grid_constant__ Progr
         }
         x.p0 = cb + 4 * tid;
         if (x.p0 < n) interpret(P, P.main_start, x);
-        if (P.n_fir > 0) __syncthreads();
+        if (BULK) {
+            // Every thread is done with this stage (and with the tiles);
+            // order those generic accesses before the next bulk copy into it.
+            fence_proxy_async_smem();
+            __syncthreads();
+            if (tid == 0) {
+                const int64_t cn = c + (int64_t)kStages * gridDim.x;
+                if (cn < nchunks) issue(cn, it % kStages);
+            }
+        } else if (P.n_fir > 0) {
+            __syncthreads();
+        }
     }
 }
 
@@ -581,22 +689,42 @@ int launch_program(Lowered& L, const std::vector<const float*>& dev_in, float* o
     if ((rc = sg::current_device(&d))) return rc;
     if (n <= 0) return 0;
     bool vec = sg::aligned16(out);
+    bool in_aligned = true;
     for (size_t k = 0; k < dev_in.size(); k++) {
         L.prog.in[k] = dev_in[k];  // element 0 of the shard; [-halo, 0) precede it
-        vec = vec && sg::aligned16(L.prog.in[k]);
+        in_aligned = in_aligned && sg::aligned16(L.prog.in[k]);
     }
-    const size_t smem = (size_t)L.prog.n_fir * (tilek::kMaxTaps + tilek::kTileF) * sizeof(float);
+    vec = vec && in_aligned;
+    // Samples a chunk's windows reach below it: the widest window's taps-1,
+    // rounded up to 16 bytes, plus tile_start's 4 floats of slack.
+    int32_t hs = 0;
+    for (int f = 0; f < L.prog.n_fir; f++)
+        hs = std::max<int32_t>(hs, (L.prog.fir[f].taps - 1 + 3) / 4 * 4 + 4);
+    const size_t base_smem =
+        (size_t)L.prog.n_fir * (tilek::kMaxTaps + tilek::kTileF) * sizeof(float);
+    const size_t bulk_smem = base_smem + (size_t)tilek::kStages * L.prog.n_in *
+                                             (tilek::kChunk + hs) * sizeof(float);
+    const bool bulk = in_aligned && halo % 4 == 0 && L.prog.n_in > 0 &&
+                      bulk_smem <= (size_t)d->max_smem_optin;
+    const size_t smem = bulk ? bulk_smem : base_smem;
+    auto kern = bulk ? tilek::k_tile<true> : tilek::k_tile<false>;
     if (smem > 48 * 1024) {
-        rc = sg::cuda_status(cudaFuncSetAttribute(tilek::k_tile,
-                                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                  (int)smem),
-                             "cudaFuncSetAttribute(tile)");
+        rc = sg::cuda_status(
+            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+            "cudaFuncSetAttribute(tile)");
         if (rc) return rc;
     }
+    int per_sm = 0;
+    rc = sg::cuda_status(
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, tilek::kThreads, smem),
+        "cudaOccupancyMaxActiveBlocksPerMultiprocessor(tile)");
+    if (rc) return rc;
     const int64_t chunks = sg::ceil_div(n, tilek::kChunk);
-    const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(chunks, (int64_t)d->sms * 4));
+    const int blocks = (int)std::max<int64_t>(
+        1, std::min<int64_t>(chunks, (int64_t)d->sms * std::max(1, per_sm)));
     sg::before_launch();
-    tilek::k_tile<<<blocks, tilek::kThreads, smem, s>>>(L.prog, out, n, halo, vec);
+    kern<<<blocks, tilek::kThreads, smem, s>>>(L.prog, out, n, halo, vec, hs,
+                                               sg::watchdog_device_ptr());
     return sg::launch_status("tile");
 }
 
