@@ -436,7 +436,7 @@ def bench_tile(args, torch, np, L, dev, sp, rank, world, barrier, max_over_ranks
     the ranks (a 32-element halo for the FIR node)."""
     from simtgo_b200 import shard, tile
 
-    total = 1 << 28
+    total = 1 << args.tile_log2
     plan = shard.tile_plan(total, world, rank, max_taps=31)
     n, halo = plan.n, plan.halo
     gen = torch.Generator(device=dev).manual_seed(6 + rank)
@@ -654,6 +654,7 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--soak-s", type=float, default=1.5)
+    ap.add_argument("--tile-log2", type=int, default=28)
     ap.add_argument("--skip-kernels", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
     args = ap.parse_args()

@@ -5,23 +5,24 @@
 // order and rounding of the reference's device code, where nvcc contracts
 // `acc += h[k] * tile[...]` (kernels/prebuilt/FIR.cu:24-27).
 //
-// B200 design. A 256-thread block produces 8192 consecutive outputs; thread
-// t owns 32 consecutive outputs, so every loaded sample feeds up to 32
-// fused multiply-adds from registers (the reference does one output per
-// thread, one shared load and one global tap load per multiply-add):
-//  * the block's signal span (its outputs plus a taps-1 halo) arrives by
-//    2-D TMA in 32-row boxes of 32 floats, 128-byte swizzled, so a row of 32
-//    samples is one 128-byte line and the chunk order within each row is
-//    permuted by the row index;
-//  * taps are staged once per block in shared memory and read as broadcast
-//    16-byte loads, eight per chunk;
-//  * per chunk of 8 taps a thread loads the 39 samples its 32 outputs need
-//    as eleven 16-byte loads -- conflict-free because lane t reads row t
-//    plus a common offset and the swizzle spreads those rows over all banks
-//    -- then issues 8 x 32 FFMA with every operand in a register;
+// B200 design. A 256-thread block produces 9216 consecutive outputs; thread
+// t owns 36 consecutive outputs, so every sample it loads from shared memory
+// feeds up to 36 fused multiply-adds from registers (the reference does one
+// output per thread, with one shared load and one global tap load per
+// multiply-add):
+//  * the block's signal span (its outputs plus the taps-1 halo) arrives by
+//    one 1-D bulk copy (cp.async.bulk, TMA) into a LINEAR shared tile;
+//  * 36 outputs per thread put lane t's window 144 bytes after lane t-1's,
+//    so the eight lanes of each 16-byte load phase hit eight different bank
+//    groups: conflict-free without any swizzle or padding, and every window
+//    load is base + a compile-time offset;
+//  * per chunk of 8 taps a thread issues twelve 16-byte shared loads (the 43
+//    samples its outputs need, aligned down) and two broadcast tap loads,
+//    then 8 x 36 FFMA with every operand in a register;
 //  * the window's alignment within a 16-byte chunk, (D - 7) mod 4, is the
-//    same for every block and chunk, so it is a template parameter and all
-//    register indices are compile-time.
+//    same for every block and chunk, so it is a template parameter;
+//  * the outputs are staged back into the same shared tile and leave by one
+//    1-D bulk store (cp.async.bulk shared -> global).
 // At 127 taps the kernel is bound by FP32 FMA issue, not by HBM.
 #include <algorithm>
 
@@ -33,141 +34,145 @@ using namespace sgd;
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int kPerThread = 32;                      // outputs per thread
-constexpr int kTileOut = kThreads * kPerThread;     // 8192 outputs per block
-constexpr int kChunk = 8;                           // taps per register chunk
-constexpr int kWin = 44;                            // window floats (11 x 16 B)
-constexpr int kBoxRows = 32;                        // TMA box: 32 rows x 32 floats
-constexpr uint32_t kBoxBytes = kBoxRows * 128;
+constexpr int kPerThread = 36;                   // outputs per thread
+constexpr int kTileOut = kThreads * kPerThread;  // 9216 outputs per block
+constexpr int kChunk = 8;                        // taps per register chunk
+constexpr int kWin4 = 12;                        // window float4s (48 floats >= 43 + 3)
 
 struct FirGeom {
     int64_t y_len;   // outputs of this launch
     int64_t x_len;   // samples in x
     int64_t halo;    // x[halo + j] is the sample of output j
     int32_t taps;
-    int32_t taps_pad;   // taps rounded up to kChunk
-    int32_t D;          // tile position of output ob + 0 at tap 0 (same for every block)
-    int32_t rows;       // shared rows staged per block (multiple of kBoxRows)
-    int64_t full_rows;  // x_len / 32: rows the tensor map covers
+    int32_t taps_pad;  // taps rounded up to kChunk
+    int32_t D;         // tile index of the sample of a block's first output
+    int32_t tile;      // floats in the shared tile (multiple of 4)
 };
 
-// Rows of the staged tile a given tap count needs (see the header comment
-// of k_fir for the bounds).
-inline int tile_rows(int taps) {
-    const int need = (taps + 8258) / 32 + 1;
-    return (int)sg::ceil_div(need, kBoxRows) * kBoxRows;
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
 }
 
+__device__ __forceinline__ void bulk_store(void* dst, const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst),
+                 "r"(smem_u32(src)), "r"(bytes)
+                 : "memory");
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+// Waits until every bulk store of this thread has finished reading shared
+// memory (the CTA may then exit or reuse it).
+__device__ __forceinline__ void bulk_store_drain() {
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+
+// One chunk of up to 8 taps for this thread's 36 outputs. w points at the
+// window's first (16-byte aligned) float: wv[i] = w[i].
 template <int SH>
-__device__ __forceinline__ void fir_chunk(const uint8_t* tile, const float* hs, int k0, int nk,
-                                          int s4, float2 (&acc)[kPerThread / 2]) {
-    // Window floats wv[i] = tile position s4 + i, i < 44.
-    float wv[kWin];
+__device__ __forceinline__ void fir_chunk(const float* __restrict__ w, const float* hs, int nk,
+                                          float (&acc)[kPerThread]) {
+    float wv[4 * kWin4];
 #pragma unroll
-    for (int c = 0; c < kWin / 4; c++) {
-        const int pos = s4 + 4 * c;
-        const float4 q =
-            *reinterpret_cast<const float4*>(tile + swz128((uint32_t)pos >> 5, ((uint32_t)pos & 31u) >> 2));
+    for (int c = 0; c < kWin4; c++) {
+        const float4 q = *reinterpret_cast<const float4*>(w + 4 * c);
         wv[4 * c] = q.x;
         wv[4 * c + 1] = q.y;
         wv[4 * c + 2] = q.z;
         wv[4 * c + 3] = q.w;
     }
-    const float4 ha = *reinterpret_cast<const float4*>(hs + k0);
-    const float4 hb = *reinterpret_cast<const float4*>(hs + k0 + 4);
+    const float4 ha = *reinterpret_cast<const float4*>(hs);
+    const float4 hb = *reinterpret_cast<const float4*>(hs + 4);
     const float hv[kChunk] = {ha.x, ha.y, ha.z, ha.w, hb.x, hb.y, hb.z, hb.w};
-    // Outputs 2i and 2i+1 advance together through one packed FP32 FMA
-    // (fma.rn.f32x2): each lane is exactly fmaf, so every output keeps its
-    // own k-ordered chain while the FMA work takes half the issue slots.
+    // Output r at tap u of the chunk reads tile position s + 7 + r - u,
+    // i.e. wv[SH + 7 + r - u].
 #pragma unroll
-    for (int u = 0; u < kChunk; u++) {
-        if (nk == kChunk || u < nk) {
-            const float2 hh = make_float2(hv[u], hv[u]);
+    for (int u = 0; u < kChunk; u++)
+        if (nk == kChunk || u < nk)
 #pragma unroll
-            for (int i = 0; i < kPerThread / 2; i++)
-                acc[i] = __ffma2_rn(hh,
-                                    make_float2(wv[SH + 7 - u + 2 * i], wv[SH + 8 - u + 2 * i]),
-                                    acc[i]);
-        }
-    }
+            for (int r = 0; r < kPerThread; r++)
+                acc[r] = __fmaf_rn(hv[u], wv[SH + 7 + r - u], acc[r]);
 }
 
-// One block = outputs [ob, ob + 8192). Tile row 0 is signal row R0 =
-// (ob + halo - D) / 32; output ob + 32t + r at tap k reads tile position
-// D + 32t + r - k, with D = a + (taps-1) + 32 and a = (halo - (taps-1)) mod 32,
-// so positions stay >= 22 (a spare row absorbs the last, partial chunk) and
-// below 32*rows.
+// One block = outputs [ob, ob + 9216). The tile holds samples
+// [A, A + tile) of x (x-index = j + halo for output j), A = ob + halo - D,
+// zero outside [0, x_len). Output ob + 36t + r at tap k reads tile index
+// D + 36t + r - k, with D = taps + 6 + ((ob + halo - taps - 6) mod 4), so
+// A is a multiple of 4 (16-byte aligned when x is) and the window of the
+// last, partial chunk (up to 7 taps past the end) stays inside the tile.
 template <int SH>
-__global__ void __launch_bounds__(kThreads, 2) k_fir(const __grid_constant__ CUtensorMap map,
-                                                      bool use_tma, float* __restrict__ y,
+__global__ void __launch_bounds__(kThreads, 2) k_fir(float* __restrict__ y,
                                                       const float* __restrict__ x,
                                                       const float* __restrict__ h, FirGeom g,
-                                                      bool vec_out, uint32_t* wd) {
+                                                      bool bulk_in, bool bulk_out, uint32_t* wd) {
     __shared__ __align__(8) uint64_t bar;
-    extern __shared__ uint8_t dyn_smem[];
-    uint8_t* tile = reinterpret_cast<uint8_t*>(
-        (reinterpret_cast<uintptr_t>(dyn_smem) + 1023) & ~uintptr_t(1023));
-    float* hs = reinterpret_cast<float*>(tile + (size_t)g.rows * 128);
+    extern __shared__ float4 dyn4[];
+    float* tile = reinterpret_cast<float*>(dyn4);
+    float* hs = tile + g.tile;
     const int tid = threadIdx.x;
     const int64_t ob = (int64_t)blockIdx.x * kTileOut;
-    const int64_t R0 = (ob + g.halo - g.D) / 32;  // exact: ob + halo - D = 0 mod 32
+    const int64_t A = ob + g.halo - g.D;
 
-    if (use_tma) {
-        if (tid == 0) {
-            mbar_init(&bar, 1);
-            fence_mbar_init();
-        }
-        __syncthreads();  // no thread may test the barrier before it exists
-        if (tid == 0) {
-            mbar_arrive_expect_tx(&bar, (uint32_t)g.rows * 128u);
-            for (int b = 0; b < g.rows / kBoxRows; b++)
-                tma_load_2d(tile + b * kBoxBytes, &map, &bar, 0, (int32_t)(R0 + b * kBoxRows));
-        }
-    } else {
-        // Unaligned or very short signal: stage with guarded loads.
-        for (int i = tid; i < g.rows * 32; i += kThreads) {
-            const int row = i >> 5, col = i & 31;
-            const int64_t src = (R0 + row) * 32 + col;
-            const float v = (src >= 0 && src < g.x_len) ? x[src] : 0.0f;
-            *reinterpret_cast<float*>(tile + swz128(row, col >> 2) + (col & 3) * 4) = v;
-        }
-    }
-    for (int k = tid; k < g.taps_pad; k += kThreads) hs[k] = k < g.taps ? h[k] : 0.0f;
-    if (use_tma) {
-        if (!mbar_wait(&bar, 0, wd)) return;
-        // The tensor map covers whole rows only; the signal's ragged last row
-        // (x_len mod 32 samples) was zero-filled and is patched here.
-        const int64_t rem = g.x_len - g.full_rows * 32;
-        const int64_t prow = g.full_rows - R0;
-        if (rem > 0 && prow >= 0 && prow < g.rows && tid < rem) {
-            *reinterpret_cast<float*>(tile + swz128((uint32_t)prow, tid >> 2) + (tid & 3) * 4) =
-                x[g.full_rows * 32 + tid];
-        }
+    // ---- stage the signal span -------------------------------------------------
+    // [c0, c1): the part of the tile that lies inside x, bulk-copied in whole
+    // 16-byte units; the rest (before x, past it, and a ragged last 1-3
+    // samples) is written by the threads.
+    const int64_t c0 = max(A, (int64_t)0);
+    const int64_t end = min(A + g.tile, g.x_len);
+    const int64_t c1 = bulk_in && end > c0 ? c0 + ((end - c0) & ~int64_t(3)) : c0;
+    if (bulk_in && tid == 0) {
+        mbar_init(&bar, 1);
+        fence_mbar_init();
     }
     __syncthreads();
+    if (bulk_in && tid == 0) {
+        mbar_arrive_expect_tx(&bar, (uint32_t)((c1 - c0) * 4));
+        if (c1 > c0) bulk_load(tile + (c0 - A), x + c0, (uint32_t)((c1 - c0) * 4), &bar);
+    }
+    for (int i = tid; i < g.tile; i += kThreads) {
+        const int64_t s = A + i;
+        if (s < c0 || s >= c1) tile[i] = (s >= 0 && s < g.x_len) ? x[s] : 0.0f;
+    }
+    for (int k = tid; k < g.taps_pad; k += kThreads) hs[k] = k < g.taps ? h[k] : 0.0f;
+    if (bulk_in && !mbar_wait(&bar, 0, wd)) return;
+    __syncthreads();
 
-    float2 acc[kPerThread / 2];  // acc[i] = outputs (2i, 2i+1) of this thread
+    // ---- 36 outputs per thread ---------------------------------------------------
+    float acc[kPerThread];
 #pragma unroll
-    for (int i = 0; i < kPerThread / 2; i++) acc[i] = make_float2(0.0f, 0.0f);
-    const int sbase = g.D + 32 * tid - 7 - SH;  // s4 at k0 = 0
+    for (int r = 0; r < kPerThread; r++) acc[r] = 0.0f;
+    // Window start at chunk k0: s4 = D - 7 - SH + 36t - k0 (a multiple of 4).
+    const float* w = tile + (g.D - 7 - SH) + kPerThread * tid;
     for (int k0 = 0; k0 < g.taps; k0 += kChunk)
-        fir_chunk<SH>(tile, hs, k0, min(kChunk, g.taps - k0), sbase - k0, acc);
+        fir_chunk<SH>(w - k0, hs + k0, min(kChunk, g.taps - k0), acc);
 
-    const int64_t j0 = ob + (int64_t)kPerThread * tid;
-    if (vec_out && j0 + kPerThread <= g.y_len) {
+    // ---- outputs: through the shared tile, then one bulk store -----------------------
+    __syncthreads();  // every window read is done
+    float* o = tile + kPerThread * tid;
 #pragma unroll
-        for (int c = 0; c < kPerThread / 4; c++)
-            st_stream_f4(y + j0 + 4 * c, make_float4(acc[2 * c].x, acc[2 * c].y,
-                                                     acc[2 * c + 1].x, acc[2 * c + 1].y));
+    for (int c = 0; c < kPerThread / 4; c++)
+        *reinterpret_cast<float4*>(o + 4 * c) =
+            make_float4(acc[4 * c], acc[4 * c + 1], acc[4 * c + 2], acc[4 * c + 3]);
+    const bool whole = ob + kTileOut <= g.y_len;
+    if (bulk_out && whole) {
+        fence_proxy_async_smem();  // the stores above, before the async-proxy read
+        __syncthreads();
+        if (tid == 0) {
+            bulk_store(y + ob, tile, kTileOut * 4u);
+            bulk_store_drain();
+        }
     } else {
-#pragma unroll
-        for (int r = 0; r < kPerThread; r++)
-            if (j0 + r < g.y_len) y[j0 + r] = (r & 1) ? acc[r / 2].y : acc[r / 2].x;
+        __syncthreads();
+        const int64_t n = min((int64_t)kTileOut, g.y_len - ob);
+        for (int i = tid; i < n; i += kThreads) y[ob + i] = tile[i];
     }
 }
 
-using FirKernel = void (*)(const CUtensorMap, bool, float*, const float*, const float*, FirGeom,
-                           bool, uint32_t*);
+using FirKernel = void (*)(float*, const float*, const float*, FirGeom, bool, bool, uint32_t*);
 
 int launch_fir(const char* K, float* y, int64_t y_len, const float* x, int64_t x_len,
                int64_t halo, const float* h, int32_t taps, void* stream) {
@@ -181,25 +186,17 @@ int launch_fir(const char* K, float* y, int64_t y_len, const float* x, int64_t x
     g.halo = halo;
     g.taps = taps;
     g.taps_pad = (int32_t)sg::ceil_div(std::max(taps, 1), kChunk) * kChunk;
-    const int64_t a = (((halo - (taps - 1)) % 32) + 32) % 32;
-    g.D = (int32_t)(a + (taps - 1) + 32);
-    g.rows = tile_rows(taps);
-    g.full_rows = x_len / 32;
-    const int sh = (int)(((g.D - 7) % 4 + 4) % 4);
+    // ob is a multiple of 4, so D (and with it SH) is the same for every block.
+    const int64_t m = (((halo - taps - 6) % 4) + 4) % 4;
+    g.D = (int32_t)(taps + 6 + m);
+    // The window loads of the last thread reach up to 4 floats past the last
+    // sample its outputs use (whole 16-byte loads): 4 floats of slack.
+    g.tile = (int32_t)sg::ceil_div(g.D + kTileOut + 4, 4) * 4;
+    const int sh = (g.D - 7) % 4;
 
-    CUtensorMap map;
-    bool use_tma = sg::aligned16(x) && g.full_rows >= 1;
-    if (use_tma) {
-        if ((rc = sg::tma_encode_2d(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, x, 32,
-                                    (uint64_t)g.full_rows, 128, 32, kBoxRows,
-                                    CU_TENSOR_MAP_SWIZZLE_128B)))
-            return rc;
-    } else {
-        memset(&map, 0, sizeof map);
-    }
     static const FirKernel kernels[4] = {k_fir<0>, k_fir<1>, k_fir<2>, k_fir<3>};
     const FirKernel kern = kernels[sh];
-    const size_t smem = 1024 + (size_t)g.rows * 128 + (size_t)g.taps_pad * 4;
+    const size_t smem = (size_t)(g.tile + g.taps_pad) * sizeof(float);
     rc = sg::cuda_status(
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
         "cudaFuncSetAttribute(FIR)");
@@ -208,7 +205,7 @@ int launch_fir(const char* K, float* y, int64_t y_len, const float* x, int64_t x
     if (blocks > 0x7fffffffLL) return sg::fail(SIMTGO_ESIZE, "%s: y_len too large", K);
     sg::before_launch();
     kern<<<(unsigned)blocks, kThreads, smem, (cudaStream_t)stream>>>(
-        map, use_tma, y, x, h, g, sg::aligned16(y), sg::watchdog_device_ptr());
+        y, x, h, g, sg::aligned16(x), sg::aligned16(y), sg::watchdog_device_ptr());
     return sg::launch_status(K);
 }
 
