@@ -276,6 +276,29 @@ int simtgo_tile_run(simtgo_tile_graph* g, simtgo_tensor t, float* dev_out, int32
 int simtgo_tile_run_shard(simtgo_tile_graph* g, simtgo_tensor t, float* dev_out,
                           int32_t out_len, int32_t halo, void* stream);
 
+/* No counterpart in the reference. MaterializeStepwise's computation
+ * (tile/run.go:89: one kernel per operation node) for callers that cannot
+ * allocate device memory -- e.g. a real-time signal-processing callback
+ * with a fixed deadline, where cudaMalloc/cudaFree may synchronise the
+ * whole device and take unbounded time, or an application whose memory pool
+ * owns the device and forbids outside allocations. It allocates no device
+ * memory: every input must be a device input (simtgo_tile_input_device),
+ * the caller passes dev_out (out_len == Len(t)), and the intermediate node
+ * values live in a fixed scratch array inside the library of
+ * SIMTGO_TILE_NOALLOC_SCRATCH_FLOATS floats (16 MiB), which every GPU that
+ * loads the library holds until the process exits. A graph whose
+ * intermediate nodes need more (each node's length rounded up to 64 floats,
+ * summed over the nodes other than t) is refused with SIMTGO_ESIZE. The
+ * first call on a device resolves the array's device address (once per
+ * device, with that device current). Every call uses the same array and
+ * leaves its values there; each node's region is written in full before it
+ * is read, so nothing needs clearing. Calls that overlap on the GPU (two
+ * streams, or two host threads) race on the array. Asynchronous on stream;
+ * the result equals simtgo_tile_run's bit for bit. */
+#define SIMTGO_TILE_NOALLOC_SCRATCH_FLOATS (1 << 22)
+int simtgo_tile_run_stepwise_noalloc(simtgo_tile_graph* g, simtgo_tensor t, float* dev_out,
+                                     int32_t out_len, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -81,6 +81,7 @@ _SIGS = {
     "simtgo_tile_materialize_stepwise": [_vp, _i32, _vp, _i32, C.POINTER(_i32)],
     "simtgo_tile_run": [_vp, _i32, _vp, _i32, _vp],
     "simtgo_tile_run_shard": [_vp, _i32, _vp, _i32, _i32, _vp],
+    "simtgo_tile_run_stepwise_noalloc": [_vp, _i32, _vp, _i32, _vp],
 }
 _RESTYPES = {
     "simtgo_last_error": C.c_char_p,

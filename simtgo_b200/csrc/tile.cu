@@ -31,6 +31,7 @@
 #include <string.h>
 
 #include <algorithm>
+#include <mutex>
 #include <string>
 #include <unordered_map>
 #include <vector>
@@ -1136,5 +1137,112 @@ int simtgo_tile_run(simtgo_tile_graph* g, simtgo_tensor t, float* dev_out, int32
                     void* stream) {
     return simtgo_tile_run_shard(g, t, dev_out, out_len, 0, stream);
 }
+
+}  // extern "C"
+
+// ---- the stepwise run without allocation ------------------------------------
+// Scratch for simtgo_tile_run_stepwise_noalloc: the values of the graph's
+// intermediate nodes. A fixed array in the module, so every GPU that loads
+// the library holds these 16 MiB until the process exits.
+namespace {
+constexpr int64_t kNoAllocFloats = SIMTGO_TILE_NOALLOC_SCRATCH_FLOATS;
+constexpr int64_t kNoAllocAlign = 64;  // floats: each node's region starts 256-byte aligned
+}  // namespace
+static __device__ __align__(256) float g_stepwise_scratch[kNoAllocFloats];
+
+namespace {
+std::mutex g_scratch_mu;
+float* g_scratch_ptr[64];
+
+// The device address of g_stepwise_scratch on the current device. Host code
+// may not use the symbol itself as an address (it names a host-side
+// stand-in); the runtime resolves it once per device, with that device
+// current.
+int stepwise_scratch(float** out) {
+    int dev = -1;
+    int rc = sg::cuda_status(cudaGetDevice(&dev), "cudaGetDevice");
+    if (rc) return rc;
+    if (dev < 0 || dev >= 64) return sg::fail(SIMTGO_EDEVICE, "device %d out of range", dev);
+    std::lock_guard<std::mutex> lk(g_scratch_mu);
+    if (!g_scratch_ptr[dev]) {
+        void* p = nullptr;
+        rc = sg::cuda_status(cudaGetSymbolAddress(&p, g_stepwise_scratch),
+                             "cudaGetSymbolAddress(stepwise scratch)");
+        if (rc) return rc;
+        g_scratch_ptr[dev] = static_cast<float*>(p);
+    }
+    *out = g_scratch_ptr[dev];
+    return 0;
+}
+}  // namespace
+
+extern "C" int simtgo_tile_run_stepwise_noalloc(simtgo_tile_graph* g, simtgo_tensor t,
+                                                float* dev_out, int32_t out_len, void* stream) {
+    sg::clear_error();
+    int rc;
+    if ((rc = check_run(g, t, out_len))) return rc;
+    if (out_len == 0) return 0;
+    if (!dev_out) return sg::fail(SIMTGO_ENULL, "tile: null output");
+    std::vector<int> order;
+    std::vector<char> seen(g->nodes.size(), 0);
+    postorder(g, t, order, seen, false);
+    // Every value must already be on the device, and every intermediate node
+    // gets its own region of the scratch array: nothing is allocated.
+    std::vector<int64_t> region(g->nodes.size(), -1);
+    int64_t used = 0;
+    for (int id : order) {
+        const Node& nd = g->nodes[id];
+        if (nd.kind == K_INPUT) {
+            if (!nd.is_taps && !nd.dev)
+                return sg::fail(SIMTGO_EARG,
+                                "tile: the allocation-free run needs device-resident inputs "
+                                "(node %d is host data)",
+                                id);
+            continue;
+        }
+        if (id == t) continue;  // the root is written straight to dev_out
+        region[id] = used;
+        used += (nd.n + kNoAllocAlign - 1) / kNoAllocAlign * kNoAllocAlign;
+    }
+    if (used > kNoAllocFloats)
+        return sg::fail(SIMTGO_ESIZE,
+                        "tile: the allocation-free stepwise run needs %lld floats of scratch for "
+                        "the graph's intermediate values; its fixed scratch holds %lld (16 MiB)",
+                        (long long)used, (long long)kNoAllocFloats);
+    float* scratch = nullptr;
+    if ((rc = stepwise_scratch(&scratch))) return rc;
+    auto value = [&](int id) -> const float* {
+        return g->nodes[id].kind == K_INPUT ? g->nodes[id].dev : scratch + region[id];
+    };
+    for (int id : order) {
+        const Node& nd = g->nodes[id];
+        if (nd.kind == K_INPUT) continue;
+        simtgo_tile_graph one;
+        const int a = simtgo_tile_input_device(&one, value(nd.a), g->nodes[nd.a].n);
+        int r;
+        if (nd.kind == K_FIR) {
+            const Node& tp = g->nodes[nd.b];
+            r = simtgo_tile_fir(&one, a, tp.taps.data(), (int32_t)tp.taps.size());
+        } else if (nd.kind == K_SCALE) {
+            r = simtgo_tile_scale(&one, a, nd.scale);
+        } else if (nd.kind == K_SQRT) {
+            r = simtgo_tile_sqrt(&one, a);
+        } else if (nd.kind == K_ABS) {
+            r = simtgo_tile_abs(&one, a);
+        } else {
+            const int b = nd.b == nd.a ? a : simtgo_tile_input_device(&one, value(nd.b), g->nodes[nd.b].n);
+            r = nd.kind == K_ADD   ? simtgo_tile_add(&one, a, b)
+                : nd.kind == K_MUL ? simtgo_tile_mul(&one, a, b)
+                                   : simtgo_tile_hypot(&one, a, b);
+        }
+        float* target = id == t ? dev_out : scratch + region[id];
+        auto resolve = [&](int nid) -> const float* { return one.nodes[nid].dev; };
+        rc = run_fused(&one, r, target, nd.n, 0, (cudaStream_t)stream, resolve, true);
+        if (rc) return rc;
+    }
+    return 0;
+}
+
+extern "C" {
 
 }  // extern "C"
