@@ -71,12 +71,8 @@ __device__ __forceinline__ void bulk_store_drain() {
     asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
 
-// One chunk of up to 8 taps for this thread's 36 outputs. w points at the
-// window's first (16-byte aligned) float: wv[i] = w[i].
-template <int SH>
-__device__ __forceinline__ void fir_chunk(const float* __restrict__ w, const float* hs, int nk,
-                                          float (&acc)[kPerThread]) {
-    float wv[4 * kWin4];
+// Loads the window of one chunk: wv[i] = w[i], i < 48, w 16-byte aligned.
+__device__ __forceinline__ void load_window(const float* __restrict__ w, float (&wv)[4 * kWin4]) {
 #pragma unroll
     for (int c = 0; c < kWin4; c++) {
         const float4 q = *reinterpret_cast<const float4*>(w + 4 * c);
@@ -85,94 +81,149 @@ __device__ __forceinline__ void fir_chunk(const float* __restrict__ w, const flo
         wv[4 * c + 2] = q.z;
         wv[4 * c + 3] = q.w;
     }
+}
+
+// A whole chunk of 8 taps for this thread's 36 outputs. Output r at tap u of
+// the chunk reads tile position s + 7 + r - u, i.e. wv[SH + 7 + r - u].
+template <int SH>
+__device__ __forceinline__ void fir_chunk(const float* __restrict__ w, const float* hs,
+                                          float (&acc)[kPerThread]) {
+    float wv[4 * kWin4];
+    load_window(w, wv);
     const float4 ha = *reinterpret_cast<const float4*>(hs);
     const float4 hb = *reinterpret_cast<const float4*>(hs + 4);
     const float hv[kChunk] = {ha.x, ha.y, ha.z, ha.w, hb.x, hb.y, hb.z, hb.w};
-    // Output r at tap u of the chunk reads tile position s + 7 + r - u,
-    // i.e. wv[SH + 7 + r - u].
 #pragma unroll
     for (int u = 0; u < kChunk; u++)
-        if (nk == kChunk || u < nk)
 #pragma unroll
-            for (int r = 0; r < kPerThread; r++)
-                acc[r] = __fmaf_rn(hv[u], wv[SH + 7 + r - u], acc[r]);
+        for (int r = 0; r < kPerThread; r++)
+            acc[r] = __fmaf_rn(hv[u], wv[SH + 7 + r - u], acc[r]);
 }
 
-// One block = outputs [ob, ob + 9216). The tile holds samples
-// [A, A + tile) of x (x-index = j + halo for output j), A = ob + halo - D,
-// zero outside [0, x_len). Output ob + 36t + r at tap k reads tile index
-// D + 36t + r - k, with D = taps + 6 + ((ob + halo - taps - 6) mod 4), so
-// A is a multiple of 4 (16-byte aligned when x is) and the window of the
-// last, partial chunk (up to 7 taps past the end) stays inside the tile.
+// The last chunk, with nk < 8 taps.
+template <int SH>
+__device__ __forceinline__ void fir_chunk_tail(const float* __restrict__ w, const float* hs,
+                                               int nk, float (&acc)[kPerThread]) {
+    float wv[4 * kWin4];
+    load_window(w, wv);
+#pragma unroll
+    for (int u = 0; u < kChunk - 1; u++)
+        if (u < nk) {
+            const float hu = hs[u];
+#pragma unroll
+            for (int r = 0; r < kPerThread; r++)
+                acc[r] = __fmaf_rn(hu, wv[SH + 7 + r - u], acc[r]);
+        }
+}
+
+// Tile t = outputs [ob, ob + 9216), ob = 9216 t. Its shared buffer holds
+// samples [A, A + tile) of x (x-index = j + halo for output j),
+// A = ob + halo - D, zero outside [0, x_len). Output ob + 36i + r at tap k
+// reads buffer index D + 36i + r - k, with D = taps + 6 + ((halo - taps - 6)
+// mod 4), so A is a multiple of 4 (16-byte aligned when x is) and the window
+// of the last, partial chunk (up to 7 taps past the end) stays inside.
+struct Span {
+    int64_t A, c0, c1;  // buffer origin; [c0, c1) arrives by bulk copy
+};
+__device__ __forceinline__ Span tile_span(int64_t t, const FirGeom& g, bool bulk_in) {
+    Span s;
+    s.A = t * kTileOut + g.halo - g.D;
+    s.c0 = max(s.A, (int64_t)0);
+    const int64_t end = min(s.A + g.tile, g.x_len);
+    s.c1 = bulk_in && end > s.c0 ? s.c0 + ((end - s.c0) & ~int64_t(3)) : s.c0;
+    return s;
+}
+
+// Persistent: each block walks tiles blockIdx.x, +gridDim.x, ... with two
+// shared buffers, so tile i+1's signal span streams in (one bulk copy,
+// completing on that buffer's mbarrier) while tile i is computed. A tile's
+// outputs are staged in its own buffer and leave by one bulk store; the
+// buffer is refilled (tile i+2) once that store has read it.
 template <int SH>
 __global__ void __launch_bounds__(kThreads, 2) k_fir(float* __restrict__ y,
                                                       const float* __restrict__ x,
                                                       const float* __restrict__ h, FirGeom g,
-                                                      bool bulk_in, bool bulk_out, uint32_t* wd) {
-    __shared__ __align__(8) uint64_t bar;
+                                                      int64_t ntiles, bool bulk_in, bool bulk_out,
+                                                      uint32_t* wd) {
+    __shared__ __align__(8) uint64_t bars[2];
     extern __shared__ float4 dyn4[];
-    float* tile = reinterpret_cast<float*>(dyn4);
-    float* hs = tile + g.tile;
+    float* const buf0 = reinterpret_cast<float*>(dyn4);
+    float* const buf1 = buf0 + g.tile;
+    float* hs = buf1 + g.tile;
     const int tid = threadIdx.x;
-    const int64_t ob = (int64_t)blockIdx.x * kTileOut;
-    const int64_t A = ob + g.halo - g.D;
 
-    // ---- stage the signal span -------------------------------------------------
-    // [c0, c1): the part of the tile that lies inside x, bulk-copied in whole
-    // 16-byte units; the rest (before x, past it, and a ragged last 1-3
-    // samples) is written by the threads.
-    const int64_t c0 = max(A, (int64_t)0);
-    const int64_t end = min(A + g.tile, g.x_len);
-    const int64_t c1 = bulk_in && end > c0 ? c0 + ((end - c0) & ~int64_t(3)) : c0;
+    auto issue = [&](int64_t t, int b) {
+        const Span s = tile_span(t, g, bulk_in);
+        mbar_arrive_expect_tx(&bars[b], (uint32_t)((s.c1 - s.c0) * 4));
+        if (s.c1 > s.c0)
+            bulk_load((b ? buf1 : buf0) + (s.c0 - s.A), x + s.c0, (uint32_t)((s.c1 - s.c0) * 4),
+                      &bars[b]);
+    };
+    for (int k = tid; k < g.taps_pad; k += kThreads) hs[k] = k < g.taps ? h[k] : 0.0f;
     if (bulk_in && tid == 0) {
-        mbar_init(&bar, 1);
+        mbar_init(&bars[0], 1);
+        mbar_init(&bars[1], 1);
         fence_mbar_init();
     }
     __syncthreads();
-    if (bulk_in && tid == 0) {
-        mbar_arrive_expect_tx(&bar, (uint32_t)((c1 - c0) * 4));
-        if (c1 > c0) bulk_load(tile + (c0 - A), x + c0, (uint32_t)((c1 - c0) * 4), &bar);
-    }
-    for (int i = tid; i < g.tile; i += kThreads) {
-        const int64_t s = A + i;
-        if (s < c0 || s >= c1) tile[i] = (s >= 0 && s < g.x_len) ? x[s] : 0.0f;
-    }
-    for (int k = tid; k < g.taps_pad; k += kThreads) hs[k] = k < g.taps ? h[k] : 0.0f;
-    if (bulk_in && !mbar_wait(&bar, 0, wd)) return;
-    __syncthreads();
+    if (bulk_in && tid == 0)
+        for (int b = 0; b < 2; b++)
+            if (blockIdx.x + (int64_t)b * gridDim.x < ntiles) issue(blockIdx.x + (int64_t)b * gridDim.x, b);
 
-    // ---- 36 outputs per thread ---------------------------------------------------
-    float acc[kPerThread];
-#pragma unroll
-    for (int r = 0; r < kPerThread; r++) acc[r] = 0.0f;
-    // Window start at chunk k0: s4 = D - 7 - SH + 36t - k0 (a multiple of 4).
-    const float* w = tile + (g.D - 7 - SH) + kPerThread * tid;
-    for (int k0 = 0; k0 < g.taps; k0 += kChunk)
-        fir_chunk<SH>(w - k0, hs + k0, min(kChunk, g.taps - k0), acc);
-
-    // ---- outputs: through the shared tile, then one bulk store -----------------------
-    __syncthreads();  // every window read is done
-    float* o = tile + kPerThread * tid;
-#pragma unroll
-    for (int c = 0; c < kPerThread / 4; c++)
-        *reinterpret_cast<float4*>(o + 4 * c) =
-            make_float4(acc[4 * c], acc[4 * c + 1], acc[4 * c + 2], acc[4 * c + 3]);
-    const bool whole = ob + kTileOut <= g.y_len;
-    if (bulk_out && whole) {
-        fence_proxy_async_smem();  // the stores above, before the async-proxy read
-        __syncthreads();
-        if (tid == 0) {
-            bulk_store(y + ob, tile, kTileOut * 4u);
-            bulk_store_drain();
+    int it = 0;
+    for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x, it++) {
+        const int b = it & 1;
+        float* tile = b ? buf1 : buf0;
+        const Span s = tile_span(t, g, bulk_in);
+        // The threads fill what the bulk copy does not: samples before x
+        // (zeros), and from c1 on (a ragged last 1-3 samples, zeros past x,
+        // or everything when x is not 16-byte aligned).
+        for (int64_t i = tid; i < s.c0 - s.A; i += kThreads) tile[i] = 0.0f;
+        for (int64_t i = (s.c1 - s.A) + tid; i < g.tile; i += kThreads) {
+            const int64_t p = s.A + i;
+            tile[i] = (p >= 0 && p < g.x_len) ? x[p] : 0.0f;
         }
-    } else {
+        if (bulk_in && !mbar_wait(&bars[b], (uint32_t)((it >> 1) & 1), wd)) return;
         __syncthreads();
-        const int64_t n = min((int64_t)kTileOut, g.y_len - ob);
-        for (int i = tid; i < n; i += kThreads) y[ob + i] = tile[i];
+
+        float acc[kPerThread];
+#pragma unroll
+        for (int r = 0; r < kPerThread; r++) acc[r] = 0.0f;
+        // Window start at chunk k0: D - 7 - SH + 36 tid - k0 (a multiple of 4).
+        const float* w = tile + (g.D - 7 - SH) + kPerThread * tid;
+        int k0 = 0;
+        for (; k0 + kChunk <= g.taps; k0 += kChunk) fir_chunk<SH>(w - k0, hs + k0, acc);
+        if (k0 < g.taps) fir_chunk_tail<SH>(w - k0, hs + k0, g.taps - k0, acc);
+
+        __syncthreads();  // every window read of this buffer is done
+        float* o = tile + kPerThread * tid;
+#pragma unroll
+        for (int c = 0; c < kPerThread / 4; c++)
+            *reinterpret_cast<float4*>(o + 4 * c) =
+                make_float4(acc[4 * c], acc[4 * c + 1], acc[4 * c + 2], acc[4 * c + 3]);
+        const int64_t ob = t * kTileOut;
+        const bool whole = ob + kTileOut <= g.y_len;
+        fence_proxy_async_smem();  // this buffer's generic accesses, before async ones
+        __syncthreads();
+        if (bulk_out && whole) {
+            if (tid == 0) {
+                bulk_store(y + ob, tile, kTileOut * 4u);
+                bulk_store_drain();
+            }
+        } else {
+            const int64_t n = min((int64_t)kTileOut, g.y_len - ob);
+            for (int64_t i = tid; i < n; i += kThreads) y[ob + i] = tile[i];
+            fence_proxy_async_smem();
+            __syncthreads();
+        }
+        if (bulk_in && tid == 0 && t + 2 * (int64_t)gridDim.x < ntiles)
+            issue(t + 2 * (int64_t)gridDim.x, b);
     }
+    if (bulk_out && tid == 0) bulk_store_drain();
 }
 
-using FirKernel = void (*)(float*, const float*, const float*, FirGeom, bool, bool, uint32_t*);
+using FirKernel = void (*)(float*, const float*, const float*, FirGeom, int64_t, bool, bool,
+                           uint32_t*);
 
 int launch_fir(const char* K, float* y, int64_t y_len, const float* x, int64_t x_len,
                int64_t halo, const float* h, int32_t taps, void* stream) {
@@ -196,16 +247,25 @@ int launch_fir(const char* K, float* y, int64_t y_len, const float* x, int64_t x
 
     static const FirKernel kernels[4] = {k_fir<0>, k_fir<1>, k_fir<2>, k_fir<3>};
     const FirKernel kern = kernels[sh];
-    const size_t smem = (size_t)(g.tile + g.taps_pad) * sizeof(float);
+    const size_t smem = (size_t)(2 * g.tile + g.taps_pad) * sizeof(float);
+    if (smem > (size_t)d->max_smem_optin)
+        return sg::fail(SIMTGO_ESIZE, "%s: %d taps need %zu bytes of shared memory", K, taps,
+                        smem);
     rc = sg::cuda_status(
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
         "cudaFuncSetAttribute(FIR)");
     if (rc) return rc;
-    const int64_t blocks = sg::ceil_div(y_len, kTileOut);
-    if (blocks > 0x7fffffffLL) return sg::fail(SIMTGO_ESIZE, "%s: y_len too large", K);
+    int per_sm = 0;
+    rc = sg::cuda_status(
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem),
+        "cudaOccupancyMaxActiveBlocksPerMultiprocessor(FIR)");
+    if (rc) return rc;
+    const int64_t ntiles = sg::ceil_div(y_len, kTileOut);
+    const int blocks =
+        (int)std::min<int64_t>(ntiles, (int64_t)d->sms * std::max(1, per_sm));
     sg::before_launch();
-    kern<<<(unsigned)blocks, kThreads, smem, (cudaStream_t)stream>>>(
-        y, x, h, g, sg::aligned16(x), sg::aligned16(y), sg::watchdog_device_ptr());
+    kern<<<blocks, kThreads, smem, (cudaStream_t)stream>>>(
+        y, x, h, g, ntiles, sg::aligned16(x), sg::aligned16(y), sg::watchdog_device_ptr());
     return sg::launch_status(K);
 }
 

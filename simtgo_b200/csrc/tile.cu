@@ -161,11 +161,12 @@ __device__ __forceinline__ int64_t tile_start(int64_t cb, int taps) {
     return ((cb - (taps - 1)) & ~int64_t(3)) - 4;
 }
 
-__device__ __forceinline__ float4 fir_acc(const Program& P, int f, const Exec& x) {
-    const int taps = P.fir[f].taps;
-    const float* tile = x.tiles + f * kTileF;
-    const float* h = x.taps_s + f * kMaxTaps;
-    const int64_t q0 = x.p0 - tile_start(x.cb, taps);  // tile index of p0, = 0 mod 4
+// The window accumulation of one thread's 4 outputs, out of line so that the
+// interpreter's eight FIRACC cases stay small. tile/h: window f's staged
+// samples and taps in shared memory; q0: the tile index of the thread's first
+// position (a multiple of 4).
+__device__ __noinline__ float4 fir_acc_window(const float* tile, const float* h, int taps,
+                                              int q0) {
     float2 a01 = make_float2(0.0f, 0.0f), a23 = make_float2(0.0f, 0.0f);
     for (int k0 = 0; k0 < taps; k0 += 4) {
         const float* w = tile + (q0 - k0 - 4);
@@ -189,6 +190,12 @@ __device__ __forceinline__ float4 fir_acc(const Program& P, int f, const Exec& x
     return make_float4(a01.x, a01.y, a23.x, a23.y);
 }
 
+__device__ __forceinline__ float4 fir_acc(const Program& P, int f, const Exec& x) {
+    const int taps = P.fir[f].taps;
+    return fir_acc_window(x.tiles + f * kTileF, x.taps_s + f * kMaxTaps, taps,
+                          (int)(x.p0 - tile_start(x.cb, taps)));
+}
+
 __device__ __forceinline__ float4 f4_add(float4 a, float4 b) {
     return make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z),
                        __fadd_rn(a.w, b.w));
@@ -197,7 +204,8 @@ __device__ __forceinline__ float4 f4_mul(float4 a, float4 b) {
     return make_float4(__fmul_rn(a.x, b.x), __fmul_rn(a.y, b.y), __fmul_rn(a.z, b.z),
                        __fmul_rn(a.w, b.w));
 }
-__device__ __forceinline__ float4 f4_hypot(float4 a, float4 b) {
+// Out of line: 64 interpreter cases call it.
+__device__ __noinline__ float4 f4_hypot(float4 a, float4 b) {
     return make_float4(hypot_go(a.x, b.x), hypot_go(a.y, b.y), hypot_go(a.z, b.z),
                        hypot_go(a.w, b.w));
 }
@@ -242,7 +250,9 @@ __device__ __forceinline__ float4 f4_abs(float4 a) {
 #define M_HYPOT(op, d, s) SG_C2(op, d, s, r[d] = f4_hypot(r[d], r[s]))
 
 // Runs the program from pc until OP_END for the thread's 4 positions.
-__device__ __noinline__ void interpret(const Program& P, int pc, const Exec& x) {
+// Inlined at its one call site in k_tile, so the program words are read
+// straight from the kernel's parameter bank and x stays in registers.
+__device__ __forceinline__ void interpret(const Program& P, int pc, const Exec& x) {
     float4 r[kSlots];
 #pragma unroll
     for (int i = 0; i < kSlots; i++) r[i] = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -368,20 +378,31 @@ __global__ void __launch_bounds__(kThreads) k_tile(const __grid_constant__ Progr
             x.sin = buf;
             x.sorg = sp.org;
         }
-        if (P.n_fir > 0) {
-            for (int f = 0; f < P.n_fir; f++) {
-                const int64_t ts = tile_start(cb, P.fir[f].taps);
-                const int64_t span = cb + kChunk - ts;
-                for (int64_t off = 4 * tid; off < span; off += 4 * kThreads) {
-                    x.p0 = ts + off;
-                    x.stage = tiles + f * kTileF + off;
-                    interpret(P, P.fir[f].start, x);
-                }
+        // Jobs f = 0 .. n_fir-1 stage window f's signal over its span (the
+        // chunk plus the halo); job n_fir is the main program over the
+        // chunk. One loop, so the interpreter is inlined exactly once.
+        const int nf = P.n_fir;
+        for (int f = 0; f <= nf; f++) {
+            int64_t base, span;
+            int pc;
+            float* st = tiles;
+            if (f < nf) {
+                base = tile_start(cb, P.fir[f].taps);
+                span = cb + kChunk - base;
+                pc = P.fir[f].start;
+                st = tiles + f * kTileF;
+            } else {
+                base = cb;
+                span = min((int64_t)kChunk, n - cb);
+                pc = P.main_start;
             }
-            __syncthreads();
+            for (int64_t off = 4 * tid; off < span; off += 4 * kThreads) {
+                x.p0 = base + off;
+                x.stage = st + off;
+                interpret(P, pc, x);
+            }
+            if (f + 1 == nf) __syncthreads();  // windows staged before main reads them
         }
-        x.p0 = cb + 4 * tid;
-        if (x.p0 < n) interpret(P, P.main_start, x);
         if (BULK) {
             // Every thread is done with this stage (and with the tiles);
             // order those generic accesses before the next bulk copy into it.
