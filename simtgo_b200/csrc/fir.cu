@@ -5,20 +5,20 @@
 // order and rounding of the reference's device code, where nvcc contracts
 // `acc += h[k] * tile[...]` (kernels/prebuilt/FIR.cu:24-27).
 //
-// B200 design. A 256-thread block produces 9216 consecutive outputs; thread
-// t owns 36 consecutive outputs, so every sample it loads from shared memory
-// feeds up to 36 fused multiply-adds from registers (the reference does one
+// B200 design. A 256-thread block produces 5120 consecutive outputs; thread
+// t owns 20 consecutive outputs, so every sample it loads from shared memory
+// feeds up to 20 fused multiply-adds from registers (the reference does one
 // output per thread, with one shared load and one global tap load per
 // multiply-add):
 //  * the block's signal span (its outputs plus the taps-1 halo) arrives by
 //    one 1-D bulk copy (cp.async.bulk, TMA) into a LINEAR shared tile;
-//  * 36 outputs per thread put lane t's window 144 bytes after lane t-1's,
-//    so the eight lanes of each 16-byte load phase hit eight different bank
-//    groups: conflict-free without any swizzle or padding, and every window
-//    load is base + a compile-time offset;
-//  * per chunk of 8 taps a thread issues twelve 16-byte shared loads (the 43
+//  * 20 outputs per thread put lane t's window 80 bytes after lane t-1's
+//    (5 x 16 B, odd), so the eight lanes of each 16-byte load phase hit
+//    eight different bank groups: conflict-free without any swizzle or
+//    padding, and every window load is base + a compile-time offset;
+//  * per chunk of 8 taps a thread issues eight 16-byte shared loads (the 27
 //    samples its outputs need, aligned down) and two broadcast tap loads,
-//    then 8 x 36 FFMA with every operand in a register;
+//    then 20 x 8 FFMA with every operand in a register;
 //  * the window's alignment within a 16-byte chunk, (D - 7) mod 4, is the
 //    same for every block and chunk, so it is a template parameter;
 //  * the outputs are staged back into the same shared tile and leave by one
@@ -34,10 +34,17 @@ using namespace sgd;
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int kPerThread = 36;                   // outputs per thread
-constexpr int kTileOut = kThreads * kPerThread;  // 9216 outputs per block
+constexpr int kMinBlocks = 4;  // blocks per SM the register budget is sized for
+// Outputs per thread: lane windows are 4*kPerThread bytes apart, so
+// kPerThread/4 must be odd for the 8 lanes of a 16-byte load phase to hit 8
+// different bank groups. 20 (with 4 blocks per SM) measured fastest of
+// 20/28/36/44: the FFMA rate depends on how the accumulators and the window
+// share the register file, not only on reuse.
+constexpr int kPerThread = 20;
+static_assert(kPerThread % 4 == 0 && (kPerThread / 4) % 2 == 1, "lane stride must be odd x 16 B");
+constexpr int kTileOut = kThreads * kPerThread;  // outputs per tile
 constexpr int kChunk = 8;                        // taps per register chunk
-constexpr int kWin4 = 12;                        // window float4s (48 floats >= 43 + 3)
+constexpr int kWin4 = (kPerThread + 10 + 3) / 4;  // window float4s: kPerThread + 7 + SH floats
 
 struct FirGeom {
     int64_t y_len;   // outputs of this launch
@@ -71,7 +78,7 @@ __device__ __forceinline__ void bulk_store_drain() {
     asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
 
-// Loads the window of one chunk: wv[i] = w[i], i < 48, w 16-byte aligned.
+// Loads the window of one chunk: wv[i] = w[i], i < 4*kWin4, w 16-byte aligned.
 __device__ __forceinline__ void load_window(const float* __restrict__ w, float (&wv)[4 * kWin4]) {
 #pragma unroll
     for (int c = 0; c < kWin4; c++) {
@@ -83,7 +90,7 @@ __device__ __forceinline__ void load_window(const float* __restrict__ w, float (
     }
 }
 
-// A whole chunk of 8 taps for this thread's 36 outputs. Output r at tap u of
+// A whole chunk of 8 taps for this thread's outputs. Output r at tap u of
 // the chunk reads tile position s + 7 + r - u, i.e. wv[SH + 7 + r - u].
 template <int SH>
 __device__ __forceinline__ void fir_chunk(const float* __restrict__ w, const float* hs,
@@ -93,10 +100,11 @@ __device__ __forceinline__ void fir_chunk(const float* __restrict__ w, const flo
     const float4 ha = *reinterpret_cast<const float4*>(hs);
     const float4 hb = *reinterpret_cast<const float4*>(hs + 4);
     const float hv[kChunk] = {ha.x, ha.y, ha.z, ha.w, hb.x, hb.y, hb.z, hb.w};
+    // Output-major: each accumulator takes its 8 taps back to back.
 #pragma unroll
-    for (int u = 0; u < kChunk; u++)
+    for (int r = 0; r < kPerThread; r++)
 #pragma unroll
-        for (int r = 0; r < kPerThread; r++)
+        for (int u = 0; u < kChunk; u++)
             acc[r] = __fmaf_rn(hv[u], wv[SH + 7 + r - u], acc[r]);
 }
 
@@ -116,10 +124,10 @@ __device__ __forceinline__ void fir_chunk_tail(const float* __restrict__ w, cons
         }
 }
 
-// Tile t = outputs [ob, ob + 9216), ob = 9216 t. Its shared buffer holds
+// Tile t = outputs [ob, ob + kTileOut), ob = kTileOut t. Its shared buffer holds
 // samples [A, A + tile) of x (x-index = j + halo for output j),
-// A = ob + halo - D, zero outside [0, x_len). Output ob + 36i + r at tap k
-// reads buffer index D + 36i + r - k, with D = taps + 6 + ((halo - taps - 6)
+// A = ob + halo - D, zero outside [0, x_len). Output ob + 20i + r at tap k
+// reads buffer index D + 20i + r - k, with D = taps + 6 + ((halo - taps - 6)
 // mod 4), so A is a multiple of 4 (16-byte aligned when x is) and the window
 // of the last, partial chunk (up to 7 taps past the end) stays inside.
 struct Span {
@@ -134,13 +142,15 @@ __device__ __forceinline__ Span tile_span(int64_t t, const FirGeom& g, bool bulk
     return s;
 }
 
-// Persistent: each block walks tiles blockIdx.x, +gridDim.x, ... with two
-// shared buffers, so tile i+1's signal span streams in (one bulk copy,
-// completing on that buffer's mbarrier) while tile i is computed. A tile's
-// outputs are staged in its own buffer and leave by one bulk store; the
-// buffer is refilled (tile i+2) once that store has read it.
+// Each block walks tiles blockIdx.x, +gridDim.x, ... with two shared
+// buffers: with fewer blocks than tiles, tile i+1's signal span streams in
+// (one bulk copy, completing on that buffer's mbarrier) while tile i is
+// computed, and a buffer is refilled (tile i+2) once the bulk store of its
+// outputs has read it. The launch gives every tile its own block, which
+// measured faster on B200: four resident blocks per SM overlap one block's
+// load with the others' FMAs without the per-tile drain.
 template <int SH>
-__global__ void __launch_bounds__(kThreads, 2) k_fir(float* __restrict__ y,
+__global__ void __launch_bounds__(kThreads, kMinBlocks) k_fir(float* __restrict__ y,
                                                       const float* __restrict__ x,
                                                       const float* __restrict__ h, FirGeom g,
                                                       int64_t ntiles, bool bulk_in, bool bulk_out,
@@ -189,7 +199,7 @@ __global__ void __launch_bounds__(kThreads, 2) k_fir(float* __restrict__ y,
         float acc[kPerThread];
 #pragma unroll
         for (int r = 0; r < kPerThread; r++) acc[r] = 0.0f;
-        // Window start at chunk k0: D - 7 - SH + 36 tid - k0 (a multiple of 4).
+        // Window start at chunk k0: D - 7 - SH + 20 tid - k0 (a multiple of 4).
         const float* w = tile + (g.D - 7 - SH) + kPerThread * tid;
         int k0 = 0;
         for (; k0 + kChunk <= g.taps; k0 += kChunk) fir_chunk<SH>(w - k0, hs + k0, acc);
@@ -240,9 +250,9 @@ int launch_fir(const char* K, float* y, int64_t y_len, const float* x, int64_t x
     // ob is a multiple of 4, so D (and with it SH) is the same for every block.
     const int64_t m = (((halo - taps - 6) % 4) + 4) % 4;
     g.D = (int32_t)(taps + 6 + m);
-    // The window loads of the last thread reach up to 4 floats past the last
-    // sample its outputs use (whole 16-byte loads): 4 floats of slack.
-    g.tile = (int32_t)sg::ceil_div(g.D + kTileOut + 4, 4) * 4;
+    // The window loads of the last thread reach a few floats past the last
+    // sample its outputs use (whole 16-byte loads): 8 floats of slack.
+    g.tile = (int32_t)sg::ceil_div(g.D + kTileOut + 8, 4) * 4;
     const int sh = (g.D - 7) % 4;
 
     static const FirKernel kernels[4] = {k_fir<0>, k_fir<1>, k_fir<2>, k_fir<3>};
@@ -261,8 +271,14 @@ int launch_fir(const char* K, float* y, int64_t y_len, const float* x, int64_t x
         "cudaOccupancyMaxActiveBlocksPerMultiprocessor(FIR)");
     if (rc) return rc;
     const int64_t ntiles = sg::ceil_div(y_len, kTileOut);
-    const int blocks =
-        (int)std::min<int64_t>(ntiles, (int64_t)d->sms * std::max(1, per_sm));
+    const int64_t resident = (int64_t)d->sms * std::max(1, per_sm);
+    // One tile per block measured faster than a persistent grid (the
+    // hardware starts the next block's load while this one computes), so
+    // the grid covers every tile; the loop in k_fir also serves a grid that
+    // does not.
+    (void)resident;
+    const int blocks = (int)ntiles;
+    if (ntiles > 0x7fffffffLL) return sg::fail(SIMTGO_ESIZE, "%s: y_len too large", K);
     sg::before_launch();
     kern<<<blocks, kThreads, smem, (cudaStream_t)stream>>>(
         y, x, h, g, ntiles, sg::aligned16(x), sg::aligned16(y), sg::watchdog_device_ptr());
