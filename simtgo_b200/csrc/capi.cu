@@ -62,6 +62,7 @@ int current_device(const DevInfo** out) {
         d.cc_major = p.major;
         d.cc_minor = p.minor;
         d.max_smem_optin = (int)p.sharedMemPerBlockOptin;
+        d.smem_per_sm = (int)p.sharedMemPerMultiprocessor;
         d.device = dev;
     }
     *out = &d;

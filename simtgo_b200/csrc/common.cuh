@@ -28,6 +28,7 @@ struct DevInfo {
     int sms = 0;
     int cc_major = 0, cc_minor = 0;
     int max_smem_optin = 0;
+    int smem_per_sm = 0;
 };
 // Properties of the current device (cached). Returns 0 or a status code.
 int current_device(const DevInfo** out);

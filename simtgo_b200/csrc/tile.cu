@@ -4,25 +4,26 @@
 //
 // The reference renders each graph as CUDA C and compiles it with NVRTC per
 // distinct graph (tile/run.go:40). Here the graph is lowered on the host to a
-// short register program that travels in the kernel's parameter block (the
-// constant bank), and ONE precompiled sm_100a kernel interprets it:
-//  * a thread owns 4 consecutive elements; values live in 8 register slots
-//    of 4 floats each;
-//  * every instruction is warp-uniform, and each (operation, slot, slot)
-//    combination is its own case of one switch, so all slot indices are
-//    compile-time and values never leave registers;
+// short register program that travels in the kernel's parameter block, and
+// ONE precompiled sm_100a kernel interprets it:
+//  * a block works on chunks of 2048 elements, a thread on 8 consecutive
+//    ones; values live in 8 register slots of 8 floats each;
+//  * the program is copied to shared memory once per block; every
+//    instruction is warp-uniform and dispatches on its kind, then on its
+//    destination (and source) slot, so all slot indices are compile-time and
+//    values never leave registers;
 //  * every input is read from HBM once: a block's chunk of each input (plus
-//    the windows' halo) is brought into shared memory by cp.async.bulk,
-//    double-buffered so the next chunk streams in while this one is
-//    interpreted (inputs that are not 16-byte aligned are loaded directly,
-//    with the loads hoisted to the program's start); the result is written
-//    once with 16-byte streaming stores -- 4 bytes per input and 4 bytes out
-//    per element, one pass over HBM;
+//    the windows' halo) is brought into shared memory by cp.async.bulk, in
+//    as many stages as the block's share of the SM's shared memory holds, so
+//    later chunks stream in while one is interpreted (inputs that are not
+//    16-byte aligned are loaded directly); the result is written once with
+//    16-byte streaming stores -- 4 bytes per input and 4 bytes out per
+//    element, one pass over HBM;
 //  * a windowed (FIR) node is evaluated as in tile/codegen.go:80-108: its
-//    signal sub-expression is run by the same interpreter over the block's
-//    span plus a halo of taps-1 (zero outside the signal), staged in shared
+//    signal sub-expression is run by the same interpreter over the chunk
+//    plus a halo of taps-1 (zero outside the signal), staged in shared
 //    memory, then each thread forms fma(h[k], tile, acc) in k order for its
-//    4 outputs from two 16-byte shared loads per 4 taps.
+//    8 outputs from three 16-byte shared loads per 4 taps.
 // Every operation is rounded on its own (Scale = k*x, Add, Mul, Sqrt
 // correctly rounded, Abs exact, Hypot = gpu.Hypot), so the fused program and
 // the stepwise one (one launch per node, tile/run.go:89) agree bit for bit.
@@ -31,6 +32,7 @@
 #include <string.h>
 
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 #include <string>
 #include <unordered_map>
@@ -45,31 +47,38 @@ using namespace sgd;
 namespace tilek {
 
 constexpr int kSlots = 8;
-constexpr int kV = 4;  // elements per thread
+constexpr int kV = 8;  // elements per thread per instruction
 constexpr int kThreads = 256;
 constexpr int kChunk = kThreads * kV;  // elements per block iteration
 constexpr int kMaxCode = 1024;
 constexpr int kMaxIn = 32;
 constexpr int kMaxFir = 8;
 constexpr int kMaxTaps = SIMTGO_TILE_MAX_TAPS;
-constexpr int kTileF = kChunk + kMaxTaps + 8;  // staged floats per window node
+constexpr int kTileF = kChunk + kMaxTaps + 16;  // staged floats per window node
+constexpr int kMaxStages = 16;                 // input stages in flight (bulk mode)
 
-// Instruction codes: one per (operation, destination slot, source slot).
-enum : uint16_t {
+// An instruction word is kind << 6 | d << 3 | s: the operation, the
+// destination slot and the source slot. The interpreter dispatches on the
+// kind (12 cases), then on d or on (d, s) (8 or 64 cases): small dense
+// switches with compile-time slot indices in every case.
+enum Op : uint16_t {
     OP_END = 0,
-    OP_LOAD = 1,      // + d            aux = input index
-    OP_STORE = 9,     // + s
-    OP_STAGE = 17,    // + s
-    OP_FIRACC = 25,   // + d            aux = window index
-    OP_SCALE = 33,    // + d (in place) imm = k
-    OP_SQRT = 41,     // + d
-    OP_ABS = 49,      // + d
-    OP_MOV = 57,      // + 8d + s
-    OP_ADD = 121,     // + 8d + s: r[d] = r[d] + r[s]
-    OP_MUL = 185,     // + 8d + s
-    OP_HYPOT = 249,   // + 8d + s
-    OP_COUNT = 313,
+    OP_LOAD,    // r[d] = input aux
+    OP_STORE,   // out = r[d]
+    OP_STAGE,   // window tile = r[d]
+    OP_FIRACC,  // r[d] = window aux accumulated at the thread's positions
+    OP_SCALE,   // r[d] = imm * r[d]
+    OP_SQRT,    // r[d] = sqrt(r[d])
+    OP_ABS,     // r[d] = |r[d]|
+    OP_MOV,     // r[d] = r[s]
+    OP_ADD,     // r[d] = r[d] + r[s]
+    OP_MUL,     // r[d] = r[d] * r[s]
+    OP_HYPOT,   // r[d] = hypot(r[d], r[s])
+    OP_KINDS,
 };
+__host__ __device__ constexpr uint16_t enc(int op, int d, int s = 0) {
+    return (uint16_t)((op << 6) | (d << 3) | s);
+}
 
 struct Insn {
     uint16_t code;
@@ -93,8 +102,26 @@ struct Program {
     Insn code[kMaxCode];
 };
 
+// Eight consecutive elements of one value.
+struct V8 {
+    float4 a, b;
+};
+
+// The program as the interpreter reads it: copied once per block from the
+// parameter bank into shared memory, where a warp-uniform word is one
+// broadcast load (the parameter bank, indexed by a run-time pc, is not).
+// Layout: code[code_cap] | in[n_in] | fir[n_fir] (start, taps), 16-byte
+// rounded.
+__host__ __device__ constexpr int meta_code_cap(int n_code) { return (n_code + 2) & ~1; }
+__host__ __device__ constexpr int meta_bytes(int n_code, int n_in, int n_fir) {
+    return ((meta_code_cap(n_code) * 8 + n_in * 8 + n_fir * 8) + 15) & ~15;
+}
+
 struct Exec {
-    int64_t p0;     // first of the thread's 4 positions
+    const Insn* code;         // shared copy of Program::code
+    const float* const* in;   // shared copy of Program::in
+    const int2* fir;          // shared (start, taps) of each window node
+    int64_t p0;     // first of the thread's 8 positions
     int64_t n;      // shard length
     int64_t halo;   // positions [-halo, n) are valid
     bool vec;       // all inputs and out are 16-byte aligned
@@ -110,49 +137,64 @@ struct Exec {
     int32_t sstride;
 };
 
-__device__ __forceinline__ float4 load_pos(const Program& P, int k, const Exec& x) {
-    const int64_t p = x.p0;
-    const bool inside = p >= -x.halo && p + 3 < x.n;
-    if (x.sin) {
-        // Shared memory: always one aligned 16-byte load; lanes outside the
-        // signal read whatever the buffer holds there and are zeroed.
-        const float4 v = *reinterpret_cast<const float4*>(x.sin + (int64_t)k * x.sstride + (p - x.sorg));
-        if (inside) return v;
-        return make_float4((p + 0 >= -x.halo && p + 0 < x.n) ? v.x : 0.0f,
-                           (p + 1 >= -x.halo && p + 1 < x.n) ? v.y : 0.0f,
-                           (p + 2 >= -x.halo && p + 2 < x.n) ? v.z : 0.0f,
-                           (p + 3 >= -x.halo && p + 3 < x.n) ? v.w : 0.0f);
+__device__ __forceinline__ float lane_of(const V8& v, int e) {
+    switch (e) {
+        case 0: return v.a.x;
+        case 1: return v.a.y;
+        case 2: return v.a.z;
+        case 3: return v.a.w;
+        case 4: return v.b.x;
+        case 5: return v.b.y;
+        case 6: return v.b.z;
+        default: return v.b.w;
     }
-    const float* base = P.in[k];
-    if (x.vec && inside) return ld_stream_f4(base + p);
-    float4 v;
-    v.x = (p + 0 >= -x.halo && p + 0 < x.n) ? base[p + 0] : 0.0f;
-    v.y = (p + 1 >= -x.halo && p + 1 < x.n) ? base[p + 1] : 0.0f;
-    v.z = (p + 2 >= -x.halo && p + 2 < x.n) ? base[p + 2] : 0.0f;
-    v.w = (p + 3 >= -x.halo && p + 3 < x.n) ? base[p + 3] : 0.0f;
-    return v;
 }
 
-__device__ __forceinline__ void store_pos(const float4 v, const Exec& x) {
+// Lanes of v at positions outside [-halo, n) replaced by 0.
+__device__ __forceinline__ V8 mask_outside(V8 v, const Exec& x) {
     const int64_t p = x.p0;
-    if (x.vec && p + 3 < x.n) {
-        st_stream_f4(x.out + p, v);
+    if (p >= -x.halo && p + 7 < x.n) return v;
+    float f[8] = {v.a.x, v.a.y, v.a.z, v.a.w, v.b.x, v.b.y, v.b.z, v.b.w};
+#pragma unroll
+    for (int e = 0; e < 8; e++)
+        if (!(p + e >= -x.halo && p + e < x.n)) f[e] = 0.0f;
+    return {make_float4(f[0], f[1], f[2], f[3]), make_float4(f[4], f[5], f[6], f[7])};
+}
+
+__device__ __forceinline__ V8 load_pos(int k, const Exec& x) {
+    const int64_t p = x.p0;
+    if (x.sin) {
+        // Shared memory: two aligned 16-byte loads; lanes outside the signal
+        // read whatever the buffer holds there and are zeroed.
+        const float* s = x.sin + (int64_t)k * x.sstride + (p - x.sorg);
+        V8 v = {*reinterpret_cast<const float4*>(s), *reinterpret_cast<const float4*>(s + 4)};
+        return mask_outside(v, x);
+    }
+    const float* base = x.in[k];
+    if (x.vec && p >= -x.halo && p + 7 < x.n)
+        return {ld_stream_f4(base + p), ld_stream_f4(base + p + 4)};
+    float f[8];
+#pragma unroll
+    for (int e = 0; e < 8; e++) f[e] = (p + e >= -x.halo && p + e < x.n) ? base[p + e] : 0.0f;
+    return {make_float4(f[0], f[1], f[2], f[3]), make_float4(f[4], f[5], f[6], f[7])};
+}
+
+__device__ __forceinline__ void store_pos(const V8& v, const Exec& x) {
+    const int64_t p = x.p0;
+    if (x.vec && p + 7 < x.n) {
+        st_stream_f4(x.out + p, v.a);
+        st_stream_f4(x.out + p + 4, v.b);
         return;
     }
-    if (p + 0 < x.n) x.out[p + 0] = v.x;
-    if (p + 1 < x.n) x.out[p + 1] = v.y;
-    if (p + 2 < x.n) x.out[p + 2] = v.z;
-    if (p + 3 < x.n) x.out[p + 3] = v.w;
+#pragma unroll
+    for (int e = 0; e < 8; e++)
+        if (p + e < x.n) x.out[p + e] = lane_of(v, e);
 }
 
-__device__ __forceinline__ void stage_pos(const float4 v, const Exec& x) {
-    const int64_t p = x.p0;
-    float4 s;
-    s.x = (p + 0 >= -x.halo && p + 0 < x.n) ? v.x : 0.0f;
-    s.y = (p + 1 >= -x.halo && p + 1 < x.n) ? v.y : 0.0f;
-    s.z = (p + 2 >= -x.halo && p + 2 < x.n) ? v.z : 0.0f;
-    s.w = (p + 3 >= -x.halo && p + 3 < x.n) ? v.w : 0.0f;
-    *reinterpret_cast<float4*>(x.stage) = s;
+__device__ __forceinline__ void stage_pos(const V8& v, const Exec& x) {
+    const V8 s = mask_outside(v, x);
+    *reinterpret_cast<float4*>(x.stage) = s.a;
+    *reinterpret_cast<float4*>(x.stage + 4) = s.b;
 }
 
 // Window start of node f for chunk cb: 16-byte aligned, 4 floats of slack
@@ -161,37 +203,37 @@ __device__ __forceinline__ int64_t tile_start(int64_t cb, int taps) {
     return ((cb - (taps - 1)) & ~int64_t(3)) - 4;
 }
 
-// The window accumulation of one thread's 4 outputs, out of line so that the
-// interpreter's eight FIRACC cases stay small. tile/h: window f's staged
-// samples and taps in shared memory; q0: the tile index of the thread's first
-// position (a multiple of 4).
-__device__ __noinline__ float4 fir_acc_window(const float* tile, const float* h, int taps,
-                                              int q0) {
-    float2 a01 = make_float2(0.0f, 0.0f), a23 = make_float2(0.0f, 0.0f);
+// The window accumulation of one thread's 8 outputs, out of line so that the
+// interpreter's FIRACC cases stay small. tile/h: the window's staged samples
+// and taps in shared memory; q0: the tile index of the thread's first
+// position (a multiple of 4). Output e at tap k0+u reads tile index
+// q0 + e - k0 - u = w[4 + e - u] with w = tile + q0 - k0 - 4.
+__device__ __noinline__ V8 fir_acc_window(const float* tile, const float* h, int taps, int q0) {
+    float acc[8];
+#pragma unroll
+    for (int e = 0; e < 8; e++) acc[e] = 0.0f;
     for (int k0 = 0; k0 < taps; k0 += 4) {
         const float* w = tile + (q0 - k0 - 4);
-        const float4 lo = *reinterpret_cast<const float4*>(w);
-        const float4 hi = *reinterpret_cast<const float4*>(w + 4);
-        const float wv[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+        const float4 w0 = *reinterpret_cast<const float4*>(w);
+        const float4 w1 = *reinterpret_cast<const float4*>(w + 4);
+        const float4 w2 = *reinterpret_cast<const float4*>(w + 8);
+        const float wv[12] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w,
+                              w2.x, w2.y, w2.z, w2.w};
         const float4 hk = *reinterpret_cast<const float4*>(h + k0);
         const float hv[4] = {hk.x, hk.y, hk.z, hk.w};
         const int nk = min(4, taps - k0);
 #pragma unroll
-        for (int u = 0; u < 4; u++) {
-            if (u < nk) {
-                // output e at tap k0+u reads position p0 + e - k0 - u = wv[4 + e - u];
-                // outputs (0,1) and (2,3) advance as packed pairs, each lane fmaf.
-                const float2 hh = make_float2(hv[u], hv[u]);
-                a01 = __ffma2_rn(hh, make_float2(wv[4 - u], wv[5 - u]), a01);
-                a23 = __ffma2_rn(hh, make_float2(wv[6 - u], wv[7 - u]), a23);
-            }
-        }
+        for (int u = 0; u < 4; u++)
+            if (u < nk)
+#pragma unroll
+                for (int e = 0; e < 8; e++) acc[e] = __fmaf_rn(hv[u], wv[4 + e - u], acc[e]);
     }
-    return make_float4(a01.x, a01.y, a23.x, a23.y);
+    return {make_float4(acc[0], acc[1], acc[2], acc[3]),
+            make_float4(acc[4], acc[5], acc[6], acc[7])};
 }
 
-__device__ __forceinline__ float4 fir_acc(const Program& P, int f, const Exec& x) {
-    const int taps = P.fir[f].taps;
+__device__ __forceinline__ V8 fir_acc(int f, const Exec& x) {
+    const int taps = x.fir[f].y;
     return fir_acc_window(x.tiles + f * kTileF, x.taps_s + f * kMaxTaps, taps,
                           (int)(x.p0 - tile_start(x.cb, taps)));
 }
@@ -204,11 +246,6 @@ __device__ __forceinline__ float4 f4_mul(float4 a, float4 b) {
     return make_float4(__fmul_rn(a.x, b.x), __fmul_rn(a.y, b.y), __fmul_rn(a.z, b.z),
                        __fmul_rn(a.w, b.w));
 }
-// Out of line: 64 interpreter cases call it.
-__device__ __noinline__ float4 f4_hypot(float4 a, float4 b) {
-    return make_float4(hypot_go(a.x, b.x), hypot_go(a.y, b.y), hypot_go(a.z, b.z),
-                       hypot_go(a.w, b.w));
-}
 __device__ __forceinline__ float4 f4_scale(float k, float4 a) {
     return make_float4(__fmul_rn(k, a.x), __fmul_rn(k, a.y), __fmul_rn(k, a.z),
                        __fmul_rn(k, a.w));
@@ -219,71 +256,125 @@ __device__ __forceinline__ float4 f4_sqrt(float4 a) {
 __device__ __forceinline__ float4 f4_abs(float4 a) {
     return make_float4(fabsf(a.x), fabsf(a.y), fabsf(a.z), fabsf(a.w));
 }
+__device__ __forceinline__ V8 v_add(const V8& p, const V8& q) {
+    return {f4_add(p.a, q.a), f4_add(p.b, q.b)};
+}
+__device__ __forceinline__ V8 v_mul(const V8& p, const V8& q) {
+    return {f4_mul(p.a, q.a), f4_mul(p.b, q.b)};
+}
+__device__ __forceinline__ V8 v_scale(float k, const V8& p) {
+    return {f4_scale(k, p.a), f4_scale(k, p.b)};
+}
+__device__ __noinline__ V8 v_sqrt(V8 p) { return {f4_sqrt(p.a), f4_sqrt(p.b)}; }
+__device__ __forceinline__ V8 v_abs(const V8& p) { return {f4_abs(p.a), f4_abs(p.b)}; }
+// Out of line: 64 interpreter cases call it.
+__device__ __noinline__ V8 v_hypot(V8 p, V8 q) {
+    return {make_float4(hypot_go(p.a.x, q.a.x), hypot_go(p.a.y, q.a.y), hypot_go(p.a.z, q.a.z),
+                        hypot_go(p.a.w, q.a.w)),
+            make_float4(hypot_go(p.b.x, q.b.x), hypot_go(p.b.y, q.b.y), hypot_go(p.b.z, q.b.z),
+                        hypot_go(p.b.w, q.b.w))};
+}
 
-#define SG_C1(op, d, body) \
-    case (op) + (d): {     \
-        body;              \
-        break;             \
-    }
-#define SG_ROW1(op, M) M(op, 0) M(op, 1) M(op, 2) M(op, 3) M(op, 4) M(op, 5) M(op, 6) M(op, 7)
-#define SG_C2(op, d, s, body)     \
-    case (op) + 8 * (d) + (s): { \
-        body;                     \
-        break;                    \
-    }
-#define SG_ROW2(op, M, d) \
-    M(op, d, 0) M(op, d, 1) M(op, d, 2) M(op, d, 3) M(op, d, 4) M(op, d, 5) M(op, d, 6) M(op, d, 7)
-#define SG_ALL2(op, M)                                                                    \
-    SG_ROW2(op, M, 0) SG_ROW2(op, M, 1) SG_ROW2(op, M, 2) SG_ROW2(op, M, 3) SG_ROW2(op, M, 4) \
-        SG_ROW2(op, M, 5) SG_ROW2(op, M, 6) SG_ROW2(op, M, 7)
+#define SG_D8(M) M(0) M(1) M(2) M(3) M(4) M(5) M(6) M(7)
+#define SG_S8(M, D) M(D, 0) M(D, 1) M(D, 2) M(D, 3) M(D, 4) M(D, 5) M(D, 6) M(D, 7)
+#define SG_DS64(M)                                                                         \
+    SG_S8(M, 0) SG_S8(M, 1) SG_S8(M, 2) SG_S8(M, 3) SG_S8(M, 4) SG_S8(M, 5) SG_S8(M, 6) \
+        SG_S8(M, 7)
 
-#define M_LOAD(op, d) SG_C1(op, d, r[d] = load_pos(P, in.aux, x))
-#define M_STORE(op, s) SG_C1(op, s, store_pos(r[s], x))
-#define M_STAGE(op, s) SG_C1(op, s, stage_pos(r[s], x))
-#define M_FIRACC(op, d) SG_C1(op, d, r[d] = fir_acc(P, in.aux, x))
-#define M_SCALE(op, d) SG_C1(op, d, r[d] = f4_scale(in.imm, r[d]))
-#define M_SQRT(op, d) SG_C1(op, d, r[d] = f4_sqrt(r[d]))
-#define M_ABS(op, d) SG_C1(op, d, r[d] = f4_abs(r[d]))
-#define M_MOV(op, d, s) SG_C2(op, d, s, r[d] = r[s])
-#define M_ADD(op, d, s) SG_C2(op, d, s, r[d] = f4_add(r[d], r[s]))
-#define M_MUL(op, d, s) SG_C2(op, d, s, r[d] = f4_mul(r[d], r[s]))
-#define M_HYPOT(op, d, s) SG_C2(op, d, s, r[d] = f4_hypot(r[d], r[s]))
+#define C_SET(D) \
+    case D:      \
+        r[D] = v;  \
+        break;
+#define C_GET(D) \
+    case D:      \
+        v = r[D];  \
+        break;
+#define C_SCALE(D)                      \
+    case D:                             \
+        r[D] = v_scale(in.imm, r[D]);   \
+        break;
+#define C_SQRT(D)           \
+    case D:                 \
+        r[D] = v_sqrt(r[D]); \
+        break;
+#define C_ABS(D)            \
+    case D:                 \
+        r[D] = v_abs(r[D]); \
+        break;
+#define C_MOV(D, S)     \
+    case 8 * D + S:     \
+        r[D] = r[S];    \
+        break;
+#define C_ADD(D, S)               \
+    case 8 * D + S:               \
+        r[D] = v_add(r[D], r[S]); \
+        break;
+#define C_MUL(D, S)               \
+    case 8 * D + S:               \
+        r[D] = v_mul(r[D], r[S]); \
+        break;
+#define C_HYPOT(D, S)               \
+    case 8 * D + S:                 \
+        r[D] = v_hypot(r[D], r[S]); \
+        break;
 
-// Runs the program from pc until OP_END for the thread's 4 positions.
-// Inlined at its one call site in k_tile, so the program words are read
-// straight from the kernel's parameter bank and x stays in registers.
-__device__ __forceinline__ void interpret(const Program& P, int pc, const Exec& x) {
-    float4 r[kSlots];
+// Runs the program from pc until OP_END for the thread's 8 positions.
+// Inlined at its one call site in k_tile, so x stays in registers. The next
+// word is loaded while this one executes (the copy holds one word past END).
+__device__ __forceinline__ void interpret(int pc, const Exec& x) {
+    V8 r[kSlots];
+    const V8 zero = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
 #pragma unroll
-    for (int i = 0; i < kSlots; i++) r[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (;; pc++) {
-        const Insn in = P.code[pc];
-        switch (in.code) {
-            case OP_END:
-                return;
-                SG_ROW1(OP_LOAD, M_LOAD)
-                SG_ROW1(OP_STORE, M_STORE)
-                SG_ROW1(OP_STAGE, M_STAGE)
-                SG_ROW1(OP_FIRACC, M_FIRACC)
-                SG_ROW1(OP_SCALE, M_SCALE)
-                SG_ROW1(OP_SQRT, M_SQRT)
-                SG_ROW1(OP_ABS, M_ABS)
-                SG_ALL2(OP_MOV, M_MOV)
-                SG_ALL2(OP_ADD, M_ADD)
-                SG_ALL2(OP_MUL, M_MUL)
-                SG_ALL2(OP_HYPOT, M_HYPOT)
+    for (int i = 0; i < kSlots; i++) r[i] = zero;
+    Insn next = x.code[pc];
+    for (;;) {
+        const Insn in = next;
+        next = x.code[++pc];
+        const int op = in.code >> 6, d = (in.code >> 3) & 7, ds = in.code & 63;
+        V8 v = zero;
+        switch (op) {
+            case OP_LOAD:
+                v = load_pos(in.aux, x);
+                switch (d) { SG_D8(C_SET) }
+                break;
+            case OP_FIRACC:
+                v = fir_acc(in.aux, x);
+                switch (d) { SG_D8(C_SET) }
+                break;
+            case OP_STORE:
+                switch (d) { SG_D8(C_GET) }
+                store_pos(v, x);
+                break;
+            case OP_STAGE:
+                switch (d) { SG_D8(C_GET) }
+                stage_pos(v, x);
+                break;
+            case OP_SCALE:
+                switch (d) { SG_D8(C_SCALE) }
+                break;
+            case OP_SQRT:
+                switch (d) { SG_D8(C_SQRT) }
+                break;
+            case OP_ABS:
+                switch (d) { SG_D8(C_ABS) }
+                break;
+            case OP_MOV:
+                switch (ds) { SG_DS64(C_MOV) }
+                break;
+            case OP_ADD:
+                switch (ds) { SG_DS64(C_ADD) }
+                break;
+            case OP_MUL:
+                switch (ds) { SG_DS64(C_MUL) }
+                break;
+            case OP_HYPOT:
+                switch (ds) { SG_DS64(C_HYPOT) }
+                break;
             default:
-                return;
+                return;  // OP_END
         }
     }
 }
-
-// Bulk-copy mode: the chunk's inputs (positions [cb - hs, cb + kChunk),
-// clipped to the signal) travel HBM -> shared memory by cp.async.bulk, one
-// copy per input, double-buffered across chunks and completing on a
-// per-stage mbarrier, so the next chunk streams in while this one is
-// interpreted. Requires every input 16-byte aligned and halo = 0 mod 4.
-constexpr int kStages = 2;
 
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,
                                          uint64_t* bar) {
@@ -307,21 +398,36 @@ __device__ __forceinline__ ChunkSpan chunk_span(int64_t cb, int hs, int64_t n, i
     return s;
 }
 
+// Bulk-copy mode (BULK): the chunk's inputs (positions [cb - hs, cb + kChunk),
+// clipped to the signal) travel HBM -> shared memory by cp.async.bulk, one
+// copy per input, in `nst` stages that complete on per-stage mbarriers, so
+// nst-1 chunks stream in while one is interpreted. Requires every input
+// 16-byte aligned and halo = 0 mod 4.
 template <bool BULK>
 __global__ void __launch_bounds__(kThreads) k_tile(const __grid_constant__ Program P,
                                                    float* __restrict__ out, int64_t n,
                                                    int64_t halo, bool vec, int32_t hs,
-                                                   uint32_t* wd) {
-    __shared__ __align__(8) uint64_t bars[kStages];
+                                                   int32_t nst, uint32_t* wd) {
+    __shared__ __align__(8) uint64_t bars[kMaxStages];
     extern __shared__ float4 sm4[];
-    float* sm = reinterpret_cast<float*>(sm4);
-    float* taps_s = sm;                       // n_fir x kMaxTaps
-    float* tiles = sm + P.n_fir * kMaxTaps;   // n_fir x kTileF
-    float* stages = tiles + P.n_fir * kTileF; // kStages x n_in x sstride (bulk mode)
-    const int32_t sstride = kChunk + hs;
+    const int code_cap = meta_code_cap(P.n_code);
+    Insn* code_s = reinterpret_cast<Insn*>(sm4);
+    const float** in_s = reinterpret_cast<const float**>(code_s + code_cap);
+    int2* fir_s = reinterpret_cast<int2*>(in_s + P.n_in);
+    float* sm = reinterpret_cast<float*>(sm4) + meta_bytes(P.n_code, P.n_in, P.n_fir) / 4;
+    float* taps_s = sm;                        // n_fir x kMaxTaps
+    float* tiles = sm + P.n_fir * kMaxTaps;    // n_fir x kTileF
+    float* stages = tiles + P.n_fir * kTileF;  // nst x n_in x sstride (bulk mode)
+    // Each input's buffer: the chunk and its halo, plus 8 floats that the
+    // last staging task's whole 8-float loads may touch past the chunk.
+    const int32_t sstride = kChunk + hs + 8;
     const int64_t stage_floats = (int64_t)P.n_in * sstride;
     const int tid = threadIdx.x;
     const int64_t nchunks = (n + kChunk - 1) / kChunk;
+    for (int i = tid; i < code_cap; i += kThreads)
+        code_s[i] = i < P.n_code ? P.code[i] : Insn{enc(OP_END, 0), 0, 0.0f};
+    for (int k = tid; k < P.n_in; k += kThreads) in_s[k] = P.in[k];
+    for (int f = tid; f < P.n_fir; f += kThreads) fir_s[f] = make_int2(P.fir[f].start, P.fir[f].taps);
     for (int f = 0; f < P.n_fir; f++)
         for (int k = tid; k < kMaxTaps; k += kThreads)
             taps_s[f * kMaxTaps + k] = P.fir[f].h[k];  // zero past taps
@@ -332,16 +438,16 @@ __global__ void __launch_bounds__(kThreads) k_tile(const __grid_constant__ Progr
         if (sp.len4 > 0)
             for (int k = 0; k < P.n_in; k++)
                 bulk_g2s(stages + s * stage_floats + (int64_t)k * sstride + (sp.lo - sp.org),
-                         P.in[k] + sp.lo, (uint32_t)(sp.len4 * 4), &bars[s]);
+                         in_s[k] + sp.lo, (uint32_t)(sp.len4 * 4), &bars[s]);
     };
     if (BULK) {
         if (tid == 0) {
-            for (int s = 0; s < kStages; s++) mbar_init(&bars[s], 1);
+            for (int s = 0; s < nst; s++) mbar_init(&bars[s], 1);
             fence_mbar_init();
         }
         __syncthreads();
         if (tid == 0)
-            for (int s = 0; s < kStages; s++) {
+            for (int s = 0; s < nst; s++) {
                 const int64_t c = blockIdx.x + (int64_t)s * gridDim.x;
                 if (c < nchunks) issue(c, s);
             }
@@ -349,6 +455,9 @@ __global__ void __launch_bounds__(kThreads) k_tile(const __grid_constant__ Progr
     __syncthreads();
 
     Exec x;
+    x.code = code_s;
+    x.in = in_s;
+    x.fir = fir_s;
     x.n = n;
     x.halo = halo;
     x.vec = vec;
@@ -356,14 +465,15 @@ __global__ void __launch_bounds__(kThreads) k_tile(const __grid_constant__ Progr
     x.taps_s = taps_s;
     x.tiles = tiles;
     x.sin = nullptr;
+    x.sorg = 0;
     x.sstride = sstride;
     int it = 0;
     for (int64_t c = blockIdx.x; c < nchunks; c += gridDim.x, it++) {
         const int64_t cb = c * kChunk;
         x.cb = cb;
         if (BULK) {
-            const int s = it % kStages;
-            if (!mbar_wait(&bars[s], (uint32_t)((it / kStages) & 1), wd)) return;
+            const int s = it % nst;
+            if (!mbar_wait(&bars[s], (uint32_t)((it / nst) & 1), wd)) return;
             const ChunkSpan sp = chunk_span(cb, hs, n, halo);
             float* buf = stages + s * stage_floats;
             // The last 0-3 samples of a ragged signal are not a whole 16-byte
@@ -372,7 +482,7 @@ __global__ void __launch_bounds__(kThreads) k_tile(const __grid_constant__ Progr
             if (tail > 0 && tid < P.n_in * 4) {
                 const int k = tid / 4, e = tid % 4;
                 const int64_t pos = sp.lo + sp.len4 + e;
-                if (e < tail) buf[(int64_t)k * sstride + (pos - sp.org)] = P.in[k][pos];
+                if (e < tail) buf[(int64_t)k * sstride + (pos - sp.org)] = in_s[k][pos];
             }
             __syncthreads();
             x.sin = buf;
@@ -387,19 +497,20 @@ __global__ void __launch_bounds__(kThreads) k_tile(const __grid_constant__ Progr
             int pc;
             float* st = tiles;
             if (f < nf) {
-                base = tile_start(cb, P.fir[f].taps);
+                const int2 fd = fir_s[f];
+                base = tile_start(cb, fd.y);
                 span = cb + kChunk - base;
-                pc = P.fir[f].start;
+                pc = fd.x;
                 st = tiles + f * kTileF;
             } else {
                 base = cb;
                 span = min((int64_t)kChunk, n - cb);
                 pc = P.main_start;
             }
-            for (int64_t off = 4 * tid; off < span; off += 4 * kThreads) {
+            for (int64_t off = kV * tid; off < span; off += kV * kThreads) {
                 x.p0 = base + off;
                 x.stage = st + off;
-                interpret(P, pc, x);
+                interpret(pc, x);
             }
             if (f + 1 == nf) __syncthreads();  // windows staged before main reads them
         }
@@ -409,8 +520,8 @@ __global__ void __launch_bounds__(kThreads) k_tile(const __grid_constant__ Progr
             fence_proxy_async_smem();
             __syncthreads();
             if (tid == 0) {
-                const int64_t cn = c + (int64_t)kStages * gridDim.x;
-                if (cn < nchunks) issue(cn, it % kStages);
+                const int64_t cn = c + (int64_t)nst * gridDim.x;
+                if (cn < nchunks) issue(cn, it % nst);
             }
         } else if (P.n_fir > 0) {
             __syncthreads();
@@ -544,7 +655,7 @@ int emit_program(const simtgo_tile_graph* g, int root, bool main, Lowered& L, bo
         } else {
             k = it->second;
         }
-        push(tilek::OP_LOAD + s, (uint16_t)k);
+        push(tilek::enc(tilek::OP_LOAD, s), (uint16_t)k);
         slot[id] = s;
         return s;
     };
@@ -570,7 +681,7 @@ int emit_program(const simtgo_tile_graph* g, int root, bool main, Lowered& L, bo
             if (d < 0) return -1;
             auto it = fir_index.find(id);
             if (it == fir_index.end()) return -3;
-            push(tilek::OP_FIRACC + d, (uint16_t)it->second);
+            push(tilek::enc(tilek::OP_FIRACC, d), (uint16_t)it->second);
             slot[id] = d;
             continue;
         }
@@ -587,18 +698,18 @@ int emit_program(const simtgo_tile_graph* g, int root, bool main, Lowered& L, bo
             } else {
                 d = alloc();
                 if (d < 0) return -1;
-                push(tilek::OP_MOV + 8 * d + sa);
+                push(tilek::enc(tilek::OP_MOV, d, sa));
                 release(n.a);
             }
-            if (n.kind == K_SCALE) push(tilek::OP_SCALE + d, 0, n.scale);
-            if (n.kind == K_SQRT) push(tilek::OP_SQRT + d);
-            if (n.kind == K_ABS) push(tilek::OP_ABS + d);
+            if (n.kind == K_SCALE) push(tilek::enc(tilek::OP_SCALE, d), 0, n.scale);
+            if (n.kind == K_SQRT) push(tilek::enc(tilek::OP_SQRT, d));
+            if (n.kind == K_ABS) push(tilek::enc(tilek::OP_ABS, d));
         } else {
             const int sb = need(n.b);
             if (sb < 0) return -1;
-            const uint16_t base = n.kind == K_ADD ? tilek::OP_ADD
-                                  : n.kind == K_MUL ? tilek::OP_MUL
-                                                    : tilek::OP_HYPOT;
+            const int bop = n.kind == K_ADD   ? tilek::OP_ADD
+                            : n.kind == K_MUL ? tilek::OP_MUL
+                                              : tilek::OP_HYPOT;
             if (n.a == n.b) {
                 if (uses[n.a] == 2) {
                     d = sa;
@@ -607,37 +718,37 @@ int emit_program(const simtgo_tile_graph* g, int root, bool main, Lowered& L, bo
                 } else {
                     d = alloc();
                     if (d < 0) return -1;
-                    push(tilek::OP_MOV + 8 * d + sa);
+                    push(tilek::enc(tilek::OP_MOV, d, sa));
                     release(n.a);
                     release(n.a);
                 }
-                push(base + 8 * d + d);
+                push(tilek::enc(bop, d, d));
             } else if (uses[n.a] == 1) {
                 d = sa;
                 slot[n.a] = -1;
                 uses[n.a] = 0;
-                push(base + 8 * d + sb);
+                push(tilek::enc(bop, d, sb));
                 release(n.b);
             } else if (uses[n.b] == 1) {
                 // Add, Mul and Hypot are commutative bit for bit.
                 d = sb;
                 slot[n.b] = -1;
                 uses[n.b] = 0;
-                push(base + 8 * d + sa);
+                push(tilek::enc(bop, d, sa));
                 release(n.a);
             } else {
                 d = alloc();
                 if (d < 0) return -1;
-                push(tilek::OP_MOV + 8 * d + sa);
-                push(base + 8 * d + sb);
+                push(tilek::enc(tilek::OP_MOV, d, sa));
+                push(tilek::enc(bop, d, sb));
                 release(n.a);
                 release(n.b);
             }
         }
         slot[id] = d;
     }
-    push((main ? tilek::OP_STORE : tilek::OP_STAGE) + slot[root]);
-    push(tilek::OP_END);
+    push(tilek::enc(main ? tilek::OP_STORE : tilek::OP_STAGE, slot[root]));
+    push(tilek::enc(tilek::OP_END, 0));
     return 0;
 }
 
@@ -723,20 +834,43 @@ int launch_program(Lowered& L, const std::vector<const float*>& dev_in, float* o
     for (int f = 0; f < L.prog.n_fir; f++)
         hs = std::max<int32_t>(hs, (L.prog.fir[f].taps - 1 + 3) / 4 * 4 + 4);
     const size_t base_smem =
+        tilek::meta_bytes(L.prog.n_code, L.prog.n_in, L.prog.n_fir) +
         (size_t)L.prog.n_fir * (tilek::kMaxTaps + tilek::kTileF) * sizeof(float);
-    const size_t bulk_smem = base_smem + (size_t)tilek::kStages * L.prog.n_in *
-                                             (tilek::kChunk + hs) * sizeof(float);
+    const size_t stage_bytes =
+        (size_t)L.prog.n_in * (tilek::kChunk + hs + 8) * sizeof(float);
+    // Both instantiations may take up to the opt-in maximum of dynamic
+    // shared memory (less 1 KB for the static mbarriers); the stage count
+    // below decides how much they use.
+    const int dyn_max = d->max_smem_optin - 1024;
+    static std::atomic<uint64_t> configured{0};
+    const uint64_t dev_bit = 1ull << (d->device & 63);
+    if (!(configured.load() & dev_bit)) {
+        for (auto k : {tilek::k_tile<true>, tilek::k_tile<false>}) {
+            rc = sg::cuda_status(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                      dyn_max),
+                                 "cudaFuncSetAttribute(tile)");
+            if (rc) return rc;
+        }
+        configured.fetch_or(dev_bit);
+    }
+    // Input stages: registers bound the blocks per SM; the stages then take
+    // that block's share of the SM's shared memory (2..kMaxStages chunks of
+    // every input in flight), since HBM latency x bandwidth per SM is tens
+    // of KB that must be outstanding at once.
+    int per_sm = 0;
+    rc = sg::cuda_status(cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+                             &per_sm, tilek::k_tile<true>, tilek::kThreads, base_smem),
+                         "cudaOccupancyMaxActiveBlocksPerMultiprocessor(tile)");
+    if (rc) return rc;
+    const int64_t share = std::min<int64_t>(dyn_max,
+                                            d->smem_per_sm / std::max(1, per_sm) - 2048);
+    int nst = (int)std::max<int64_t>(2, (share - (int64_t)base_smem) / (int64_t)stage_bytes);
+    nst = std::min(nst, tilek::kMaxStages);
+    const size_t bulk_smem = base_smem + nst * stage_bytes;
     const bool bulk = in_aligned && halo % 4 == 0 && L.prog.n_in > 0 &&
-                      bulk_smem <= (size_t)d->max_smem_optin;
+                      bulk_smem <= (size_t)dyn_max;
     const size_t smem = bulk ? bulk_smem : base_smem;
     auto kern = bulk ? tilek::k_tile<true> : tilek::k_tile<false>;
-    if (smem > 48 * 1024) {
-        rc = sg::cuda_status(
-            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
-            "cudaFuncSetAttribute(tile)");
-        if (rc) return rc;
-    }
-    int per_sm = 0;
     rc = sg::cuda_status(
         cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, tilek::kThreads, smem),
         "cudaOccupancyMaxActiveBlocksPerMultiprocessor(tile)");
@@ -745,7 +879,7 @@ int launch_program(Lowered& L, const std::vector<const float*>& dev_in, float* o
     const int blocks = (int)std::max<int64_t>(
         1, std::min<int64_t>(chunks, (int64_t)d->sms * std::max(1, per_sm)));
     sg::before_launch();
-    kern<<<blocks, tilek::kThreads, smem, s>>>(L.prog, out, n, halo, vec, hs,
+    kern<<<blocks, tilek::kThreads, smem, s>>>(L.prog, out, n, halo, vec, hs, nst,
                                                sg::watchdog_device_ptr());
     return sg::launch_status("tile");
 }
@@ -982,28 +1116,28 @@ static std::string listing(const simtgo_tile_graph* g, const Lowered& L) {
             }
         if (pc == L.prog.main_start) s += "main\n";
         const Insn& in = L.prog.code[pc];
-        const int c = in.code;
         using namespace tilek;
-        if (c == OP_END)
-            snprintf(line, sizeof line, "%d end\n", pc);
-        else if (c < OP_STORE)
-            snprintf(line, sizeof line, "%d load r%d in%d\n", pc, c - OP_LOAD, in.aux);
-        else if (c < OP_STAGE)
-            snprintf(line, sizeof line, "%d store r%d\n", pc, c - OP_STORE);
-        else if (c < OP_FIRACC)
-            snprintf(line, sizeof line, "%d stage r%d\n", pc, c - OP_STAGE);
-        else if (c < OP_SCALE)
-            snprintf(line, sizeof line, "%d firacc r%d w%d\n", pc, c - OP_FIRACC, in.aux);
-        else if (c < OP_SQRT)
-            snprintf(line, sizeof line, "%d scale r%d %a\n", pc, c - OP_SCALE, (double)in.imm);
-        else if (c < OP_ABS)
-            snprintf(line, sizeof line, "%d sqrt r%d\n", pc, c - OP_SQRT);
-        else if (c < OP_MOV)
-            snprintf(line, sizeof line, "%d abs r%d\n", pc, c - OP_ABS);
-        else {
-            const char* name = c < OP_ADD ? "mov" : c < OP_MUL ? "add" : c < OP_HYPOT ? "mul" : "hypot";
-            const int base = c < OP_ADD ? OP_MOV : c < OP_MUL ? OP_ADD : c < OP_HYPOT ? OP_MUL : OP_HYPOT;
-            snprintf(line, sizeof line, "%d %s r%d r%d\n", pc, name, (c - base) / 8, (c - base) % 8);
+        const int op = in.code >> 6, d = (in.code >> 3) & 7, sl = in.code & 7;
+        switch (op) {
+            case OP_END: snprintf(line, sizeof line, "%d end\n", pc); break;
+            case OP_LOAD: snprintf(line, sizeof line, "%d load r%d in%d\n", pc, d, in.aux); break;
+            case OP_STORE: snprintf(line, sizeof line, "%d store r%d\n", pc, d); break;
+            case OP_STAGE: snprintf(line, sizeof line, "%d stage r%d\n", pc, d); break;
+            case OP_FIRACC:
+                snprintf(line, sizeof line, "%d firacc r%d w%d\n", pc, d, in.aux);
+                break;
+            case OP_SCALE:
+                snprintf(line, sizeof line, "%d scale r%d %a\n", pc, d, (double)in.imm);
+                break;
+            case OP_SQRT: snprintf(line, sizeof line, "%d sqrt r%d\n", pc, d); break;
+            case OP_ABS: snprintf(line, sizeof line, "%d abs r%d\n", pc, d); break;
+            default: {
+                const char* name = op == OP_MOV   ? "mov"
+                                   : op == OP_ADD ? "add"
+                                   : op == OP_MUL ? "mul"
+                                                  : "hypot";
+                snprintf(line, sizeof line, "%d %s r%d r%d\n", pc, name, d, sl);
+            }
         }
         s += line;
     }
