@@ -4,29 +4,36 @@
 //
 // The reference renders each graph as CUDA C and compiles it with NVRTC per
 // distinct graph (tile/run.go:40). Here the graph is lowered on the host to a
-// short register program that travels in the kernel's parameter block, and
-// ONE precompiled sm_100a kernel interprets it:
-//  * a block works on chunks of 2048 elements, a thread on 8 consecutive
-//    ones; values live in 8 register slots of 8 floats each;
-//  * the program is copied to shared memory once per block; every
-//    instruction is warp-uniform and dispatches on its kind, then on its
-//    destination (and source) slot, so all slot indices are compile-time and
-//    values never leave registers;
+// short program for an accumulator machine that travels in the kernel's
+// parameter block, and ONE precompiled sm_100a kernel interprets it:
+//  * a block works on chunks of 2048 elements; a thread owns 2 float4 groups
+//    of each chunk (groups t and t + 256, so a warp's 16-byte shared-memory
+//    accesses are consecutive and conflict-free) held in an accumulator of
+//    8 registers;
+//  * every instruction combines the accumulator with at most one operand in
+//    shared memory -- a staged input, a temporary, or a window's staged
+//    signal -- so the interpreter dispatches on the operation alone and the
+//    operand is an address, not a register index: a dispatch costs a few
+//    instructions for 8 elements, and a thread needs few registers, so many
+//    warps hide the latency;
 //  * every input is read from HBM once: a block's chunk of each input (plus
 //    the windows' halo) is brought into shared memory by cp.async.bulk, in
 //    as many stages as the block's share of the SM's shared memory holds, so
 //    later chunks stream in while one is interpreted (inputs that are not
-//    16-byte aligned are loaded directly); the result is written once with
-//    16-byte streaming stores -- 4 bytes per input and 4 bytes out per
+//    16-byte aligned are copied by the threads); the result is written once
+//    with 16-byte streaming stores -- 4 bytes per input and 4 bytes out per
 //    element, one pass over HBM;
 //  * a windowed (FIR) node is evaluated as in tile/codegen.go:80-108: its
 //    signal sub-expression is run by the same interpreter over the chunk
 //    plus a halo of taps-1 (zero outside the signal), staged in shared
 //    memory, then each thread forms fma(h[k], tile, acc) in k order for its
-//    8 outputs from three 16-byte shared loads per 4 taps.
+//    8 outputs, one new 16-byte shared load per group per 4 taps. The staged
+//    signal also serves the main program wherever it uses that node.
 // Every operation is rounded on its own (Scale = k*x, Add, Mul, Sqrt
 // correctly rounded, Abs exact, Hypot = gpu.Hypot), so the fused program and
 // the stepwise one (one launch per node, tile/run.go:89) agree bit for bit.
+// Add, Mul and Hypot are commutative bit for bit, which lets the lowering
+// keep either operand in the accumulator.
 #include <stdarg.h>
 #include <stdio.h>
 #include <string.h>
@@ -46,49 +53,54 @@ using namespace sgd;
 
 namespace tilek {
 
-constexpr int kSlots = 8;
-constexpr int kV = 8;  // elements per thread per instruction
 constexpr int kThreads = 256;
-constexpr int kChunk = kThreads * kV;  // elements per block iteration
+constexpr int kG = 2;                  // float4 groups per thread
+constexpr int kChunk = kThreads * 4 * kG;  // elements per block iteration
+constexpr int kChunk4 = kChunk / 4;
 constexpr int kMaxCode = 1024;
 constexpr int kMaxIn = 32;
 constexpr int kMaxFir = 8;
+constexpr int kMaxTmp = 8;
 constexpr int kMaxTaps = SIMTGO_TILE_MAX_TAPS;
-constexpr int kTileF = kChunk + kMaxTaps + 16;  // staged floats per window node
-constexpr int kMaxStages = 16;                 // input stages in flight (bulk mode)
+// Samples a chunk's window reaches below it: taps-1 rounded up to 16 bytes,
+// plus 4 of slack so that the first 16-byte window load stays in the tile.
+__host__ __device__ constexpr int window_reach(int taps) { return (taps - 1 + 3) / 4 * 4 + 4; }
+constexpr int kTileF = kChunk + window_reach(kMaxTaps) + 4;  // staged floats per window node
+constexpr int kMaxStages = 16;
 
-// An instruction word is kind << 6 | d << 3 | s: the operation, the
-// destination slot and the source slot. The interpreter dispatches on the
-// kind (12 cases), then on d or on (d, s) (8 or 64 cases): small dense
-// switches with compile-time slot indices in every case.
-enum Op : uint16_t {
+// Operations of the accumulator machine. A is the accumulator (the thread's
+// 8 elements), M the instruction's operand in shared memory.
+enum Op : uint8_t {
     OP_END = 0,
-    OP_LOAD,    // r[d] = input aux
-    OP_STORE,   // out = r[d]
-    OP_STAGE,   // window tile = r[d]
-    OP_FIRACC,  // r[d] = window aux accumulated at the thread's positions
-    OP_SCALE,   // r[d] = imm * r[d]
-    OP_SQRT,    // r[d] = sqrt(r[d])
-    OP_ABS,     // r[d] = |r[d]|
-    OP_MOV,     // r[d] = r[s]
-    OP_ADD,     // r[d] = r[d] + r[s]
-    OP_MUL,     // r[d] = r[d] * r[s]
-    OP_HYPOT,   // r[d] = hypot(r[d], r[s])
+    OP_LDA,     // A = M
+    OP_STA,     // M = A (a temporary)
+    OP_ADD,     // A = A + M
+    OP_MUL,     // A = A * M
+    OP_HYPOT,   // A = hypot(A, M)
+    OP_SCALE,   // A = imm * A
+    OP_SQRT,    // A = sqrt(A)
+    OP_ABS,     // A = |A|
+    OP_FIRACC,  // A = window arg accumulated at the thread's positions
+    OP_STAGE,   // window arg's tile = A (zero outside the signal)
+    OP_STORE,   // out = A
     OP_KINDS,
 };
-__host__ __device__ constexpr uint16_t enc(int op, int d, int s = 0) {
-    return (uint16_t)((op << 6) | (d << 3) | s);
-}
+// Operand flags.
+constexpr uint8_t F_IN = 1;    // M is a staged input: arg is relative to the current stage
+constexpr uint8_t F_SELF = 2;  // M is A itself (x op x)
 
 struct Insn {
-    uint16_t code;
-    uint16_t aux;
+    uint8_t op;
+    uint8_t flags;
+    uint16_t arg;  // operand: float4 offset in shared memory; or a window index
     float imm;
 };
 
 struct FirDesc {
     int32_t start;  // pc of the staging program
     int32_t taps;
+    int32_t reach;  // window_reach(taps)
+    int32_t tile4;  // float4 offset of the window's tile in shared memory
     float h[kMaxTaps];  // the coefficients travel in the parameter block
 };
 
@@ -102,141 +114,35 @@ struct Program {
     Insn code[kMaxCode];
 };
 
-// Eight consecutive elements of one value.
-struct V8 {
-    float4 a, b;
-};
-
 // The program as the interpreter reads it: copied once per block from the
 // parameter bank into shared memory, where a warp-uniform word is one
-// broadcast load (the parameter bank, indexed by a run-time pc, is not).
-// Layout: code[code_cap] | in[n_in] | fir[n_fir] (start, taps), 16-byte
-// rounded.
+// broadcast load. Layout: code[code_cap] | fir[n_fir] (start, taps, reach,
+// tile4) | in[n_in], 16-byte rounded.
 __host__ __device__ constexpr int meta_code_cap(int n_code) { return (n_code + 2) & ~1; }
 __host__ __device__ constexpr int meta_bytes(int n_code, int n_in, int n_fir) {
-    return ((meta_code_cap(n_code) * 8 + n_in * 8 + n_fir * 8) + 15) & ~15;
+    return ((meta_code_cap(n_code) * 8 + n_in * 8 + n_fir * 16) + 15) & ~15;
 }
 
-struct Exec {
-    const Insn* code;         // shared copy of Program::code
-    const float* const* in;   // shared copy of Program::in
-    const int2* fir;          // shared (start, taps) of each window node
-    int64_t p0;     // first of the thread's 8 positions
-    int64_t n;      // shard length
-    int64_t halo;   // positions [-halo, n) are valid
-    bool vec;       // all inputs and out are 16-byte aligned
-    float* out;
-    float* stage;   // STAGE target (tile + offset of p0)
-    const float* taps_s;
-    const float* tiles;
-    int64_t cb;     // chunk base (for FIRACC)
-    // Inputs staged in shared memory (bulk-copy mode), or null: position p
-    // of input k is sin[k * sstride + (p - sorg)].
-    const float* sin;
-    int64_t sorg;
-    int32_t sstride;
+// One run of a program over kChunk (or, for a window's halo, fewer)
+// positions.
+struct Run {
+    int32_t sh_in;   // added to F_IN operands: the stage and the run's position
+    int32_t sh_st;   // added to STAGE destinations (the halo run's offset)
+    uint32_t gm;     // which of the thread's groups take part
+    int64_t p0;      // position of the run's element 0
+    bool edge;       // some positions of the run lie outside [-halo, n)
 };
 
-__device__ __forceinline__ float lane_of(const V8& v, int e) {
-    switch (e) {
-        case 0: return v.a.x;
-        case 1: return v.a.y;
-        case 2: return v.a.z;
-        case 3: return v.a.w;
-        case 4: return v.b.x;
-        case 5: return v.b.y;
-        case 6: return v.b.z;
-        default: return v.b.w;
-    }
-}
-
-// Lanes of v at positions outside [-halo, n) replaced by 0.
-__device__ __forceinline__ V8 mask_outside(V8 v, const Exec& x) {
-    const int64_t p = x.p0;
-    if (p >= -x.halo && p + 7 < x.n) return v;
-    float f[8] = {v.a.x, v.a.y, v.a.z, v.a.w, v.b.x, v.b.y, v.b.z, v.b.w};
-#pragma unroll
-    for (int e = 0; e < 8; e++)
-        if (!(p + e >= -x.halo && p + e < x.n)) f[e] = 0.0f;
-    return {make_float4(f[0], f[1], f[2], f[3]), make_float4(f[4], f[5], f[6], f[7])};
-}
-
-__device__ __forceinline__ V8 load_pos(int k, const Exec& x) {
-    const int64_t p = x.p0;
-    if (x.sin) {
-        // Shared memory: two aligned 16-byte loads; lanes outside the signal
-        // read whatever the buffer holds there and are zeroed.
-        const float* s = x.sin + (int64_t)k * x.sstride + (p - x.sorg);
-        V8 v = {*reinterpret_cast<const float4*>(s), *reinterpret_cast<const float4*>(s + 4)};
-        return mask_outside(v, x);
-    }
-    const float* base = x.in[k];
-    if (x.vec && p >= -x.halo && p + 7 < x.n)
-        return {ld_stream_f4(base + p), ld_stream_f4(base + p + 4)};
-    float f[8];
-#pragma unroll
-    for (int e = 0; e < 8; e++) f[e] = (p + e >= -x.halo && p + e < x.n) ? base[p + e] : 0.0f;
-    return {make_float4(f[0], f[1], f[2], f[3]), make_float4(f[4], f[5], f[6], f[7])};
-}
-
-__device__ __forceinline__ void store_pos(const V8& v, const Exec& x) {
-    const int64_t p = x.p0;
-    if (x.vec && p + 7 < x.n) {
-        st_stream_f4(x.out + p, v.a);
-        st_stream_f4(x.out + p + 4, v.b);
-        return;
-    }
-#pragma unroll
-    for (int e = 0; e < 8; e++)
-        if (p + e < x.n) x.out[p + e] = lane_of(v, e);
-}
-
-__device__ __forceinline__ void stage_pos(const V8& v, const Exec& x) {
-    const V8 s = mask_outside(v, x);
-    *reinterpret_cast<float4*>(x.stage) = s.a;
-    *reinterpret_cast<float4*>(x.stage + 4) = s.b;
-}
-
-// Window start of node f for chunk cb: 16-byte aligned, 4 floats of slack
-// below the first halo sample.
-__device__ __forceinline__ int64_t tile_start(int64_t cb, int taps) {
-    return ((cb - (taps - 1)) & ~int64_t(3)) - 4;
-}
-
-// The window accumulation of one thread's 8 outputs, out of line so that the
-// interpreter's FIRACC cases stay small. tile/h: the window's staged samples
-// and taps in shared memory; q0: the tile index of the thread's first
-// position (a multiple of 4). Output e at tap k0+u reads tile index
-// q0 + e - k0 - u = w[4 + e - u] with w = tile + q0 - k0 - 4.
-__device__ __noinline__ V8 fir_acc_window(const float* tile, const float* h, int taps, int q0) {
-    float acc[8];
-#pragma unroll
-    for (int e = 0; e < 8; e++) acc[e] = 0.0f;
-    for (int k0 = 0; k0 < taps; k0 += 4) {
-        const float* w = tile + (q0 - k0 - 4);
-        const float4 w0 = *reinterpret_cast<const float4*>(w);
-        const float4 w1 = *reinterpret_cast<const float4*>(w + 4);
-        const float4 w2 = *reinterpret_cast<const float4*>(w + 8);
-        const float wv[12] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w,
-                              w2.x, w2.y, w2.z, w2.w};
-        const float4 hk = *reinterpret_cast<const float4*>(h + k0);
-        const float hv[4] = {hk.x, hk.y, hk.z, hk.w};
-        const int nk = min(4, taps - k0);
-#pragma unroll
-        for (int u = 0; u < 4; u++)
-            if (u < nk)
-#pragma unroll
-                for (int e = 0; e < 8; e++) acc[e] = __fmaf_rn(hv[u], wv[4 + e - u], acc[e]);
-    }
-    return {make_float4(acc[0], acc[1], acc[2], acc[3]),
-            make_float4(acc[4], acc[5], acc[6], acc[7])};
-}
-
-__device__ __forceinline__ V8 fir_acc(int f, const Exec& x) {
-    const int taps = x.fir[f].y;
-    return fir_acc_window(x.tiles + f * kTileF, x.taps_s + f * kMaxTaps, taps,
-                          (int)(x.p0 - tile_start(x.cb, taps)));
-}
+struct Ctx {
+    float4* S;               // dynamic shared memory
+    const float* taps_s;     // n_fir x kMaxTaps coefficients, zero past taps
+    const int4* fir;         // shared (start, taps, reach, tile4)
+    const float* const* in;  // shared copy of Program::in
+    float* out;
+    int64_t n, halo;
+    bool vec;                // out is 16-byte aligned
+    bool in_vec;             // every input is 16-byte aligned
+};
 
 __device__ __forceinline__ float4 f4_add(float4 a, float4 b) {
     return make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z),
@@ -256,119 +162,162 @@ __device__ __forceinline__ float4 f4_sqrt(float4 a) {
 __device__ __forceinline__ float4 f4_abs(float4 a) {
     return make_float4(fabsf(a.x), fabsf(a.y), fabsf(a.z), fabsf(a.w));
 }
-__device__ __forceinline__ V8 v_add(const V8& p, const V8& q) {
-    return {f4_add(p.a, q.a), f4_add(p.b, q.b)};
+__device__ __forceinline__ float4 f4_hypot(float4 a, float4 b) {
+    return make_float4(hypot_go(a.x, b.x), hypot_go(a.y, b.y), hypot_go(a.z, b.z),
+                       hypot_go(a.w, b.w));
 }
-__device__ __forceinline__ V8 v_mul(const V8& p, const V8& q) {
-    return {f4_mul(p.a, q.a), f4_mul(p.b, q.b)};
-}
-__device__ __forceinline__ V8 v_scale(float k, const V8& p) {
-    return {f4_scale(k, p.a), f4_scale(k, p.b)};
-}
-__device__ __noinline__ V8 v_sqrt(V8 p) { return {f4_sqrt(p.a), f4_sqrt(p.b)}; }
-__device__ __forceinline__ V8 v_abs(const V8& p) { return {f4_abs(p.a), f4_abs(p.b)}; }
-// Out of line: 64 interpreter cases call it.
-__device__ __noinline__ V8 v_hypot(V8 p, V8 q) {
-    return {make_float4(hypot_go(p.a.x, q.a.x), hypot_go(p.a.y, q.a.y), hypot_go(p.a.z, q.a.z),
-                        hypot_go(p.a.w, q.a.w)),
-            make_float4(hypot_go(p.b.x, q.b.x), hypot_go(p.b.y, q.b.y), hypot_go(p.b.z, q.b.z),
-                        hypot_go(p.b.w, q.b.w))};
+__device__ __forceinline__ float f4_get(const float4& v, int j) {
+    return j == 0 ? v.x : j == 1 ? v.y : j == 2 ? v.z : v.w;
 }
 
-#define SG_D8(M) M(0) M(1) M(2) M(3) M(4) M(5) M(6) M(7)
-#define SG_S8(M, D) M(D, 0) M(D, 1) M(D, 2) M(D, 3) M(D, 4) M(D, 5) M(D, 6) M(D, 7)
-#define SG_DS64(M)                                                                         \
-    SG_S8(M, 0) SG_S8(M, 1) SG_S8(M, 2) SG_S8(M, 3) SG_S8(M, 4) SG_S8(M, 5) SG_S8(M, 6) \
-        SG_S8(M, 7)
-
-#define C_SET(D) \
-    case D:      \
-        r[D] = v;  \
-        break;
-#define C_GET(D) \
-    case D:      \
-        v = r[D];  \
-        break;
-#define C_SCALE(D)                      \
-    case D:                             \
-        r[D] = v_scale(in.imm, r[D]);   \
-        break;
-#define C_SQRT(D)           \
-    case D:                 \
-        r[D] = v_sqrt(r[D]); \
-        break;
-#define C_ABS(D)            \
-    case D:                 \
-        r[D] = v_abs(r[D]); \
-        break;
-#define C_MOV(D, S)     \
-    case 8 * D + S:     \
-        r[D] = r[S];    \
-        break;
-#define C_ADD(D, S)               \
-    case 8 * D + S:               \
-        r[D] = v_add(r[D], r[S]); \
-        break;
-#define C_MUL(D, S)               \
-    case 8 * D + S:               \
-        r[D] = v_mul(r[D], r[S]); \
-        break;
-#define C_HYPOT(D, S)               \
-    case 8 * D + S:                 \
-        r[D] = v_hypot(r[D], r[S]); \
-        break;
-
-// Runs the program from pc until OP_END for the thread's 8 positions.
-// Inlined at its one call site in k_tile, so x stays in registers. The next
-// word is loaded while this one executes (the copy holds one word past END).
-__device__ __forceinline__ void interpret(int pc, const Exec& x) {
-    V8 r[kSlots];
-    const V8 zero = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
+// The window accumulation for the thread's groups: output j of group k sits
+// at tile index b_k + j, b_k = 4 (t + 256 k) + reach, and takes
+// fma(h[i], tile[b_k + j - i], acc) for i = 0 .. taps-1 in order. With
+// W = tile[b_k - i0 - 4 .. b_k - i0 + 3] for taps i0 .. i0+3, the sample of
+// output j at tap i0+u is W[4 + j - u]; the upper half of W is the lower
+// half of the previous step, so each step loads one new float4 per group.
+__device__ __forceinline__ void fir_acc(float4 (&A)[kG], const Ctx& c, int f) {
+    const int4 fd = c.fir[f];
+    const int taps = fd.y;
+    const float4* tile4 = c.S + fd.w;
+    const float4* h4 = reinterpret_cast<const float4*>(c.taps_s + f * kMaxTaps);
+    const int t = threadIdx.x;
+    float acc[kG][4];
+    float4 hi[kG];
 #pragma unroll
-    for (int i = 0; i < kSlots; i++) r[i] = zero;
-    Insn next = x.code[pc];
+    for (int k = 0; k < kG; k++) {
+#pragma unroll
+        for (int j = 0; j < 4; j++) acc[k][j] = 0.0f;
+        hi[k] = tile4[t + kThreads * k + fd.z / 4];
+    }
+    for (int i0 = 0; i0 < taps; i0 += 4) {
+        const float4 hk = h4[i0 / 4];
+        const float hv[4] = {hk.x, hk.y, hk.z, hk.w};
+        const int nk = min(4, taps - i0);
+#pragma unroll
+        for (int k = 0; k < kG; k++) {
+            const float4 lo = tile4[t + kThreads * k + (fd.z - i0) / 4 - 1];
+            const float w[8] = {lo.x, lo.y, lo.z, lo.w, hi[k].x, hi[k].y, hi[k].z, hi[k].w};
+#pragma unroll
+            for (int u = 0; u < 4; u++)
+                if (u < nk)
+#pragma unroll
+                    for (int j = 0; j < 4; j++) acc[k][j] = __fmaf_rn(hv[u], w[4 + j - u], acc[k][j]);
+            hi[k] = lo;
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < kG; k++) A[k] = make_float4(acc[k][0], acc[k][1], acc[k][2], acc[k][3]);
+}
+
+// Positions p .. p+3 of input b read from HBM (DIRECT mode), 0 outside
+// [-halo, n).
+__device__ __forceinline__ float4 gload4(const float* b, int64_t p, const Ctx& c) {
+    if (p >= -c.halo && p + 3 < c.n)
+        return c.in_vec ? ld_stream_f4(b + p) : make_float4(b[p], b[p + 1], b[p + 2], b[p + 3]);
+    float f[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) f[j] = (p + j >= -c.halo && p + j < c.n) ? b[p + j] : 0.0f;
+    return make_float4(f[0], f[1], f[2], f[3]);
+}
+
+// Zeroes the lanes of v whose positions (p .. p+3) lie outside [-halo, n).
+__device__ __forceinline__ float4 mask_outside(float4 v, int64_t p, const Ctx& c) {
+    if (p >= -c.halo && p + 3 < c.n) return v;
+    float f[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int j = 0; j < 4; j++)
+        if (!(p + j >= -c.halo && p + j < c.n)) f[j] = 0.0f;
+    return make_float4(f[0], f[1], f[2], f[3]);
+}
+
+// Runs the program from pc until OP_END. Inlined into k_tile twice: FULL
+// for runs where all of the thread's groups take part (the chunk), and the
+// general form for a window's halo run; the next word is loaded while this
+// one executes (the shared copy holds one word past the last END). In
+// DIRECT mode (BULK false) an input operand is read from HBM at the run's
+// positions.
+template <bool BULK, bool FULL>
+__device__ __forceinline__ void interpret(const Insn* code, int pc, const Ctx& c, const Run& r) {
+    const int t = threadIdx.x;
+    float4 A[kG];
+#pragma unroll
+    for (int k = 0; k < kG; k++) A[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    Insn next = code[pc];
     for (;;) {
         const Insn in = next;
-        next = x.code[++pc];
-        const int op = in.code >> 6, d = (in.code >> 3) & 7, ds = in.code & 63;
-        V8 v = zero;
-        switch (op) {
-            case OP_LOAD:
-                v = load_pos(in.aux, x);
-                switch (d) { SG_D8(C_SET) }
+        next = code[++pc];
+        const int off = (int)in.arg + ((in.flags & F_IN) ? r.sh_in : 0) + t;
+        // Group k of operand M (inactive groups: A itself, nothing is read).
+        auto operand = [&](int k) -> float4 {
+            if (!FULL && !((r.gm >> k) & 1)) return A[k];
+            if (!BULK && (in.flags & F_IN))
+                return gload4(c.in[in.arg], r.p0 + 4 * (t + kThreads * k), c);
+            return c.S[off + kThreads * k];
+        };
+        float4 M[kG];
+        if (in.op == OP_ADD || in.op == OP_MUL || in.op == OP_HYPOT) {
+#pragma unroll
+            for (int k = 0; k < kG; k++) M[k] = (in.flags & F_SELF) ? A[k] : operand(k);
+        }
+        switch (in.op) {
+            case OP_LDA:
+#pragma unroll
+                for (int k = 0; k < kG; k++) A[k] = operand(k);
                 break;
-            case OP_FIRACC:
-                v = fir_acc(in.aux, x);
-                switch (d) { SG_D8(C_SET) }
-                break;
-            case OP_STORE:
-                switch (d) { SG_D8(C_GET) }
-                store_pos(v, x);
-                break;
-            case OP_STAGE:
-                switch (d) { SG_D8(C_GET) }
-                stage_pos(v, x);
-                break;
-            case OP_SCALE:
-                switch (d) { SG_D8(C_SCALE) }
-                break;
-            case OP_SQRT:
-                switch (d) { SG_D8(C_SQRT) }
-                break;
-            case OP_ABS:
-                switch (d) { SG_D8(C_ABS) }
-                break;
-            case OP_MOV:
-                switch (ds) { SG_DS64(C_MOV) }
+            case OP_STA:
+#pragma unroll
+                for (int k = 0; k < kG; k++)
+                    if (FULL || ((r.gm >> k) & 1)) c.S[off + kThreads * k] = A[k];
                 break;
             case OP_ADD:
-                switch (ds) { SG_DS64(C_ADD) }
+#pragma unroll
+                for (int k = 0; k < kG; k++) A[k] = f4_add(A[k], M[k]);
                 break;
             case OP_MUL:
-                switch (ds) { SG_DS64(C_MUL) }
+#pragma unroll
+                for (int k = 0; k < kG; k++) A[k] = f4_mul(A[k], M[k]);
                 break;
             case OP_HYPOT:
-                switch (ds) { SG_DS64(C_HYPOT) }
+#pragma unroll
+                for (int k = 0; k < kG; k++) A[k] = f4_hypot(A[k], M[k]);
+                break;
+            case OP_SCALE:
+#pragma unroll
+                for (int k = 0; k < kG; k++) A[k] = f4_scale(in.imm, A[k]);
+                break;
+            case OP_SQRT:
+#pragma unroll
+                for (int k = 0; k < kG; k++) A[k] = f4_sqrt(A[k]);
+                break;
+            case OP_ABS:
+#pragma unroll
+                for (int k = 0; k < kG; k++) A[k] = f4_abs(A[k]);
+                break;
+            case OP_FIRACC:
+                fir_acc(A, c, in.arg);
+                break;
+            case OP_STAGE: {
+                float4* dst = c.S + c.fir[in.arg].w + r.sh_st + t;
+#pragma unroll
+                for (int k = 0; k < kG; k++)
+                    if (FULL || ((r.gm >> k) & 1))
+                        dst[kThreads * k] =
+                            r.edge ? mask_outside(A[k], r.p0 + 4 * (t + kThreads * k), c) : A[k];
+                break;
+            }
+            case OP_STORE:
+#pragma unroll
+                for (int k = 0; k < kG; k++) {
+                    const int64_t p = r.p0 + 4 * (t + kThreads * k);
+                    if (c.vec && p + 3 < c.n) {
+                        st_stream_f4(c.out + p, A[k]);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 4; j++)
+                            if (p + j < c.n) c.out[p + j] = f4_get(A[k], j);
+                    }
+                }
                 break;
             default:
                 return;  // OP_END
@@ -398,36 +347,38 @@ __device__ __forceinline__ ChunkSpan chunk_span(int64_t cb, int hs, int64_t n, i
     return s;
 }
 
-// Bulk-copy mode (BULK): the chunk's inputs (positions [cb - hs, cb + kChunk),
-// clipped to the signal) travel HBM -> shared memory by cp.async.bulk, one
-// copy per input, in `nst` stages that complete on per-stage mbarriers, so
-// nst-1 chunks stream in while one is interpreted. Requires every input
-// 16-byte aligned and halo = 0 mod 4.
+// Shared memory (float4 units): meta | taps (n_fir x kMaxTaps floats) |
+// tiles (n_fir x kTileF floats) | temporaries (n_tmp x kChunk floats) |
+// stages (nst x n_in x (hs + kChunk) floats, BULK only). Input k of a stage
+// holds positions [cb - hs, cb + kChunk) of the chunk at cb.
+//
+// Bulk-copy mode (BULK): the chunk's inputs travel HBM -> shared memory by
+// cp.async.bulk, one copy per input, in `nst` stages that complete on
+// per-stage mbarriers, so nst-1 chunks stream in while one is interpreted.
+// Requires every input 16-byte aligned and halo = 0 mod 4. Otherwise
+// (DIRECT) the interpreter reads input operands from HBM itself.
 template <bool BULK>
-__global__ void __launch_bounds__(kThreads) k_tile(const __grid_constant__ Program P,
+__global__ void __launch_bounds__(kThreads, 3) k_tile(const __grid_constant__ Program P,
                                                    float* __restrict__ out, int64_t n,
-                                                   int64_t halo, bool vec, int32_t hs,
-                                                   int32_t nst, uint32_t* wd) {
+                                                   int64_t halo, bool vec, bool in_vec, int32_t hs,
+                                                   int32_t stages4, int32_t nst, uint32_t* wd) {
     __shared__ __align__(8) uint64_t bars[kMaxStages];
     extern __shared__ float4 sm4[];
     const int code_cap = meta_code_cap(P.n_code);
     Insn* code_s = reinterpret_cast<Insn*>(sm4);
-    const float** in_s = reinterpret_cast<const float**>(code_s + code_cap);
-    int2* fir_s = reinterpret_cast<int2*>(in_s + P.n_in);
-    float* sm = reinterpret_cast<float*>(sm4) + meta_bytes(P.n_code, P.n_in, P.n_fir) / 4;
-    float* taps_s = sm;                        // n_fir x kMaxTaps
-    float* tiles = sm + P.n_fir * kMaxTaps;    // n_fir x kTileF
-    float* stages = tiles + P.n_fir * kTileF;  // nst x n_in x sstride (bulk mode)
-    // Each input's buffer: the chunk and its halo, plus 8 floats that the
-    // last staging task's whole 8-float loads may touch past the chunk.
-    const int32_t sstride = kChunk + hs + 8;
-    const int64_t stage_floats = (int64_t)P.n_in * sstride;
+    int4* fir_s = reinterpret_cast<int4*>(code_s + code_cap);
+    const float** in_s = reinterpret_cast<const float**>(fir_s + P.n_fir);
+    float* taps_s = reinterpret_cast<float*>(sm4) + meta_bytes(P.n_code, P.n_in, P.n_fir) / 4;
+    const int32_t sstride = hs + kChunk;  // floats per staged input
+    const int32_t stage_floats = P.n_in * sstride;
+    float* stages = reinterpret_cast<float*>(sm4 + stages4);
     const int tid = threadIdx.x;
     const int64_t nchunks = (n + kChunk - 1) / kChunk;
     for (int i = tid; i < code_cap; i += kThreads)
-        code_s[i] = i < P.n_code ? P.code[i] : Insn{enc(OP_END, 0), 0, 0.0f};
+        code_s[i] = i < P.n_code ? P.code[i] : Insn{OP_END, 0, 0, 0.0f};
     for (int k = tid; k < P.n_in; k += kThreads) in_s[k] = P.in[k];
-    for (int f = tid; f < P.n_fir; f += kThreads) fir_s[f] = make_int2(P.fir[f].start, P.fir[f].taps);
+    for (int f = tid; f < P.n_fir; f += kThreads)
+        fir_s[f] = make_int4(P.fir[f].start, P.fir[f].taps, P.fir[f].reach, P.fir[f].tile4);
     for (int f = 0; f < P.n_fir; f++)
         for (int k = tid; k < kMaxTaps; k += kThreads)
             taps_s[f * kMaxTaps + k] = P.fir[f].h[k];  // zero past taps
@@ -437,7 +388,7 @@ __global__ void __launch_bounds__(kThreads) k_tile(const __grid_constant__ Progr
         mbar_arrive_expect_tx(&bars[s], (uint32_t)(sp.len4 * 4 * P.n_in));
         if (sp.len4 > 0)
             for (int k = 0; k < P.n_in; k++)
-                bulk_g2s(stages + s * stage_floats + (int64_t)k * sstride + (sp.lo - sp.org),
+                bulk_g2s(stages + s * stage_floats + k * sstride + (sp.lo - sp.org),
                          in_s[k] + sp.lo, (uint32_t)(sp.len4 * 4), &bars[s]);
     };
     if (BULK) {
@@ -454,27 +405,25 @@ __global__ void __launch_bounds__(kThreads) k_tile(const __grid_constant__ Progr
     }
     __syncthreads();
 
-    Exec x;
-    x.code = code_s;
-    x.in = in_s;
-    x.fir = fir_s;
-    x.n = n;
-    x.halo = halo;
-    x.vec = vec;
-    x.out = out;
-    x.taps_s = taps_s;
-    x.tiles = tiles;
-    x.sin = nullptr;
-    x.sorg = 0;
-    x.sstride = sstride;
+    Ctx cx;
+    cx.S = sm4;
+    cx.taps_s = taps_s;
+    cx.fir = fir_s;
+    cx.in = in_s;
+    cx.out = out;
+    cx.n = n;
+    cx.halo = halo;
+    cx.vec = vec;
+    cx.in_vec = in_vec;
+    const int nf = P.n_fir;
     int it = 0;
     for (int64_t c = blockIdx.x; c < nchunks; c += gridDim.x, it++) {
         const int64_t cb = c * kChunk;
-        x.cb = cb;
+        const ChunkSpan sp = chunk_span(cb, hs, n, halo);
+        int s = 0;
         if (BULK) {
-            const int s = it % nst;
+            s = it % nst;
             if (!mbar_wait(&bars[s], (uint32_t)((it / nst) & 1), wd)) return;
-            const ChunkSpan sp = chunk_span(cb, hs, n, halo);
             float* buf = stages + s * stage_floats;
             // The last 0-3 samples of a ragged signal are not a whole 16-byte
             // unit: plain loads.
@@ -482,49 +431,48 @@ __global__ void __launch_bounds__(kThreads) k_tile(const __grid_constant__ Progr
             if (tail > 0 && tid < P.n_in * 4) {
                 const int k = tid / 4, e = tid % 4;
                 const int64_t pos = sp.lo + sp.len4 + e;
-                if (e < tail) buf[(int64_t)k * sstride + (pos - sp.org)] = in_s[k][pos];
+                if (e < tail) buf[k * sstride + (pos - sp.org)] = in_s[k][pos];
             }
             __syncthreads();
-            x.sin = buf;
-            x.sorg = sp.org;
         }
-        // Jobs f = 0 .. n_fir-1 stage window f's signal over its span (the
-        // chunk plus the halo); job n_fir is the main program over the
-        // chunk. One loop, so the interpreter is inlined exactly once.
-        const int nf = P.n_fir;
-        for (int f = 0; f <= nf; f++) {
-            int64_t base, span;
+        const int32_t in4 = stages4 + s * stage_floats / 4;
+        const bool edge = cb - (int64_t)hs < -halo || cb + kChunk > n;
+        // Jobs 2f and 2f+1 stage window f over its tile (the chunk, then the
+        // reach below it); job 2 nf is the main program over the chunk. One
+        // loop, so the interpreter is inlined once per form.
+        for (int j = 0; j <= 2 * nf; j++) {
+            Run r;
             int pc;
-            float* st = tiles;
-            if (f < nf) {
-                const int2 fd = fir_s[f];
-                base = tile_start(cb, fd.y);
-                span = cb + kChunk - base;
+            if (j < 2 * nf) {
+                const int4 fd = fir_s[j >> 1];
+                const bool halo_run = j & 1;
                 pc = fd.x;
-                st = tiles + f * kTileF;
+                r.sh_in = in4 + (hs - fd.z) / 4 + (halo_run ? kChunk4 : 0);
+                r.sh_st = halo_run ? kChunk4 : 0;
+                r.gm = halo_run ? (tid < fd.z / 4 ? 1u : 0u) : (1u << kG) - 1;
+                r.p0 = cb - fd.z + (halo_run ? kChunk : 0);
             } else {
-                base = cb;
-                span = min((int64_t)kChunk, n - cb);
                 pc = P.main_start;
+                r.sh_in = in4 + hs / 4;
+                r.sh_st = 0;
+                r.gm = (1u << kG) - 1;
+                r.p0 = cb;
             }
-            for (int64_t off = kV * tid; off < span; off += kV * kThreads) {
-                x.p0 = base + off;
-                x.stage = st + off;
-                interpret(pc, x);
-            }
-            if (f + 1 == nf) __syncthreads();  // windows staged before main reads them
+            r.edge = edge;
+            if (r.gm == (1u << kG) - 1)
+                interpret<BULK, true>(code_s, pc, cx, r);
+            else if (r.gm)
+                interpret<BULK, false>(code_s, pc, cx, r);
+            if (j + 1 == 2 * nf) __syncthreads();  // windows staged before main reads them
         }
-        if (BULK) {
-            // Every thread is done with this stage (and with the tiles);
-            // order those generic accesses before the next bulk copy into it.
-            fence_proxy_async_smem();
-            __syncthreads();
-            if (tid == 0) {
-                const int64_t cn = c + (int64_t)nst * gridDim.x;
-                if (cn < nchunks) issue(cn, it % nst);
-            }
-        } else if (P.n_fir > 0) {
-            __syncthreads();
+        // Every thread is done with this stage (and with the tiles and
+        // temporaries); order those generic accesses before the next bulk
+        // copy into it.
+        if (BULK) fence_proxy_async_smem();
+        __syncthreads();
+        if (BULK && tid == 0) {
+            const int64_t cn = c + (int64_t)nst * gridDim.x;
+            if (cn < nchunks) issue(cn, it % nst);
         }
     }
 }
@@ -603,161 +551,213 @@ void postorder(const simtgo_tile_graph* g, int id, std::vector<int>& out, std::v
     out.push_back(id);
 }
 
-struct Lowered {
-    Program prog;
-    std::vector<int> in_nodes;   // data input node ids, in prog.in order
-    std::vector<int> fir_nodes;  // window node ids, in prog.fir order
-    std::vector<int> param_of;   // reference parameter index pK of each data input
+// A lowered instruction, before the shared-memory layout of a launch gives
+// its operand an address.
+enum Space : uint8_t { SP_NONE = 0, SP_IN, SP_TMP, SP_WIN, SP_SELF };
+struct LInsn {
+    uint8_t op;
+    uint8_t space;
+    uint16_t idx;  // input, temporary or window index
+    float imm;
 };
 
-// Emits one program computing `root` (main: root's value, window nodes read
-// from their tiles; staging: a window's signal, stopped at nothing since a
-// signal contains no window). Register slots are assigned linearly over the
-// postorder; a slot is reused as soon as its value has no uses left.
-int emit_program(const simtgo_tile_graph* g, int root, bool main, Lowered& L, bool hoist,
-                 std::unordered_map<int, int>& input_index,
-                 std::unordered_map<int, int>& fir_index, std::vector<Insn>& code) {
-    std::vector<int> order;
-    std::vector<char> seen(g->nodes.size(), 0);
-    postorder(g, root, order, seen, main);
-    std::vector<int> uses(g->nodes.size(), 0);
-    for (int id : order) {
-        const Node& n = g->nodes[id];
-        if (main && n.kind == K_FIR) continue;
-        if (n.kind == K_INPUT) continue;
-        if (n.a >= 0) uses[n.a]++;
-        if (n.b >= 0) uses[n.b]++;
-    }
-    std::vector<int> slot(g->nodes.size(), -1);
-    bool free_slot[tilek::kSlots];
-    for (bool& f : free_slot) f = true;
-    auto alloc = [&]() -> int {
-        for (int s = 0; s < tilek::kSlots; s++)
-            if (free_slot[s]) {
-                free_slot[s] = false;
-                return s;
-            }
-        return -1;
-    };
-    auto push = [&](uint16_t c, uint16_t aux = 0, float imm = 0.0f) {
-        code.push_back(Insn{c, aux, imm});
-    };
-    auto load = [&](int id) -> int {
-        int s = alloc();
-        if (s < 0) return -1;
-        auto it = input_index.find(id);
-        int k;
-        if (it == input_index.end()) {
-            k = (int)L.in_nodes.size();
-            if (k >= tilek::kMaxIn) return -2;
-            input_index[id] = k;
-            L.in_nodes.push_back(id);
-        } else {
-            k = it->second;
-        }
-        push(tilek::enc(tilek::OP_LOAD, s), (uint16_t)k);
-        slot[id] = s;
-        return s;
-    };
-    if (hoist)
-        for (int id : order)
-            if (g->nodes[id].kind == K_INPUT && slot[id] < 0)
-                if (load(id) < 0) return -1;
-    auto need = [&](int id) -> int {
-        if (slot[id] >= 0) return slot[id];
-        return load(id);  // not hoisted
-    };
-    auto release = [&](int id) {
-        if (--uses[id] == 0 && slot[id] >= 0) free_slot[slot[id]] = true;
-    };
-    for (int id : order) {
-        const Node& n = g->nodes[id];
-        if (n.kind == K_INPUT) {
-            if (id == root && need(id) < 0) return -1;
-            continue;
-        }
-        if (main && n.kind == K_FIR) {
-            int d = alloc();
-            if (d < 0) return -1;
-            auto it = fir_index.find(id);
-            if (it == fir_index.end()) return -3;
-            push(tilek::enc(tilek::OP_FIRACC, d), (uint16_t)it->second);
-            slot[id] = d;
-            continue;
-        }
-        if (n.kind == K_FIR) return -3;  // a window inside a signal is refused at build
-        const bool unary = (n.kind == K_SCALE || n.kind == K_SQRT || n.kind == K_ABS);
-        const int sa = need(n.a);
-        if (sa < 0) return -1;
-        int d;
-        if (unary) {
-            if (uses[n.a] == 1) {
-                d = sa;
-                slot[n.a] = -1;
-                uses[n.a] = 0;
-            } else {
-                d = alloc();
-                if (d < 0) return -1;
-                push(tilek::enc(tilek::OP_MOV, d, sa));
-                release(n.a);
-            }
-            if (n.kind == K_SCALE) push(tilek::enc(tilek::OP_SCALE, d), 0, n.scale);
-            if (n.kind == K_SQRT) push(tilek::enc(tilek::OP_SQRT, d));
-            if (n.kind == K_ABS) push(tilek::enc(tilek::OP_ABS, d));
-        } else {
-            const int sb = need(n.b);
-            if (sb < 0) return -1;
-            const int bop = n.kind == K_ADD   ? tilek::OP_ADD
-                            : n.kind == K_MUL ? tilek::OP_MUL
-                                              : tilek::OP_HYPOT;
-            if (n.a == n.b) {
-                if (uses[n.a] == 2) {
-                    d = sa;
-                    slot[n.a] = -1;
-                    uses[n.a] = 0;
-                } else {
-                    d = alloc();
-                    if (d < 0) return -1;
-                    push(tilek::enc(tilek::OP_MOV, d, sa));
-                    release(n.a);
-                    release(n.a);
-                }
-                push(tilek::enc(bop, d, d));
-            } else if (uses[n.a] == 1) {
-                d = sa;
-                slot[n.a] = -1;
-                uses[n.a] = 0;
-                push(tilek::enc(bop, d, sb));
-                release(n.b);
-            } else if (uses[n.b] == 1) {
-                // Add, Mul and Hypot are commutative bit for bit.
-                d = sb;
-                slot[n.b] = -1;
-                uses[n.b] = 0;
-                push(tilek::enc(bop, d, sa));
-                release(n.a);
-            } else {
-                d = alloc();
-                if (d < 0) return -1;
-                push(tilek::enc(tilek::OP_MOV, d, sa));
-                push(tilek::enc(bop, d, sb));
-                release(n.a);
-                release(n.b);
-            }
-        }
-        slot[id] = d;
-    }
-    push(tilek::enc(main ? tilek::OP_STORE : tilek::OP_STAGE, slot[root]));
-    push(tilek::enc(tilek::OP_END, 0));
-    return 0;
-}
+struct Lowered {
+    std::vector<LInsn> code;
+    int32_t main_start = 0;
+    std::vector<int32_t> fir_start;  // pc of each window's staging program
+    int n_tmp = 0;                   // temporaries the programs use at once
+    std::vector<int> in_nodes;       // data input node ids, in input order
+    std::vector<int> fir_nodes;      // window node ids, in window order
+    std::vector<int> param_of;       // reference parameter index pK of each data input
+};
 
-// Lowers the graph rooted at t. Returns 0 or a status (message recorded).
+// Emits one program for the accumulator machine: a window's signal (ending
+// in STAGE) or the main program (ending in STORE). Values live in the
+// accumulator; a value with uses still to come is stored once to a
+// temporary. A binary node whose operands are both unstored evaluates the
+// operand that needs more temporaries first, stores it, then the other
+// (Sethi-Ullman order). In the main program a window node is FIRACC, and a
+// window's signal root is read from the window's tile rather than computed
+// again.
+struct Gen {
+    const simtgo_tile_graph* g;
+    bool main;
+    Lowered& L;
+    std::unordered_map<int, int>& input_index;
+    const std::unordered_map<int, int>& fir_index;
+    std::vector<int> uses;         // references still to be consumed, per node
+    std::vector<int8_t> space;     // where a node's value is stored (Space), or SP_NONE
+    std::vector<int> where;        // its index in that space
+    std::vector<int> need_memo;
+    bool tmp_busy[tilek::kMaxTmp] = {};
+    int status = 0;                // -1 temporaries exhausted, -2 inputs exhausted
+
+    Gen(const simtgo_tile_graph* g_, bool main_, Lowered& L_, std::unordered_map<int, int>& ii,
+        const std::unordered_map<int, int>& fi)
+        : g(g_), main(main_), L(L_), input_index(ii), fir_index(fi) {
+        const size_t nn = g->nodes.size();
+        uses.assign(nn, 0);
+        space.assign(nn, SP_NONE);
+        where.assign(nn, -1);
+        need_memo.assign(nn, -1);
+    }
+    void push(uint8_t op, uint8_t sp = SP_NONE, int idx = 0, float imm = 0.0f) {
+        L.code.push_back(LInsn{op, sp, (uint16_t)idx, imm});
+    }
+    bool leaf(int id) const {
+        const Node& n = g->nodes[id];
+        return n.kind == K_INPUT || (main && n.kind == K_FIR);
+    }
+    // Counts references inside this program (a window node is a leaf of the
+    // main program).
+    void count(int root) {
+        std::vector<int> order;
+        std::vector<char> seen(g->nodes.size(), 0);
+        postorder(g, root, order, seen, main);
+        for (int id : order) {
+            if (leaf(id)) continue;
+            const Node& n = g->nodes[id];
+            if (n.a >= 0) uses[n.a]++;
+            if (n.b >= 0) uses[n.b]++;
+        }
+    }
+    // Temporaries an unstored node needs while it is evaluated.
+    int need(int id) {
+        if (space[id] != SP_NONE || leaf(id)) return 0;
+        if (need_memo[id] >= 0) return need_memo[id];
+        const Node& n = g->nodes[id];
+        int r;
+        if (n.b < 0 || n.a == n.b) {
+            r = need(n.a);
+        } else if (space[n.a] != SP_NONE || leaf(n.a) || space[n.b] != SP_NONE || leaf(n.b)) {
+            r = std::max(need(n.a), need(n.b));
+        } else {
+            const int na = need(n.a), nb = need(n.b);
+            r = na == nb ? na + 1 : std::max(na, nb);
+        }
+        return need_memo[id] = r;
+    }
+    int alloc_tmp() {
+        for (int j = 0; j < tilek::kMaxTmp; j++)
+            if (!tmp_busy[j]) {
+                tmp_busy[j] = true;
+                L.n_tmp = std::max(L.n_tmp, j + 1);
+                return j;
+            }
+        status = -1;
+        return -1;
+    }
+    void consume(int id) {
+        if (--uses[id] == 0 && space[id] == SP_TMP) {
+            tmp_busy[where[id]] = false;
+            space[id] = SP_NONE;
+        }
+    }
+    // The memory operand of a stored node or an input, or false.
+    bool operand(int id, uint8_t* sp, int* idx) {
+        const Node& n = g->nodes[id];
+        if (space[id] != SP_NONE) {
+            *sp = (uint8_t)space[id];
+            *idx = where[id];
+            return true;
+        }
+        if (n.kind == K_INPUT) {
+            auto it = input_index.find(id);
+            int k;
+            if (it == input_index.end()) {
+                k = (int)L.in_nodes.size();
+                if (k >= tilek::kMaxIn) {
+                    status = -2;
+                    return false;
+                }
+                input_index[id] = k;
+                L.in_nodes.push_back(id);
+            } else {
+                k = it->second;
+            }
+            *sp = SP_IN;
+            *idx = k;
+            return true;
+        }
+        return false;
+    }
+    bool stored(int id) { return space[id] != SP_NONE || g->nodes[id].kind == K_INPUT; }
+    // Leaves the value of id in the accumulator.
+    void emit(int id) {
+        if (status) return;
+        uint8_t sp;
+        int idx;
+        if (operand(id, &sp, &idx)) {
+            push(tilek::OP_LDA, sp, idx);
+            return;
+        }
+        if (status) return;
+        const Node& n = g->nodes[id];
+        if (n.kind == K_FIR) {  // main program only
+            push(tilek::OP_FIRACC, SP_NONE, fir_index.at(id));
+        } else if (n.kind == K_SCALE || n.kind == K_SQRT || n.kind == K_ABS) {
+            emit(n.a);
+            consume(n.a);
+            if (n.kind == K_SCALE) push(tilek::OP_SCALE, SP_NONE, 0, n.scale);
+            if (n.kind == K_SQRT) push(tilek::OP_SQRT);
+            if (n.kind == K_ABS) push(tilek::OP_ABS);
+        } else {
+            const uint8_t op = n.kind == K_ADD   ? tilek::OP_ADD
+                               : n.kind == K_MUL ? tilek::OP_MUL
+                                                 : tilek::OP_HYPOT;
+            if (n.a == n.b) {
+                emit(n.a);
+                consume(n.a);
+                consume(n.a);
+                push(op, SP_SELF);
+            } else {
+                // The operand kept in memory: one already stored, else the
+                // one evaluated first (and stored) -- the needier one.
+                int first = n.b, second = n.a;
+                if (stored(n.a) && !stored(n.b)) {
+                    first = n.a;
+                    second = n.b;
+                } else if (!stored(n.b) && need(n.a) > need(n.b)) {
+                    first = n.a;
+                    second = n.b;
+                }
+                if (!stored(first)) {
+                    emit(first);
+                    if (status) return;
+                    if (space[first] == SP_NONE) {  // not stored by emit: keep it for this use
+                        const int j = alloc_tmp();
+                        if (j < 0) return;
+                        push(tilek::OP_STA, SP_TMP, j);
+                        space[first] = SP_TMP;
+                        where[first] = j;
+                    }
+                }
+                emit(second);
+                if (status) return;
+                if (!operand(first, &sp, &idx)) {
+                    status = status ? status : -1;
+                    return;
+                }
+                push(op, sp, idx);
+                consume(second);
+                consume(first);
+            }
+        }
+        if (status) return;
+        // More uses to come after the current one: store it once.
+        if (uses[id] > 1 && space[id] == SP_NONE) {
+            const int j = alloc_tmp();
+            if (j < 0) return;
+            push(tilek::OP_STA, SP_TMP, j);
+            space[id] = SP_TMP;
+            where[id] = j;
+        }
+    }
+};
+
+// Lowers the graph rooted at root. Returns 0 or a status (message recorded).
 int lower(const simtgo_tile_graph* g, int root, Lowered& L) {
-    memset(&L.prog, 0, sizeof L.prog);
-    L.in_nodes.clear();
-    L.fir_nodes.clear();
-    L.param_of.clear();
+    L = Lowered();
     // The reference's parameter numbering: every input node, taps included,
     // in postorder (tile/codegen.go:24-35).
     {
@@ -765,82 +765,134 @@ int lower(const simtgo_tile_graph* g, int root, Lowered& L) {
         std::vector<char> seen(g->nodes.size(), 0);
         postorder(g, root, order, seen, false);
         int p = 0;
-        std::unordered_map<int, int> pidx;
+        L.param_of.assign(g->nodes.size(), -1);
         for (int id : order)
-            if (g->nodes[id].kind == K_INPUT) pidx[id] = p++;
+            if (g->nodes[id].kind == K_INPUT) L.param_of[id] = p++;
         for (int id : order)
             if (g->nodes[id].kind == K_FIR) L.fir_nodes.push_back(id);
-        L.param_of.resize(g->nodes.size(), -1);
-        for (auto& kv : pidx) L.param_of[kv.first] = kv.second;
     }
     if ((int)L.fir_nodes.size() > tilek::kMaxFir)
         return sg::fail(SIMTGO_ESIZE, "tile: %zu windowed operations; the fused kernel stages at most %d",
                         L.fir_nodes.size(), tilek::kMaxFir);
-    std::unordered_map<int, int> fir_index;
+    std::unordered_map<int, int> fir_index, input_index;
     for (size_t i = 0; i < L.fir_nodes.size(); i++) fir_index[L.fir_nodes[i]] = (int)i;
-    for (int hoist = 1; hoist >= 0; hoist--) {
-        std::vector<Insn> code;
-        std::unordered_map<int, int> input_index;
-        L.in_nodes.clear();
-        int rc = 0;
-        for (size_t f = 0; f < L.fir_nodes.size() && rc == 0; f++) {
-            const Node& fn = g->nodes[L.fir_nodes[f]];
-            L.prog.fir[f].start = (int32_t)code.size();
-            const std::vector<float>& h = g->nodes[fn.b].taps;
-            L.prog.fir[f].taps = (int32_t)h.size();
-            for (size_t k = 0; k < h.size(); k++) L.prog.fir[f].h[k] = h[k];
-            rc = emit_program(g, fn.a, false, L, hoist, input_index, fir_index, code);
-        }
-        if (rc == 0) {
-            L.prog.main_start = (int32_t)code.size();
-            rc = emit_program(g, root, true, L, hoist, input_index, fir_index, code);
-        }
-        if (rc == -2)
-            return sg::fail(SIMTGO_ESIZE, "tile: more than %d distinct inputs", tilek::kMaxIn);
-        if (rc == -3) return sg::fail(SIMTGO_EGRAPH, "tile: a windowed operation inside a window");
-        if (rc == -1) continue;  // out of slots: retry without hoisting the loads
-        if (code.size() > (size_t)tilek::kMaxCode)
-            return sg::fail(SIMTGO_ESIZE, "tile: the program has %zu instructions (max %d)",
-                            code.size(), tilek::kMaxCode);
-        memcpy(L.prog.code, code.data(), code.size() * sizeof(Insn));
-        L.prog.n_code = (int32_t)code.size();
-        L.prog.n_fir = (int32_t)L.fir_nodes.size();
-        L.prog.n_in = (int32_t)L.in_nodes.size();
-        return 0;
+    int status = 0;
+    for (size_t f = 0; f < L.fir_nodes.size() && !status; f++) {
+        const int sig = g->nodes[L.fir_nodes[f]].a;
+        if (contains_fir(g, sig))
+            return sg::fail(SIMTGO_EGRAPH, "tile: a windowed operation inside a window");
+        L.fir_start.push_back((int32_t)L.code.size());
+        Gen gen(g, false, L, input_index, fir_index);
+        gen.count(sig);
+        gen.uses[sig]++;  // the STAGE
+        gen.emit(sig);
+        gen.push(tilek::OP_STAGE, SP_NONE, (int)f);
+        gen.push(tilek::OP_END);
+        status = gen.status;
     }
-    return sg::fail(SIMTGO_ESIZE,
-                    "tile: the graph keeps more than %d values live at once; materialise part of it",
-                    tilek::kSlots);
+    if (!status) {
+        L.main_start = (int32_t)L.code.size();
+        Gen gen(g, true, L, input_index, fir_index);
+        gen.count(root);
+        gen.uses[root]++;  // the STORE
+        // Each window's signal root is in its tile over the chunk.
+        for (size_t f = 0; f < L.fir_nodes.size(); f++) {
+            const int sig = g->nodes[L.fir_nodes[f]].a;
+            if (g->nodes[sig].kind != K_INPUT && gen.space[sig] == SP_NONE) {
+                gen.space[sig] = SP_WIN;
+                gen.where[sig] = (int)f;
+            }
+        }
+        gen.emit(root);
+        gen.push(tilek::OP_STORE);
+        gen.push(tilek::OP_END);
+        status = gen.status;
+    }
+    if (status == -2)
+        return sg::fail(SIMTGO_ESIZE, "tile: more than %d distinct inputs", tilek::kMaxIn);
+    if (status == -1)
+        return sg::fail(SIMTGO_ESIZE,
+                        "tile: the graph keeps more than %d values live at once; materialise part of it",
+                        tilek::kMaxTmp);
+    if (L.code.size() > (size_t)tilek::kMaxCode)
+        return sg::fail(SIMTGO_ESIZE, "tile: the program has %zu instructions (max %d)",
+                        L.code.size(), tilek::kMaxCode);
+    return 0;
+}
+
+// The launch's shared-memory layout (float4 offsets) and its program.
+struct Layout {
+    int32_t taps4, tiles4, temps4, stages4, sstride, nst;
+    size_t smem;
+};
+
+void build_program(const simtgo_tile_graph* g, const Lowered& L, const Layout& Y, bool bulk,
+                   tilek::Program& P) {
+    memset(&P, 0, sizeof P);
+    P.main_start = L.main_start;
+    P.n_fir = (int32_t)L.fir_nodes.size();
+    P.n_in = (int32_t)L.in_nodes.size();
+    P.n_code = (int32_t)L.code.size();
+    for (int f = 0; f < P.n_fir; f++) {
+        const Node& fn = g->nodes[L.fir_nodes[f]];
+        const std::vector<float>& h = g->nodes[fn.b].taps;
+        P.fir[f].start = L.fir_start[f];
+        P.fir[f].taps = (int32_t)h.size();
+        P.fir[f].reach = tilek::window_reach((int)h.size());
+        P.fir[f].tile4 = Y.tiles4 + f * tilek::kTileF / 4;
+        for (size_t k = 0; k < h.size(); k++) P.fir[f].h[k] = h[k];
+    }
+    for (size_t pc = 0; pc < L.code.size(); pc++) {
+        const LInsn& li = L.code[pc];
+        tilek::Insn& in = P.code[pc];
+        in.op = li.op;
+        in.imm = li.imm;
+        in.flags = 0;
+        in.arg = 0;
+        switch (li.space) {
+            case SP_IN:
+                in.flags = tilek::F_IN;
+                in.arg = (uint16_t)(bulk ? li.idx * Y.sstride / 4 : li.idx);
+                break;
+            case SP_TMP: in.arg = (uint16_t)(Y.temps4 + li.idx * tilek::kChunk4); break;
+            case SP_WIN:
+                in.arg = (uint16_t)(P.fir[li.idx].tile4 + P.fir[li.idx].reach / 4);
+                break;
+            case SP_SELF: in.flags = tilek::F_SELF; break;
+            default: in.arg = li.idx; break;  // FIRACC / STAGE: the window
+        }
+    }
 }
 
 // Launches a lowered program. dev_in[k] = device data of L.in_nodes[k] (halo
 // elements first).
-int launch_program(Lowered& L, const std::vector<const float*>& dev_in, float* out, int64_t n,
-                   int64_t halo, cudaStream_t s) {
+int launch_program(const simtgo_tile_graph* g, const Lowered& L,
+                   const std::vector<const float*>& dev_in, float* out, int64_t n, int64_t halo,
+                   cudaStream_t s) {
     const sg::DevInfo* d;
     int rc;
     if ((rc = sg::current_device(&d))) return rc;
     if (n <= 0) return 0;
-    bool vec = sg::aligned16(out);
+    const int n_in = (int)L.in_nodes.size(), n_fir = (int)L.fir_nodes.size();
     bool in_aligned = true;
-    for (size_t k = 0; k < dev_in.size(); k++) {
-        L.prog.in[k] = dev_in[k];  // element 0 of the shard; [-halo, 0) precede it
-        in_aligned = in_aligned && sg::aligned16(L.prog.in[k]);
-    }
-    vec = vec && in_aligned;
-    // Samples a chunk's windows reach below it: the widest window's taps-1,
-    // rounded up to 16 bytes, plus tile_start's 4 floats of slack.
+    for (const float* p : dev_in) in_aligned = in_aligned && sg::aligned16(p);
+    const bool vec = sg::aligned16(out);
+    // Samples a chunk's windows reach below it.
     int32_t hs = 0;
-    for (int f = 0; f < L.prog.n_fir; f++)
-        hs = std::max<int32_t>(hs, (L.prog.fir[f].taps - 1 + 3) / 4 * 4 + 4);
-    const size_t base_smem =
-        tilek::meta_bytes(L.prog.n_code, L.prog.n_in, L.prog.n_fir) +
-        (size_t)L.prog.n_fir * (tilek::kMaxTaps + tilek::kTileF) * sizeof(float);
-    const size_t stage_bytes =
-        (size_t)L.prog.n_in * (tilek::kChunk + hs + 8) * sizeof(float);
+    for (int f = 0; f < n_fir; f++) {
+        const Node& fn = g->nodes[L.fir_nodes[f]];
+        hs = std::max<int32_t>(hs, tilek::window_reach((int)g->nodes[fn.b].taps.size()));
+    }
+    Layout Y;
+    Y.taps4 = tilek::meta_bytes((int)L.code.size(), n_in, n_fir) / 16;
+    Y.tiles4 = Y.taps4 + n_fir * tilek::kMaxTaps / 4;
+    Y.temps4 = Y.tiles4 + n_fir * tilek::kTileF / 4;
+    Y.stages4 = Y.temps4 + L.n_tmp * tilek::kChunk4;
+    Y.sstride = hs + tilek::kChunk;
+    const size_t base_smem = (size_t)Y.stages4 * 16;
+    const size_t stage_bytes = (size_t)n_in * Y.sstride * sizeof(float);
     // Both instantiations may take up to the opt-in maximum of dynamic
-    // shared memory (less 1 KB for the static mbarriers); the stage count
-    // below decides how much they use.
+    // shared memory (less 1 KB for the static mbarriers).
     const int dyn_max = d->max_smem_optin - 1024;
     static std::atomic<uint64_t> configured{0};
     const uint64_t dev_bit = 1ull << (d->device & 63);
@@ -853,34 +905,58 @@ int launch_program(Lowered& L, const std::vector<const float*>& dev_in, float* o
         }
         configured.fetch_or(dev_bit);
     }
-    // Input stages: registers bound the blocks per SM; the stages then take
-    // that block's share of the SM's shared memory (2..kMaxStages chunks of
-    // every input in flight), since HBM latency x bandwidth per SM is tens
-    // of KB that must be outstanding at once.
-    int per_sm = 0;
+    // Blocks per SM and input stages: registers bound the blocks; each
+    // block's stages take its share of the SM's shared memory. The choice is
+    // the most blocks whose stages keep >= 64 KB per SM in flight (HBM
+    // latency x bandwidth per SM), else the most bytes in flight. With
+    // unaligned inputs, or fewer than two stages' room, the inputs are read
+    // from HBM by the interpreter itself (DIRECT).
+    int reg_blocks = 0;
     rc = sg::cuda_status(cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-                             &per_sm, tilek::k_tile<true>, tilek::kThreads, base_smem),
+                             &reg_blocks, tilek::k_tile<true>, tilek::kThreads, base_smem),
                          "cudaOccupancyMaxActiveBlocksPerMultiprocessor(tile)");
     if (rc) return rc;
-    const int64_t share = std::min<int64_t>(dyn_max,
-                                            d->smem_per_sm / std::max(1, per_sm) - 2048);
-    int nst = (int)std::max<int64_t>(2, (share - (int64_t)base_smem) / (int64_t)stage_bytes);
-    nst = std::min(nst, tilek::kMaxStages);
-    const size_t bulk_smem = base_smem + nst * stage_bytes;
-    const bool bulk = in_aligned && halo % 4 == 0 && L.prog.n_in > 0 &&
-                      bulk_smem <= (size_t)dyn_max;
-    const size_t smem = bulk ? bulk_smem : base_smem;
+    bool bulk = false;
+    Y.nst = 0;
+    if (in_aligned && halo % 4 == 0 && n_in > 0) {
+        int64_t best_inflight = -1;
+        for (int per_sm = std::max(1, reg_blocks); per_sm >= 1; per_sm--) {
+            const int64_t share =
+                std::min<int64_t>(dyn_max, d->smem_per_sm / per_sm - 2048);
+            const int64_t fit = (share - (int64_t)base_smem) / (int64_t)stage_bytes;
+            const int nst = (int)std::min<int64_t>(fit, tilek::kMaxStages);
+            if (nst < 2) continue;
+            const int64_t inflight = (int64_t)per_sm * (nst - 1) * (int64_t)stage_bytes;
+            if (inflight > best_inflight) {
+                best_inflight = inflight;
+                Y.nst = nst;
+            }
+            if (inflight >= 64 * 1024) {
+                Y.nst = nst;
+                break;
+            }
+        }
+        bulk = Y.nst >= 2;
+    }
+    Y.smem = bulk ? base_smem + Y.nst * stage_bytes : base_smem;
+    if (Y.smem > (size_t)dyn_max)
+        return sg::fail(SIMTGO_ESIZE, "tile: the program needs %zu bytes of shared memory (max %d)",
+                        Y.smem, dyn_max);
+    static thread_local tilek::Program P;
+    build_program(g, L, Y, bulk, P);
+    for (int k = 0; k < n_in; k++) P.in[k] = dev_in[k];  // element 0; [-halo, 0) precede it
     auto kern = bulk ? tilek::k_tile<true> : tilek::k_tile<false>;
+    int per_sm = 0;
     rc = sg::cuda_status(
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, tilek::kThreads, smem),
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, tilek::kThreads, Y.smem),
         "cudaOccupancyMaxActiveBlocksPerMultiprocessor(tile)");
     if (rc) return rc;
     const int64_t chunks = sg::ceil_div(n, tilek::kChunk);
     const int blocks = (int)std::max<int64_t>(
         1, std::min<int64_t>(chunks, (int64_t)d->sms * std::max(1, per_sm)));
     sg::before_launch();
-    kern<<<blocks, tilek::kThreads, smem, s>>>(L.prog, out, n, halo, vec, hs, nst,
-                                               sg::watchdog_device_ptr());
+    kern<<<blocks, tilek::kThreads, Y.smem, s>>>(P, out, n, halo, vec, in_aligned, hs, Y.stages4,
+                                                 Y.nst, sg::watchdog_device_ptr());
     return sg::launch_status("tile");
 }
 
@@ -943,7 +1019,7 @@ int run_fused(const simtgo_tile_graph* g, int root, float* out, int64_t n, int64
         dev_in.push_back(p);
     }
     if (check_alias && (rc = check_out_alias(L, g, out, n, dev_in, halo))) return rc;
-    return launch_program(L, dev_in, out, n, halo, s);
+    return launch_program(g, L, dev_in, out, n, halo, s);
 }
 
 }  // namespace
@@ -1085,63 +1161,55 @@ int simtgo_tile_program_size(simtgo_tile_graph* g, simtgo_tensor t, int32_t* n_i
     Lowered L;
     int rc = lower(g, t, L);
     if (rc) return rc;
-    if (n_instructions) *n_instructions = L.prog.n_code;
-    if (n_inputs) *n_inputs = L.prog.n_in;
-    if (n_windows) *n_windows = L.prog.n_fir;
+    if (n_instructions) *n_instructions = (int32_t)L.code.size();
+    if (n_inputs) *n_inputs = (int32_t)L.in_nodes.size();
+    if (n_windows) *n_windows = (int32_t)L.fir_nodes.size();
     return 0;
 }
 
 // The listing of a lowered program, one instruction per line:
-//   "window <f> taps <T>" / "main" section headers, then
-//   "<pc> load r<d> in<k>", "scale r<d> <k as %a>", "sqrt r<d>", "abs r<d>",
-//   "mov r<d> r<s>", "add|mul|hypot r<d> r<s>", "firacc r<d> w<f>",
-//   "store r<s>", "stage r<s>", "end".
+//   "window <f> taps <T> node <id>" / "main" section headers, then
+//   "<pc> lda <m>", "sta t<j>", "add|mul|hypot <m>", "scale <k as %a>",
+//   "sqrt", "abs", "firacc w<f>", "stage w<f>", "store", "end",
+// where an operand <m> is in<k> (input k), t<j> (temporary j), w<f> (the
+// signal of window f over the chunk) or acc (the accumulator itself).
 static std::string listing(const simtgo_tile_graph* g, const Lowered& L) {
     std::string s;
     char line[160];
-    snprintf(line, sizeof line, "; simtgo_b200 tile program: %d instructions, %d inputs, %d windows\n",
-             L.prog.n_code, L.prog.n_in, L.prog.n_fir);
+    snprintf(line, sizeof line, "; simtgo_b200 tile program: %zu instructions, %zu inputs, %zu windows, %d temporaries\n",
+             L.code.size(), L.in_nodes.size(), L.fir_nodes.size(), L.n_tmp);
     s += line;
-    for (int k = 0; k < L.prog.n_in; k++) {
-        snprintf(line, sizeof line, "; in%d = node %d (p%d)\n", k, L.in_nodes[k],
+    for (size_t k = 0; k < L.in_nodes.size(); k++) {
+        snprintf(line, sizeof line, "; in%zu = node %d (p%d)\n", k, L.in_nodes[k],
                  L.param_of[L.in_nodes[k]]);
         s += line;
     }
-    for (int pc = 0; pc < L.prog.n_code; pc++) {
-        for (int f = 0; f < L.prog.n_fir; f++)
-            if (L.prog.fir[f].start == pc) {
-                snprintf(line, sizeof line, "window %d taps %d node %d\n", f, L.prog.fir[f].taps,
-                         L.fir_nodes[f]);
+    static const char* const names[tilek::OP_KINDS] = {
+        "end", "lda", "sta", "add", "mul", "hypot", "scale", "sqrt", "abs", "firacc", "stage", "store"};
+    for (size_t pc = 0; pc < L.code.size(); pc++) {
+        for (size_t f = 0; f < L.fir_nodes.size(); f++)
+            if (L.fir_start[f] == (int32_t)pc) {
+                const Node& fn = g->nodes[L.fir_nodes[f]];
+                snprintf(line, sizeof line, "window %zu taps %zu node %d\n", f,
+                         g->nodes[fn.b].taps.size(), L.fir_nodes[f]);
                 s += line;
             }
-        if (pc == L.prog.main_start) s += "main\n";
-        const Insn& in = L.prog.code[pc];
-        using namespace tilek;
-        const int op = in.code >> 6, d = (in.code >> 3) & 7, sl = in.code & 7;
-        switch (op) {
-            case OP_END: snprintf(line, sizeof line, "%d end\n", pc); break;
-            case OP_LOAD: snprintf(line, sizeof line, "%d load r%d in%d\n", pc, d, in.aux); break;
-            case OP_STORE: snprintf(line, sizeof line, "%d store r%d\n", pc, d); break;
-            case OP_STAGE: snprintf(line, sizeof line, "%d stage r%d\n", pc, d); break;
-            case OP_FIRACC:
-                snprintf(line, sizeof line, "%d firacc r%d w%d\n", pc, d, in.aux);
-                break;
-            case OP_SCALE:
-                snprintf(line, sizeof line, "%d scale r%d %a\n", pc, d, (double)in.imm);
-                break;
-            case OP_SQRT: snprintf(line, sizeof line, "%d sqrt r%d\n", pc, d); break;
-            case OP_ABS: snprintf(line, sizeof line, "%d abs r%d\n", pc, d); break;
-            default: {
-                const char* name = op == OP_MOV   ? "mov"
-                                   : op == OP_ADD ? "add"
-                                   : op == OP_MUL ? "mul"
-                                                  : "hypot";
-                snprintf(line, sizeof line, "%d %s r%d r%d\n", pc, name, d, sl);
-            }
+        if ((int32_t)pc == L.main_start) s += "main\n";
+        const LInsn& in = L.code[pc];
+        char opnd[48] = "";
+        switch (in.space) {
+            case SP_IN: snprintf(opnd, sizeof opnd, " in%d", in.idx); break;
+            case SP_TMP: snprintf(opnd, sizeof opnd, " t%d", in.idx); break;
+            case SP_WIN: snprintf(opnd, sizeof opnd, " w%d", in.idx); break;
+            case SP_SELF: snprintf(opnd, sizeof opnd, " acc"); break;
+            default:
+                if (in.op == tilek::OP_SCALE) snprintf(opnd, sizeof opnd, " %a", (double)in.imm);
+                if (in.op == tilek::OP_FIRACC || in.op == tilek::OP_STAGE)
+                    snprintf(opnd, sizeof opnd, " w%d", in.idx);
         }
+        snprintf(line, sizeof line, "%zu %s%s\n", pc, names[in.op], opnd);
         s += line;
     }
-    (void)g;
     return s;
 }
 

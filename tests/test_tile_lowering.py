@@ -1,10 +1,11 @@
 """The tile track's lowering, checked on the CPU: the library's listing of
 the fused program (Tensor.Source, tile/run.go:10) is executed here by a
-small emulator of the device interpreter's instruction set -- 8 register
-slots, per-position values, windows staged with zeros outside the signal,
-fma accumulation in tap order -- and must reproduce the oracle's node-by-node
-evaluation bit for bit. This pins register allocation, hoisted loads,
-in-place reuse and the window programs without a GPU."""
+small emulator of the device interpreter's accumulator machine -- one
+accumulator, operands in inputs, temporaries and window tiles, per-position
+values, windows staged with zeros outside the signal, fma accumulation in
+tap order -- and must reproduce the oracle's node-by-node evaluation bit for
+bit. This pins evaluation order, temporaries, operand reuse and the window
+programs without a GPU."""
 import ctypes
 import re
 
@@ -46,43 +47,46 @@ def emulate(listing, inputs, n, halo=0):
     span = n + halo
 
     def run(prog, tiles, taps_vals):
-        r = [None] * 8
+        acc = None
+        temps = {}
         out = None
+
+        def val(m):
+            if m == "acc":
+                return acc
+            k = int(m[1:] if m[0] in "tw" else m[2:])
+            return {"i": inputs, "t": temps, "w": tiles}[m[0]][k].astype(f32)
+
         for op, a in prog:
-            idx = lambda s: int(s.lstrip("rinw"))  # noqa: E731
-            if op == "load":
-                r[idx(a[0])] = inputs[idx(a[1])].astype(f32).copy()
+            if op == "lda":
+                acc = val(a[0]).copy()
+            elif op == "sta":
+                temps[int(a[0][1:])] = acc.copy()
             elif op == "scale":
-                r[idx(a[0])] = (f32(float.fromhex(a[1])) * r[idx(a[0])]).astype(f32)
+                acc = (f32(float.fromhex(a[0])) * acc).astype(f32)
             elif op == "sqrt":
-                r[idx(a[0])] = np.sqrt(r[idx(a[0])].astype(np.float64)).astype(f32)
+                acc = np.sqrt(acc.astype(np.float64)).astype(f32)
             elif op == "abs":
-                r[idx(a[0])] = np.abs(r[idx(a[0])])
-            elif op == "mov":
-                r[idx(a[0])] = r[idx(a[1])].copy()
+                acc = np.abs(acc)
             elif op in ("add", "mul"):
-                d, s = idx(a[0]), idx(a[1])
-                r[d] = (r[d] + r[s] if op == "add" else r[d] * r[s]).astype(f32)
+                m = val(a[0])
+                acc = (acc + m if op == "add" else acc * m).astype(f32)
             elif op == "hypot":
-                d, s = idx(a[0]), idx(a[1])
-                r[d] = np.array([O.oracle().oracle_hypot(float(u), float(v))
-                                 for u, v in zip(r[d], r[s])], f32)
+                m = val(a[0])
+                acc = np.array([O.oracle().oracle_hypot(float(u), float(v))
+                                for u, v in zip(acc, m)], f32)
             elif op == "firacc":
-                d, w = idx(a[0]), idx(a[1])
+                w = int(a[0][1:])
                 t = tiles[w]
-                acc = np.zeros(span, f32)
+                s = np.zeros(span, f32)
                 for k in range(taps_of[w]):
                     shifted = np.zeros(span, f32)   # samples before the signal read 0
                     shifted[k:] = t[: span - k]
                     hk = float(taps_vals[w][k])
-                    acc = np.array([_fmaf(hk, float(x), float(y)) for x, y in zip(shifted, acc)],
-                                   f32)
-                r[d] = acc
-            elif op == "store":
-                out = r[idx(a[0])]
-            elif op == "stage":
-                v = r[idx(a[0])].copy()
-                out = v
+                    s = np.array([_fmaf(hk, float(x), float(y)) for x, y in zip(shifted, s)], f32)
+                acc = s
+            elif op in ("store", "stage"):
+                out = acc.copy()
             elif op == "end":
                 break
         return out
@@ -141,8 +145,8 @@ def test_twelve_node_listing_matches_oracle(halo):
 
 
 def test_register_reuse_under_pressure():
-    """A graph with many simultaneously live values forces unhoisted loads
-    and in-place reuse; the listing still computes the oracle's values."""
+    """A graph with many simultaneously live values needs several
+    temporaries at once; the listing still computes the oracle's values."""
     n = 64
     rng = np.random.default_rng(2)
     xs = [rng.uniform(0.5, 2, n).astype(f32) for _ in range(12)]
@@ -178,3 +182,71 @@ def test_source_of_an_error_graph_raises():
     out = tile.Add(g.Input(np.zeros(3)), g.Input(np.zeros(4)))
     with pytest.raises(Exception, match="does not match"):
         out.Source()
+
+
+def _random_graph(seed, n, halo):
+    """A random DAG over the track's seven operations with shared values,
+    x-op-x nodes and up to two windows (none inside another): the tile graph
+    and the oracle's node table, in the same creation order."""
+    rng = np.random.default_rng(seed)
+    g = tile.New()
+    nodes, ts, has_fir, values = [], [], [], []
+
+    def add(t, nd, fir):
+        assert t.node == len(nodes)
+        values.append(len(nodes))
+        nodes.append(nd)
+        ts.append(t)
+        has_fir.append(fir)
+
+    for _ in range(int(rng.integers(1, 4))):
+        d = rng.uniform(-4, 4, n + halo).astype(f32)
+        add(g.Input(d[halo:]), {"kind": "input", "data": d}, False)
+    windows = 0
+    for _ in range(int(rng.integers(4, 14))):
+        pick = lambda: values[int(rng.integers(0, len(values)))]  # noqa: E731
+        kind = rng.choice(["scale", "abs", "sqrtabs", "add", "mul", "hypot", "fir"])
+        i = pick()
+        if kind == "fir":
+            if windows == 2 or has_fir[i]:
+                kind = "abs"
+            else:
+                windows += 1
+                h = (rng.uniform(-1, 1, int(rng.integers(1, 12))) / 4).astype(f32)
+                add_taps = len(nodes)
+                t = tile.FIR(ts[i], h)
+                nodes.append({"kind": "input", "data": h})
+                ts.append(None)
+                has_fir.append(False)
+                assert t.node == add_taps + 1
+                add(t, {"kind": "fir", "a": i, "taps": h}, True)
+                continue
+        if kind == "scale":
+            k = float(rng.choice([0.5, -1.25, 3.0, -0.1]))
+            add(tile.Scale(ts[i], k), {"kind": "scale", "a": i, "scale": k}, has_fir[i])
+        elif kind == "abs":
+            add(tile.Abs(ts[i]), {"kind": "abs", "a": i}, has_fir[i])
+        elif kind == "sqrtabs":
+            add(tile.Abs(ts[i]), {"kind": "abs", "a": i}, has_fir[i])
+            j = len(ts) - 1
+            add(tile.Sqrt(ts[j]), {"kind": "sqrt", "a": j}, has_fir[i])
+        else:
+            j = i if rng.random() < 0.2 else pick()
+            op = {"add": tile.Add, "mul": tile.Mul, "hypot": tile.Hypot}[kind]
+            add(op(ts[i], ts[j]), {"kind": kind, "a": i, "b": j}, has_fir[i] or has_fir[j])
+    return ts[values[-1]], nodes
+
+
+@pytest.mark.parametrize("seed", range(24))
+def test_random_graph_listing_matches_oracle(seed):
+    n, halo = 40, (8 if seed % 3 == 0 else 0)
+    root, nodes = _random_graph(seed, n, halo)
+    src = root.Source()
+    node_of = [int(m) for m in re.findall(r"; in\d+ = node (\d+)", src)]
+    taps = {}
+    for m in re.finditer(r"window (\d+) taps \d+ node (\d+)", src):
+        taps[int(m.group(1))] = nodes[int(m.group(2))]["taps"]
+    got = run_listing(src, [nodes[i]["data"] for i in node_of], n, taps, halo)
+    rc, want = O.tile_eval(nodes, len(nodes) - 1, n, halo)
+    assert rc == 0
+    np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))
