@@ -68,8 +68,9 @@ __host__ __device__ constexpr int window_reach(int taps) { return (taps - 1 + 3)
 constexpr int kTileF = kChunk + window_reach(kMaxTaps) + 4;  // staged floats per window node
 constexpr int kMaxStages = 16;
 
-// Operations of the accumulator machine. A is the accumulator (the thread's
-// 8 elements), M the instruction's operand in shared memory.
+// Steps of the accumulator machine. A is the accumulator (the thread's
+// 8 elements), M an operand in shared memory. The lowering emits these one
+// by one; a device instruction fuses a run of them (below).
 enum Op : uint8_t {
     OP_END = 0,
     OP_LDA,     // A = M
@@ -80,21 +81,34 @@ enum Op : uint8_t {
     OP_SCALE,   // A = imm * A
     OP_SQRT,    // A = sqrt(A)
     OP_ABS,     // A = |A|
-    OP_FIRACC,  // A = window arg accumulated at the thread's positions
-    OP_STAGE,   // window arg's tile = A (zero outside the signal)
+    OP_FIRACC,  // A = window b accumulated at the thread's positions
+    OP_STAGE,   // window's tile = A (zero outside the signal)
     OP_STORE,   // out = A
     OP_KINDS,
 };
-// Operand flags.
-constexpr uint8_t F_IN = 1;    // M is a staged input: arg is relative to the current stage
-constexpr uint8_t F_SELF = 2;  // M is A itself (x op x)
+// A device instruction is one dispatch doing, in order: [A = M(a)] if
+// F_LOADA; the operation op (ADD/MUL/HYPOT with operand M(b), SCALE, SQRT,
+// ABS, FIRACC of window b; OP_END: none); [M(d) = A] if F_STA; [tile of
+// window d = A] if F_STAGE; [out = A] if F_STORE; return if F_END.
+constexpr uint8_t F_LOADA = 1;
+constexpr uint8_t F_IN_A = 2;   // M(a) is a staged input: a is relative to the current stage
+constexpr uint8_t F_IN_B = 4;   // M(b) likewise
+constexpr uint8_t F_SELF = 8;   // M(b) is A itself (x op x)
+constexpr uint8_t F_STA = 16;
+constexpr uint8_t F_STAGE = 32;
+constexpr uint8_t F_STORE = 64;
+constexpr uint8_t F_END = 128;
 
 struct Insn {
     uint8_t op;
     uint8_t flags;
-    uint16_t arg;  // operand: float4 offset in shared memory; or a window index
-    float imm;
+    uint16_t a;  // F_LOADA operand: float4 offset in shared memory (or input index, DIRECT)
+    uint16_t b;  // binary operand likewise, or the FIRACC window
+    uint16_t d;  // F_STA temporary (float4 offset) or F_STAGE window
+    float imm;   // SCALE factor
+    uint32_t pad;
 };
+static_assert(sizeof(Insn) == 16, "one 16-byte shared load per instruction");
 
 struct FirDesc {
     int32_t start;  // pc of the staging program
@@ -118,16 +132,16 @@ struct Program {
 // parameter bank into shared memory, where a warp-uniform word is one
 // broadcast load. Layout: code[code_cap] | fir[n_fir] (start, taps, reach,
 // tile4) | in[n_in], 16-byte rounded.
-__host__ __device__ constexpr int meta_code_cap(int n_code) { return (n_code + 2) & ~1; }
+__host__ __device__ constexpr int meta_code_cap(int n_code) { return n_code + 1; }
 __host__ __device__ constexpr int meta_bytes(int n_code, int n_in, int n_fir) {
-    return ((meta_code_cap(n_code) * 8 + n_in * 8 + n_fir * 16) + 15) & ~15;
+    return ((meta_code_cap(n_code) * 16 + n_in * 8 + n_fir * 16) + 15) & ~15;
 }
 
 // One run of a program over kChunk (or, for a window's halo, fewer)
 // positions.
 struct Run {
     int32_t sh_in;   // added to F_IN operands: the stage and the run's position
-    int32_t sh_st;   // added to STAGE destinations (the halo run's offset)
+    int32_t sh_st;   // added to STAGE destinations (the run's offset in the tile)
     uint32_t gm;     // which of the thread's groups take part
     int64_t p0;      // position of the run's element 0
     bool edge;       // some positions of the run lie outside [-halo, n)
@@ -176,33 +190,56 @@ __device__ __forceinline__ float f4_get(const float4& v, int j) {
 // W = tile[b_k - i0 - 4 .. b_k - i0 + 3] for taps i0 .. i0+3, the sample of
 // output j at tap i0+u is W[4 + j - u]; the upper half of W is the lower
 // half of the previous step, so each step loads one new float4 per group.
+// Four taps (hv[0..nk-1]) on the 4 outputs of one group, with
+// w = tile[b - i0 - 4 .. b - i0 + 3] given as its halves lo, hi.
+template <bool PART>
+__device__ __forceinline__ void fir_step(float (&acc)[4], const float4& lo, const float4& hi,
+                                         const float (&hv)[4], int nk) {
+    const float w[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+#pragma unroll
+    for (int u = 0; u < 4; u++)
+        if (!PART || u < nk)
+#pragma unroll
+            for (int j = 0; j < 4; j++) acc[j] = __fmaf_rn(hv[u], w[4 + j - u], acc[j]);
+}
+
 __device__ __forceinline__ void fir_acc(float4 (&A)[kG], const Ctx& c, int f) {
     const int4 fd = c.fir[f];
     const int taps = fd.y;
-    const float4* tile4 = c.S + fd.w;
     const float4* h4 = reinterpret_cast<const float4*>(c.taps_s + f * kMaxTaps);
-    const int t = threadIdx.x;
+    // Group k's window float4 at tap i0 (a multiple of 4): tw[k][-i0/4].
+    const float4* tw = c.S + fd.w + threadIdx.x + fd.z / 4;
     float acc[kG][4];
     float4 hi[kG];
 #pragma unroll
     for (int k = 0; k < kG; k++) {
 #pragma unroll
         for (int j = 0; j < 4; j++) acc[k][j] = 0.0f;
-        hi[k] = tile4[t + kThreads * k + fd.z / 4];
+        hi[k] = tw[kThreads * k];
     }
-    for (int i0 = 0; i0 < taps; i0 += 4) {
+    // Whole steps of 8 taps, two window loads per group, no predicates.
+    int i0 = 0;
+    for (; i0 + 8 <= taps; i0 += 8) {
+        const float4 ha = h4[i0 / 4], hb = h4[i0 / 4 + 1];
+        const float hva[4] = {ha.x, ha.y, ha.z, ha.w}, hvb[4] = {hb.x, hb.y, hb.z, hb.w};
+#pragma unroll
+        for (int k = 0; k < kG; k++) {
+            const float4 m = tw[kThreads * k - i0 / 4 - 1];
+            const float4 lo = tw[kThreads * k - i0 / 4 - 2];
+            fir_step<false>(acc[k], m, hi[k], hva, 4);
+            fir_step<false>(acc[k], lo, m, hvb, 4);
+            hi[k] = lo;
+        }
+    }
+    // The last 1-7 taps, 4 at a time.
+    for (; i0 < taps; i0 += 4) {
         const float4 hk = h4[i0 / 4];
         const float hv[4] = {hk.x, hk.y, hk.z, hk.w};
         const int nk = min(4, taps - i0);
 #pragma unroll
         for (int k = 0; k < kG; k++) {
-            const float4 lo = tile4[t + kThreads * k + (fd.z - i0) / 4 - 1];
-            const float w[8] = {lo.x, lo.y, lo.z, lo.w, hi[k].x, hi[k].y, hi[k].z, hi[k].w};
-#pragma unroll
-            for (int u = 0; u < 4; u++)
-                if (u < nk)
-#pragma unroll
-                    for (int j = 0; j < 4; j++) acc[k][j] = __fmaf_rn(hv[u], w[4 + j - u], acc[k][j]);
+            const float4 lo = tw[kThreads * k - i0 / 4 - 1];
+            fir_step<true>(acc[k], lo, hi[k], hv, nk);
             hi[k] = lo;
         }
     }
@@ -231,12 +268,12 @@ __device__ __forceinline__ float4 mask_outside(float4 v, int64_t p, const Ctx& c
     return make_float4(f[0], f[1], f[2], f[3]);
 }
 
-// Runs the program from pc until OP_END. Inlined into k_tile twice: FULL
-// for runs where all of the thread's groups take part (the chunk), and the
-// general form for a window's halo run; the next word is loaded while this
-// one executes (the shared copy holds one word past the last END). In
-// DIRECT mode (BULK false) an input operand is read from HBM at the run's
-// positions.
+// Runs the program from pc until an instruction with F_END. Inlined into
+// k_tile twice: FULL for runs where all of the thread's groups take part
+// (the chunk), and the general form for a window's head run; the next
+// instruction is loaded while this one executes (the shared copy holds one
+// past the last). In DIRECT mode (BULK false) an input operand is read from
+// HBM at the run's positions.
 template <bool BULK, bool FULL>
 __device__ __forceinline__ void interpret(const Insn* code, int pc, const Ctx& c, const Run& r) {
     const int t = threadIdx.x;
@@ -247,40 +284,32 @@ __device__ __forceinline__ void interpret(const Insn* code, int pc, const Ctx& c
     for (;;) {
         const Insn in = next;
         next = code[++pc];
-        const int off = (int)in.arg + ((in.flags & F_IN) ? r.sh_in : 0) + t;
-        // Group k of operand M (inactive groups: A itself, nothing is read).
-        auto operand = [&](int k) -> float4 {
+        // Group k of operand M(x) (inactive groups: A itself, nothing is read).
+        auto operand = [&](int x, bool input, int k) -> float4 {
             if (!FULL && !((r.gm >> k) & 1)) return A[k];
-            if (!BULK && (in.flags & F_IN))
-                return gload4(c.in[in.arg], r.p0 + 4 * (t + kThreads * k), c);
-            return c.S[off + kThreads * k];
+            if (!BULK && input) return gload4(c.in[x], r.p0 + 4 * (t + kThreads * k), c);
+            return c.S[x + (input ? r.sh_in : 0) + t + kThreads * k];
         };
-        float4 M[kG];
-        if (in.op == OP_ADD || in.op == OP_MUL || in.op == OP_HYPOT) {
+        if (in.flags & F_LOADA) {
 #pragma unroll
-            for (int k = 0; k < kG; k++) M[k] = (in.flags & F_SELF) ? A[k] : operand(k);
+            for (int k = 0; k < kG; k++) A[k] = operand(in.a, in.flags & F_IN_A, k);
         }
+        // The second operand of a binary operation, read inside its case.
+        auto binop = [&](int k) -> float4 {
+            return (in.flags & F_SELF) ? A[k] : operand(in.b, in.flags & F_IN_B, k);
+        };
         switch (in.op) {
-            case OP_LDA:
-#pragma unroll
-                for (int k = 0; k < kG; k++) A[k] = operand(k);
-                break;
-            case OP_STA:
-#pragma unroll
-                for (int k = 0; k < kG; k++)
-                    if (FULL || ((r.gm >> k) & 1)) c.S[off + kThreads * k] = A[k];
-                break;
             case OP_ADD:
 #pragma unroll
-                for (int k = 0; k < kG; k++) A[k] = f4_add(A[k], M[k]);
+                for (int k = 0; k < kG; k++) A[k] = f4_add(A[k], binop(k));
                 break;
             case OP_MUL:
 #pragma unroll
-                for (int k = 0; k < kG; k++) A[k] = f4_mul(A[k], M[k]);
+                for (int k = 0; k < kG; k++) A[k] = f4_mul(A[k], binop(k));
                 break;
             case OP_HYPOT:
 #pragma unroll
-                for (int k = 0; k < kG; k++) A[k] = f4_hypot(A[k], M[k]);
+                for (int k = 0; k < kG; k++) A[k] = f4_hypot(A[k], binop(k));
                 break;
             case OP_SCALE:
 #pragma unroll
@@ -295,18 +324,26 @@ __device__ __forceinline__ void interpret(const Insn* code, int pc, const Ctx& c
                 for (int k = 0; k < kG; k++) A[k] = f4_abs(A[k]);
                 break;
             case OP_FIRACC:
-                fir_acc(A, c, in.arg);
+                fir_acc(A, c, in.b);
                 break;
-            case OP_STAGE: {
-                float4* dst = c.S + c.fir[in.arg].w + r.sh_st + t;
+            default:
+                break;  // OP_END: no operation
+        }
+        if (in.flags & (F_STA | F_STAGE | F_STORE | F_END)) {
+            if (in.flags & F_STA) {
+#pragma unroll
+                for (int k = 0; k < kG; k++)
+                    if (FULL || ((r.gm >> k) & 1)) c.S[in.d + t + kThreads * k] = A[k];
+            }
+            if (in.flags & F_STAGE) {
+                float4* dst = c.S + c.fir[in.d].w + r.sh_st + t;
 #pragma unroll
                 for (int k = 0; k < kG; k++)
                     if (FULL || ((r.gm >> k) & 1))
                         dst[kThreads * k] =
                             r.edge ? mask_outside(A[k], r.p0 + 4 * (t + kThreads * k), c) : A[k];
-                break;
             }
-            case OP_STORE:
+            if (in.flags & F_STORE) {
 #pragma unroll
                 for (int k = 0; k < kG; k++) {
                     const int64_t p = r.p0 + 4 * (t + kThreads * k);
@@ -318,9 +355,8 @@ __device__ __forceinline__ void interpret(const Insn* code, int pc, const Ctx& c
                             if (p + j < c.n) c.out[p + j] = f4_get(A[k], j);
                     }
                 }
-                break;
-            default:
-                return;  // OP_END
+            }
+            if (in.flags & F_END) return;
         }
     }
 }
@@ -338,10 +374,14 @@ struct ChunkSpan {
     int64_t org, lo, len4, hi;  // buffer origin, copied [lo, lo+len4), valid [lo, hi)
 };
 
-__device__ __forceinline__ ChunkSpan chunk_span(int64_t cb, int hs, int64_t n, int64_t halo) {
+// The input span a chunk needs: with its halo (the first chunk of a block's
+// range, whose window heads are computed) or without (later chunks carry
+// the heads over from the chunk before).
+__device__ __forceinline__ ChunkSpan chunk_span(int64_t cb, int hs, int64_t n, int64_t halo,
+                                                bool with_halo) {
     ChunkSpan s;
     s.org = cb - hs;
-    s.lo = max(s.org, -halo);
+    s.lo = max(with_halo ? s.org : cb, -halo);
     s.hi = min(cb + (int64_t)kChunk, n);
     s.len4 = s.hi > s.lo ? ((s.hi - s.lo) & ~int64_t(3)) : 0;
     return s;
@@ -350,7 +390,14 @@ __device__ __forceinline__ ChunkSpan chunk_span(int64_t cb, int hs, int64_t n, i
 // Shared memory (float4 units): meta | taps (n_fir x kMaxTaps floats) |
 // tiles (n_fir x kTileF floats) | temporaries (n_tmp x kChunk floats) |
 // stages (nst x n_in x (hs + kChunk) floats, BULK only). Input k of a stage
-// holds positions [cb - hs, cb + kChunk) of the chunk at cb.
+// holds positions [cb - hs, cb + kChunk) of the chunk at cb (the part below
+// cb only for the first chunk of the block's range).
+//
+// A block works through a contiguous range of chunks. Window f's tile holds
+// positions [cb - reach, cb + kChunk): the chunk's own positions are staged
+// by one run of the window's program; the head below cb is the previous
+// chunk's last reach positions, copied within the tile, and is computed by
+// a short head run only for the first chunk of the range.
 //
 // Bulk-copy mode (BULK): the chunk's inputs travel HBM -> shared memory by
 // cp.async.bulk, one copy per input, in `nst` stages that complete on
@@ -375,7 +422,7 @@ __global__ void __launch_bounds__(kThreads, 3) k_tile(const __grid_constant__ Pr
     const int tid = threadIdx.x;
     const int64_t nchunks = (n + kChunk - 1) / kChunk;
     for (int i = tid; i < code_cap; i += kThreads)
-        code_s[i] = i < P.n_code ? P.code[i] : Insn{OP_END, 0, 0, 0.0f};
+        code_s[i] = i < P.n_code ? P.code[i] : Insn{OP_END, F_END, 0, 0, 0, 0.0f, 0};
     for (int k = tid; k < P.n_in; k += kThreads) in_s[k] = P.in[k];
     for (int f = tid; f < P.n_fir; f += kThreads)
         fir_s[f] = make_int4(P.fir[f].start, P.fir[f].taps, P.fir[f].reach, P.fir[f].tile4);
@@ -383,8 +430,11 @@ __global__ void __launch_bounds__(kThreads, 3) k_tile(const __grid_constant__ Pr
         for (int k = tid; k < kMaxTaps; k += kThreads)
             taps_s[f * kMaxTaps + k] = P.fir[f].h[k];  // zero past taps
 
+    const int64_t per_block = (nchunks + gridDim.x - 1) / gridDim.x;
+    const int64_t c0 = blockIdx.x * per_block;
+    const int64_t c1 = min(c0 + per_block, nchunks);
     auto issue = [&](int64_t c, int s) {
-        const ChunkSpan sp = chunk_span(c * kChunk, hs, n, halo);
+        const ChunkSpan sp = chunk_span(c * kChunk, hs, n, halo, c == c0);
         mbar_arrive_expect_tx(&bars[s], (uint32_t)(sp.len4 * 4 * P.n_in));
         if (sp.len4 > 0)
             for (int k = 0; k < P.n_in; k++)
@@ -398,10 +448,8 @@ __global__ void __launch_bounds__(kThreads, 3) k_tile(const __grid_constant__ Pr
         }
         __syncthreads();
         if (tid == 0)
-            for (int s = 0; s < nst; s++) {
-                const int64_t c = blockIdx.x + (int64_t)s * gridDim.x;
-                if (c < nchunks) issue(c, s);
-            }
+            for (int s = 0; s < nst; s++)
+                if (c0 + s < c1) issue(c0 + s, s);
     }
     __syncthreads();
 
@@ -417,9 +465,10 @@ __global__ void __launch_bounds__(kThreads, 3) k_tile(const __grid_constant__ Pr
     cx.in_vec = in_vec;
     const int nf = P.n_fir;
     int it = 0;
-    for (int64_t c = blockIdx.x; c < nchunks; c += gridDim.x, it++) {
+    for (int64_t c = c0; c < c1; c++, it++) {
         const int64_t cb = c * kChunk;
-        const ChunkSpan sp = chunk_span(cb, hs, n, halo);
+        const bool first = c == c0;
+        const ChunkSpan sp = chunk_span(cb, hs, n, halo, first);
         int s = 0;
         if (BULK) {
             s = it % nst;
@@ -437,20 +486,36 @@ __global__ void __launch_bounds__(kThreads, 3) k_tile(const __grid_constant__ Pr
         }
         const int32_t in4 = stages4 + s * stage_floats / 4;
         const bool edge = cb - (int64_t)hs < -halo || cb + kChunk > n;
-        // Jobs 2f and 2f+1 stage window f over its tile (the chunk, then the
-        // reach below it); job 2 nf is the main program over the chunk. One
+        // Jobs 2f and 2f+1 stage window f: its head (first chunk only) and
+        // the chunk itself; job 2 nf is the main program over the chunk. One
         // loop, so the interpreter is inlined once per form.
         for (int j = 0; j <= 2 * nf; j++) {
             Run r;
             int pc;
             if (j < 2 * nf) {
                 const int4 fd = fir_s[j >> 1];
-                const bool halo_run = j & 1;
+                const int head4 = fd.z / 4;
                 pc = fd.x;
-                r.sh_in = in4 + (hs - fd.z) / 4 + (halo_run ? kChunk4 : 0);
-                r.sh_st = halo_run ? kChunk4 : 0;
-                r.gm = halo_run ? (tid < fd.z / 4 ? 1u : 0u) : (1u << kG) - 1;
-                r.p0 = cb - fd.z + (halo_run ? kChunk : 0);
+                if (!(j & 1)) {  // head: tile [0, reach) = positions [cb - reach, cb)
+                    r.sh_in = in4 + (hs - fd.z) / 4;
+                    r.sh_st = 0;
+                    r.gm = first && tid < head4 ? 1u : 0u;
+                    r.p0 = cb - fd.z;
+                } else {  // the chunk: tile [reach, reach + kChunk)
+                    // Carry the head over: the previous chunk's last reach
+                    // positions sit at tile [kChunk, kChunk + reach). The
+                    // thread that copies a float4 is the one whose staging
+                    // below overwrites it, so no barrier is needed.
+                    if (!first && tid >= kThreads - head4) {
+                        float4* tile = cx.S + fd.w;
+                        const int q = tid - (kThreads - head4);
+                        tile[q] = tile[kChunk4 + q];
+                    }
+                    r.sh_in = in4 + hs / 4;
+                    r.sh_st = head4;
+                    r.gm = (1u << kG) - 1;
+                    r.p0 = cb;
+                }
             } else {
                 pc = P.main_start;
                 r.sh_in = in4 + hs / 4;
@@ -470,10 +535,7 @@ __global__ void __launch_bounds__(kThreads, 3) k_tile(const __grid_constant__ Pr
         // copy into it.
         if (BULK) fence_proxy_async_smem();
         __syncthreads();
-        if (BULK && tid == 0) {
-            const int64_t cn = c + (int64_t)nst * gridDim.x;
-            if (cn < nchunks) issue(cn, it % nst);
-        }
+        if (BULK && tid == 0 && c + nst < c1) issue(c + nst, it % nst);
     }
 }
 
@@ -561,8 +623,75 @@ struct LInsn {
     float imm;
 };
 
+// A device instruction before the layout gives its operands addresses: a
+// fused run of lowered steps (see tilek::Insn).
+struct FInsn {
+    uint8_t op = tilek::OP_END;  // the operation, or OP_END for none
+    bool loada = false, sta = false, stage = false, store = false, end = false;
+    uint8_t a_space = SP_NONE, b_space = SP_NONE;
+    uint16_t a_idx = 0, b_idx = 0;  // b: binary operand, or the FIRACC window
+    uint16_t d_idx = 0;             // the STA temporary or the STAGE window
+    float imm = 0.0f;
+};
+
+// Fuses a program's steps into device instructions: each takes an optional
+// load, one operation, an optional store to a temporary, to a window tile or
+// to the output, and the end, in that order.
+void fuse(const std::vector<LInsn>& raw, std::vector<FInsn>& out) {
+    FInsn cur;
+    bool open = false;
+    auto flush = [&]() {
+        if (open) out.push_back(cur);
+        cur = FInsn();
+        open = false;
+    };
+    for (const LInsn& li : raw) {
+        switch (li.op) {
+            case tilek::OP_LDA:
+                flush();
+                cur.loada = true;
+                cur.a_space = li.space;
+                cur.a_idx = li.idx;
+                open = true;
+                break;
+            case tilek::OP_STA:
+                if (!open || cur.sta || cur.stage || cur.store) flush();
+                cur.sta = true;
+                cur.d_idx = li.idx;
+                open = true;
+                break;
+            case tilek::OP_STAGE:
+            case tilek::OP_STORE:
+                if (!open || cur.stage || cur.store) flush();
+                if (li.op == tilek::OP_STAGE) {
+                    if (cur.sta) flush();
+                    cur.stage = true;
+                    cur.d_idx = li.idx;
+                } else {
+                    cur.store = true;
+                }
+                open = true;
+                break;
+            case tilek::OP_END:
+                cur.end = true;
+                open = true;
+                flush();
+                break;
+            default:  // an operation: joins a pending load, else starts anew
+                if (open && !(cur.op == tilek::OP_END && !cur.sta && !cur.stage && !cur.store))
+                    flush();
+                cur.op = li.op;
+                cur.b_space = li.space;
+                cur.b_idx = li.idx;
+                cur.imm = li.imm;
+                open = true;
+        }
+    }
+    flush();
+}
+
 struct Lowered {
-    std::vector<LInsn> code;
+    std::vector<FInsn> code;
     int32_t main_start = 0;
     std::vector<int32_t> fir_start;  // pc of each window's staging program
     int n_tmp = 0;                   // temporaries the programs use at once
@@ -589,6 +718,7 @@ struct Gen {
     std::vector<int8_t> space;     // where a node's value is stored (Space), or SP_NONE
     std::vector<int> where;        // its index in that space
     std::vector<int> need_memo;
+    std::vector<LInsn> raw;        // the program's steps, fused at the end
     bool tmp_busy[tilek::kMaxTmp] = {};
     int status = 0;                // -1 temporaries exhausted, -2 inputs exhausted
 
@@ -602,7 +732,7 @@ struct Gen {
         need_memo.assign(nn, -1);
     }
     void push(uint8_t op, uint8_t sp = SP_NONE, int idx = 0, float imm = 0.0f) {
-        L.code.push_back(LInsn{op, sp, (uint16_t)idx, imm});
+        raw.push_back(LInsn{op, sp, (uint16_t)idx, imm});
     }
     bool leaf(int id) const {
         const Node& n = g->nodes[id];
@@ -788,6 +918,7 @@ int lower(const simtgo_tile_graph* g, int root, Lowered& L) {
         gen.emit(sig);
         gen.push(tilek::OP_STAGE, SP_NONE, (int)f);
         gen.push(tilek::OP_END);
+        fuse(gen.raw, L.code);
         status = gen.status;
     }
     if (!status) {
@@ -806,6 +937,7 @@ int lower(const simtgo_tile_graph* g, int root, Lowered& L) {
         gen.emit(root);
         gen.push(tilek::OP_STORE);
         gen.push(tilek::OP_END);
+        fuse(gen.raw, L.code);
         status = gen.status;
     }
     if (status == -2)
@@ -842,25 +974,47 @@ void build_program(const simtgo_tile_graph* g, const Lowered& L, const Layout& Y
         P.fir[f].tile4 = Y.tiles4 + f * tilek::kTileF / 4;
         for (size_t k = 0; k < h.size(); k++) P.fir[f].h[k] = h[k];
     }
-    for (size_t pc = 0; pc < L.code.size(); pc++) {
-        const LInsn& li = L.code[pc];
-        tilek::Insn& in = P.code[pc];
-        in.op = li.op;
-        in.imm = li.imm;
-        in.flags = 0;
-        in.arg = 0;
-        switch (li.space) {
-            case SP_IN:
-                in.flags = tilek::F_IN;
-                in.arg = (uint16_t)(bulk ? li.idx * Y.sstride / 4 : li.idx);
-                break;
-            case SP_TMP: in.arg = (uint16_t)(Y.temps4 + li.idx * tilek::kChunk4); break;
-            case SP_WIN:
-                in.arg = (uint16_t)(P.fir[li.idx].tile4 + P.fir[li.idx].reach / 4);
-                break;
-            case SP_SELF: in.flags = tilek::F_SELF; break;
-            default: in.arg = li.idx; break;  // FIRACC / STAGE: the window
+    // A lowered operand's address: inputs relative to the run's stage
+    // (BULK) or their index (DIRECT), temporaries and window signals absolute.
+    auto addr = [&](uint8_t space, int idx, bool* input) -> uint16_t {
+        *input = space == SP_IN;
+        switch (space) {
+            case SP_IN: return (uint16_t)(bulk ? idx * Y.sstride / 4 : idx);
+            case SP_TMP: return (uint16_t)(Y.temps4 + idx * tilek::kChunk4);
+            case SP_WIN: return (uint16_t)(P.fir[idx].tile4 + P.fir[idx].reach / 4);
+            default: return (uint16_t)idx;
         }
+    };
+    for (size_t pc = 0; pc < L.code.size(); pc++) {
+        const FInsn& fi = L.code[pc];
+        tilek::Insn& in = P.code[pc];
+        memset(&in, 0, sizeof in);
+        in.op = fi.op;
+        in.imm = fi.imm;
+        bool input;
+        if (fi.loada) {
+            in.flags |= tilek::F_LOADA;
+            in.a = addr(fi.a_space, fi.a_idx, &input);
+            if (input) in.flags |= tilek::F_IN_A;
+        }
+        if (fi.op == tilek::OP_FIRACC) {
+            in.b = fi.b_idx;
+        } else if (fi.b_space == SP_SELF) {
+            in.flags |= tilek::F_SELF;
+        } else if (fi.b_space != SP_NONE) {
+            in.b = addr(fi.b_space, fi.b_idx, &input);
+            if (input) in.flags |= tilek::F_IN_B;
+        }
+        if (fi.sta) {
+            in.flags |= tilek::F_STA;
+            in.d = (uint16_t)(Y.temps4 + fi.d_idx * tilek::kChunk4);
+        }
+        if (fi.stage) {
+            in.flags |= tilek::F_STAGE;
+            in.d = fi.d_idx;
+        }
+        if (fi.store) in.flags |= tilek::F_STORE;
+        if (fi.end) in.flags |= tilek::F_END;
     }
 }
 
@@ -1167,16 +1321,18 @@ int simtgo_tile_program_size(simtgo_tile_graph* g, simtgo_tensor t, int32_t* n_i
     return 0;
 }
 
-// The listing of a lowered program, one instruction per line:
+// The listing of a lowered program, one device instruction per line:
 //   "window <f> taps <T> node <id>" / "main" section headers, then
-//   "<pc> lda <m>", "sta t<j>", "add|mul|hypot <m>", "scale <k as %a>",
-//   "sqrt", "abs", "firacc w<f>", "stage w<f>", "store", "end",
+//   "<pc> <step> | <step> ...", the steps the instruction fuses, in order:
+//   "lda <m>", "add|mul|hypot <m>", "scale <k as %a>", "sqrt", "abs",
+//   "firacc w<f>", "sta t<j>", "stage w<f>", "store", "end",
 // where an operand <m> is in<k> (input k), t<j> (temporary j), w<f> (the
 // signal of window f over the chunk) or acc (the accumulator itself).
 static std::string listing(const simtgo_tile_graph* g, const Lowered& L) {
     std::string s;
-    char line[160];
-    snprintf(line, sizeof line, "; simtgo_b200 tile program: %zu instructions, %zu inputs, %zu windows, %d temporaries\n",
+    char line[256];
+    snprintf(line, sizeof line,
+             "; simtgo_b200 tile program: %zu instructions, %zu inputs, %zu windows, %d temporaries\n",
              L.code.size(), L.in_nodes.size(), L.fir_nodes.size(), L.n_tmp);
     s += line;
     for (size_t k = 0; k < L.in_nodes.size(); k++) {
@@ -1186,6 +1342,16 @@ static std::string listing(const simtgo_tile_graph* g, const Lowered& L) {
     }
     static const char* const names[tilek::OP_KINDS] = {
         "end", "lda", "sta", "add", "mul", "hypot", "scale", "sqrt", "abs", "firacc", "stage", "store"};
+    auto operand = [](uint8_t space, int idx) -> std::string {
+        char b[32];
+        switch (space) {
+            case SP_IN: snprintf(b, sizeof b, "in%d", idx); break;
+            case SP_TMP: snprintf(b, sizeof b, "t%d", idx); break;
+            case SP_WIN: snprintf(b, sizeof b, "w%d", idx); break;
+            default: snprintf(b, sizeof b, "acc"); break;
+        }
+        return b;
+    };
     for (size_t pc = 0; pc < L.code.size(); pc++) {
         for (size_t f = 0; f < L.fir_nodes.size(); f++)
             if (L.fir_start[f] == (int32_t)pc) {
@@ -1195,20 +1361,26 @@ static std::string listing(const simtgo_tile_graph* g, const Lowered& L) {
                 s += line;
             }
         if ((int32_t)pc == L.main_start) s += "main\n";
-        const LInsn& in = L.code[pc];
-        char opnd[48] = "";
-        switch (in.space) {
-            case SP_IN: snprintf(opnd, sizeof opnd, " in%d", in.idx); break;
-            case SP_TMP: snprintf(opnd, sizeof opnd, " t%d", in.idx); break;
-            case SP_WIN: snprintf(opnd, sizeof opnd, " w%d", in.idx); break;
-            case SP_SELF: snprintf(opnd, sizeof opnd, " acc"); break;
-            default:
-                if (in.op == tilek::OP_SCALE) snprintf(opnd, sizeof opnd, " %a", (double)in.imm);
-                if (in.op == tilek::OP_FIRACC || in.op == tilek::OP_STAGE)
-                    snprintf(opnd, sizeof opnd, " w%d", in.idx);
+        const FInsn& in = L.code[pc];
+        std::vector<std::string> steps;
+        if (in.loada) steps.push_back("lda " + operand(in.a_space, in.a_idx));
+        if (in.op == tilek::OP_SCALE) {
+            snprintf(line, sizeof line, "scale %a", (double)in.imm);
+            steps.push_back(line);
+        } else if (in.op == tilek::OP_FIRACC) {
+            steps.push_back("firacc w" + std::to_string(in.b_idx));
+        } else if (in.op == tilek::OP_ADD || in.op == tilek::OP_MUL || in.op == tilek::OP_HYPOT) {
+            steps.push_back(std::string(names[in.op]) + " " + operand(in.b_space, in.b_idx));
+        } else if (in.op != tilek::OP_END) {
+            steps.push_back(names[in.op]);
         }
-        snprintf(line, sizeof line, "%zu %s%s\n", pc, names[in.op], opnd);
-        s += line;
+        if (in.sta) steps.push_back("sta t" + std::to_string(in.d_idx));
+        if (in.stage) steps.push_back("stage w" + std::to_string(in.d_idx));
+        if (in.store) steps.push_back("store");
+        if (in.end) steps.push_back("end");
+        std::string text = std::to_string(pc) + " ";
+        for (size_t i = 0; i < steps.size(); i++) text += (i ? " | " : "") + steps[i];
+        s += text + "\n";
     }
     return s;
 }

@@ -42,8 +42,10 @@ def emulate(listing, inputs, n, halo=0):
             cur = ("main",)
             progs[cur] = []
             continue
-        pc, op, *args = line.split()
-        progs[cur].append((op, args))
+        pc, _, rest = line.partition(" ")
+        for step in rest.split(" | "):   # the steps one device instruction fuses
+            op, *args = step.split()
+            progs[cur].append((op, args))
     span = n + halo
 
     def run(prog, tiles, taps_vals):
