@@ -240,11 +240,26 @@ struct ClassifyOp {
 };
 
 // ---- BandGain --------------------------------------------------------------------
-// Bands are staged in shared memory (up to kMaxSharedBands; a longer curve is
-// read from global memory). The 4-tap window x[i-2..i+1] of a vector unit
-// needs x[4v-2], x[4v-1] and x[4v+4] beyond its own float4; those come
-// through L1, where the neighbouring units' loads already put them.
+// kernels/bandgain.go:42-74. The gain is that of the first band, in order,
+// whose Upper is >= x[i], else the floor. With U_j = max(Upper_0..Upper_j)
+// (NaN uppers skipped; NaN until the first number), that band is the first
+// j with x[i] <= U_j: every earlier band has Upper < x[i], so U < x[i]
+// there, while U_j >= Upper_j >= x[i]. U is non-decreasing, so a branch-free
+// binary search finds j in the same ceil(log2(n+1)) steps on every lane.
+// Each block builds U in shared memory (a warp's shuffle prefix max per 32
+// bands, carried along), next to gain/4 in float64: float64(sum)/4 *
+// float64(gain) + bias is then one fma, as sum*gain/4 of two float32 values
+// is exact in float64. A curve longer than kMaxSharedBands is searched in
+// order from global memory. Curves of at most K bands (K = 4 or 8) keep U in
+// registers, padded with +inf: the band index is then the number of j < K
+// with !(x[i] <= U_j), at most n -- K compares and no shared-memory loads.
+//
+// The 4-tap window x[i-2..i+1] of a vector unit needs x[4v-2], x[4v-1] (the
+// previous unit's last two) and x[4v+4] (the next unit's first): the
+// neighbouring lanes of the warp hold those units, so they come by shuffle;
+// a lane whose neighbour is not there loads them.
 constexpr int kMaxSharedBands = 1024;
+template <int K>
 struct BandGainOp {
     float* y;
     const float* x;
@@ -255,54 +270,91 @@ struct BandGainOp {
     float count_f;
     double bias;
     static constexpr int W = 4;
-    struct In {
-        float4 c;
-        float m2, m1, p4;
-    };
-    mutable const float* sb;
+    using In = float4;
+    mutable const float* su;   // prefix-max uppers (shared), or null: search in order
+    mutable const double* sq;  // gain/4 per band, then the floor's
+    mutable int top;           // the largest power of two <= n_bands (0 if none)
+    mutable float ur[K > 0 ? K : 1];  // U in registers (K > 0)
 
     __device__ void prologue() const {
-        __shared__ float s_bands[2 * kMaxSharedBands];
+        __shared__ float s_up[kMaxSharedBands];
+        __shared__ double s_q[kMaxSharedBands + 1];
+        su = nullptr;
         if (n_bands <= kMaxSharedBands) {
-            for (int j = threadIdx.x; j < 2 * n_bands; j += blockDim.x) s_bands[j] = bands[j];
-            sb = s_bands;
-        } else {
-            sb = bands;
+            if (threadIdx.x < 32) {
+                const int lane = threadIdx.x;
+                float carry = __int_as_float(0x7fc00000);  // NaN: no number yet
+                for (int j0 = 0; j0 < n_bands; j0 += 32) {
+                    const int j = j0 + lane;
+                    float u = j < n_bands ? bands[2 * j] : __int_as_float(0x7fc00000);
+#pragma unroll
+                    for (int d = 1; d < 32; d <<= 1) {
+                        const float o = __shfl_up_sync(0xffffffffu, u, d);
+                        if (lane >= d) u = fmaxf(u, o);  // fmaxf skips NaN
+                    }
+                    u = fmaxf(u, carry);
+                    if (j < n_bands) s_up[j] = u;
+                    carry = __shfl_sync(0xffffffffu, u, 31);
+                }
+            }
+            for (int j = threadIdx.x; j <= n_bands; j += blockDim.x)
+                s_q[j] = 0.25 * (double)(j < n_bands ? bands[2 * j + 1] : floor_gain);
+            su = s_up;
+            sq = s_q;
         }
+        top = 0;
+        while (2 * top <= n_bands && n_bands > 0) top = top ? 2 * top : 1;
         __syncthreads();
+        if (K > 0) {
+#pragma unroll
+            for (int j = 0; j < (K > 0 ? K : 1); j++)
+                ur[j] = j < n_bands ? s_up[j] : __int_as_float(0x7f800000);
+        }
     }
     __device__ float xat(int64_t k) const { return (k >= 0 && k < x_len) ? __ldg(x + k) : 0.0f; }
     __device__ float one(float v, float t0, float t1, float t2, float t3) const {
-        float gain = floor_gain;
-        for (int32_t j = 0; j < n_bands; j++) {
-            if (v <= sb[2 * j]) {
-                gain = sb[2 * j + 1];
-                break;
-            }
+        double q;
+        if (K > 0) {
+            int pos = 0;
+#pragma unroll
+            for (int j = 0; j < (K > 0 ? K : 1); j++) pos += !(v <= ur[j]);
+            q = sq[min(pos, (int)n_bands)];
+        } else if (su) {
+            int pos = 0;  // bands before the first with v <= U
+            for (int step = top; step > 0; step >>= 1)
+                if (pos + step <= n_bands && !(v <= su[pos + step - 1])) pos += step;
+            q = sq[pos];
+        } else {
+            float gain = floor_gain;
+            for (int32_t j = 0; j < n_bands; j++)
+                if (v <= bands[2 * j]) {
+                    gain = bands[2 * j + 1];
+                    break;
+                }
+            q = 0.25 * (double)gain;
         }
         float sum = __fadd_rn(0.0f, t0);
         sum = __fadd_rn(sum, t1);
         sum = __fadd_rn(sum, t2);
         sum = __fadd_rn(sum, t3);
-        double acc = __dmul_rn((double)sum, 0.25);  // == (double)sum / 4, exactly
-        acc = __dmul_rn(acc, (double)gain);
-        acc = __dadd_rn(acc, bias);
-        return __fmul_rn(__double2float_rn(acc), count_f);
+        return __fmul_rn(__double2float_rn(fma((double)sum, q, bias)), count_f);
     }
-    __device__ In load(int64_t v) const {
-        In in;
-        in.c = __ldg(reinterpret_cast<const float4*>(x) + v);
-        in.m2 = xat(4 * v - 2);
-        in.m1 = xat(4 * v - 1);
-        in.p4 = xat(4 * v + 4);
-        return in;
-    }
-    __device__ void store(int64_t v, const In& in) const {
-        const float4 c = in.c;
-        st_stream_f4(y + 4 * v, make_float4(one(c.x, in.m2, in.m1, c.x, c.y),
-                                            one(c.y, in.m1, c.x, c.y, c.z),
+    __device__ In load(int64_t v) const { return __ldg(reinterpret_cast<const float4*>(x) + v); }
+    __device__ void store(int64_t v, const float4& c) const {
+        const unsigned mask = __activemask();
+        const int lane = threadIdx.x & 31;
+        const int vl = (int)v;
+        const float pz = __shfl_up_sync(mask, c.z, 1), pw = __shfl_up_sync(mask, c.w, 1);
+        const float nx = __shfl_down_sync(mask, c.x, 1);
+        const int pv = __shfl_up_sync(mask, vl, 1), nv = __shfl_down_sync(mask, vl, 1);
+        const bool have_prev = lane > 0 && ((mask >> (lane - 1)) & 1) && pv == vl - 1;
+        const bool have_next = lane < 31 && ((mask >> (lane + 1)) & 1) && nv == vl + 1;
+        const float m2 = have_prev ? pz : xat(4 * v - 2);
+        const float m1 = have_prev ? pw : xat(4 * v - 1);
+        const float p4 = have_next ? nx : xat(4 * v + 4);
+        st_stream_f4(y + 4 * v, make_float4(one(c.x, m2, m1, c.x, c.y), one(c.y, m1, c.x, c.y, c.z),
                                             one(c.z, c.x, c.y, c.z, c.w),
-                                            one(c.w, c.y, c.z, c.w, in.p4)));
+                                            one(c.w, c.y, c.z, c.w, p4)));
     }
     __device__ void scalar(int64_t i) const {
         y[i] = one(x[i], xat(i - 2), xat(i - 1), xat(i), xat(i + 1));
@@ -621,16 +673,20 @@ int simtgo_BandGain(float* y, int32_t y_len, const float* x, int32_t x_len,
                                   {"x", x, 4LL * x_len, false},
                                   {"bands", bands, 8LL * bands_len, false}})))
         return rc;
-    BandGainOp op;
-    op.y = y;
-    op.x = x;
-    op.x_len = x_len;
-    op.bands = reinterpret_cast<const float*>(bands);
-    op.n_bands = bands_len;
-    op.floor_gain = cfg->floor_gain;
-    op.count_f = (float)cfg->count;  // float32(cfg.Count): int32 -> nearest float32
-    op.bias = cfg->bias;
-    return run_ew(K, op, m / 4, m, sg::aligned16(y) && sg::aligned16(x), stream);
+    auto run = [&](auto op) {
+        op.y = y;
+        op.x = x;
+        op.x_len = x_len;
+        op.bands = reinterpret_cast<const float*>(bands);
+        op.n_bands = bands_len;
+        op.floor_gain = cfg->floor_gain;
+        op.count_f = (float)cfg->count;  // float32(cfg.Count): int32 -> nearest float32
+        op.bias = cfg->bias;
+        return run_ew(K, op, m / 4, m, sg::aligned16(y) && sg::aligned16(x), stream);
+    };
+    if (bands_len <= 4) return run(BandGainOp<4>());
+    if (bands_len <= 8) return run(BandGainOp<8>());
+    return run(BandGainOp<0>());
 }
 
 int simtgo_Quantize(int32_t* code, int32_t code_len, int64_t* energy, int32_t energy_len,

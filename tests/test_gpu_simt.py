@@ -259,7 +259,29 @@ def test_classify_parity(edges):
     assert_agree("classify", host(out), want)
 
 
-@pytest.mark.parametrize("nb", [0, 1, 4, 1500])
+@pytest.mark.parametrize("nb", [3, 7, 37, 1500])
+def test_bandgain_unsorted_curve(nb):
+    """First match in order on an unsorted curve with repeated and NaN
+    uppers (shadowed bands, a NaN band first), NaN and infinite samples:
+    the register, shared-memory and in-order search paths all agree with
+    the emulator."""
+    n = 20011
+    rng = np.random.default_rng(40 + nb)
+    ups = rng.uniform(-2, 2, nb).astype(np.float32)
+    ups[0] = np.nan
+    if nb > 2:
+        ups[2] = ups[1]
+    bands = [(float(u), float(gn)) for u, gn in zip(ups, rng.uniform(0, 3, nb))]
+    x = normal(n, 41)
+    x[:4] = [np.nan, np.inf, -np.inf, 0.0]
+    rc, want = O.bandgain(x, bands, 0.125, 3, 0.001, (n + 255) // 256, 256)
+    y = dev(np.zeros(n, np.float32))
+    simt.build("BandGain").launch_n(n, 256, y, dev(x), simt.bands_tensor(bands),
+                                    simt.Shape(0.125, 3, 0.001))
+    assert_agree("bandgain", host(y), want)
+
+
+@pytest.mark.parametrize("nb", [0, 1, 4, 6, 100, 1500])
 def test_bandgain_parity(nb):
     n = 50003
     rng = np.random.default_rng(12)
