@@ -185,6 +185,18 @@ int simtgo_FIR(float* y, int32_t y_len, const float* x, int32_t x_len,
 int simtgo_FIR_shard(float* y, int64_t y_len, const float* x, int64_t x_len, int64_t halo,
                      const float* h, int32_t taps, void* stream);
 
+/* simtgo_FIR_shard with y, x and h in host memory (pinned for full speed;
+ * pageable memory works): the shard streams through the GPU in chunks of
+ * 2^22 outputs on three internal streams, so the upload of one chunk, the
+ * kernel of the next and the download of the one before overlap. The calling
+ * thread only enqueues: y is complete when `stream` reaches the point of the
+ * call (as with cudaMemcpyAsync). The library keeps three 48 MB sets of
+ * device buffers per device for it, allocated on first use; calls are
+ * serialised. No counterpart in the reference: it is the cuda.Upload ->
+ * FIR -> Download sequence of one shard, pipelined. */
+int simtgo_FIR_shard_host(float* y, int64_t y_len, const float* x, int64_t x_len, int64_t halo,
+                          const float* h, int32_t taps, void* stream);
+
 /* kernels/histogram.go:23 over a 64-bit extent: adds the counts of every
  * x[i], i < x_len, into bins[k], k < bins_len. */
 int simtgo_Histogram_shard(int32_t* bins, int32_t bins_len, const int32_t* x, int64_t x_len,

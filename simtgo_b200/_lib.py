@@ -55,6 +55,7 @@ _SIGS = {
     "simtgo_WarpReduceSum": [_vp, _i32, _vp, _i32, _i32, _i32, _vp],
     "simtgo_FIR": [_vp, _i32, _vp, _i32, _vp, _i32, _i32, _i32, _vp],
     "simtgo_FIR_shard": [_vp, _i64, _vp, _i64, _i64, _vp, _i32, _vp],
+    "simtgo_FIR_shard_host": [_vp, _i64, _vp, _i64, _i64, _vp, _i32, _vp],
     "simtgo_Histogram_shard": [_vp, _i32, _vp, _i64, _vp],
     "simtgo_comm_unique_id": [C.c_char_p],
     "simtgo_comm_init": [C.POINTER(_vp), C.c_char_p, _i32, _i32],

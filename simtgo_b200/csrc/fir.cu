@@ -25,6 +25,7 @@
 //    1-D bulk store (cp.async.bulk shared -> global).
 // At 127 taps the kernel is bound by FP32 FMA issue, not by HBM.
 #include <algorithm>
+#include <mutex>
 
 #include "common.cuh"
 #include "tma.cuh"
@@ -285,6 +286,48 @@ int launch_fir(const char* K, float* y, int64_t y_len, const float* x, int64_t x
     return sg::launch_status(K);
 }
 
+// ---- the shard from host memory ----------------------------------------------
+// simtgo_FIR_shard_host streams a shard that lives in host memory through the
+// GPU in chunks: chunk j's input (with the taps-1 samples before it) goes up,
+// the kernel runs, and its output comes down, on one of kPipe streams, so the
+// upload of one chunk, the kernel of the next and the download of the one
+// before overlap (the two copy directions run at once). The device buffers
+// are kept per device and reused by later calls; calls are serialised.
+constexpr int kPipe = 3;
+constexpr int64_t kPipeChunk = 1 << 22;  // outputs per chunk (16 MB)
+constexpr int64_t kPipePad = SIMTGO_FIR_SHARD_MAX_TAPS;  // >= taps-1, keeps 16-byte alignment
+
+struct HostPipe {
+    float* xbuf[kPipe] = {};  // kPipePad + kPipeChunk samples
+    float* ybuf[kPipe] = {};
+    float* hbuf[kPipe] = {};
+    cudaStream_t st[kPipe] = {};
+    cudaEvent_t ev[kPipe] = {};
+    bool ready = false;
+};
+
+int host_pipe(int device, HostPipe** out) {
+    static HostPipe pipes[64];
+    if (device < 0 || device >= 64) return sg::fail(SIMTGO_EDEVICE, "FIR_shard_host: device %d", device);
+    HostPipe& P = pipes[device];
+    if (!P.ready) {
+        int rc;
+        for (int s = 0; s < kPipe; s++) {
+            if ((rc = sg::cuda_status(cudaMalloc(&P.xbuf[s], (kPipePad + kPipeChunk) * 4), "cudaMalloc")) ||
+                (rc = sg::cuda_status(cudaMalloc(&P.ybuf[s], kPipeChunk * 4), "cudaMalloc")) ||
+                (rc = sg::cuda_status(cudaMalloc(&P.hbuf[s], SIMTGO_FIR_SHARD_MAX_TAPS * 4), "cudaMalloc")) ||
+                (rc = sg::cuda_status(cudaStreamCreateWithFlags(&P.st[s], cudaStreamNonBlocking),
+                                      "cudaStreamCreate")) ||
+                (rc = sg::cuda_status(cudaEventCreateWithFlags(&P.ev[s], cudaEventDisableTiming),
+                                      "cudaEventCreate")))
+                return rc;
+        }
+        P.ready = true;
+    }
+    *out = &P;
+    return 0;
+}
+
 }  // namespace
 
 extern "C" {
@@ -339,6 +382,66 @@ int simtgo_FIR_shard(float* y, int64_t y_len, const float* x, int64_t x_len, int
                                   {"h", h, 4LL * taps, false}})))
         return rc;
     return launch_fir(K, y, y_len, x, x_len, halo, h, taps, stream);
+}
+
+int simtgo_FIR_shard_host(float* y, int64_t y_len, const float* x, int64_t x_len, int64_t halo,
+                          const float* h, int32_t taps, void* stream) {
+    const char* K = "FIR_shard_host";
+    sg::clear_error();
+    int rc;
+    if (y_len < 0 || x_len < 0 || halo < 0 || halo > x_len)
+        return sg::fail(SIMTGO_EARG, "%s: negative length or halo, or halo past x", K);
+    if (taps < 1 || taps > SIMTGO_FIR_SHARD_MAX_TAPS)
+        return sg::fail(SIMTGO_ETAPS, "%s: %d taps is outside 1..%d", K, taps,
+                        SIMTGO_FIR_SHARD_MAX_TAPS);
+    if (y_len == 0) return 0;
+    if ((rc = sg::check_ptr(K, "y", y, y_len)) || (rc = sg::check_ptr(K, "x", x, x_len)) ||
+        (rc = sg::check_ptr(K, "h", h, taps)))
+        return rc;
+    const sg::DevInfo* d;
+    if ((rc = sg::current_device(&d))) return rc;
+    static std::mutex mu;
+    std::lock_guard<std::mutex> lock(mu);
+    HostPipe* P;
+    if ((rc = host_pipe(d->device, &P))) return rc;
+    cudaStream_t caller = (cudaStream_t)stream;
+    cudaEvent_t start = P->ev[0];
+    if ((rc = sg::cuda_status(cudaEventRecord(start, caller), K))) return rc;
+    for (int s = 0; s < kPipe; s++) {
+        if ((rc = sg::cuda_status(cudaStreamWaitEvent(P->st[s], start, 0), K)) ||
+            (rc = sg::cuda_status(cudaMemcpyAsync(P->hbuf[s], h, (size_t)taps * 4,
+                                                  cudaMemcpyHostToDevice, P->st[s]), K)))
+            return rc;
+    }
+    const int64_t body = x_len - halo;  // samples of the shard itself
+    const int64_t H = taps - 1;
+    for (int64_t j = 0, o0 = 0; o0 < y_len; j++, o0 += kPipeChunk) {
+        const int s = (int)(j % kPipe);
+        const int64_t cn = std::min<int64_t>(kPipeChunk, y_len - o0);
+        // The chunk reads shard positions [o0 - hj, o0 + cn), x[halo + p];
+        // those at or past the end of x (body) read as zero and are not
+        // copied. hj <= halo + o0, so the start is inside x.
+        const int64_t hj = std::min<int64_t>(H, halo + o0);
+        const int64_t nx = std::max<int64_t>(0, std::min<int64_t>(o0 + cn, body) - (o0 - hj));
+        // xd is 16-byte aligned (the kernel's bulk-copy path) whatever hj is.
+        float* xd = P->xbuf[s] + kPipePad - ((hj + 3) & ~int64_t(3));
+        if (nx > 0 &&
+            (rc = sg::cuda_status(cudaMemcpyAsync(xd, x + halo + o0 - hj, (size_t)nx * 4,
+                                                  cudaMemcpyHostToDevice, P->st[s]), K)))
+            return rc;
+        if ((rc = launch_fir(K, P->ybuf[s], cn, xd, nx, hj, P->hbuf[s], taps, P->st[s])))
+            return rc;
+        if ((rc = sg::cuda_status(cudaMemcpyAsync(y + o0, P->ybuf[s], (size_t)cn * 4,
+                                                  cudaMemcpyDeviceToHost, P->st[s]), K)))
+            return rc;
+    }
+    // The caller's stream continues once every chunk is down.
+    for (int s = 0; s < kPipe; s++) {
+        if ((rc = sg::cuda_status(cudaEventRecord(P->ev[s], P->st[s]), K)) ||
+            (rc = sg::cuda_status(cudaStreamWaitEvent(caller, P->ev[s], 0), K)))
+            return rc;
+    }
+    return 0;
 }
 
 }  // extern "C"

@@ -44,6 +44,35 @@ def test_fir_shard_parity(n, taps, halo):
         assert_agree("fir_shard", yd.cpu().numpy(), want)
 
 
+@pytest.mark.parametrize("n,taps,halo,short,pinned", [
+    (1, 1, 0, 0, True), (5000, 127, 126, 0, True), ((1 << 22) + 12345, 127, 126, 0, True),
+    ((1 << 23) + 3, 63, 0, 0, False), (3 * (1 << 22), 1024, 1023, 0, True),
+    ((1 << 22) + 100, 31, 30, 5000, True), ((1 << 22) + 100, 31, 7, (1 << 22) + 60, True)])
+def test_fir_shard_host_equals_device(n, taps, halo, short, pinned):
+    """The host-memory form (chunks of 2^22 on three streams) gives the
+    device form's bits: ragged chunk counts, halos shorter than taps-1,
+    signals that end before the outputs do (zeros read past x), pinned and
+    pageable buffers."""
+    rng = np.random.default_rng(n + taps + halo)
+    xl = n + halo - short
+    x = rng.uniform(-1, 1, xl).astype(np.float32)
+    h = (rng.uniform(-1, 1, taps) / taps).astype(np.float32)
+    xt = torch.from_numpy(x)
+    yt = torch.full((n,), np.nan, dtype=torch.float32)
+    ht = torch.from_numpy(h)
+    if pinned:
+        xt, yt, ht = xt.pin_memory(), yt.pin_memory(), ht.pin_memory()
+    L = _lib.load()
+    s = torch.cuda.current_stream()
+    _lib.check(L.simtgo_FIR_shard_host(P(yt.data_ptr()), n, P(xt.data_ptr()), xl, halo,
+                                       P(ht.data_ptr()), taps, P(s.cuda_stream)))
+    s.synchronize()
+    _lib.check(L.simtgo_stream_sync(None))
+    yd = torch.empty(n, device="cuda")
+    fir_shard(yd, torch.from_numpy(x).cuda(), halo, torch.from_numpy(h).cuda())
+    assert_equal("fir_shard_host", yt.numpy().view(np.uint32), yd.cpu().numpy().view(np.uint32))
+
+
 def test_fir_shards_concatenate_to_whole():
     """Eight shards of one signal, each with a 126-sample halo, equal the
     unsharded FIR over the whole (127 taps): the 2^31-sample workload's

@@ -295,6 +295,24 @@ def test_bandgain_parity(nb):
     assert_agree("bandgain", host(y), want)
 
 
+@pytest.mark.parametrize("step", [0.3, -0.5, 2.0 ** -20, 2.0 ** 100, 2.0 ** 127, 2.0 ** -149])
+def test_quantize_steps(step):
+    """x/step rounded as the emulator does for steps of every kind: not a
+    power of two, negative, tiny and huge powers of two (subnormal and
+    overflowing quotients, the smallest subnormal step), with zeros,
+    infinities and NaN among the samples."""
+    n = 4099
+    x = normal(n, 15) * 4
+    x[:10] = [np.inf, -np.inf, np.nan, 0.0, -0.0, 1e-38, -1e-45, 3e38, -3e38, 1.5e-39]
+    rc, code, energy, clipped = O.quantize(x, step, 12345, (n + 255) // 256, 256)
+    dc, de = dev(np.zeros(n, np.int32)), dev(np.zeros(n, np.int64))
+    dk = dev(np.zeros(n, np.bool_))
+    simt.build("Quantize").launch_n(n, 256, dc, de, dk, dev(x), step, 12345)
+    assert_equal("code", host(dc), code)
+    assert_equal("energy", host(de), energy)
+    assert_equal("clipped", host(dk).astype(np.uint8), clipped)
+
+
 @pytest.mark.parametrize("n", SIZES)
 def test_quantize_parity(n):
     x = normal(n, 14) * 4
