@@ -484,7 +484,7 @@ def bench_kernels(args, torch, np, L, dev, sp, events, peaks):
     steps, warm = max(5, min(args.steps, 20)), 3
     hbm = peaks["hbm_gbs"]
     out = {}
-    N = 1 << 28
+    N = 1 << args.kernels_log2
     gen = torch.Generator(device=dev).manual_seed(11)
 
     def rec(name, ms, nbytes, units, unit_name):
@@ -570,8 +570,8 @@ def bench_kernels(args, torch, np, L, dev, sp, events, peaks):
                                             grid(npx), 256, sp), steps, warm, stream, events,
                       flush=flush), 4.0 * npx, npx, "pixels (L2 flushed before each launch)")
     del rgb, luma
-    # Transpose 16384^2.
-    T = 16384
+    # Transpose 16384^2 (at the default size; T*T = N).
+    T = 1 << (args.kernels_log2 // 2)
     rec("Transpose", timed(lambda: L.simtgo_Transpose(pc, T * T, pa, T * T, T, T, T // 16,
                                                       T // 16, 16, 16, sp), steps, warm, stream,
                            events), 8.0 * T * T, T * T, "elements")
@@ -673,11 +673,15 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--soak-s", type=float, default=1.5)
     ap.add_argument("--tile-log2", type=int, default=28)
+    ap.add_argument("--kernels-log2", type=int, default=28,
+                    help="elements per kernel in the per-kernel table (20..28; 28 = the workloads)")
     ap.add_argument("--skip-kernels", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if not 20 <= args.kernels_log2 <= 28:
+        ap.error("--kernels-log2 must be within 20..28")
     if args.impl == "reference":
         run_reference(args)
     else:
