@@ -221,3 +221,19 @@ def test_input_only_and_unaligned():
     torch.cuda.synchronize()
     want = np.array([O.oracle().oracle_hypot(float(v), float(v)) for v in x[1:]], np.float32)
     assert_agree("unaligned device inputs", out.cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("seed", range(16))
+def test_random_graphs(seed):
+    """Random DAGs over the seven operations (shared values, x-op-x nodes,
+    up to two windows) on the device, bit for bit against the oracle: 3001
+    elements (one chunk per block) and 2^21+77 (several chunks per block, so
+    the window heads are carried between chunks)."""
+    from test_tile_lowering import _random_graph
+
+    for n in (3001, (1 << 21) + 77):
+        root, nodes = _random_graph(seed, n, 0)
+        got = root.Materialize()
+        rc, want = O.tile_eval(nodes, len(nodes) - 1, n, 0)
+        assert rc == 0
+        assert_agree(f"random graph {seed} n={n}", got, want)
