@@ -40,6 +40,7 @@ _SIGS = {
     "simtgo_version": [],
     "simtgo_device_info": [C.POINTER(_i32), C.POINTER(_i32), C.POINTER(_i32)],
     "simtgo_stream_sync": [_vp],
+    "simtgo_shutdown": [],
     "simtgo_VecAdd": [_vp, _i32, _vp, _i32, _vp, _i32, _i32, _i32, _vp],
     "simtgo_Scale": [_vp, _i32, _vp, _i32, _f32, _i32, _i32, _vp],
     "simtgo_Magnitude": [_vp, _i32, _vp, _i32, _vp, _i32, _i32, _i32, _vp],

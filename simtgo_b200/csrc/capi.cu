@@ -159,6 +159,11 @@ const char* simtgo_last_error(void) { return t_msg; }
 
 const char* simtgo_version(void) { return "simtgo_b200 0.1.0 (sm_100a)"; }
 
+int simtgo_shutdown(void) {
+    sg::clear_error();
+    return sg::fir_host_release();
+}
+
 int simtgo_device_info(int32_t* sm_count, int32_t* cc_major, int32_t* cc_minor) {
     const sg::DevInfo* d = nullptr;
     int rc = sg::current_device(&d);

@@ -43,6 +43,9 @@ enum : uint32_t {
 uint32_t* watchdog_device_ptr();  // device address of the flag word (current device)
 int watchdog_check_and_clear(uint32_t* bits);
 
+// Private resources released by simtgo_shutdown (fir.cu).
+int fir_host_release();
+
 // ---- launch-contract checks (simt/kernel.go:293-369, :488-514) -------------
 // The covered thread extent of a 1-D launch, or a status code. Refuses what
 // cuLaunchKernel refuses (grid or block <= 0, block > 1024) and, if

@@ -306,10 +306,12 @@ struct HostPipe {
     bool ready = false;
 };
 
+HostPipe g_pipes[64];
+std::mutex g_pipe_mu;  // serialises simtgo_FIR_shard_host and simtgo_shutdown
+
 int host_pipe(int device, HostPipe** out) {
-    static HostPipe pipes[64];
     if (device < 0 || device >= 64) return sg::fail(SIMTGO_EDEVICE, "FIR_shard_host: device %d", device);
-    HostPipe& P = pipes[device];
+    HostPipe& P = g_pipes[device];
     if (!P.ready) {
         int rc;
         for (int s = 0; s < kPipe; s++) {
@@ -327,6 +329,36 @@ int host_pipe(int device, HostPipe** out) {
     *out = &P;
     return 0;
 }
+
+}  // namespace
+
+namespace sg {
+// Frees every device's host-pipe resources (simtgo_shutdown).
+int fir_host_release() {
+    std::lock_guard<std::mutex> lock(g_pipe_mu);
+    int prev = 0, rc = 0;
+    cudaGetDevice(&prev);
+    for (int dev = 0; dev < 64; dev++) {
+        HostPipe& P = g_pipes[dev];
+        if (!P.ready) continue;
+        int r = cuda_status(cudaSetDevice(dev), "cudaSetDevice");
+        for (int s = 0; s < kPipe && !r; s++) {
+            if (P.st[s]) r = cuda_status(cudaStreamSynchronize(P.st[s]), "cudaStreamSynchronize");
+            if (!r && P.ev[s]) r = cuda_status(cudaEventDestroy(P.ev[s]), "cudaEventDestroy");
+            if (!r && P.st[s]) r = cuda_status(cudaStreamDestroy(P.st[s]), "cudaStreamDestroy");
+            if (!r) r = cuda_status(cudaFree(P.xbuf[s]), "cudaFree");
+            if (!r) r = cuda_status(cudaFree(P.ybuf[s]), "cudaFree");
+            if (!r) r = cuda_status(cudaFree(P.hbuf[s]), "cudaFree");
+        }
+        if (!r) P = HostPipe();
+        if (r && !rc) rc = r;
+    }
+    cudaSetDevice(prev);
+    return rc;
+}
+}  // namespace sg
+
+namespace {
 
 }  // namespace
 
@@ -400,8 +432,7 @@ int simtgo_FIR_shard_host(float* y, int64_t y_len, const float* x, int64_t x_len
         return rc;
     const sg::DevInfo* d;
     if ((rc = sg::current_device(&d))) return rc;
-    static std::mutex mu;
-    std::lock_guard<std::mutex> lock(mu);
+    std::lock_guard<std::mutex> lock(g_pipe_mu);
     HostPipe* P;
     if ((rc = host_pipe(d->device, &P))) return rc;
     cudaStream_t caller = (cudaStream_t)stream;

@@ -73,6 +73,25 @@ def test_fir_shard_host_equals_device(n, taps, halo, short, pinned):
     assert_equal("fir_shard_host", yt.numpy().view(np.uint32), yd.cpu().numpy().view(np.uint32))
 
 
+def test_shutdown_releases_and_host_form_recovers():
+    """simtgo_shutdown frees the host form's device buffers; the next call
+    allocates them again and gives the same bits."""
+    L = _lib.load()
+    n, taps = (1 << 22) + 9, 63
+    rng = np.random.default_rng(5)
+    x = torch.from_numpy(rng.uniform(-1, 1, n).astype(np.float32)).pin_memory()
+    h = torch.from_numpy((rng.uniform(-1, 1, taps) / taps).astype(np.float32)).pin_memory()
+    outs = []
+    for _ in range(2):
+        y = torch.empty(n, dtype=torch.float32).pin_memory()
+        _lib.check(L.simtgo_FIR_shard_host(P(y.data_ptr()), n, P(x.data_ptr()), n, 0,
+                                           P(h.data_ptr()), taps, None))
+        _lib.check(L.simtgo_stream_sync(None))
+        outs.append(y.numpy().copy())
+        _lib.check(L.simtgo_shutdown())
+    assert_equal("after shutdown", outs[1].view(np.uint32), outs[0].view(np.uint32))
+
+
 def test_fir_shards_concatenate_to_whole():
     """Eight shards of one signal, each with a 126-sample halo, equal the
     unsharded FIR over the whole (127 taps): the 2^31-sample workload's
