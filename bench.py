@@ -558,6 +558,14 @@ def bench_kernels(args, torch, np, L, dev, sp, events, peaks):
     rec("Histogram_zipf", timed(lambda: L.simtgo_Histogram(P(bins.data_ptr()), 256,
                                                            P(xi.data_ptr()), N, G, 256, sp),
                                 steps, warm, stream, events), 4.0 * N, N, "samples (Zipf 1.2)")
+    # The launch-sized tile (LaunchShared): 4096 bins, uniform samples.
+    xi = torch.randint(0, 4096, (N,), dtype=torch.int32, device=dev, generator=gen)
+    bins4k = torch.zeros(4096, dtype=torch.int32, device=dev)
+    rec("HistogramDyn_4096", timed(lambda: L.simtgo_HistogramDyn(P(bins4k.data_ptr()), 4096,
+                                                                 P(xi.data_ptr()), N, 4096, G,
+                                                                 256, sp),
+                                   steps, warm, stream, events), 4.0 * N, N,
+        "samples (4096-bin launch-sized tile)")
     del xi
     torch.cuda.empty_cache()
     # Gray 7680x4320: 133 MB of traffic, about the size of L2, so L2 is

@@ -153,6 +153,16 @@ int simtgo_Gray(uint8_t* out, int32_t out_len, const uint8_t* rgb, int32_t rgb_l
 int simtgo_Histogram(int32_t* bins, int32_t bins_len, const int32_t* x, int32_t x_len,
                      int32_t grid, int32_t block, void* stream);
 
+/* simt Kernel.LaunchShared (simt/kernel.go:444-481) with a launch-sized
+ * int32 tile of tile_len elements, on the DynProbe body
+ * (simt/shared_parity_cuda_test.go:117-138): ADDS the counts of x[i] in
+ * [0, tile_len), i < min(x_len, grid*block), into bins[k] for
+ * k < min(tile_len, bins_len); other samples are dropped. A tile larger than
+ * a block's shared memory (~57 K elements on B200) is refused before the
+ * launch with SIMTGO_ESIZE (simt.SharedMemoryError). Exact. */
+int simtgo_HistogramDyn(int32_t* bins, int32_t bins_len, const int32_t* x, int32_t x_len,
+                        int32_t tile_len, int32_t grid, int32_t block, void* stream);
+
 /* kernels/transpose.go:15-38 Transpose; Transpose.cu. out[x*h+y] = in[y*w+x]
  * for x < min(w, 16*grid_x), y < min(h, 16*grid_y). block_x*block_y must be
  * 256 (AssumeBlockDim(TransposeTile*TransposeTile)). Exact. */

@@ -24,6 +24,7 @@
 #define E_LAUNCH (-5)
 #define E_TAPS (-6)
 #define E_GRAPH (-7)
+#define E_ARG (-11)
 
 static int g_threads = 1;
 void oracle_set_threads(int n) { g_threads = n < 1 ? 1 : n; }
@@ -462,6 +463,56 @@ int oracle_histogram(int32_t* bins, int32_t bins_len, const int32_t* x, int32_t 
     ctx.block = block;
     pthread_mutex_init(&ctx.mu, NULL);
     par_for((m + block - 1) / block, hist_range, &ctx);
+    pthread_mutex_destroy(&ctx.mu);
+    return 0;
+}
+
+/* The launch-sized tile (simt Kernel.LaunchShared, simt/kernel.go:444-481)
+ * on the DynProbe body (simt/shared_parity_cuda_test.go:117-138): each block
+ * zeroes a tile of tile_len int32, counts its samples x[i] in [0, tile_len)
+ * with gpu.AtomicAddI32, then adds every non-zero tile[k], k < bins_len,
+ * into bins[k]. Integer sums are order-free, so one pass per block range is
+ * the same result. */
+typedef struct {
+    int32_t* bins;
+    int32_t n_bins, tile;
+    const int32_t* x;
+    int64_t m, block;
+    pthread_mutex_t mu;
+} hdyn_ctx;
+static void hdyn_range(int64_t lo, int64_t hi, void* p) {
+    hdyn_ctx* c = (hdyn_ctx*)p;
+    int32_t* acc = (int32_t*)calloc((size_t)(c->tile > 0 ? c->tile : 1), sizeof(int32_t));
+    for (int64_t blk = lo; blk < hi; blk++) {
+        int64_t i0 = blk * c->block, i1 = min64(i0 + c->block, c->m);
+        for (int64_t i = i0; i < i1; i++) {
+            int32_t v = c->x[i];
+            if (v >= 0 && v < c->tile) acc[v]++;
+        }
+    }
+    pthread_mutex_lock(&c->mu);
+    for (int32_t k = 0; k < c->tile && k < c->n_bins; k++)
+        c->bins[k] = (int32_t)((uint32_t)c->bins[k] + (uint32_t)acc[k]);
+    pthread_mutex_unlock(&c->mu);
+    free(acc);
+}
+int oracle_histogram_dyn(int32_t* bins, int32_t bins_len, const int32_t* x, int32_t x_len,
+                         int32_t tile_len, int64_t grid, int64_t block) {
+    int64_t nt;
+    int rc = launch_extent(grid, block, &nt);
+    if (rc) return rc;
+    if (tile_len < 0) return E_ARG;
+    int64_t m = min64(x_len, nt);
+    if (m <= 0 || tile_len == 0) return 0;
+    hdyn_ctx ctx;
+    ctx.bins = bins;
+    ctx.n_bins = bins_len;
+    ctx.tile = tile_len;
+    ctx.x = x;
+    ctx.m = m;
+    ctx.block = block;
+    pthread_mutex_init(&ctx.mu, NULL);
+    par_for((m + block - 1) / block, hdyn_range, &ctx);
     pthread_mutex_destroy(&ctx.mu);
     return 0;
 }

@@ -79,6 +79,11 @@ int oracle_fir_shard(float* y, int64_t y_len, const float* x, int64_t x_len, int
 /* The same shard with the emulator's separately rounded multiply and add. */
 int oracle_fir_shard_runcpu(float* y, int64_t y_len, const float* x, int64_t x_len,
                             int64_t halo, const float* h, int32_t taps);
+/* Histogram with a launch-sized tile of tile_len bins (LaunchShared on the
+ * DynProbe body): adds the counts of x[i] in [0, tile_len) into bins[k] for
+ * k < min(tile_len, bins_len). */
+int oracle_histogram_dyn(int32_t* bins, int32_t bins_len, const int32_t* x, int32_t x_len,
+                         int32_t tile_len, int64_t grid, int64_t block);
 /* Histogram over a 64-bit extent (simtgo_Histogram_shard). */
 int oracle_histogram_shard(int32_t* bins, int32_t bins_len, const int32_t* x, int64_t x_len);
 

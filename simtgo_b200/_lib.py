@@ -52,6 +52,7 @@ _SIGS = {
     "simtgo_Quantize": [_vp, _i32, _vp, _i32, _vp, _i32, _vp, _i32, _f32, _u32, _i32, _i32, _vp],
     "simtgo_Gray": [_vp, _i32, _vp, _i32, _i32, _i32, _vp],
     "simtgo_Histogram": [_vp, _i32, _vp, _i32, _i32, _i32, _vp],
+    "simtgo_HistogramDyn": [_vp, _i32, _vp, _i32, _i32, _i32, _i32, _vp],
     "simtgo_Transpose": [_vp, _i32, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _vp],
     "simtgo_WarpReduceSum": [_vp, _i32, _vp, _i32, _i32, _i32, _vp],
     "simtgo_FIR": [_vp, _i32, _vp, _i32, _vp, _i32, _i32, _i32, _vp],

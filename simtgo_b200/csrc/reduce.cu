@@ -176,6 +176,61 @@ int launch_histogram(const char* K, int32_t* bins, int32_t bins_len, const int32
     return sg::launch_status(K);
 }
 
+// ---- Histogram with a launch-sized tile -----------------------------------------
+// simt Kernel.LaunchShared (simt/kernel.go:444-481) on the DynProbe body
+// (simt/shared_parity_cuda_test.go:117-138): tile_len bins sized at the
+// launch. `copies` private tables per block in dynamic shared memory (one
+// per warp while they fit 64 KB, fewer for wide tiles); the same persistent
+// grid and 16-byte loads as k_histogram; one global atomic per non-zero bin
+// k < min(tile_len, n_bins) per block.
+__global__ void __launch_bounds__(kHistThreads) k_histogram_dyn(int* __restrict__ bins,
+                                                                int n_bins,
+                                                                const int* __restrict__ x,
+                                                                int64_t m, int tile, int copies,
+                                                                bool vec) {
+    extern __shared__ int shd[];
+    for (int k = threadIdx.x; k < copies * tile; k += blockDim.x) shd[k] = 0;
+    __syncthreads();
+    int* mine = shd + ((threadIdx.x / 32) % copies) * tile;
+    auto add = [&](int v) {
+        if ((unsigned)v < (unsigned)tile) atomicAdd(mine + v, 1);
+    };
+    const int64_t stride = grid_threads();
+    int64_t done = 0;
+    if (vec) {
+        const int64_t nvec = m / 4;
+        int64_t v = global_tid();
+        for (; v + 3 * stride < nvec; v += 4 * stride) {
+            int4 q[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) q[u] = ld_stream_i4(x + 4 * (v + u * stride));
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                add(q[u].x);
+                add(q[u].y);
+                add(q[u].z);
+                add(q[u].w);
+            }
+        }
+        for (; v < nvec; v += stride) {
+            const int4 q = ld_stream_i4(x + 4 * v);
+            add(q.x);
+            add(q.y);
+            add(q.z);
+            add(q.w);
+        }
+        done = nvec * 4;
+    }
+    for (int64_t i = done + global_tid(); i < m; i += stride) add(x[i]);
+    __syncthreads();
+    const int kmax = min(tile, n_bins);
+    for (int k = threadIdx.x; k < kmax; k += blockDim.x) {
+        int c = 0;
+        for (int w = 0; w < copies; w++) c += shd[w * tile + k];
+        if (c != 0) atomicAdd(bins + k, c);
+    }
+}
+
 }  // namespace
 
 namespace sg {
@@ -266,6 +321,52 @@ int simtgo_Histogram(int32_t* bins, int32_t bins_len, const int32_t* x, int32_t 
         return rc;
     if ((rc = sg::current_device(&d))) return rc;
     return launch_histogram(K, bins, bins_len, x, m, d, stream);
+}
+
+int simtgo_HistogramDyn(int32_t* bins, int32_t bins_len, const int32_t* x, int32_t x_len,
+                        int32_t tile_len, int32_t grid, int32_t block, void* stream) {
+    const char* K = "HistogramDyn";
+    sg::clear_error();
+    int64_t nt;
+    const sg::DevInfo* d;
+    int rc;
+    if (bins_len < 0 || x_len < 0 || tile_len < 0)
+        return sg::fail(SIMTGO_EARG, "simt: %s: negative length or tile", K);
+    if ((rc = sg::launch_extent_1d(K, grid, block, 0, &nt))) return rc;
+    if ((rc = sg::current_device(&d))) return rc;
+    // simt.SharedMemoryError (simt/shared_parity_cuda_test.go:216-227): a
+    // tile larger than a block's shared memory is refused before the launch.
+    const int64_t limit = (d->max_smem_optin - 1024) / 4;
+    if (tile_len > limit)
+        return sg::fail(SIMTGO_ESIZE,
+                        "simt: %s: a shared tile of %d int32 elements (%lld bytes) exceeds the "
+                        "%lld bytes a block can have",
+                        K, tile_len, 4LL * tile_len, 4LL * limit);
+    const int64_t m = std::min<int64_t>(x_len, nt);
+    if (m <= 0 || bins_len == 0 || tile_len == 0) return 0;
+    if ((rc = sg::check_ptr(K, "bins", bins, bins_len)) || (rc = sg::check_ptr(K, "x", x, m)))
+        return rc;
+    if ((rc = sg::check_alias(K, {{"bins", bins, 4LL * bins_len, true},
+                                  {"x", x, 4LL * x_len, false}})))
+        return rc;
+    int copies = kHistWarps;
+    while (copies > 1 && (int64_t)copies * tile_len * 4 > 64 * 1024) copies /= 2;
+    const size_t smem = (size_t)copies * tile_len * 4;
+    if (smem > 48 * 1024 &&
+        (rc = sg::cuda_status(cudaFuncSetAttribute(k_histogram_dyn,
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   (int)smem),
+                              "cudaFuncSetAttribute(HistogramDyn)")))
+        return rc;
+    // Enough samples per block that the per-block flush of the tile (one
+    // atomic per non-zero bin) stays small next to the counting.
+    const int64_t want = std::min(sg::ceil_div(sg::ceil_div(m, 16), kHistThreads),
+                                  sg::ceil_div(m, 8LL * tile_len));
+    const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(want, (int64_t)d->sms * 2));
+    sg::before_launch();
+    k_histogram_dyn<<<blocks, kHistThreads, smem, (cudaStream_t)stream>>>(
+        bins, bins_len, x, m, tile_len, copies, sg::aligned16(x));
+    return sg::launch_status(K);
 }
 
 int simtgo_Histogram_shard(int32_t* bins, int32_t bins_len, const int32_t* x, int64_t x_len,

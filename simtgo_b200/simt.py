@@ -5,6 +5,8 @@
     k.launch(grid, block, y, x, h)        # Kernel.Launch (synchronous)
     k.launch_dim((gx, gy), (16, 16), out, inp, w, h)   # Kernel.LaunchDim
     k.launch_on(stream, grid, block, ...) # Kernel.LaunchOn (asynchronous)
+    simt.build("HistogramDyn").launch_shared(grid, block, tile, bins, x)
+                                          # Kernel.LaunchShared (launch-sized tile)
 
 Arguments follow the Go kernel's parameters minus the gpu.Ctx: device
 buffers (CUDA torch tensors: the device pointer and element count travel,
@@ -38,7 +40,13 @@ KERNELS = {
     "Transpose": [("out", "f32"), ("in", "f32"), ("w", "i32s"), ("h", "i32s")],
     "WarpReduceSum": [("out", "f32"), ("x", "f32")],
     "FIR": [("y", "f32"), ("x", "f32"), ("h", "f32")],
+    # The DynProbe body (simt/shared_parity_cuda_test.go:117-138): a histogram
+    # whose int32 tile is sized at the launch (Kernel.LaunchShared).
+    "HistogramDyn": [("bins", "i32"), ("x", "i32")],
 }
+
+# Kernels with a launch-sized shared tile: launched through launch_shared only.
+DYNAMIC = {"HistogramDyn"}
 
 # kernels.FIRBlock, WarpReduceBlock, TransposeTile^2 (AssumeBlockDim).
 REQUIRED_BLOCK = {"FIR": 256, "WarpReduceSum": 128, "Transpose": 256}
@@ -49,6 +57,20 @@ _DTYPES = {"f32": "float32", "i32": "int32", "i64": "int64", "u8": "uint8", "boo
 
 class ArgCountError(TypeError):
     """simt.ArgCountError (simt/kernel.go:266-284)."""
+
+
+class DynamicSharedError(TypeError):
+    """simt.DynamicSharedError (simt/kernel.go:236-250): a kernel with a
+    launch-sized tile launched without a size (dynamic=True), or one without
+    such a tile handed a size (dynamic=False)."""
+
+    def __init__(self, msg, dynamic):
+        super().__init__(msg)
+        self.dynamic = dynamic
+
+
+class SharedMemoryError(_lib.SimtgoError):
+    """simt.SharedMemoryError: the tile exceeds a block's shared memory."""
 
 
 def _slice(t, kind, kernel, pname):
@@ -83,7 +105,15 @@ class Kernel:
     params: list
     required_block: int = 0
 
-    def _call(self, grid, block, args, stream, sync):
+    def _call(self, grid, block, args, stream, sync, tile=None):
+        dynamic = self.name in DYNAMIC
+        if dynamic and tile is None:
+            raise DynamicSharedError(f"simt: {self.name} has a launch-sized shared tile; launch "
+                                     "it with launch_shared", True)
+        if not dynamic and tile is not None:
+            raise DynamicSharedError(f"simt: {self.name} has no launch-sized shared tile; "
+                                     "launch_shared hands it a size it has no parameter for",
+                                     False)
         if len(args) != len(self.params):
             raise ArgCountError(f"simt: {self.name} takes {len(self.params)} launch "
                                 f"argument(s), got {len(args)}")
@@ -109,8 +139,12 @@ class Kernel:
         if self.name == "Transpose":
             (gx, gy), (bx, by) = grid, block
             rc = fn(*flat, gx, gy, bx, by, sp)
+        elif dynamic:
+            rc = fn(*flat, int(tile), int(grid), int(block), sp)
         else:
             rc = fn(*flat, int(grid), int(block), sp)
+        if dynamic and rc == _lib.ESIZE:
+            raise SharedMemoryError(rc, L.simtgo_last_error().decode(errors="replace"))
         check(rc)
         if sync:
             check(L.simtgo_stream_sync(sp))
@@ -134,6 +168,10 @@ class Kernel:
     def launch_n(self, n, block, *args, stream=None):
         """Kernel.LaunchN: enough blocks to cover n threads."""
         return self.launch((n + block - 1) // block, block, *args, stream=stream)
+
+    def launch_shared(self, grid, block, tile, *args, stream=None):
+        """Kernel.LaunchShared: runs with a tile of `tile` elements and waits."""
+        self._call(grid, block, args, stream, True, tile=tile)
 
     def launch_on(self, stream, grid, block, *args):
         """Kernel.LaunchOn: queued on stream, not waited for."""
@@ -168,5 +206,5 @@ def bands_tensor(bands, device="cuda"):
     return torch.tensor([v for b in bands for v in b], dtype=torch.float32, device=device)
 
 
-__all__ = ["build", "Kernel", "KERNELS", "Band", "Shape", "ArgCountError", "stream_sync",
-           "bands_tensor"]
+__all__ = ["build", "Kernel", "KERNELS", "Band", "Shape", "ArgCountError", "DynamicSharedError",
+           "SharedMemoryError", "stream_sync", "bands_tensor"]

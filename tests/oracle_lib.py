@@ -192,6 +192,13 @@ def histogram(x, n_bins, grid, block, bins=None):
     return rc, bins
 
 
+def histogram_dyn(x, n_bins, tile, grid, block, bins=None):
+    bins = np.zeros(n_bins, np.int32) if bins is None else bins.copy()
+    rc = oracle().oracle_histogram_dyn(_ptr(bins, _i32p), _i32(len(bins)), _ptr(x, _i32p),
+                                       _i32(len(x)), _i32(tile), _i64(grid), _i64(block))
+    return rc, bins
+
+
 def histogram_shard(x, n_bins=256, bins=None):
     bins = np.zeros(n_bins, np.int32) if bins is None else bins.copy()
     rc = oracle().oracle_histogram_shard(_ptr(bins, _i32p), _i32(len(bins)), _ptr(x, _i32p),

@@ -204,3 +204,22 @@ def test_tile_wide_graph_falls_back_then_refuses():
     while len(level) > 1:
         level = [tile.Mul(level[i], level[i + 1]) for i in range(0, len(level), 2)]
     assert level[0].ProgramSize()[1] == 32
+
+
+def test_launch_shared_spelling_refused():
+    """simt/shared_parity_cuda_test.go:185-213: a kernel with a launch-sized
+    tile launched without a size, and one without such a tile handed a
+    size, are refused before anything reaches the device."""
+    from simtgo_b200 import simt
+
+    dyn = simt.Kernel("HistogramDyn", simt.KERNELS["HistogramDyn"])
+    plain = simt.Kernel("VecAdd", simt.KERNELS["VecAdd"])
+    with pytest.raises(simt.DynamicSharedError) as e:
+        dyn.launch(1, 32, None, None)
+    assert e.value.dynamic
+    with pytest.raises(simt.DynamicSharedError) as e:
+        dyn.launch_on(object(), 1, 32, None, None)
+    assert e.value.dynamic
+    with pytest.raises(simt.DynamicSharedError) as e:
+        plain.launch_shared(1, 32, 8, None, None, None)
+    assert not e.value.dynamic

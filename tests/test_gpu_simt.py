@@ -374,6 +374,46 @@ def test_histogram_parity(n, dist):
     assert_equal("bins", host(b), want)
 
 
+def test_histogram_dyn_known_answer():
+    """TestDynamicSharedTileParity (simt/shared_parity_cuda_test.go:146-178):
+    x[i] = i*i % 311 - 8, n = 2^15, 192 bins through LaunchShared."""
+    n = 1 << 15
+    i = np.arange(n, dtype=np.int64)
+    x = ((i * i) % 311 - 8).astype(np.int32)
+    b = dev(np.zeros(192, np.int32))
+    simt.build("HistogramDyn").launch_shared((n + 255) // 256, 256, 192, b, dev(x))
+    want = np.bincount(x[(x >= 0) & (x < 192)], minlength=192).astype(np.int32)
+    assert_equal("bins", host(b), want)
+
+
+@pytest.mark.parametrize("tile,nbins", [(1, 1), (192, 192), (256, 300), (1000, 600),
+                                        (5000, 5000), (33000, 10), (57000, 57000)])
+@pytest.mark.parametrize("offset", [0, 1])
+def test_histogram_dyn_parity(tile, nbins, offset):
+    """Launch-sized tiles from 1 to ~57 K bins (one private table per warp
+    down to one per block), bins shorter and longer than the tile, samples
+    outside the tile, a grid covering part of x, unaligned x; the counts
+    are added to bins that start non-zero."""
+    rng = np.random.default_rng(tile + nbins + offset)
+    n = 200003
+    x = rng.integers(-10, tile + 10, n, dtype=np.int32)
+    bins0 = rng.integers(0, 100, nbins, dtype=np.int32)
+    grid = n // 256 - 3
+    rc, want = O.histogram_dyn(x, nbins, tile, grid, 256, bins=bins0)
+    assert rc == 0
+    b = dev(bins0)
+    simt.build("HistogramDyn").launch_shared(grid, 256, tile, b, dev(x, offset))
+    assert_equal("bins", host(b), want)
+
+
+def test_histogram_dyn_tile_too_large():
+    """A tile beyond a block's shared memory is a SharedMemoryError before
+    the launch (simt/shared_parity_cuda_test.go:216-227)."""
+    b = dev(np.zeros(8, np.int32))
+    with pytest.raises(simt.SharedMemoryError):
+        simt.build("HistogramDyn").launch_shared(1, 32, 1 << 20, b, dev(np.zeros(8, np.int32)))
+
+
 def test_histogram_short_bins_and_partial_grid():
     x = np.random.default_rng(17).integers(0, 256, 100000, dtype=np.int32)
     rc, want = O.histogram(x, 100, 37, 512)

@@ -122,3 +122,28 @@ def test_fir(golden, tag):
                                len(g["h"]), O._i64(grid), O._i64(block))
     assert rc == 0
     assert_agree("fir", y, g["y"])
+
+
+def test_histogram_dyn_known_answer():
+    """The DynProbe parity test's input (simt/shared_parity_cuda_test.go:
+    156-160): x[i] = i*i % 311 - 8, n = 2^15, a 192-bin launch-sized tile;
+    the oracle's counts equal a direct count, and with a 256-bin tile it
+    agrees with the fixed Histogram."""
+    n = 1 << 15
+    i = np.arange(n, dtype=np.int64)
+    x = ((i * i) % 311 - 8).astype(np.int32)
+    rc, got = O.histogram_dyn(x, 192, 192, (n + 255) // 256, 256)
+    assert rc == 0
+    want = np.bincount(x[(x >= 0) & (x < 192)], minlength=192).astype(np.int32)
+    assert_equal("histogram_dyn", got, want)
+    rc, h256 = O.histogram(x, 300, (n + 255) // 256, 256)
+    rc2, d256 = O.histogram_dyn(x, 300, 256, (n + 255) // 256, 256)
+    assert rc == rc2 == 0
+    assert_equal("dyn vs fixed", d256, h256)
+    # bins shorter than the tile keep only their own; a tile shorter than
+    # the bins leaves the rest untouched.
+    rc, short = O.histogram_dyn(x, 50, 192, (n + 255) // 256, 256)
+    assert_equal("short bins", short, want[:50])
+    rc, wide = O.histogram_dyn(x, 400, 100, (n + 255) // 256, 256)
+    assert_equal("short tile", wide[:100], want[:100])
+    assert not wide[100:].any()
