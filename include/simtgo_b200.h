@@ -277,7 +277,8 @@ int simtgo_tile_program_size(simtgo_tile_graph* g, simtgo_tensor t, int32_t* n_i
 
 /* tile/run.go:10 Tensor.Source: the program the tensor would be computed by,
  * as text, without running anything -- here the listing of the lowered
- * register program (one instruction per line). Writes at most cap bytes
+ * accumulator-machine program (one fused device instruction per line, its
+ * steps separated by " | "). Writes at most cap bytes
  * (NUL-terminated) and returns the size the whole listing needs, or a
  * negative status. */
 int32_t simtgo_tile_source(simtgo_tile_graph* g, simtgo_tensor t, char* buf, int32_t cap);

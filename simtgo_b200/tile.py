@@ -80,7 +80,8 @@ class Tensor:
 
     def Source(self) -> str:
         """tile/run.go:10: the program this tensor would be computed by,
-        without running it (the listing of the lowered register program)."""
+        without running it (the listing of the lowered accumulator-machine
+        program, one fused device instruction per line)."""
         L, g = self.g._L, self.g._h
         need = L.simtgo_tile_source(g, self.node, None, 0)
         check(need if need < 0 else 0)
