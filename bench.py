@@ -420,22 +420,34 @@ def bench_histogram(args, torch, L, dev, sp, rank, world, barrier, max_over_rank
         _lib.check(L.simtgo_comm_unique_id(uid))
     _lib.check(L.simtgo_comm_init(C.byref(comm), uid, world, rank))
 
-    def step():
-        bins.zero_()
-        rc = L.simtgo_Histogram_allreduce(comm, P(bins.data_ptr()), 256, P(x.data_ptr()), n, sp)
-        if rc:
-            _lib.check(rc)
+    def run(fn):
+        def step():
+            bins.zero_()
+            rc = fn(comm, P(bins.data_ptr()), 256, P(x.data_ptr()), n, sp)
+            if rc:
+                _lib.check(rc)
 
+        barrier()
+        ms = max_over_ranks(timed(step, args.steps, args.warmup, torch.cuda.current_stream(),
+                                  events))
+        _lib.check(L.simtgo_stream_sync(sp))
+        return ms, int(bins.sum().item()) == total
+
+    ms, ok = run(L.simtgo_Histogram_allreduce)
+    ms_f, ok_f = run(L.simtgo_Histogram_allreduce_fused)
     barrier()
-    ms = timed(step, args.steps, args.warmup, torch.cuda.current_stream(), events)
-    ms = max_over_ranks(ms)
-    ok = int(bins.sum().item()) == total
     _lib.check(L.simtgo_comm_destroy(comm))
     return {"samples_total": total, "ms_per_step": round(ms, 4),
             "gbs": round(4.0 * total / (ms * 1e-3) / 1e9, 1),
             "gsamples_per_s": round(total / (ms * 1e-3) / 1e9, 2),
             "scaling": "strong", "bins_sum_ok": ok,
-            "step": "zero bins; local privatised histogram; NCCL all-reduce of 256 int32"}
+            "step": "zero bins; local privatised histogram; NCCL all-reduce of 256 int32",
+            "fused": {"ms_per_step": round(ms_f, 4),
+                      "gsamples_per_s": round(total / (ms_f * 1e-3) / 1e9, 2),
+                      "bins_sum_ok": ok_f,
+                      "step": "zero bins; one kernel: local histogram, then its last block "
+                              "stores the bins to every rank over NVLink and sums the "
+                              "ranks' slots (simtgo_Histogram_allreduce_fused)"}}
 
 
 def twelve(tile, g, a, b, c, h):

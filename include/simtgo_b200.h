@@ -234,6 +234,19 @@ int simtgo_comm_allreduce_i32(simtgo_comm* comm, int32_t* buf, int32_t n, void* 
  * all ranks, so every rank ends with the histogram of the whole input. */
 int simtgo_Histogram_allreduce(simtgo_comm* comm, int32_t* bins, int32_t bins_len,
                                const int32_t* x, int64_t x_len, void* stream);
+/* The same result in ONE kernel over NVLink peer memory instead of a local
+ * histogram followed by an NCCL all-reduce: the grid counts its shard, its
+ * last block stores this rank's bins (its own plus the counts) into a slot
+ * of every rank's exchange buffer, raises a flag on each rank (system-scope
+ * release), waits for every rank's flag (acquire) and sums the slots into
+ * bins. bins_len <= 4096 (more is SIMTGO_ESIZE). A collective: every rank
+ * calls it, in the same order; the first call maps every rank's exchange
+ * buffer with CUDA IPC (handles shared by an NCCL all-gather). The wait is
+ * bounded (about a second): a rank that does not arrive leaves the others'
+ * bins unchanged and raises the watchdog, which simtgo_stream_sync reports
+ * as SIMTGO_EDEVICE. */
+int simtgo_Histogram_allreduce_fused(simtgo_comm* comm, int32_t* bins, int32_t bins_len,
+                                     const int32_t* x, int64_t x_len, void* stream);
 
 /* ---- the tile track (package tile) -------------------------------------- */
 

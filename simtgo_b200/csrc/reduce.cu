@@ -18,6 +18,7 @@
 #include <algorithm>
 
 #include "common.cuh"
+#include "histogram.cuh"
 #include "tma.cuh"
 
 using namespace sgd;
@@ -114,13 +115,7 @@ __global__ void __launch_bounds__(256) k_warpreduce_rows(float* __restrict__ out
 }
 
 // ---- Histogram -----------------------------------------------------------------
-constexpr int kHistThreads = 512;
-constexpr int kHistWarps = kHistThreads / 32;
-constexpr int kBins = 256;
-
-__device__ __forceinline__ void hist_add(int* t, int v) {
-    if ((unsigned)v < (unsigned)kBins) atomicAdd(t + v, 1);
-}
+constexpr int kBins = kHistBins;
 
 __global__ void __launch_bounds__(kHistThreads) k_histogram(int* __restrict__ bins, int n_bins,
                                                             const int* __restrict__ x, int64_t m,
@@ -129,33 +124,9 @@ __global__ void __launch_bounds__(kHistThreads) k_histogram(int* __restrict__ bi
     for (int k = threadIdx.x; k < kHistWarps * kBins; k += blockDim.x) (&sh[0][0])[k] = 0;
     __syncthreads();
     int* mine = sh[threadIdx.x / 32];
-    const int64_t stride = grid_threads();
-    int64_t done = 0;
-    if (vec) {
-        const int64_t nvec = m / 4;
-        int64_t v = global_tid();
-        for (; v + 3 * stride < nvec; v += 4 * stride) {
-            int4 q[4];
-#pragma unroll
-            for (int u = 0; u < 4; u++) q[u] = ld_stream_i4(x + 4 * (v + u * stride));
-#pragma unroll
-            for (int u = 0; u < 4; u++) {
-                hist_add(mine, q[u].x);
-                hist_add(mine, q[u].y);
-                hist_add(mine, q[u].z);
-                hist_add(mine, q[u].w);
-            }
-        }
-        for (; v < nvec; v += stride) {
-            const int4 q = ld_stream_i4(x + 4 * v);
-            hist_add(mine, q.x);
-            hist_add(mine, q.y);
-            hist_add(mine, q.z);
-            hist_add(mine, q.w);
-        }
-        done = nvec * 4;
-    }
-    for (int64_t i = done + global_tid(); i < m; i += stride) hist_add(mine, x[i]);
+    hist_count(x, m, vec, [&](int v) {
+        if ((unsigned)v < (unsigned)kBins) atomicAdd(mine + v, 1);
+    });
     __syncthreads();
     for (int k = threadIdx.x; k < kBins; k += blockDim.x) {
         int c = 0;
@@ -192,36 +163,9 @@ __global__ void __launch_bounds__(kHistThreads) k_histogram_dyn(int* __restrict_
     for (int k = threadIdx.x; k < copies * tile; k += blockDim.x) shd[k] = 0;
     __syncthreads();
     int* mine = shd + ((threadIdx.x / 32) % copies) * tile;
-    auto add = [&](int v) {
+    hist_count(x, m, vec, [&](int v) {
         if ((unsigned)v < (unsigned)tile) atomicAdd(mine + v, 1);
-    };
-    const int64_t stride = grid_threads();
-    int64_t done = 0;
-    if (vec) {
-        const int64_t nvec = m / 4;
-        int64_t v = global_tid();
-        for (; v + 3 * stride < nvec; v += 4 * stride) {
-            int4 q[4];
-#pragma unroll
-            for (int u = 0; u < 4; u++) q[u] = ld_stream_i4(x + 4 * (v + u * stride));
-#pragma unroll
-            for (int u = 0; u < 4; u++) {
-                add(q[u].x);
-                add(q[u].y);
-                add(q[u].z);
-                add(q[u].w);
-            }
-        }
-        for (; v < nvec; v += stride) {
-            const int4 q = ld_stream_i4(x + 4 * v);
-            add(q.x);
-            add(q.y);
-            add(q.z);
-            add(q.w);
-        }
-        done = nvec * 4;
-    }
-    for (int64_t i = done + global_tid(); i < m; i += stride) add(x[i]);
+    });
     __syncthreads();
     const int kmax = min(tile, n_bins);
     for (int k = threadIdx.x; k < kmax; k += blockDim.x) {

@@ -163,3 +163,35 @@ def test_histogram_allreduce_single_rank():
         assert torch.equal(bins, torch.bincount(x.long(), minlength=256).to(torch.int32))
     finally:
         _lib.check(L.simtgo_comm_destroy(comm))
+
+
+@pytest.mark.parametrize("bins_len", [1, 100, 256, 1000, 4096])
+def test_histogram_allreduce_fused_single_rank(bins_len):
+    """The fused kernel with one rank (its own buffer is the only slot):
+    five calls in a row (both slot halves, flags counting up) give the
+    oracle's counts added to non-zero starting bins; bins past 256 keep
+    their starting values; more than 4096 bins is refused."""
+    L = _lib.load()
+    uid = C.create_string_buffer(128)
+    _lib.check(L.simtgo_comm_unique_id(uid))
+    comm = P()
+    _lib.check(L.simtgo_comm_init(C.byref(comm), uid, 1, 0))
+    try:
+        rng = np.random.default_rng(bins_len)
+        for call in range(5):
+            n = 100003 + 7 * call
+            x = rng.integers(-20, 300, n, dtype=np.int32)
+            bins0 = rng.integers(0, 50, bins_len, dtype=np.int32)
+            rc, want = O.histogram_shard(x, bins_len, bins=bins0)
+            assert rc == 0
+            b = torch.from_numpy(bins0).cuda()
+            xd = torch.from_numpy(x).cuda()
+            _lib.check(L.simtgo_Histogram_allreduce_fused(comm, P(b.data_ptr()), bins_len,
+                                                          P(xd.data_ptr()), n, None))
+            _lib.check(L.simtgo_stream_sync(None))
+            assert_equal(f"call {call}", b.cpu().numpy(), want)
+        big = torch.zeros(4097, dtype=torch.int32, device="cuda")
+        assert L.simtgo_Histogram_allreduce_fused(comm, P(big.data_ptr()), 4097,
+                                                  P(xd.data_ptr()), n, None) == _lib.ESIZE
+    finally:
+        _lib.check(L.simtgo_comm_destroy(comm))
