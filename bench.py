@@ -483,10 +483,38 @@ def bench_tile(args, torch, np, L, dev, sp, rank, world, barrier, max_over_ranks
     barrier()
     ms = timed(step, args.steps, args.warmup, stream, events)
     ms = max_over_ranks(ms)
-    return {"elements_total": total, "ms_per_step": round(ms, 4),
-            "gbs": round(16.0 * total / (ms * 1e-3) / 1e9, 1),
-            "gelements_per_s": round(total / (ms * 1e-3) / 1e9, 2),
-            "scaling": "strong", "bytes_per_element": 16}
+    res = {"elements_total": total, "ms_per_step": round(ms, 4),
+           "gbs": round(16.0 * total / (ms * 1e-3) / 1e9, 1),
+           "gelements_per_s": round(total / (ms * 1e-3) / 1e9, 2),
+           "scaling": "strong", "bytes_per_element": 16}
+    if world == 1:
+        # Other graphs over the same inputs: what the interpreter costs per
+        # kind of node (the twelve-node graph is compute-heavy: a 31-tap
+        # window, the exact hypot and a square root per element).
+        peak = measured_peaks()[0]["hbm_gbs"]
+        graphs = {
+            "identity": (lambda: a, 8),
+            "add3": (lambda: tile.Add(tile.Add(a, b), c), 16),
+            "mul_chain8": (lambda: _chain(tile, a, b, 8), 12),
+            "hypot": (lambda: tile.Hypot(a, b), 12),
+            "fir31": (lambda: tile.FIR(a, np.full(31, 1 / 31, np.float32)), 8),
+        }
+        res["graphs"] = {}
+        for name, (make, nbytes) in graphs.items():
+            r = make()
+            gms = timed(lambda: r.Run(out, stream, halo=halo), args.steps, args.warmup, stream,
+                        events)
+            gbs = nbytes * total / (gms * 1e-3) / 1e9
+            res["graphs"][name] = {"ms": round(gms, 4), "gbs": round(gbs, 1),
+                                   "frac_hbm": round(gbs / peak, 4), "bytes_per_element": nbytes}
+    return res
+
+
+def _chain(tile, a, b, k):
+    r = a
+    for _ in range(k):
+        r = tile.Mul(r, b)
+    return r
 
 
 def bench_kernels(args, torch, np, L, dev, sp, events, peaks):
