@@ -194,7 +194,12 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks) k_fir(float* __restrict_
             const int64_t p = s.A + i;
             tile[i] = (p >= 0 && p < g.x_len) ? x[p] : 0.0f;
         }
-        if (bulk_in && !mbar_wait(&bars[b], (uint32_t)((it >> 1) & 1), wd)) return;
+        if (bulk_in && !mbar_wait(&bars[b], (uint32_t)((it >> 1) & 1), wd)) {
+            // Gave up (the watchdog is raised): the other buffer's copy, if
+            // one is in flight, lands (bounded wait) before the block exits.
+            if (t + gridDim.x < ntiles) mbar_wait(&bars[b ^ 1], (uint32_t)(((it + 1) >> 1) & 1), wd);
+            return;
+        }
         __syncthreads();
 
         float acc[kPerThread];

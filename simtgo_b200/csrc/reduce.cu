@@ -70,7 +70,13 @@ __global__ void __launch_bounds__(kWrRows) k_warpreduce_tma(const __grid_constan
     int it = 0;
     for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x, it++) {
         const int s = it % kWrStages;
-        if (!mbar_wait(&bars[s], (uint32_t)((it / kWrStages) & 1), wd)) return;
+        if (!mbar_wait(&bars[s], (uint32_t)((it / kWrStages) & 1), wd)) {
+            // Gave up (the watchdog is raised): the other stage's copy, if
+            // one is in flight, lands (bounded wait) before the block exits.
+            if (t + gridDim.x < ntiles)
+                mbar_wait(&bars[(it + 1) % kWrStages], (uint32_t)(((it + 1) / kWrStages) & 1), wd);
+            return;
+        }
         const int64_t row = t * kWrRows + tid;
         if (row < rows) {
             const uint8_t* tile = tiles + s * kWrTileBytes;

@@ -472,7 +472,13 @@ __global__ void __launch_bounds__(kThreads, 3) k_tile(const __grid_constant__ Pr
         int s = 0;
         if (BULK) {
             s = it % nst;
-            if (!mbar_wait(&bars[s], (uint32_t)((it / nst) & 1), wd)) return;
+            if (!mbar_wait(&bars[s], (uint32_t)((it / nst) & 1), wd)) {
+                // Gave up (the watchdog is raised): let the block's other
+                // copies in flight land, each wait bounded, before exiting.
+                for (int j = 1; j < nst && c + j < c1; j++)
+                    mbar_wait(&bars[(it + j) % nst], (uint32_t)(((it + j) / nst) & 1), wd);
+                return;
+            }
             float* buf = stages + s * stage_floats;
             // The last 0-3 samples of a ragged signal are not a whole 16-byte
             // unit: plain loads.
