@@ -4,7 +4,8 @@
  * of package kernels and for the tile track's fused graph.
  *
  * Only the test suite, the smoke check and the benchmark's CPU-baseline leg
- * use this library, and only as the checker or as the timed CPU baseline. The
+ * use this library, and only as the reference result or as the timed CPU
+ * baseline. The
  * product (libsimtgo_b200.so) neither links nor calls it.
  *
  * Every function mirrors the matching simtgo_* entry point of

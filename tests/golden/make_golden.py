@@ -10,7 +10,7 @@ shapes and special values follow the reference's own parity tests
 simt/warp_parity_cuda_test.go).
 
 Run here (needs the reference tree):  python tests/golden/make_golden.py
-The .npz files are committed; the GPU box only reads them.
+The .npz files are committed; the GPU tests only read them.
 """
 from __future__ import annotations
 

@@ -1,5 +1,5 @@
-"""The multi-rank host logic on CPU: two gloo ranks (one process each, as on
-the GPU box) follow the shard plans of simtgo_b200.shard, compute their
+"""The multi-rank host logic on CPU: two gloo ranks (one process each, as one
+process per GPU) follow the shard plans of simtgo_b200.shard, compute their
 part with the oracle, and exchange what the sharded workloads exchange:
 
   FIR        nothing on the data path (the halo is part of the shard);

@@ -531,7 +531,7 @@ def test_launch_on_stream_is_async_then_syncs():
 
 def test_magnitudefast_max_ulp_logged():
     """simt/parity_test.go:1314: the reference's fast-math build is within
-    1e-5; this build is exact, 0 ulp from the emulator."""
+    1e-5; this implementation is exact, 0 ulp from the emulator."""
     n = 1 << 14
     re, im = normal(n, 1), normal(n, 2)
     rc, want = O.magnitudefast(re, im, 3.0, n // 256, 256)
