@@ -5,8 +5,7 @@
  *
  * Only the test suite, the smoke check and the benchmark's CPU-baseline leg
  * use this library, and only as the reference result or as the timed CPU
- * baseline. The
- * product (libsimtgo_b200.so) neither links nor calls it.
+ * baseline. The product (libsimtgo_b200.so) neither links nor calls it.
  *
  * Every function mirrors the matching simtgo_* entry point of
  * include/simtgo_b200.h minus the stream, computes on the host, and returns
