@@ -134,10 +134,9 @@ __device__ __forceinline__ void fir_chunk_tail(const float* __restrict__ w, cons
 struct Span {
     int64_t A, c0, c1;  // buffer origin; [c0, c1) arrives by bulk copy
 };
-__device__ __forceinline__ Span tile_span(int64_t t, int64_t tile_out, const FirGeom& g,
-                                          bool bulk_in) {
+__device__ __forceinline__ Span tile_span(int64_t t, const FirGeom& g, bool bulk_in) {
     Span s;
-    s.A = t * tile_out + g.halo - g.D;
+    s.A = t * kTileOut + g.halo - g.D;
     s.c0 = max(s.A, (int64_t)0);
     const int64_t end = min(s.A + g.tile, g.x_len);
     s.c1 = bulk_in && end > s.c0 ? s.c0 + ((end - s.c0) & ~int64_t(3)) : s.c0;
@@ -150,11 +149,9 @@ __device__ __forceinline__ Span tile_span(int64_t t, int64_t tile_out, const Fir
 // computed, and a buffer is refilled (tile i+2) once the bulk store of its
 // outputs has read it. The launch gives every tile its own block, which
 // measured faster on B200: four resident blocks per SM overlap one block's
-// load with the others' FMAs without the per-tile drain. NT threads per
-// block: 256 (5120 outputs per tile) normally, 64 (1280) when the signal is
-// too short to give every SM a few 256-thread tiles.
-template <int SH, int NT>
-__global__ void __launch_bounds__(NT, NT == kThreads ? kMinBlocks : 8) k_fir(float* __restrict__ y,
+// load with the others' FMAs without the per-tile drain.
+template <int SH>
+__global__ void __launch_bounds__(kThreads, kMinBlocks) k_fir(float* __restrict__ y,
                                                       const float* __restrict__ x,
                                                       const float* __restrict__ h, FirGeom g,
                                                       int64_t ntiles, bool bulk_in, bool bulk_out,
@@ -165,16 +162,15 @@ __global__ void __launch_bounds__(NT, NT == kThreads ? kMinBlocks : 8) k_fir(flo
     float* const buf1 = buf0 + g.tile;
     float* hs = buf1 + g.tile;
     const int tid = threadIdx.x;
-    constexpr int kTileOutNT = NT * kPerThread;
 
     auto issue = [&](int64_t t, int b) {
-        const Span s = tile_span(t, kTileOutNT, g, bulk_in);
+        const Span s = tile_span(t, g, bulk_in);
         mbar_arrive_expect_tx(&bars[b], (uint32_t)((s.c1 - s.c0) * 4));
         if (s.c1 > s.c0)
             bulk_load((b ? buf1 : buf0) + (s.c0 - s.A), x + s.c0, (uint32_t)((s.c1 - s.c0) * 4),
                       &bars[b]);
     };
-    for (int k = tid; k < g.taps_pad; k += NT) hs[k] = k < g.taps ? h[k] : 0.0f;
+    for (int k = tid; k < g.taps_pad; k += kThreads) hs[k] = k < g.taps ? h[k] : 0.0f;
     if (bulk_in && tid == 0) {
         mbar_init(&bars[0], 1);
         mbar_init(&bars[1], 1);
@@ -189,12 +185,12 @@ __global__ void __launch_bounds__(NT, NT == kThreads ? kMinBlocks : 8) k_fir(flo
     for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x, it++) {
         const int b = it & 1;
         float* tile = b ? buf1 : buf0;
-        const Span s = tile_span(t, kTileOutNT, g, bulk_in);
+        const Span s = tile_span(t, g, bulk_in);
         // The threads fill what the bulk copy does not: samples before x
         // (zeros), and from c1 on (a ragged last 1-3 samples, zeros past x,
         // or everything when x is not 16-byte aligned).
-        for (int64_t i = tid; i < s.c0 - s.A; i += NT) tile[i] = 0.0f;
-        for (int64_t i = (s.c1 - s.A) + tid; i < g.tile; i += NT) {
+        for (int64_t i = tid; i < s.c0 - s.A; i += kThreads) tile[i] = 0.0f;
+        for (int64_t i = (s.c1 - s.A) + tid; i < g.tile; i += kThreads) {
             const int64_t p = s.A + i;
             tile[i] = (p >= 0 && p < g.x_len) ? x[p] : 0.0f;
         }
@@ -221,18 +217,18 @@ __global__ void __launch_bounds__(NT, NT == kThreads ? kMinBlocks : 8) k_fir(flo
         for (int c = 0; c < kPerThread / 4; c++)
             *reinterpret_cast<float4*>(o + 4 * c) =
                 make_float4(acc[4 * c], acc[4 * c + 1], acc[4 * c + 2], acc[4 * c + 3]);
-        const int64_t ob = t * kTileOutNT;
-        const bool whole = ob + kTileOutNT <= g.y_len;
+        const int64_t ob = t * kTileOut;
+        const bool whole = ob + kTileOut <= g.y_len;
         fence_proxy_async_smem();  // this buffer's generic accesses, before async ones
         __syncthreads();
         if (bulk_out && whole) {
             if (tid == 0) {
-                bulk_store(y + ob, tile, kTileOutNT * 4u);
+                bulk_store(y + ob, tile, kTileOut * 4u);
                 bulk_store_drain();
             }
         } else {
-            const int64_t n = min((int64_t)kTileOutNT, g.y_len - ob);
-            for (int64_t i = tid; i < n; i += NT) y[ob + i] = tile[i];
+            const int64_t n = min((int64_t)kTileOut, g.y_len - ob);
+            for (int64_t i = tid; i < n; i += kThreads) y[ob + i] = tile[i];
             fence_proxy_async_smem();
             __syncthreads();
         }
@@ -262,18 +258,11 @@ int launch_fir(const char* K, float* y, int64_t y_len, const float* x, int64_t x
     g.D = (int32_t)(taps + 6 + m);
     // The window loads of the last thread reach a few floats past the last
     // sample its outputs use (whole 16-byte loads): 8 floats of slack.
-    // A signal too short for two 256-thread tiles per SM takes 64-thread
-    // tiles, four times as many, so more SMs load and compute at once.
-    const bool small = sg::ceil_div(y_len, kTileOut) < 2 * (int64_t)d->sms;
-    const int nt = small ? 64 : kThreads;
-    const int64_t tile_out = (int64_t)nt * kPerThread;
-    g.tile = (int32_t)sg::ceil_div(g.D + tile_out + 8, 4) * 4;
+    g.tile = (int32_t)sg::ceil_div(g.D + kTileOut + 8, 4) * 4;
     const int sh = (g.D - 7) % 4;
 
-    static const FirKernel kernels[2][4] = {
-        {k_fir<0, kThreads>, k_fir<1, kThreads>, k_fir<2, kThreads>, k_fir<3, kThreads>},
-        {k_fir<0, 64>, k_fir<1, 64>, k_fir<2, 64>, k_fir<3, 64>}};
-    const FirKernel kern = kernels[small ? 1 : 0][sh];
+    static const FirKernel kernels[4] = {k_fir<0>, k_fir<1>, k_fir<2>, k_fir<3>};
+    const FirKernel kern = kernels[sh];
     const size_t smem = (size_t)(2 * g.tile + g.taps_pad) * sizeof(float);
     if (smem > (size_t)d->max_smem_optin)
         return sg::fail(SIMTGO_ESIZE, "%s: %d taps need %zu bytes of shared memory", K, taps,
@@ -284,10 +273,10 @@ int launch_fir(const char* K, float* y, int64_t y_len, const float* x, int64_t x
     if (rc) return rc;
     int per_sm = 0;
     rc = sg::cuda_status(
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, nt, smem),
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem),
         "cudaOccupancyMaxActiveBlocksPerMultiprocessor(FIR)");
     if (rc) return rc;
-    const int64_t ntiles = sg::ceil_div(y_len, tile_out);
+    const int64_t ntiles = sg::ceil_div(y_len, kTileOut);
     const int64_t resident = (int64_t)d->sms * std::max(1, per_sm);
     // One tile per block measured faster than a persistent grid (the
     // hardware starts the next block's load while this one computes), so
@@ -297,7 +286,7 @@ int launch_fir(const char* K, float* y, int64_t y_len, const float* x, int64_t x
     const int blocks = (int)ntiles;
     if (ntiles > 0x7fffffffLL) return sg::fail(SIMTGO_ESIZE, "%s: y_len too large", K);
     sg::before_launch();
-    kern<<<blocks, nt, smem, (cudaStream_t)stream>>>(
+    kern<<<blocks, kThreads, smem, (cudaStream_t)stream>>>(
         y, x, h, g, ntiles, sg::aligned16(x), sg::aligned16(y), sg::watchdog_device_ptr());
     return sg::launch_status(K);
 }
