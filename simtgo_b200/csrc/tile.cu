@@ -130,8 +130,8 @@ struct Program {
 
 // The program as the interpreter reads it: copied once per block from the
 // parameter bank into shared memory, where a warp-uniform word is one
-// broadcast load. Layout: code[code_cap] | fir[n_fir] (start, taps, reach,
-// tile4) | in[n_in], 16-byte rounded.
+// broadcast load. Layout: code[code_cap] (the program and one END) |
+// fir[n_fir] (start, taps, reach, tile4) | in[n_in], 16-byte rounded.
 __host__ __device__ constexpr int meta_code_cap(int n_code) { return n_code + 1; }
 __host__ __device__ constexpr int meta_bytes(int n_code, int n_in, int n_fir) {
     return ((meta_code_cap(n_code) * 16 + n_in * 8 + n_fir * 16) + 15) & ~15;
@@ -270,20 +270,18 @@ __device__ __forceinline__ float4 mask_outside(float4 v, int64_t p, const Ctx& c
 
 // Runs the program from pc until an instruction with F_END. Inlined into
 // k_tile twice: FULL for runs where all of the thread's groups take part
-// (the chunk), and the general form for a window's head run; the next
-// instruction is loaded while this one executes (the shared copy holds one
-// past the last). In DIRECT mode (BULK false) an input operand is read from
-// HBM at the run's positions.
+// (the chunk), and the general form for a window's head run. (Loading the
+// next instruction ahead measured slower: it costs more instructions than
+// the shared-load latency it hides.) In DIRECT mode (BULK false) an input
+// operand is read from HBM at the run's positions.
 template <bool BULK, bool FULL>
 __device__ __forceinline__ void interpret(const Insn* code, int pc, const Ctx& c, const Run& r) {
     const int t = threadIdx.x;
     float4 A[kG];
 #pragma unroll
     for (int k = 0; k < kG; k++) A[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-    Insn next = code[pc];
     for (;;) {
-        const Insn in = next;
-        next = code[++pc];
+        const Insn in = code[pc++];
         // Group k of operand M(x) (inactive groups: A itself, nothing is read).
         auto operand = [&](int x, bool input, int k) -> float4 {
             if (!FULL && !((r.gm >> k) & 1)) return A[k];
