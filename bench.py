@@ -366,33 +366,34 @@ def spot_check(np, x_host, y, h, halo):
         yh.view(np.uint32), want.view(np.uint32)))}
 
 
-def timed(fn, steps, warmup, stream, events, flush=None):
-    """Mean ms per launch of fn on stream. With `flush` (a device buffer
-    larger than L2), the buffer is rewritten before every launch and only
-    the launch itself is timed: for working sets that would fit in L2."""
+def in_turn(fns):
+    """One callable that runs fns[0], fns[1], ... in turn, so that
+    consecutive launches read different buffers whose total is larger than
+    L2: each launch starts with its inputs out of L2, with no flush."""
+    state = {"i": 0}
+
+    def run():
+        fns[state["i"] % len(fns)]()
+        state["i"] += 1
+
+    return run
+
+
+def timed(fn, steps, warmup, stream, events):
+    """Mean ms per launch of fn on stream: `steps` launches back to back
+    between two CUDA events, after `warmup` untimed ones."""
     for _ in range(warmup):
         fn()
     import torch
 
     torch.cuda.synchronize()
-    if flush is None:
-        e0, e1 = events()
-        e0.record(stream)
-        for _ in range(steps):
-            fn()
-        e1.record(stream)
-        e1.synchronize()
-        return e0.elapsed_time(e1) / steps
-    pairs = []
+    e0, e1 = events()
+    e0.record(stream)
     for _ in range(steps):
-        flush.zero_()
-        e0, e1 = events()
-        e0.record(stream)
         fn()
-        e1.record(stream)
-        pairs.append((e0, e1))
-    torch.cuda.synchronize()
-    return sum(a.elapsed_time(b) for a, b in pairs) / steps
+    e1.record(stream)
+    e1.synchronize()
+    return e0.elapsed_time(e1) / steps
 
 
 def bench_histogram(args, torch, L, dev, sp, rank, world, barrier, max_over_ranks, events):
@@ -608,30 +609,36 @@ def bench_kernels(args, torch, np, L, dev, sp, events, peaks):
         "samples (4096-bin launch-sized tile)")
     del xi
     torch.cuda.empty_cache()
-    # Gray 7680x4320: 133 MB of traffic, about the size of L2, so L2 is
-    # flushed (a 512 MB write) before every timed launch.
-    flush = torch.empty(1 << 27, dtype=torch.float32, device=dev)
+    # Gray 7680x4320: 133 MB of traffic per image, about the size of L2, so
+    # four images are converted in turn (532 MB).
     npx = 7680 * 4320
-    rgb = torch.randint(0, 256, (3 * npx,), dtype=torch.uint8, device=dev, generator=gen)
-    luma = torch.empty(npx, dtype=torch.uint8, device=dev)
-    rec("Gray", timed(lambda: L.simtgo_Gray(P(luma.data_ptr()), npx, P(rgb.data_ptr()), 3 * npx,
-                                            grid(npx), 256, sp), steps, warm, stream, events,
-                      flush=flush), 4.0 * npx, npx, "pixels (L2 flushed before each launch)")
-    del rgb, luma
+    imgs = [(torch.empty(npx, dtype=torch.uint8, device=dev),
+             torch.randint(0, 256, (3 * npx,), dtype=torch.uint8, device=dev, generator=gen))
+            for _ in range(4)]
+    rec("Gray", timed(in_turn([
+        (lambda lu=lu, rgb=rgb: L.simtgo_Gray(P(lu.data_ptr()), npx, P(rgb.data_ptr()), 3 * npx,
+                                              grid(npx), 256, sp)) for lu, rgb in imgs]),
+        steps, warm, stream, events), 4.0 * npx, npx,
+        "pixels (4 images in turn, 532 MB: inputs larger than L2, no flush)")
+    del imgs
     # Transpose 16384^2 (at the default size; T*T = N).
     T = 1 << (args.kernels_log2 // 2)
     rec("Transpose", timed(lambda: L.simtgo_Transpose(pc, T * T, pa, T * T, T, T, T // 16,
                                                       T // 16, 16, 16, sp), steps, warm, stream,
                            events), 8.0 * T * T, T * T, "elements")
-    # FIR of the 2^20-sample, 31-tap case (L2-resident, launch-bound).
+    # FIR of the 2^20-sample, 31-tap case: 32 signals filtered in turn
+    # (256 MB), so each launch starts with its 8 MB out of L2.
     n20 = 1 << 20
     h31 = torch.rand(31, device=dev, generator=gen)
     h31 /= h31.sum()
-    rec("FIR_31taps_2^20", timed(lambda: L.simtgo_FIR(pc, n20, pa, n20, P(h31.data_ptr()), 31,
-                                                      n20 // 256, 256, sp), steps, warm, stream,
-                                 events, flush=flush), 8.0 * n20, n20,
-        "outputs (8 MB working set; L2 flushed before each launch; launch-latency bound)")
-    del flush
+    sig = [(torch.empty(n20, device=dev), torch.randn(n20, device=dev, generator=gen))
+           for _ in range(32)]
+    rec("FIR_31taps_2^20", timed(in_turn([
+        (lambda y=y, x=x: L.simtgo_FIR(P(y.data_ptr()), n20, P(x.data_ptr()), n20,
+                                       P(h31.data_ptr()), 31, n20 // 256, 256, sp))
+        for y, x in sig]), steps, warm, stream, events), 8.0 * n20, n20,
+        "outputs (32 signals in turn, 256 MB: inputs larger than L2, no flush)")
+    del sig
     return out
 
 

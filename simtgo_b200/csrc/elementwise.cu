@@ -5,14 +5,14 @@
 // Gray (gray.go:34).
 //
 // B200 design: every kernel is HBM-bound, so one template does the data
-// movement for all of them: a persistent grid (4 blocks of 256 threads per
-// SM) strides over 16-byte vector units, each thread issuing the loads of
-// four units before it computes any (64 B of every input stream in flight
-// per thread), with L1-bypassing 128-bit loads and evict-first 128-bit
-// stores. Pointers that are not 16-byte aligned take a scalar variant of the
+// movement for all of them: blocks of 256 threads take contiguous ranges of
+// 16-byte vector units, each thread issuing the loads of four units before
+// it computes any (64 B of every input stream in flight per thread), with
+// L1-bypassing 128-bit loads and evict-first 128-bit stores. Pointers that are not 16-byte aligned take a scalar variant of the
 // same arithmetic. The arithmetic itself is exact.cuh: the emulator's result,
 // bit for bit. The caller's grid*block still bounds which indices are written.
 #include <algorithm>
+#include <type_traits>
 
 #include "common.cuh"
 #include "exact.cuh"
@@ -28,20 +28,86 @@ constexpr int kUnroll = 4;
 // Op provides: W (elements per vector unit), In (the loaded unit),
 // load(v), store(v, in) for unit v, scalar(i) for element i, and
 // prologue() (block set-up before the loop; may use shared memory).
+//
+// Block b takes a contiguous range of about kPerThread units per thread
+// (Op::kUnitsPerThread where declared); its threads step through it
+// kThreads units apart, kUnroll units per step, so every load and store
+// instruction of a warp is one contiguous run. The grid has many more
+// blocks than are resident at once, and the hardware hands the next range
+// to whichever SM finishes first: on the two-die B200 that measured 5-35%
+// faster than a persistent grid striding over the whole array, except for
+// Gray's short image (Op::kStrided), which keeps the persistent grid.
+// Op::kPipe (where declared true): the loads of a thread's next kUnroll
+// units are issued before the stores of the current ones, so they stay in
+// flight while it computes.
+constexpr int kPerThread = 8;
+
+template <class Op, class = void>
+struct Pipelined : std::false_type {};
+template <class Op>
+struct Pipelined<Op, std::void_t<decltype(Op::kPipe)>> : std::bool_constant<Op::kPipe> {};
+template <class Op, class = void>
+struct Strided : std::false_type {};
+template <class Op>
+struct Strided<Op, std::void_t<decltype(Op::kStrided)>> : std::bool_constant<Op::kStrided> {};
+template <class Op, class = void>
+struct UnitsPerThread : std::integral_constant<int, kPerThread> {};
+template <class Op>
+struct UnitsPerThread<Op, std::void_t<decltype(Op::kUnitsPerThread)>>
+    : std::integral_constant<int, Op::kUnitsPerThread> {};
+
 template <class Op>
 __global__ void __launch_bounds__(kThreads) k_vec(Op op, int64_t nvec, int64_t m) {
     op.prologue();
-    const int64_t stride = grid_threads();
-    int64_t v = global_tid();
-    for (; v + (kUnroll - 1) * stride < nvec; v += kUnroll * stride) {
-        typename Op::In in[kUnroll];
+    if constexpr (Strided<Op>::value) {
+        const int64_t stride = grid_threads();
+        int64_t v = global_tid();
+        for (; v + (kUnroll - 1) * stride < nvec; v += kUnroll * stride) {
+            typename Op::In in[kUnroll];
 #pragma unroll
-        for (int u = 0; u < kUnroll; u++) in[u] = op.load(v + u * stride);
+            for (int u = 0; u < kUnroll; u++) in[u] = op.load(v + u * stride);
 #pragma unroll
-        for (int u = 0; u < kUnroll; u++) op.store(v + u * stride, in[u]);
+            for (int u = 0; u < kUnroll; u++) op.store(v + u * stride, in[u]);
+        }
+        for (; v < nvec; v += stride) op.store(v, op.load(v));
+    } else {
+        constexpr int64_t kStep = (int64_t)kThreads * kUnroll;
+        const int64_t per_block = (nvec + gridDim.x - 1) / gridDim.x;
+        const int64_t per = (per_block + kThreads - 1) / kThreads * kThreads;
+        const int64_t end = min((int64_t)(blockIdx.x + 1) * per, nvec);
+        int64_t v = (int64_t)blockIdx.x * per + threadIdx.x;
+        if constexpr (Pipelined<Op>::value) {
+            typename Op::In in[kUnroll];
+            if (v + (kUnroll - 1) * kThreads < end) {
+#pragma unroll
+                for (int u = 0; u < kUnroll; u++) in[u] = op.load(v + u * kThreads);
+            }
+            for (; v + (kUnroll - 1) * kThreads < end; v += kStep) {
+                const bool more = v + kStep + (kUnroll - 1) * kThreads < end;
+                typename Op::In nx[kUnroll];
+                if (more) {
+#pragma unroll
+                    for (int u = 0; u < kUnroll; u++) nx[u] = op.load(v + kStep + u * kThreads);
+                }
+#pragma unroll
+                for (int u = 0; u < kUnroll; u++) op.store(v + u * kThreads, in[u]);
+                if (more) {
+#pragma unroll
+                    for (int u = 0; u < kUnroll; u++) in[u] = nx[u];
+                }
+            }
+        } else {
+            for (; v + (kUnroll - 1) * kThreads < end; v += kStep) {
+                typename Op::In in[kUnroll];
+#pragma unroll
+                for (int u = 0; u < kUnroll; u++) in[u] = op.load(v + u * kThreads);
+#pragma unroll
+                for (int u = 0; u < kUnroll; u++) op.store(v + u * kThreads, in[u]);
+            }
+        }
+        for (; v < end; v += kThreads) op.store(v, op.load(v));
     }
-    for (; v < nvec; v += stride) op.store(v, op.load(v));
-    for (int64_t i = nvec * Op::W + global_tid(); i < m; i += stride) op.scalar(i);
+    for (int64_t i = nvec * Op::W + global_tid(); i < m; i += grid_threads()) op.scalar(i);
 }
 
 template <class Op>
@@ -58,14 +124,19 @@ int run_ew(const char* name, const Op& op, int64_t nvec, int64_t m, bool vec_ok,
     const sg::DevInfo* d;
     if (int rc = sg::current_device(&d)) return rc;
     cudaStream_t s = (cudaStream_t)stream;
-    const int64_t units = vec_ok ? std::max<int64_t>(nvec, 1) : m;
-    const int64_t want = sg::ceil_div(units, kThreads);
-    const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(want, (int64_t)d->sms * 4));
+    int64_t blocks;
+    if (vec_ok && !Strided<Op>::value) {
+        blocks = sg::ceil_div(std::max<int64_t>(nvec, 1),
+                              (int64_t)kThreads * UnitsPerThread<Op>::value);
+    } else {  // a persistent grid striding over the units (or the elements)
+        const int64_t units = vec_ok ? std::max<int64_t>(nvec, 1) : m;
+        blocks = std::min<int64_t>(sg::ceil_div(units, (int64_t)kThreads), (int64_t)d->sms * 4);
+    }
     sg::before_launch();
     if (vec_ok)
-        k_vec<Op><<<blocks, kThreads, 0, s>>>(op, nvec, m);
+        k_vec<Op><<<(unsigned)blocks, kThreads, 0, s>>>(op, nvec, m);
     else
-        k_scalar<Op><<<blocks, kThreads, 0, s>>>(op, m);
+        k_scalar<Op><<<(unsigned)blocks, kThreads, 0, s>>>(op, m);
     return sg::launch_status(name);
 }
 
@@ -261,6 +332,7 @@ struct ClassifyOp {
 constexpr int kMaxSharedBands = 1024;
 template <int K>
 struct BandGainOp {
+    static constexpr int kUnitsPerThread = 32;  // amortises the band-table prologue
     float* y;
     const float* x;
     int64_t x_len;
@@ -363,6 +435,7 @@ struct BandGainOp {
 
 // ---- Quantize ---------------------------------------------------------------------
 struct QuantizeOp : NoPrologue {
+    static constexpr bool kPipe = true;
     int32_t* code;
     long long* energy;
     uint8_t* clipped;
@@ -400,9 +473,11 @@ struct QuantizeOp : NoPrologue {
         one(i + 1, a.y, q.y, e01.y, c1);
         one(i + 2, a.z, q.z, e23.x, c2);
         one(i + 3, a.w, q.w, e23.y, c3);
-        st_stream_i4(code + i, q);
-        st_stream_i4(energy + i, *reinterpret_cast<const int4*>(&e01));
-        st_stream_i4(energy + i + 2, *reinterpret_cast<const int4*>(&e23));
+        // Plain (write-back) stores: 13 of the 17 bytes per element are
+        // written, and evict-first stores measured slower on that mix.
+        *reinterpret_cast<int4*>(code + i) = q;
+        *reinterpret_cast<longlong2*>(energy + i) = e01;
+        *reinterpret_cast<longlong2*>(energy + i + 2) = e23;
         *reinterpret_cast<uint32_t*>(clipped + i) = c0 | (c1 << 8) | (c2 << 16) | (c3 << 24);
     }
     __device__ void scalar(int64_t i) const {
@@ -421,6 +496,7 @@ struct QuantizeOp : NoPrologue {
 // 16 bytes of luma out. Two pixels share one 32-bit multiply-add, since
 // 77r + 150g + 29b + 128 <= 65408 fits 16 bits (gray.go:12-15, :52).
 struct GrayOp : NoPrologue {
+    static constexpr bool kStrided = true;
     uint8_t* out;
     const uint8_t* rgb;
     int64_t rgb_len;
