@@ -307,6 +307,8 @@ def run_ours(args):
                                                      barrier, max_over_ranks, events)
     sharded["tile_graph"] = bench_tile(args, torch, np, L, dev, sp, rank, world, barrier,
                                        max_over_ranks, events)
+    sharded["tile_reduce"] = bench_tile_reduce(args, torch, L, dev, rank, world, barrier,
+                                               max_over_ranks, events)
 
     kernels = None
     cpu = None
@@ -396,16 +398,11 @@ def timed(fn, steps, warmup, stream, events):
     return e0.elapsed_time(e1) / steps
 
 
-def bench_histogram(args, torch, L, dev, sp, rank, world, barrier, max_over_ranks, events):
-    """2^28 samples in total, uniform over [0,255], split over the ranks;
-    each rank counts its part and the bins are all-reduced (NCCL)."""
-    from simtgo_b200 import _lib, shard
+def make_comm(torch, L, dev, rank, world):
+    """The library's communicator over the job's ranks (rank 0's NCCL id
+    broadcast through torch.distributed)."""
+    from simtgo_b200 import _lib
 
-    total = 1 << 28
-    n = shard.histogram_plan(total, world, rank).n
-    gen = torch.Generator(device=dev).manual_seed(4 + rank)
-    x = torch.randint(0, 256, (n,), dtype=torch.int32, device=dev, generator=gen)
-    bins = torch.zeros(256, dtype=torch.int32, device=dev)
     comm = P()
     uid = C.create_string_buffer(128)
     if world > 1:
@@ -420,6 +417,20 @@ def bench_histogram(args, torch, L, dev, sp, rank, world, barrier, max_over_rank
     else:
         _lib.check(L.simtgo_comm_unique_id(uid))
     _lib.check(L.simtgo_comm_init(C.byref(comm), uid, world, rank))
+    return comm
+
+
+def bench_histogram(args, torch, L, dev, sp, rank, world, barrier, max_over_ranks, events):
+    """2^28 samples in total, uniform over [0,255], split over the ranks;
+    each rank counts its part and the bins are all-reduced (NCCL)."""
+    from simtgo_b200 import _lib, shard
+
+    total = 1 << 28
+    n = shard.histogram_plan(total, world, rank).n
+    gen = torch.Generator(device=dev).manual_seed(4 + rank)
+    x = torch.randint(0, 256, (n,), dtype=torch.int32, device=dev, generator=gen)
+    bins = torch.zeros(256, dtype=torch.int32, device=dev)
+    comm = make_comm(torch, L, dev, rank, world)
 
     def run(fn):
         def step():
@@ -508,6 +519,40 @@ def bench_tile(args, torch, np, L, dev, sp, rank, world, barrier, max_over_ranks
             gbs = nbytes * total / (gms * 1e-3) / 1e9
             res["graphs"][name] = {"ms": round(gms, 4), "gbs": round(gbs, 1),
                                    "frac_hbm": round(gbs / peak, 4), "bytes_per_element": nbytes}
+    return res
+
+
+def bench_tile_reduce(args, torch, L, dev, rank, world, barrier, max_over_ranks, events):
+    """Tile reductions over 2^28 uniform[-4,4] samples split over the ranks
+    in whole blocks of 2048 (tile.ShardRange): the sum of squares and the
+    argmax, each one fused pass over HBM plus, for N > 1, the NCCL
+    all-gather of the block partials; every rank ends with the whole
+    signal's result."""
+    from simtgo_b200 import _lib, tile
+
+    total = 1 << args.tile_log2
+    start, n = tile.ShardRange(total, world, rank)
+    gen = torch.Generator(device=dev).manual_seed(12 + rank)
+    x = torch.rand(n, device=dev, generator=gen) * 8 - 4
+    g = tile.New()
+    a = g.InputDevice(x)
+    comm = make_comm(torch, L, dev, rank, world)
+    v = torch.zeros(1, device=dev)
+    i = torch.zeros(1, dtype=torch.int64, device=dev)
+    stream = torch.cuda.current_stream()
+    peak = measured_peaks()[0]["hbm_gbs"]
+    res = {"elements_total": total, "scaling": "strong", "bytes_per_element": 4,
+           "split": "whole blocks of 2048 per rank (tile.ShardRange)"}
+    for name, red in (("sum_of_squares", tile.Sum(tile.Mul(a, a))), ("argmax", tile.ArgMax(a))):
+        barrier()
+        ms = max_over_ranks(timed(lambda: red.RunShard(comm, total, v, i, stream=stream),
+                                  args.steps, args.warmup, stream, events))
+        gbs = 4.0 * total / (ms * 1e-3) / 1e9
+        res[name] = {"ms": round(ms, 4), "gbs": round(gbs, 1),
+                     "frac_hbm_per_gpu": round(gbs / world / peak, 4),
+                     "value": float(v.item()), "index": int(i.item()) if name == "argmax" else None}
+    barrier()
+    _lib.check(L.simtgo_comm_destroy(comm))
     return res
 
 

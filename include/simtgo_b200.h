@@ -342,6 +342,60 @@ int simtgo_tile_run_shard(simtgo_tile_graph* g, simtgo_tensor t, float* dev_out,
 int simtgo_tile_run_stepwise_noalloc(simtgo_tile_graph* g, simtgo_tensor t, float* dev_out,
                                      int32_t out_len, void* stream);
 
+/* ---- tile reductions (no counterpart in the reference) --------------------
+ * The reference's tile track has no reductions; its plan lists sum, min, max
+ * and argmax "with the shared-memory + warp pattern" as the next step
+ * (PLAN.md, Phase 6, "Reductions"). Here a reduction consumes the fused
+ * graph's values inside the same single pass over HBM (no output array is
+ * written) and yields one value:
+ *   SIMTGO_TILE_SUM     the float32 sum, in the fixed order below (a NaN
+ *                       result is written as 0x7fc00000);
+ *   SIMTGO_TILE_MIN,    Go's min / max: NaN (written as 0x7fc00000) if any
+ *   SIMTGO_TILE_MAX     element is NaN, and -0 < +0;
+ *   SIMTGO_TILE_ARGMAX  the first index whose value is MAX bit for bit (+0
+ *                       wins over -0, the first NaN wins), with that value.
+ * Empty tensors give SUM +0, MIN +Inf, MAX -Inf, ARGMAX index -1 (value -Inf).
+ * Summation order: the values are cut into blocks of 2048, zero-padded past
+ * the end. Block b's partial is ((w0+w1)+(w2+w3))+((w4+w5)+(w6+w7)), where
+ * w_k is the butterfly sum of t_l over lanes l = 0..31 (each lane adds the
+ * lane l^16, then l^8, l^4, l^2, l^1) and
+ *   t_l = ((x[e]+x[e+1]) + (x[e+2]+x[e+3])) + ((x[f]+x[f+1]) + (x[f+2]+x[f+3])),
+ *   e = 2048 b + 4 (32 k + l), f = e + 1024.
+ * While more than one partial remains, the partials are reduced the same
+ * way, as values of their own. So the sum is reproducible bit for bit, on one
+ * GPU or sharded (simtgo_tile_reduce_shard). */
+#define SIMTGO_TILE_SUM 0
+#define SIMTGO_TILE_MIN 1
+#define SIMTGO_TILE_MAX 2
+#define SIMTGO_TILE_ARGMAX 3
+/* Reduces t (every input a device input) into dev_value (one float) and,
+ * for ARGMAX, dev_index (one int64; may be null for the other kinds).
+ * Asynchronous on stream; allocates its partials stream-ordered
+ * (cudaMallocAsync) and frees them the same way. */
+int simtgo_tile_reduce(simtgo_tile_graph* g, simtgo_tensor t, int32_t kind, float* dev_value,
+                       int64_t* dev_index, void* stream);
+/* The same with host inputs uploaded and host results (Materialize's
+ * counterpart). Synchronous. */
+int simtgo_tile_reduce_materialize(simtgo_tile_graph* g, simtgo_tensor t, int32_t kind,
+                                   float* value, int64_t* index);
+/* The shard of a signal of n_total elements that rank `rank` of `nranks`
+ * holds for simtgo_tile_reduce_shard: [rank*per, min(n_total, (rank+1)*per))
+ * with per = ceil(ceil(n_total / nranks) / 2048) * 2048 (whole blocks of
+ * the summation order; trailing ranks may hold nothing). */
+int simtgo_tile_shard_range(int64_t n_total, int32_t nranks, int32_t rank, int64_t* start,
+                            int64_t* len);
+/* One rank's part of the reduction of a graph sharded over the ranks of
+ * comm (a collective: every rank calls it, in the same order). Len(t) must
+ * be this rank's simtgo_tile_shard_range length; device inputs carry `halo`
+ * preceding samples as in simtgo_tile_run_shard. Each rank computes the
+ * partials of its own blocks, an NCCL all-gather assembles every block's
+ * partial on every rank, and each rank finishes the same tree: the result
+ * equals simtgo_tile_reduce over the whole signal, bit for bit, on every
+ * rank; ARGMAX indices are global. Asynchronous on stream. */
+int simtgo_tile_reduce_shard(simtgo_tile_graph* g, simtgo_tensor t, int32_t kind, int32_t halo,
+                             int64_t n_total, simtgo_comm* comm, float* dev_value,
+                             int64_t* dev_index, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -747,3 +747,166 @@ int oracle_tile_eval(const oracle_tile_node* nodes, int32_t n_nodes, int32_t roo
     free(val);
     return rc;
 }
+
+/* ---- tile reductions -----------------------------------------------------
+ * No counterpart in the reference (its PLAN.md, Phase 6, lists tile
+ * reductions as future work): the semantics are the library's own, stated
+ * in include/simtgo_b200.h (SIMTGO_TILE_SUM ..). Restated here from that
+ * statement, element by element, as the check on the GPU tree. */
+typedef struct {
+    float v;
+    int64_t i;
+} rval;
+#define RED_CHUNK 2048
+#define NO_INDEX INT64_MAX
+
+static float f_of(uint32_t u) {
+    float f;
+    memcpy(&f, &u, 4);
+    return f;
+}
+static uint32_t u_of(float f) {
+    uint32_t u;
+    memcpy(&u, &f, 4);
+    return u;
+}
+static rval red_id(int kind) {
+    rval r = {0.0f, 0};
+    if (kind == 1) r.v = f_of(0x7f800000u);
+    if (kind >= 2) r.v = f_of(0xff800000u);
+    if (kind == 3) r.i = NO_INDEX;
+    return r;
+}
+/* Go's min/max on float32: NaN if either is NaN; -0 < +0. */
+static float go_minf(float a, float b) {
+    if (a != a || b != b) return f_of(0x7fc00000u);
+    if (a < b) return a;
+    if (b < a) return b;
+    return (u_of(a) >> 31) ? a : b;
+}
+static float go_maxf(float a, float b) {
+    if (a != a || b != b) return f_of(0x7fc00000u);
+    if (a > b) return a;
+    if (b > a) return b;
+    return (u_of(a) >> 31) ? b : a;
+}
+/* ARGMAX: NaN first, then larger value (+0 above -0), then smaller index. */
+static int am_first(rval a, rval b) {
+    int na = a.v != a.v, nb = b.v != b.v;
+    if (na || nb) return (na && nb) ? a.i < b.i : na;
+    if (a.v > b.v) return 1;
+    if (b.v > a.v) return 0;
+    if ((u_of(a.v) >> 31) != (u_of(b.v) >> 31)) return !(u_of(a.v) >> 31);
+    return a.i < b.i;
+}
+static rval red2(int kind, rval a, rval b) {
+    rval r = {0.0f, 0};
+    switch (kind) {
+        case 0: r.v = a.v + b.v; return r;
+        case 1: r.v = go_minf(a.v, b.v); return r;
+        case 2: r.v = go_maxf(a.v, b.v); return r;
+        default: return am_first(a, b) ? a : b;
+    }
+}
+/* One block of 2048 (value, index) entries, padded with the identity:
+ * per lane t ((x[e]+x[e+1])+(x[e+2]+x[e+3]))+((x[f]..)), e = 4t, f = 1024+4t;
+ * per warp the butterfly (l with l^16, ^8, ^4, ^2, ^1); then the eight warps
+ * as ((w0 w1)(w2 w3))((w4 w5)(w6 w7)). */
+static rval red_block(int kind, const rval* x) {
+    rval lane[256], w[8];
+    for (int t = 0; t < 256; t++) {
+        const rval* g0 = x + 4 * t;
+        const rval* g1 = x + 1024 + 4 * t;
+        lane[t] = red2(kind, red2(kind, red2(kind, g0[0], g0[1]), red2(kind, g0[2], g0[3])),
+                       red2(kind, red2(kind, g1[0], g1[1]), red2(kind, g1[2], g1[3])));
+    }
+    for (int k = 0; k < 8; k++) {
+        rval v[32], nv[32];
+        memcpy(v, lane + 32 * k, sizeof v);
+        for (int m = 16; m >= 1; m >>= 1) {
+            for (int l = 0; l < 32; l++) nv[l] = red2(kind, v[l], v[l ^ m]);
+            memcpy(v, nv, sizeof v);
+        }
+        w[k] = v[0];
+    }
+    return red2(kind, red2(kind, red2(kind, w[0], w[1]), red2(kind, w[2], w[3])),
+                red2(kind, red2(kind, w[4], w[5]), red2(kind, w[6], w[7])));
+}
+/* Level 1: the partial of each block of 2048 values of x (index of x[0] is
+ * idx_base) into pv/pi (ceil(n/2048) entries; pi may be null). */
+int oracle_tile_reduce_partials(const float* x, int64_t n, int32_t kind, int64_t idx_base,
+                                float* pv, int64_t* pi) {
+    if (kind < 0 || kind > 3 || n < 0) return E_ARG;
+    if (n > 0 && (!x || !pv)) return E_NULL;
+    rval* blk = (rval*)malloc(RED_CHUNK * sizeof(rval));
+    if (!blk) return E_ARG;
+    for (int64_t b = 0; b * RED_CHUNK < n; b++) {
+        for (int e = 0; e < RED_CHUNK; e++) {
+            const int64_t p = b * RED_CHUNK + e;
+            if (p < n) {
+                blk[e].v = x[p];
+                blk[e].i = idx_base + p;
+            } else {
+                blk[e] = red_id(kind);
+            }
+        }
+        const rval r = red_block(kind, blk);
+        pv[b] = r.v;
+        if (pi) pi[b] = r.i;
+    }
+    free(blk);
+    return 0;
+}
+/* The levels above: m partials (pv, pi) reduced to one value (index -1 for
+ * an empty ARGMAX). m = 1 is the result itself; m = 0 the identity. */
+int oracle_tile_reduce_levels(const float* pv, const int64_t* pi, int64_t m, int32_t kind,
+                              float* value, int64_t* index) {
+    if (kind < 0 || kind > 3 || m < 0 || !value) return E_ARG;
+    rval* cur = (rval*)malloc((size_t)(m > 0 ? m : 1) * sizeof(rval));
+    rval* blk = (rval*)malloc(RED_CHUNK * sizeof(rval));
+    if (!cur || !blk) {
+        free(cur);
+        free(blk);
+        return E_ARG;
+    }
+    for (int64_t e = 0; e < m; e++) {
+        cur[e].v = pv[e];
+        cur[e].i = pi ? pi[e] : 0;
+    }
+    rval r = red_id(kind);
+    if (m == 0) {
+        rval x[RED_CHUNK];
+        for (int e = 0; e < RED_CHUNK; e++) x[e] = red_id(kind);
+        r = red_block(kind, x);
+    }
+    while (m > 1) {
+        const int64_t nb = (m + RED_CHUNK - 1) / RED_CHUNK;
+        for (int64_t b = 0; b < nb; b++) {
+            for (int e = 0; e < RED_CHUNK; e++) {
+                const int64_t p = b * RED_CHUNK + e;
+                blk[e] = p < m ? cur[p] : red_id(kind);
+            }
+            cur[b] = red_block(kind, blk);
+        }
+        m = nb;
+    }
+    if (m == 1) r = cur[0];
+    free(cur);
+    free(blk);
+    if (kind == 0 && r.v != r.v) r.v = f_of(0x7fc00000u); /* NaN payloads differ by platform */
+    *value = r.v;
+    if (index) *index = (kind == 3 && r.i == NO_INDEX) ? -1 : r.i;
+    return 0;
+}
+int oracle_tile_reduce(const float* x, int64_t n, int32_t kind, int64_t idx_base, float* value,
+                       int64_t* index) {
+    if (kind < 0 || kind > 3 || n < 0 || !value) return E_ARG;
+    const int64_t m = (n + RED_CHUNK - 1) / RED_CHUNK;
+    float* pv = (float*)malloc((size_t)(m > 0 ? m : 1) * sizeof(float));
+    int64_t* pi = (int64_t*)malloc((size_t)(m > 0 ? m : 1) * sizeof(int64_t));
+    int rc = (pv && pi) ? oracle_tile_reduce_partials(x, n, kind, idx_base, pv, pi) : E_ARG;
+    if (!rc) rc = oracle_tile_reduce_levels(pv, pi, m, kind, value, index);
+    free(pv);
+    free(pi);
+    return rc;
+}

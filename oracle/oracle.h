@@ -108,6 +108,18 @@ typedef struct oracle_tile_node {
 int oracle_tile_eval(const oracle_tile_node* nodes, int32_t n_nodes, int32_t root,
                      float* out, int32_t n, int32_t halo);
 
+/* ---- tile reductions ----------------------------------------------------
+ * No counterpart in the reference: the library's own SUM (0), MIN (1),
+ * MAX (2) and ARGMAX (3) over n values x (index of x[0] = idx_base), in the
+ * tree include/simtgo_b200.h states. _partials gives the first level (one
+ * entry per block of 2048 values), _levels the rest. */
+int oracle_tile_reduce(const float* x, int64_t n, int32_t kind, int64_t idx_base, float* value,
+                       int64_t* index);
+int oracle_tile_reduce_partials(const float* x, int64_t n, int32_t kind, int64_t idx_base,
+                                float* pv, int64_t* pi);
+int oracle_tile_reduce_levels(const float* pv, const int64_t* pi, int64_t m, int32_t kind,
+                              float* value, int64_t* index);
+
 #ifdef __cplusplus
 }
 #endif

@@ -86,6 +86,12 @@ _SIGS = {
     "simtgo_tile_run": [_vp, _i32, _vp, _i32, _vp],
     "simtgo_tile_run_shard": [_vp, _i32, _vp, _i32, _i32, _vp],
     "simtgo_tile_run_stepwise_noalloc": [_vp, _i32, _vp, _i32, _vp],
+    "simtgo_tile_reduce": [_vp, _i32, _i32, _vp, _vp, _vp],
+    "simtgo_tile_reduce_materialize": [_vp, _i32, _i32, C.POINTER(C.c_float),
+                                       C.POINTER(C.c_int64)],
+    "simtgo_tile_shard_range": [C.c_int64, _i32, _i32, C.POINTER(C.c_int64),
+                                C.POINTER(C.c_int64)],
+    "simtgo_tile_reduce_shard": [_vp, _i32, _i32, _i32, C.c_int64, _vp, _vp, _vp, _vp],
 }
 _RESTYPES = {
     "simtgo_last_error": C.c_char_p,

@@ -233,6 +233,23 @@ void p2p_release(simtgo_comm* c) {
 
 }  // namespace
 
+namespace sg {
+// The communicator's size and this process's rank.
+int comm_rank(const simtgo_comm* c, int* nranks, int* rank) {
+    if (!c) return sg::fail(SIMTGO_ECOMM, "null communicator");
+    *nranks = c->nranks;
+    *rank = c->rank;
+    return 0;
+}
+// NCCL all-gather of `bytes` bytes from every rank into recv (rank order).
+int comm_allgather(simtgo_comm* c, const void* send, void* recv, size_t bytes, cudaStream_t s) {
+    int rc;
+    if ((rc = need_nccl())) return rc;
+    return nccl_status(g_nccl.AllGather(send, recv, bytes, ncclUint8, c->comm, s),
+                       "ncclAllGather");
+}
+}  // namespace sg
+
 extern "C" {
 
 int simtgo_comm_unique_id(uint8_t out_id[128]) {

@@ -118,8 +118,13 @@ struct FirDesc {
     float h[kMaxTaps];  // the coefficients travel in the parameter block
 };
 
+// Reductions (SIMTGO_TILE_SUM ..): the main program's value is reduced
+// instead of stored.
+enum Reduce : int32_t { RED_NONE = -1, RED_SUM = 0, RED_MIN = 1, RED_MAX = 2, RED_ARGMAX = 3 };
+
 struct Program {
     int32_t main_start;
+    int32_t reduce;  // RED_NONE, or the reduction of the main program's value
     int32_t n_fir;
     int32_t n_in;
     int32_t n_code;
@@ -268,16 +273,17 @@ __device__ __forceinline__ float4 mask_outside(float4 v, int64_t p, const Ctx& c
     return make_float4(f[0], f[1], f[2], f[3]);
 }
 
-// Runs the program from pc until an instruction with F_END. Inlined into
+// Runs the program from pc until an instruction with F_END, leaving the
+// last value in A (which a reduction consumes). Inlined into
 // k_tile twice: FULL for runs where all of the thread's groups take part
 // (the chunk), and the general form for a window's head run. (Loading the
 // next instruction ahead measured slower: it costs more instructions than
 // the shared-load latency it hides.) In DIRECT mode (BULK false) an input
 // operand is read from HBM at the run's positions.
 template <bool BULK, bool FULL>
-__device__ __forceinline__ void interpret(const Insn* code, int pc, const Ctx& c, const Run& r) {
+__device__ __forceinline__ void interpret(const Insn* code, int pc, const Ctx& c, const Run& r,
+                                          float4 (&A)[kG]) {
     const int t = threadIdx.x;
-    float4 A[kG];
 #pragma unroll
     for (int k = 0; k < kG; k++) A[k] = make_float4(0.f, 0.f, 0.f, 0.f);
     for (;;) {
@@ -359,6 +365,183 @@ __device__ __forceinline__ void interpret(const Insn* code, int pc, const Ctx& c
     }
 }
 
+// ---- reductions ---------------------------------------------------------------
+// A value and, for ARGMAX, its index. The empty identity of ARGMAX is
+// (-inf, INT64_MAX): any element beats it. Every step is a template on the
+// reduction, so a chunk's reduction is straight-line code.
+struct RVal {
+    float v;
+    int64_t i;
+};
+constexpr int64_t kNoIndex = INT64_MAX;
+constexpr uint32_t kQNaN = 0x7fc00000u;
+
+template <int KIND>
+__device__ __forceinline__ RVal red_identity() {
+    if (KIND == RED_SUM) return {0.0f, 0};
+    if (KIND == RED_MIN) return {__int_as_float(0x7f800000), 0};
+    return {__int_as_float((int)0xff800000u), kNoIndex};
+}
+// Go's min and max (NaN wins, -0 < +0); NaN is returned as 0x7fc00000.
+__device__ __forceinline__ float go_min(float a, float b) {
+    if (a != a || b != b) return __uint_as_float(kQNaN);
+    if (a < b) return a;
+    if (b < a) return b;
+    return (__float_as_uint(a) & 0x80000000u) ? a : b;
+}
+__device__ __forceinline__ float go_max(float a, float b) {
+    if (a != a || b != b) return __uint_as_float(kQNaN);
+    if (a > b) return a;
+    if (b > a) return b;
+    return (__float_as_uint(a) & 0x80000000u) ? b : a;
+}
+// ARGMAX order: NaN above everything, then value (+0 above -0), then the
+// smaller index. A strict total order on distinct indices, so any tree of
+// pairwise choices finds the same element.
+__device__ __forceinline__ bool am_before(const RVal& a, const RVal& b) {
+    const bool na = a.v != a.v, nb = b.v != b.v;
+    if (na || nb) return na && nb ? a.i < b.i : na;
+    if (a.v > b.v) return true;
+    if (b.v > a.v) return false;
+    const bool sa = __float_as_uint(a.v) >> 31, sb = __float_as_uint(b.v) >> 31;
+    if (sa != sb) return !sa;
+    return a.i < b.i;
+}
+template <int KIND>
+__device__ __forceinline__ RVal red2(const RVal& a, const RVal& b) {
+    if (KIND == RED_SUM) return {__fadd_rn(a.v, b.v), 0};
+    if (KIND == RED_MIN) return {go_min(a.v, b.v), 0};
+    if (KIND == RED_MAX) return {go_max(a.v, b.v), 0};
+    return am_before(a, b) ? a : b;
+}
+// The caller's result: a NaN sum as 0x7fc00000 (NaN payloads differ by
+// platform), ARGMAX's empty index as -1.
+template <int KIND>
+__device__ __forceinline__ RVal red_final(RVal r) {
+    if (KIND == RED_SUM && r.v != r.v) r.v = __uint_as_float(kQNaN);
+    if (KIND == RED_ARGMAX && r.i == kNoIndex) r.i = -1;
+    return r;
+}
+// A thread's eight values: x[0..3] its group at 4t, x[4..7] at 1024 + 4t.
+template <int KIND>
+__device__ __forceinline__ RVal red_thread(const RVal (&x)[8]) {
+    return red2<KIND>(red2<KIND>(red2<KIND>(x[0], x[1]), red2<KIND>(x[2], x[3])),
+                      red2<KIND>(red2<KIND>(x[4], x[5]), red2<KIND>(x[6], x[7])));
+}
+// Butterfly over the warp: every lane ends with the same value (each step
+// combines a commutative pair).
+template <int KIND>
+__device__ __forceinline__ RVal red_warp(RVal v) {
+#pragma unroll
+    for (int m = 16; m >= 1; m >>= 1) {
+        RVal o;
+        o.v = __shfl_xor_sync(0xffffffffu, v.v, m);
+        o.i = KIND == RED_ARGMAX ? __shfl_xor_sync(0xffffffffu, v.i, m) : 0;
+        v = red2<KIND>(v, o);
+    }
+    return v;
+}
+// The eight warps of a block, as ((w0 w1)(w2 w3))((w4 w5)(w6 w7)).
+template <int KIND>
+__device__ __forceinline__ RVal red_block8(const float* wv, const int64_t* wi) {
+    RVal w[8];
+#pragma unroll
+    for (int k = 0; k < 8; k++) w[k] = {wv[k], KIND == RED_ARGMAX ? wi[k] : 0};
+    return red2<KIND>(red2<KIND>(red2<KIND>(w[0], w[1]), red2<KIND>(w[2], w[3])),
+                      red2<KIND>(red2<KIND>(w[4], w[5]), red2<KIND>(w[6], w[7])));
+}
+static_assert(kThreads == 256 && kG == 2, "the reduction tree assumes 8 warps of 2 x float4");
+
+// A chunk's warp partials into wv/wi: A holds the values at positions
+// cb + 4 (t + 256 k) + j; positions >= n take the identity.
+template <int KIND>
+__device__ __forceinline__ void chunk_warps(const float4 (&A)[kG], int64_t cb, int64_t n,
+                                            int64_t idx_base, float* wv, int64_t* wi) {
+    const int t = threadIdx.x;
+    const bool full = cb + kChunk <= n;
+    RVal x[8];
+#pragma unroll
+    for (int k = 0; k < kG; k++)
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            const int64_t p = cb + 4 * (t + kThreads * k) + e;
+            x[4 * k + e] = (full || p < n)
+                               ? RVal{f4_get(A[k], e), KIND == RED_ARGMAX ? idx_base + p : 0}
+                               : red_identity<KIND>();
+        }
+    const RVal w = red_warp<KIND>(red_thread<KIND>(x));
+    if ((t & 31) == 0) {
+        wv[t >> 5] = w.v;
+        if (KIND == RED_ARGMAX) wi[t >> 5] = w.i;
+    }
+}
+// The chunk's partial from its warps' into out[c] (and out_idx[c]); `only`:
+// the launch's sole chunk, whose partial is the caller's result.
+template <int KIND>
+__device__ __forceinline__ void chunk_block(const float* wv, const int64_t* wi, float* out,
+                                            int64_t* out_idx, int64_t c, bool only) {
+    RVal b = red_block8<KIND>(wv, wi);
+    if (only) b = red_final<KIND>(b);
+    out[c] = b.v;
+    if (KIND == RED_ARGMAX) out_idx[c] = b.i;
+}
+
+// One level of the reduction tree over m partials (value, index): block b
+// reduces partials [kChunk b, kChunk b + kChunk) with the tree above into
+// ov[b] (and oi[b]). With m = 0 one block writes the identity. `last`: the
+// caller's result (red_final).
+template <int KIND>
+__global__ void __launch_bounds__(kThreads) k_red_level(const float* __restrict__ v,
+                                                        const int64_t* __restrict__ vi, int64_t m,
+                                                        float* ov, int64_t* oi, bool last) {
+    __shared__ float wv[8];
+    __shared__ int64_t wi[8];
+    const int t = threadIdx.x;
+    if (m == 1) {  // one partial is the result itself (no identity added)
+        if (blockIdx.x == 0 && t == 0) {
+            RVal b = {v[0], KIND == RED_ARGMAX ? vi[0] : 0};
+            if (last) b = red_final<KIND>(b);
+            ov[0] = b.v;
+            if (KIND == RED_ARGMAX) oi[0] = b.i;
+        }
+        return;
+    }
+    const int64_t base = (int64_t)blockIdx.x * kChunk;
+    RVal x[8];
+#pragma unroll
+    for (int k = 0; k < kG; k++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int64_t e = base + 4 * (t + kThreads * k) + j;
+            x[4 * k + j] =
+                e < m ? RVal{v[e], KIND == RED_ARGMAX ? vi[e] : 0} : red_identity<KIND>();
+        }
+    const RVal r = red_warp<KIND>(red_thread<KIND>(x));
+    if ((t & 31) == 0) {
+        wv[t >> 5] = r.v;
+        wi[t >> 5] = r.i;
+    }
+    __syncthreads();
+    if (t == 0) {
+        RVal b = red_block8<KIND>(wv, wi);
+        if (last) b = red_final<KIND>(b);
+        ov[blockIdx.x] = b.v;
+        if (KIND == RED_ARGMAX) oi[blockIdx.x] = b.i;
+    }
+}
+
+// Partials [from, to) set to the identity (a rank's slots past its own
+// chunks in the sharded reduction's all-gather).
+template <int KIND>
+__global__ void k_red_fill(float* v, int64_t* vi, int64_t from, int64_t to) {
+    const RVal id = red_identity<KIND>();
+    for (int64_t e = from + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < to;
+         e += (int64_t)gridDim.x * blockDim.x) {
+        v[e] = id.v;
+        if (vi) vi[e] = id.i;
+    }
+}
+
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,
                                          uint64_t* bar) {
     asm volatile(
@@ -402,12 +585,21 @@ __device__ __forceinline__ ChunkSpan chunk_span(int64_t cb, int hs, int64_t n, i
 // per-stage mbarriers, so nst-1 chunks stream in while one is interpreted.
 // Requires every input 16-byte aligned and halo = 0 mod 4. Otherwise
 // (DIRECT) the interpreter reads input operands from HBM itself.
+//
+// A reduction (P.reduce) writes no output array: each chunk's values are
+// reduced (red_thread, red_warp, red_block8) into out[c] and, for ARGMAX,
+// out_idx[c], c the chunk's index in the launch; idx_base + p is the index
+// of position p.
 template <bool BULK>
 __global__ void __launch_bounds__(kThreads, 3) k_tile(const __grid_constant__ Program P,
                                                    float* __restrict__ out, int64_t n,
                                                    int64_t halo, bool vec, bool in_vec, int32_t hs,
-                                                   int32_t stages4, int32_t nst, uint32_t* wd) {
+                                                   int32_t stages4, int32_t nst, uint32_t* wd,
+                                                   int64_t* __restrict__ out_idx,
+                                                   int64_t idx_base) {
     __shared__ __align__(8) uint64_t bars[kMaxStages];
+    __shared__ float red_v[2][8];  // warp results, by chunk parity
+    __shared__ int64_t red_i[2][8];
     extern __shared__ float4 sm4[];
     const int code_cap = meta_code_cap(P.n_code);
     Insn* code_s = reinterpret_cast<Insn*>(sm4);
@@ -462,6 +654,7 @@ __global__ void __launch_bounds__(kThreads, 3) k_tile(const __grid_constant__ Pr
     cx.vec = vec;
     cx.in_vec = in_vec;
     const int nf = P.n_fir;
+    float4 A[kG];  // the last run's values (the main program's, for a reduction)
     int it = 0;
     for (int64_t c = c0; c < c1; c++, it++) {
         const int64_t cb = c * kChunk;
@@ -481,12 +674,14 @@ __global__ void __launch_bounds__(kThreads, 3) k_tile(const __grid_constant__ Pr
             // The last 0-3 samples of a ragged signal are not a whole 16-byte
             // unit: plain loads.
             const int64_t tail = sp.hi - (sp.lo + sp.len4);
-            if (tail > 0 && tid < P.n_in * 4) {
-                const int k = tid / 4, e = tid % 4;
-                const int64_t pos = sp.lo + sp.len4 + e;
-                if (e < tail) buf[k * sstride + (pos - sp.org)] = in_s[k][pos];
+            if (tail > 0) {  // uniform over the block
+                if (tid < P.n_in * 4) {
+                    const int k = tid / 4, e = tid % 4;
+                    const int64_t pos = sp.lo + sp.len4 + e;
+                    if (e < tail) buf[k * sstride + (pos - sp.org)] = in_s[k][pos];
+                }
+                __syncthreads();
             }
-            __syncthreads();
         }
         const int32_t in4 = stages4 + s * stage_floats / 4;
         const bool edge = cb - (int64_t)hs < -halo || cb + kChunk > n;
@@ -529,10 +724,19 @@ __global__ void __launch_bounds__(kThreads, 3) k_tile(const __grid_constant__ Pr
             }
             r.edge = edge;
             if (r.gm == (1u << kG) - 1)
-                interpret<BULK, true>(code_s, pc, cx, r);
+                interpret<BULK, true>(code_s, pc, cx, r, A);
             else if (r.gm)
-                interpret<BULK, false>(code_s, pc, cx, r);
+                interpret<BULK, false>(code_s, pc, cx, r, A);
             if (j + 1 == 2 * nf) __syncthreads();  // windows staged before main reads them
+        }
+        switch (P.reduce) {  // uniform: one branch per chunk
+            case RED_SUM: chunk_warps<RED_SUM>(A, cb, n, idx_base, red_v[it & 1], red_i[it & 1]); break;
+            case RED_MIN: chunk_warps<RED_MIN>(A, cb, n, idx_base, red_v[it & 1], red_i[it & 1]); break;
+            case RED_MAX: chunk_warps<RED_MAX>(A, cb, n, idx_base, red_v[it & 1], red_i[it & 1]); break;
+            case RED_ARGMAX:
+                chunk_warps<RED_ARGMAX>(A, cb, n, idx_base, red_v[it & 1], red_i[it & 1]);
+                break;
+            default: break;
         }
         // Every thread is done with this stage (and with the tiles and
         // temporaries); order those generic accesses before the next bulk
@@ -540,6 +744,20 @@ __global__ void __launch_bounds__(kThreads, 3) k_tile(const __grid_constant__ Pr
         if (BULK) fence_proxy_async_smem();
         __syncthreads();
         if (BULK && tid == 0 && c + nst < c1) issue(c + nst, it % nst);
+        // The warps write red_v[it & 1] before the barrier above and next
+        // write it two chunks on, past the next chunk's barrier, which thread
+        // 0 reaches only after this read.
+        if (P.reduce != RED_NONE && tid == 0) {
+            const float* wv = red_v[it & 1];
+            const int64_t* wi = red_i[it & 1];
+            const bool only = nchunks == 1;
+            switch (P.reduce) {
+                case RED_SUM: chunk_block<RED_SUM>(wv, wi, out, out_idx, c, only); break;
+                case RED_MIN: chunk_block<RED_MIN>(wv, wi, out, out_idx, c, only); break;
+                case RED_MAX: chunk_block<RED_MAX>(wv, wi, out, out_idx, c, only); break;
+                default: chunk_block<RED_ARGMAX>(wv, wi, out, out_idx, c, only); break;
+            }
+        }
     }
 }
 
@@ -702,6 +920,7 @@ struct Lowered {
     std::vector<int> in_nodes;       // data input node ids, in input order
     std::vector<int> fir_nodes;      // window node ids, in window order
     std::vector<int> param_of;       // reference parameter index pK of each data input
+    int32_t reduce = tilek::RED_NONE;  // the main program's value is reduced, not stored
 };
 
 // Emits one program for the accumulator machine: a window's signal (ending
@@ -889,9 +1108,11 @@ struct Gen {
     }
 };
 
-// Lowers the graph rooted at root. Returns 0 or a status (message recorded).
-int lower(const simtgo_tile_graph* g, int root, Lowered& L) {
+// Lowers the graph rooted at root (its value reduced by `reduce` instead of
+// stored, unless RED_NONE). Returns 0 or a status (message recorded).
+int lower(const simtgo_tile_graph* g, int root, Lowered& L, int32_t reduce = tilek::RED_NONE) {
     L = Lowered();
+    L.reduce = reduce;
     // The reference's parameter numbering: every input node, taps included,
     // in postorder (tile/codegen.go:24-35).
     {
@@ -939,7 +1160,7 @@ int lower(const simtgo_tile_graph* g, int root, Lowered& L) {
             }
         }
         gen.emit(root);
-        gen.push(tilek::OP_STORE);
+        if (reduce == tilek::RED_NONE) gen.push(tilek::OP_STORE);
         gen.push(tilek::OP_END);
         fuse(gen.raw, L.code);
         status = gen.status;
@@ -966,6 +1187,7 @@ void build_program(const simtgo_tile_graph* g, const Lowered& L, const Layout& Y
                    tilek::Program& P) {
     memset(&P, 0, sizeof P);
     P.main_start = L.main_start;
+    P.reduce = L.reduce;
     P.n_fir = (int32_t)L.fir_nodes.size();
     P.n_in = (int32_t)L.in_nodes.size();
     P.n_code = (int32_t)L.code.size();
@@ -1024,9 +1246,11 @@ void build_program(const simtgo_tile_graph* g, const Lowered& L, const Layout& Y
 
 // Launches a lowered program. dev_in[k] = device data of L.in_nodes[k] (halo
 // elements first).
+// For a reduction, out (and out_idx, ARGMAX) receive one partial per chunk
+// and idx_base is the index of element 0.
 int launch_program(const simtgo_tile_graph* g, const Lowered& L,
                    const std::vector<const float*>& dev_in, float* out, int64_t n, int64_t halo,
-                   cudaStream_t s) {
+                   cudaStream_t s, int64_t* out_idx = nullptr, int64_t idx_base = 0) {
     const sg::DevInfo* d;
     int rc;
     if ((rc = sg::current_device(&d))) return rc;
@@ -1118,7 +1342,8 @@ int launch_program(const simtgo_tile_graph* g, const Lowered& L,
         1, std::min<int64_t>(chunks, (int64_t)d->sms * std::max(1, per_sm) * 8));
     sg::before_launch();
     kern<<<blocks, tilek::kThreads, Y.smem, s>>>(P, out, n, halo, vec, in_aligned, hs, Y.stages4,
-                                                 Y.nst, sg::watchdog_device_ptr());
+                                                 Y.nst, sg::watchdog_device_ptr(), out_idx,
+                                                 idx_base);
     return sg::launch_status("tile");
 }
 
@@ -1184,7 +1409,125 @@ int run_fused(const simtgo_tile_graph* g, int root, float* out, int64_t n, int64
     return launch_program(g, L, dev_in, out, n, halo, s);
 }
 
+// ---- reductions ----------------------------------------------------------------
+
+// Stream-ordered device scratch, released on its stream when it goes out of
+// scope (after everything enqueued before).
+struct AsyncBuf {
+    void* p = nullptr;
+    cudaStream_t s = 0;
+    ~AsyncBuf() {
+        if (p) cudaFreeAsync(p, s);
+    }
+    int alloc(size_t bytes, cudaStream_t st) {
+        s = st;
+        return sg::cuda_status(cudaMallocAsync(&p, std::max<size_t>(bytes, 16), st),
+                               "cudaMallocAsync");
+    }
+};
+
+int64_t n_partials(int64_t n) { return (n + tilek::kChunk - 1) / tilek::kChunk; }
+// Entries the levels above m partials need (each level but the last).
+int64_t upper_slots(int64_t m) {
+    int64_t total = 0;
+    while (m > tilek::kChunk) {
+        m = n_partials(m);
+        total += m;
+    }
+    return total + 1;
+}
+
+// Reduces m partials (v, and vi for ARGMAX) into the caller's value (and
+// index): one k_red_level launch per level of the tree; uv/ui hold the
+// levels between.
+int red_level(int kind, unsigned blocks, const float* v, const int64_t* vi, int64_t m, float* ov,
+              int64_t* oi, bool last, cudaStream_t s) {
+    sg::before_launch();
+    switch (kind) {
+        case tilek::RED_SUM:
+            tilek::k_red_level<tilek::RED_SUM><<<blocks, tilek::kThreads, 0, s>>>(v, vi, m, ov, oi, last);
+            break;
+        case tilek::RED_MIN:
+            tilek::k_red_level<tilek::RED_MIN><<<blocks, tilek::kThreads, 0, s>>>(v, vi, m, ov, oi, last);
+            break;
+        case tilek::RED_MAX:
+            tilek::k_red_level<tilek::RED_MAX><<<blocks, tilek::kThreads, 0, s>>>(v, vi, m, ov, oi, last);
+            break;
+        default:
+            tilek::k_red_level<tilek::RED_ARGMAX><<<blocks, tilek::kThreads, 0, s>>>(v, vi, m, ov, oi,
+                                                                                     last);
+    }
+    return sg::launch_status("tile reduce");
+}
+
+int finish_levels(int kind, const float* v, const int64_t* vi, int64_t m, float* value,
+                  int64_t* index, cudaStream_t s, float* uv, int64_t* ui) {
+    const bool am = kind == tilek::RED_ARGMAX;
+    if (m <= 1) return red_level(kind, 1, v, vi, m, value, am ? index : nullptr, true, s);
+    while (m > 1) {
+        const int64_t nb = n_partials(m);
+        const bool last = nb == 1;
+        float* ov = last ? value : uv;
+        int64_t* oi = am ? (last ? index : ui) : nullptr;
+        if (int rc = red_level(kind, (unsigned)nb, v, vi, m, ov, oi, last, s)) return rc;
+        v = ov;
+        vi = oi;
+        uv += nb;
+        if (am) ui += nb;
+        m = nb;
+    }
+    return 0;
+}
+
+// The fused reduction of root over n elements (inputs resolved by
+// `resolve`, halo preceding samples) into value/index; idx_base is the
+// index of element 0.
+template <class Resolve>
+int reduce_fused(const simtgo_tile_graph* g, int root, int kind, int64_t n, int64_t halo,
+                 int64_t idx_base, cudaStream_t s, Resolve resolve, float* value, int64_t* index) {
+    const bool am = kind == tilek::RED_ARGMAX;
+    if (n == 0) return finish_levels(kind, nullptr, nullptr, 0, value, index, s, nullptr, nullptr);
+    Lowered L;
+    int rc = lower(g, root, L, kind);
+    if (rc) return rc;
+    std::vector<const float*> dev_in;
+    for (int id : L.in_nodes) {
+        const float* p = resolve(id);
+        if (!p) return sg::fail(SIMTGO_EARG, "tile: input node %d has no device data", id);
+        dev_in.push_back(p);
+    }
+    const int64_t m = n_partials(n);
+    if (m == 1)  // one chunk: its partial is the result
+        return launch_program(g, L, dev_in, value, n, halo, s, am ? index : nullptr, idx_base);
+    const int64_t slots = m + upper_slots(m);
+    AsyncBuf bv, bi;
+    if ((rc = bv.alloc(slots * sizeof(float), s))) return rc;
+    if (am && (rc = bi.alloc(slots * sizeof(int64_t), s))) return rc;
+    float* pv = (float*)bv.p;
+    int64_t* pi = (int64_t*)bi.p;
+    if ((rc = launch_program(g, L, dev_in, pv, n, halo, s, pi, idx_base))) return rc;
+    return finish_levels(kind, pv, pi, m, value, index, s, pv + m, am ? pi + m : nullptr);
+}
+
+int check_reduce(simtgo_tile_graph* g, simtgo_tensor t, int32_t kind, const void* value,
+                 const void* index) {
+    if (!g) return sg::fail(SIMTGO_ENULL, "tile: null graph");
+    if (!g->err.empty()) return sg::fail(SIMTGO_EGRAPH, "%s", g->err.c_str());
+    if (!valid(g, t)) return sg::fail(SIMTGO_EARG, "tile: unknown tensor %d", t);
+    if (kind < tilek::RED_SUM || kind > tilek::RED_ARGMAX)
+        return sg::fail(SIMTGO_EARG, "tile: unknown reduction %d", kind);
+    if (!value) return sg::fail(SIMTGO_ENULL, "tile: null reduction value");
+    if (kind == tilek::RED_ARGMAX && !index)
+        return sg::fail(SIMTGO_ENULL, "tile: ARGMAX needs an index");
+    return 0;
+}
+
 }  // namespace
+
+namespace sg {
+int comm_rank(const simtgo_comm* c, int* nranks, int* rank);
+int comm_allgather(simtgo_comm* c, const void* send, void* recv, size_t bytes, cudaStream_t s);
+}  // namespace sg
 
 extern "C" {
 
@@ -1539,6 +1882,144 @@ int simtgo_tile_run_shard(simtgo_tile_graph* g, simtgo_tensor t, float* dev_out,
 int simtgo_tile_run(simtgo_tile_graph* g, simtgo_tensor t, float* dev_out, int32_t out_len,
                     void* stream) {
     return simtgo_tile_run_shard(g, t, dev_out, out_len, 0, stream);
+}
+
+int simtgo_tile_reduce(simtgo_tile_graph* g, simtgo_tensor t, int32_t kind, float* dev_value,
+                       int64_t* dev_index, void* stream) {
+    sg::clear_error();
+    int rc;
+    if ((rc = check_reduce(g, t, kind, dev_value, dev_index))) return rc;
+    const sg::DevInfo* d;
+    if ((rc = sg::current_device(&d))) return rc;
+    auto resolve = [&](int id) -> const float* { return g->nodes[id].dev; };
+    return reduce_fused(g, t, kind, g->nodes[t].n, 0, 0, (cudaStream_t)stream, resolve,
+                        dev_value, dev_index);
+}
+
+int simtgo_tile_reduce_materialize(simtgo_tile_graph* g, simtgo_tensor t, int32_t kind,
+                                   float* value, int64_t* index) {
+    sg::clear_error();
+    int rc;
+    if ((rc = check_reduce(g, t, kind, value, index))) return rc;
+    const sg::DevInfo* d;
+    if ((rc = sg::current_device(&d))) return rc;
+    std::vector<DevBuf> owned;
+    std::unordered_map<int, const float*> uploaded;
+    DevBuf res;
+    if ((rc = sg::cuda_status(cudaMalloc(&res.p, 16), "cudaMalloc"))) return rc;
+    int err = 0;
+    auto resolve = [&](int id) -> const float* {
+        const Node& nd = g->nodes[id];
+        if (nd.dev) return nd.dev;
+        auto it = uploaded.find(id);
+        if (it != uploaded.end()) return it->second;
+        owned.emplace_back();
+        if (int r = upload(nd.host, nd.n, owned.back())) {
+            err = r;
+            return nullptr;
+        }
+        uploaded[id] = owned.back().p;
+        return owned.back().p;
+    };
+    int64_t* res_i = reinterpret_cast<int64_t*>(res.p + 2);
+    rc = reduce_fused(g, t, kind, g->nodes[t].n, 0, 0, 0, resolve, res.p, res_i);
+    if (err) return err;
+    if (rc) return rc;
+    if ((rc = sg::cuda_status(cudaStreamSynchronize(0), "tile reduce"))) return rc;
+    if ((rc = sg::cuda_status(cudaMemcpy(value, res.p, sizeof(float), cudaMemcpyDeviceToHost),
+                              "download")))
+        return rc;
+    if (kind == tilek::RED_ARGMAX)
+        rc = sg::cuda_status(cudaMemcpy(index, res_i, sizeof(int64_t), cudaMemcpyDeviceToHost),
+                             "download");
+    return rc;
+}
+
+int simtgo_tile_shard_range(int64_t n_total, int32_t nranks, int32_t rank, int64_t* start,
+                            int64_t* len) {
+    sg::clear_error();
+    if (!start || !len) return sg::fail(SIMTGO_ENULL, "tile: null shard range output");
+    if (n_total < 0 || nranks < 1 || rank < 0 || rank >= nranks)
+        return sg::fail(SIMTGO_EARG, "tile: shard %d of %d over %lld elements", rank, nranks,
+                        (long long)n_total);
+    const int64_t per = n_partials((n_total + nranks - 1) / nranks) * tilek::kChunk;
+    *start = std::min<int64_t>((int64_t)rank * per, n_total);
+    *len = std::min<int64_t>(*start + per, n_total) - *start;
+    return 0;
+}
+
+int simtgo_tile_reduce_shard(simtgo_tile_graph* g, simtgo_tensor t, int32_t kind, int32_t halo,
+                             int64_t n_total, simtgo_comm* comm, float* dev_value,
+                             int64_t* dev_index, void* stream) {
+    sg::clear_error();
+    int rc;
+    if ((rc = check_reduce(g, t, kind, dev_value, dev_index))) return rc;
+    if (halo < 0) return sg::fail(SIMTGO_EARG, "tile: negative halo");
+    int nranks, rank;
+    if ((rc = sg::comm_rank(comm, &nranks, &rank))) return rc;
+    int64_t start, len;
+    if ((rc = simtgo_tile_shard_range(n_total, nranks, rank, &start, &len))) return rc;
+    if (g->nodes[t].n != len)
+        return sg::fail(SIMTGO_ELENGTH,
+                        "tile: rank %d of %d holds elements [%lld, %lld) of %lld, the tensor has %d",
+                        rank, nranks, (long long)start, (long long)(start + len),
+                        (long long)n_total, g->nodes[t].n);
+    const sg::DevInfo* d;
+    if ((rc = sg::current_device(&d))) return rc;
+    cudaStream_t s = (cudaStream_t)stream;
+    auto resolve = [&](int id) -> const float* { return g->nodes[id].dev; };
+    // Every rank takes the same steps: n_total, and so C, are the same on all.
+    if (n_total == 0 || nranks == 1)
+        return reduce_fused(g, t, kind, len, halo, start, s, resolve, dev_value, dev_index);
+    const bool am = kind == tilek::RED_ARGMAX;
+    int64_t s0, per;
+    if ((rc = simtgo_tile_shard_range(n_total, nranks, 0, &s0, &per))) return rc;
+    const int64_t C = per / tilek::kChunk;  // chunk slots per rank
+    const int64_t mine = n_partials(len);
+    const int64_t m = n_partials(n_total);
+    const int64_t slots = C + C * nranks + upper_slots(m);
+    AsyncBuf bv, bi;
+    if ((rc = bv.alloc(slots * sizeof(float), s))) return rc;
+    if (am && (rc = bi.alloc(slots * sizeof(int64_t), s))) return rc;
+    float* send_v = (float*)bv.p;
+    float* recv_v = send_v + C;
+    int64_t* send_i = am ? (int64_t*)bi.p : nullptr;
+    int64_t* recv_i = am ? send_i + C : nullptr;
+    if (len > 0) {
+        Lowered L;
+        if ((rc = lower(g, t, L, kind))) return rc;
+        std::vector<const float*> dev_in;
+        for (int id : L.in_nodes) {
+            const float* p = resolve(id);
+            if (!p) return sg::fail(SIMTGO_EARG, "tile: input node %d has no device data", id);
+            dev_in.push_back(p);
+        }
+        if ((rc = launch_program(g, L, dev_in, send_v, len, halo, s, send_i, start))) return rc;
+    }
+    if (mine < C) {
+        sg::before_launch();
+        switch (kind) {
+            case tilek::RED_SUM:
+                tilek::k_red_fill<tilek::RED_SUM><<<1, tilek::kThreads, 0, s>>>(send_v, send_i, mine, C);
+                break;
+            case tilek::RED_MIN:
+                tilek::k_red_fill<tilek::RED_MIN><<<1, tilek::kThreads, 0, s>>>(send_v, send_i, mine, C);
+                break;
+            case tilek::RED_MAX:
+                tilek::k_red_fill<tilek::RED_MAX><<<1, tilek::kThreads, 0, s>>>(send_v, send_i, mine, C);
+                break;
+            default:
+                tilek::k_red_fill<tilek::RED_ARGMAX><<<1, tilek::kThreads, 0, s>>>(send_v, send_i, mine,
+                                                                                  C);
+        }
+        if ((rc = sg::launch_status("tile reduce"))) return rc;
+    }
+    if ((rc = sg::comm_allgather(comm, send_v, recv_v, C * sizeof(float), s))) return rc;
+    if (am && (rc = sg::comm_allgather(comm, send_i, recv_i, C * sizeof(int64_t), s))) return rc;
+    // Ranks hold whole chunks in order, so the first m gathered slots are the
+    // partials of the whole signal's chunks.
+    return finish_levels(kind, recv_v, recv_i, m, dev_value, dev_index, s,
+                         recv_v + C * nranks, am ? recv_i + C * nranks : nullptr);
 }
 
 }  // extern "C"

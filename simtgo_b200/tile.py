@@ -10,6 +10,11 @@ this module only keeps the host arrays alive and spells the Go API:
 Device-resident values (the `dev` field of tile/tile.go:46):
     a = g.InputDevice(tensor)               # a CUDA float32 tensor
     out.Run(dev_out, stream)                 # no upload, no download
+
+Reductions (no counterpart in the reference, whose plan lists them as the
+tile track's next step), fused into the same single pass:
+    total = tile.Sum(tile.Mul(x, x)).Materialize()
+    i, v = tile.ArgMax(out).Materialize()
 """
 from __future__ import annotations
 
@@ -111,6 +116,72 @@ class Tensor:
                                               int(halo), sp))
 
 
+SUM, MIN, MAX, ARGMAX = 0, 1, 2, 3
+
+
+class Reduction:
+    """A tensor reduced to one value in the fused pass: Sum (float32, in the
+    library's fixed tree order), Min and Max (Go's min/max: NaN wins, -0 <
+    +0), ArgMax (the first index of the maximum, with the maximum)."""
+
+    def __init__(self, t: Tensor, kind: int):
+        self.t = t
+        self.kind = kind
+
+    def Materialize(self):
+        """Host inputs uploaded, one fused kernel: the value, or for ArgMax
+        (index, value)."""
+        v, i = C.c_float(), C.c_int64()
+        check(self.t.g._L.simtgo_tile_reduce_materialize(self.t.g._h, self.t.node, self.kind,
+                                                         C.byref(v), C.byref(i)))
+        val = np.float32(v.value)
+        return (i.value, val) if self.kind == ARGMAX else val
+
+    def Run(self, dev_value, dev_index=None, stream=None):
+        """Device-resident: dev_value (a CUDA float32 tensor of >= 1
+        element) and, for ArgMax, dev_index (CUDA int64); asynchronous."""
+        sp = getattr(stream, "cuda_stream", stream)
+        di = C.c_void_p(dev_index.data_ptr()) if dev_index is not None else None
+        check(self.t.g._L.simtgo_tile_reduce(self.t.g._h, self.t.node, self.kind,
+                                             C.c_void_p(dev_value.data_ptr()), di, sp))
+
+    def RunShard(self, comm, n_total: int, dev_value, dev_index=None, halo: int = 0,
+                 stream=None):
+        """This rank's part of the reduction of a signal sharded as
+        ShardRange(n_total, nranks, rank) says (a collective over comm, a
+        simtgo_comm handle): every rank gets the whole signal's result."""
+        sp = getattr(stream, "cuda_stream", stream)
+        di = C.c_void_p(dev_index.data_ptr()) if dev_index is not None else None
+        check(self.t.g._L.simtgo_tile_reduce_shard(self.t.g._h, self.t.node, self.kind, int(halo),
+                                                   int(n_total), comm,
+                                                   C.c_void_p(dev_value.data_ptr()), di, sp))
+
+
+def Sum(t: Tensor) -> Reduction:
+    return Reduction(t, SUM)
+
+
+def Min(t: Tensor) -> Reduction:
+    return Reduction(t, MIN)
+
+
+def Max(t: Tensor) -> Reduction:
+    return Reduction(t, MAX)
+
+
+def ArgMax(t: Tensor) -> Reduction:
+    return Reduction(t, ARGMAX)
+
+
+def ShardRange(n_total: int, nranks: int, rank: int):
+    """(start, length) of rank's shard for Reduction.RunShard: whole blocks
+    of 2048, the last ranks possibly empty."""
+    s, n = C.c_int64(), C.c_int64()
+    check(_lib.load().simtgo_tile_shard_range(int(n_total), int(nranks), int(rank), C.byref(s),
+                                              C.byref(n)))
+    return s.value, n.value
+
+
 def New() -> Graph:
     return Graph()
 
@@ -151,4 +222,5 @@ def _same(a: Tensor, b: Tensor) -> int:
 
 
 __all__ = ["New", "Graph", "Tensor", "Add", "Mul", "Hypot", "Scale", "Sqrt", "Abs", "FIR",
-           "BlockSize", "MaxTaps"]
+           "BlockSize", "MaxTaps", "Reduction", "Sum", "Min", "Max", "ArgMax", "ShardRange",
+           "SUM", "MIN", "MAX", "ARGMAX"]

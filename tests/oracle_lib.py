@@ -265,6 +265,41 @@ def tile_eval(nodes, root, n, halo=0):
     return rc, out
 
 
+TILE_REDUCE = {"sum": 0, "min": 1, "max": 2, "argmax": 3}
+
+
+def tile_reduce(x, kind, idx_base=0):
+    """(value, index) of the library's tile reduction `kind` over x."""
+    x = np.ascontiguousarray(x, np.float32)
+    v, i = C.c_float(), C.c_int64()
+    rc = oracle().oracle_tile_reduce(_ptr(x, _f32p), _i64(len(x)), _i32(TILE_REDUCE[kind]),
+                                     _i64(idx_base), C.byref(v), C.byref(i))
+    assert rc == 0, rc
+    return np.float32(v.value), i.value
+
+
+def tile_reduce_partials(x, kind, idx_base=0):
+    """The first level: one (value, index) per block of 2048."""
+    x = np.ascontiguousarray(x, np.float32)
+    m = (len(x) + 2047) // 2048
+    pv, pi = np.zeros(max(m, 1), np.float32), np.zeros(max(m, 1), np.int64)
+    rc = oracle().oracle_tile_reduce_partials(_ptr(x, _f32p), _i64(len(x)),
+                                              _i32(TILE_REDUCE[kind]), _i64(idx_base),
+                                              _ptr(pv, _f32p), _ptr(pi, _i64p))
+    assert rc == 0, rc
+    return pv[:m], pi[:m]
+
+
+def tile_reduce_levels(pv, pi, kind):
+    pv = np.ascontiguousarray(pv, np.float32)
+    pi = np.ascontiguousarray(pi, np.int64)
+    v, i = C.c_float(), C.c_int64()
+    rc = oracle().oracle_tile_reduce_levels(_ptr(pv, _f32p), _ptr(pi, _i64p), _i64(len(pv)),
+                                            _i32(TILE_REDUCE[kind]), C.byref(v), C.byref(i))
+    assert rc == 0, rc
+    return np.float32(v.value), i.value
+
+
 # ---- the reference's kernels built for the host (pinning only) -------------
 
 def ref_call(name, *args):

@@ -23,6 +23,14 @@ def _whole():
     return np.random.default_rng(77).integers(-5, 300, TOTAL, dtype=np.int32)
 
 
+def _whole_f32():
+    return np.random.default_rng(78).standard_normal(TOTAL).astype(np.float32)
+
+
+def _taps():
+    return (np.arange(1, 12, dtype=np.float32) / 40).astype(np.float32)
+
+
 def _child(rank, uid, mode, q, bar):
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     try:
@@ -48,6 +56,22 @@ def _child(rank, uid, mode, q, bar):
                                                 xs.numel(), None))
                     _lib.check(L.simtgo_stream_sync(None))
                     out[(name, call)] = b.cpu().numpy()
+        elif mode == "reduce":  # the tile reductions over shards with a halo
+            from simtgo_b200 import tile
+
+            xf = _whole_f32()
+            start, ln = tile.ShardRange(TOTAL, WORLD, rank)
+            halo = min(start, 16)
+            buf = t.from_numpy(xf[start - halo:start + ln].copy()).cuda()
+            g = tile.New()
+            a = g.InputDevice(buf[halo:])
+            y = tile.Add(tile.FIR(a, _taps()), tile.Abs(a))
+            for kind in (tile.SUM, tile.MIN, tile.MAX, tile.ARGMAX):
+                v = t.zeros(1, device="cuda")
+                i = t.zeros(1, dtype=t.int64, device="cuda")
+                tile.Reduction(y, kind).RunShard(comm, TOTAL, v, i, halo=halo)
+                t.cuda.synchronize()
+                out[kind] = (float(v.item()), int(i.item()))
         else:  # "absent": rank 1 maps the buffers, then skips the second call
             b = t.zeros(256, dtype=t.int32, device="cuda")
             _lib.check(L.simtgo_Histogram_allreduce_fused(comm, P(b.data_ptr()), 256,
@@ -124,3 +148,27 @@ def test_absent_rank_times_out_with_a_status():
     assert res[0]["status"] == _lib.EDEVICE, res[0]
     assert "watchdog" in res[0]["msg"]
     assert res[0]["after"] == 4
+
+
+def test_tile_reduce_shards_equal_the_whole():
+    """Each rank reduces its shard (FIR over a 16-sample halo); after the
+    all-gather of the block partials every rank holds the whole signal's
+    result, bit for bit as the oracle's tree over the whole signal."""
+    import oracle_lib as O
+
+    res = _run("reduce")
+    x = _whole_f32()
+    h = _taps()
+    nodes = [{"kind": "input", "data": x}, {"kind": "input", "data": h},
+             {"kind": "fir", "a": 0, "taps": h}, {"kind": "abs", "a": 0},
+             {"kind": "add", "a": 2, "b": 3}]
+    rc, vals = O.tile_eval(nodes, 4, TOTAL, 0)
+    assert rc == 0
+    for kind, name in enumerate(("sum", "min", "max", "argmax")):
+        wv, wi = O.tile_reduce(vals, name)
+        for rank in range(WORLD):
+            gv, gi = res[rank][kind]
+            assert np.float32(gv).view(np.uint32) == np.float32(wv).view(np.uint32), \
+                (name, rank, gv, wv)
+            if name == "argmax":
+                assert gi == wi, (rank, gi, wi)
