@@ -452,8 +452,9 @@ __device__ __forceinline__ RVal red_block8(const float* wv, const int64_t* wi) {
 }
 static_assert(kThreads == 256 && kG == 2, "the reduction tree assumes 8 warps of 2 x float4");
 
-// A chunk's warp partials into wv/wi: A holds the values at positions
-// cb + 4 (t + 256 k) + j; positions >= n take the identity.
+// A chunk's warp partials into wv[warp] (and wi[warp]): A holds the
+// values at positions cb + 4 (t + 256 k) + j; positions >= n take the
+// identity.
 template <int KIND>
 __device__ __forceinline__ void chunk_warps(const float4 (&A)[kG], int64_t cb, int64_t n,
                                             int64_t idx_base, float* wv, int64_t* wi) {
@@ -475,31 +476,31 @@ __device__ __forceinline__ void chunk_warps(const float4 (&A)[kG], int64_t cb, i
         if (KIND == RED_ARGMAX) wi[t >> 5] = w.i;
     }
 }
-// The chunk's partial from its warps' into out[c] (and out_idx[c]); `only`:
-// the launch's sole chunk, whose partial is the caller's result.
+// Partial e of a level: entry e itself, or (warps8, the first level) the
+// eight warp partials of chunk e combined.
 template <int KIND>
-__device__ __forceinline__ void chunk_block(const float* wv, const int64_t* wi, float* out,
-                                            int64_t* out_idx, int64_t c, bool only) {
-    RVal b = red_block8<KIND>(wv, wi);
-    if (only) b = red_final<KIND>(b);
-    out[c] = b.v;
-    if (KIND == RED_ARGMAX) out_idx[c] = b.i;
+__device__ __forceinline__ RVal red_entry(const float* v, const int64_t* vi, int64_t e,
+                                          bool warps8) {
+    if (warps8) return red_block8<KIND>(v + 8 * e, KIND == RED_ARGMAX ? vi + 8 * e : nullptr);
+    return {v[e], KIND == RED_ARGMAX ? vi[e] : 0};
 }
 
 // One level of the reduction tree over m partials (value, index): block b
 // reduces partials [kChunk b, kChunk b + kChunk) with the tree above into
-// ov[b] (and oi[b]). With m = 0 one block writes the identity. `last`: the
-// caller's result (red_final).
+// ov[b] (and oi[b]). With m = 0 one block writes the identity; with m = 1
+// the partial is the result itself. `last`: the caller's result
+// (red_final).
 template <int KIND>
 __global__ void __launch_bounds__(kThreads) k_red_level(const float* __restrict__ v,
                                                         const int64_t* __restrict__ vi, int64_t m,
-                                                        float* ov, int64_t* oi, bool last) {
+                                                        float* ov, int64_t* oi, bool last,
+                                                        bool warps8) {
     __shared__ float wv[8];
     __shared__ int64_t wi[8];
     const int t = threadIdx.x;
-    if (m == 1) {  // one partial is the result itself (no identity added)
+    if (m == 1) {  // no identity is added to a lone partial
         if (blockIdx.x == 0 && t == 0) {
-            RVal b = {v[0], KIND == RED_ARGMAX ? vi[0] : 0};
+            RVal b = red_entry<KIND>(v, vi, 0, warps8);
             if (last) b = red_final<KIND>(b);
             ov[0] = b.v;
             if (KIND == RED_ARGMAX) oi[0] = b.i;
@@ -513,8 +514,7 @@ __global__ void __launch_bounds__(kThreads) k_red_level(const float* __restrict_
 #pragma unroll
         for (int j = 0; j < 4; j++) {
             const int64_t e = base + 4 * (t + kThreads * k) + j;
-            x[4 * k + j] =
-                e < m ? RVal{v[e], KIND == RED_ARGMAX ? vi[e] : 0} : red_identity<KIND>();
+            x[4 * k + j] = e < m ? red_entry<KIND>(v, vi, e, warps8) : red_identity<KIND>();
         }
     const RVal r = red_warp<KIND>(red_thread<KIND>(x));
     if ((t & 31) == 0) {
@@ -586,10 +586,16 @@ __device__ __forceinline__ ChunkSpan chunk_span(int64_t cb, int hs, int64_t n, i
 // Requires every input 16-byte aligned and halo = 0 mod 4. Otherwise
 // (DIRECT) the interpreter reads input operands from HBM itself.
 //
-// A reduction (P.reduce) writes no output array: each chunk's values are
-// reduced (red_thread, red_warp, red_block8) into out[c] and, for ARGMAX,
-// out_idx[c], c the chunk's index in the launch; idx_base + p is the index
-// of position p.
+// A reduction (P.reduce) writes no output array: each warp's values of
+// chunk c (its index in the launch) are reduced (red_thread, red_warp) into
+// out[8 c + warp] and, for ARGMAX, out_idx[8 c + warp]; idx_base + p is the
+// index of position p. The level kernels combine the eight warps.
+//
+// A graph without windows has no shared value that one thread writes and
+// another reads (temporaries and staged operands are per thread): its warps
+// run ahead of each other, and the last of the eight warps to finish with a
+// stage (a shared counter per stage) refills it, instead of thread 0 after a
+// block barrier.
 template <bool BULK>
 __global__ void __launch_bounds__(kThreads, 3) k_tile(const __grid_constant__ Program P,
                                                    float* __restrict__ out, int64_t n,
@@ -597,9 +603,8 @@ __global__ void __launch_bounds__(kThreads, 3) k_tile(const __grid_constant__ Pr
                                                    int32_t stages4, int32_t nst, uint32_t* wd,
                                                    int64_t* __restrict__ out_idx,
                                                    int64_t idx_base) {
-    __shared__ __align__(8) uint64_t bars[kMaxStages];
-    __shared__ float red_v[2][8];  // warp results, by chunk parity
-    __shared__ int64_t red_i[2][8];
+    __shared__ __align__(8) uint64_t bars[kMaxStages];   // stage s loaded
+    __shared__ int rel[kMaxStages];  // warps done with stage s (window-free graphs)
     extern __shared__ float4 sm4[];
     const int code_cap = meta_code_cap(P.n_code);
     Insn* code_s = reinterpret_cast<Insn*>(sm4);
@@ -633,7 +638,10 @@ __global__ void __launch_bounds__(kThreads, 3) k_tile(const __grid_constant__ Pr
     };
     if (BULK) {
         if (tid == 0) {
-            for (int s = 0; s < nst; s++) mbar_init(&bars[s], 1);
+            for (int s = 0; s < nst; s++) {
+                mbar_init(&bars[s], 1);
+                rel[s] = 0;
+            }
             fence_mbar_init();
         }
         __syncthreads();
@@ -654,6 +662,7 @@ __global__ void __launch_bounds__(kThreads, 3) k_tile(const __grid_constant__ Pr
     cx.vec = vec;
     cx.in_vec = in_vec;
     const int nf = P.n_fir;
+    const bool free_run = nf == 0;
     float4 A[kG];  // the last run's values (the main program's, for a reduction)
     int it = 0;
     for (int64_t c = c0; c < c1; c++, it++) {
@@ -729,34 +738,41 @@ __global__ void __launch_bounds__(kThreads, 3) k_tile(const __grid_constant__ Pr
                 interpret<BULK, false>(code_s, pc, cx, r, A);
             if (j + 1 == 2 * nf) __syncthreads();  // windows staged before main reads them
         }
-        switch (P.reduce) {  // uniform: one branch per chunk
-            case RED_SUM: chunk_warps<RED_SUM>(A, cb, n, idx_base, red_v[it & 1], red_i[it & 1]); break;
-            case RED_MIN: chunk_warps<RED_MIN>(A, cb, n, idx_base, red_v[it & 1], red_i[it & 1]); break;
-            case RED_MAX: chunk_warps<RED_MAX>(A, cb, n, idx_base, red_v[it & 1], red_i[it & 1]); break;
-            case RED_ARGMAX:
-                chunk_warps<RED_ARGMAX>(A, cb, n, idx_base, red_v[it & 1], red_i[it & 1]);
-                break;
-            default: break;
-        }
-        // Every thread is done with this stage (and with the tiles and
-        // temporaries); order those generic accesses before the next bulk
-        // copy into it.
-        if (BULK) fence_proxy_async_smem();
-        __syncthreads();
-        if (BULK && tid == 0 && c + nst < c1) issue(c + nst, it % nst);
-        // The warps write red_v[it & 1] before the barrier above and next
-        // write it two chunks on, past the next chunk's barrier, which thread
-        // 0 reaches only after this read.
-        if (P.reduce != RED_NONE && tid == 0) {
-            const float* wv = red_v[it & 1];
-            const int64_t* wi = red_i[it & 1];
-            const bool only = nchunks == 1;
-            switch (P.reduce) {
-                case RED_SUM: chunk_block<RED_SUM>(wv, wi, out, out_idx, c, only); break;
-                case RED_MIN: chunk_block<RED_MIN>(wv, wi, out, out_idx, c, only); break;
-                case RED_MAX: chunk_block<RED_MAX>(wv, wi, out, out_idx, c, only); break;
-                default: chunk_block<RED_ARGMAX>(wv, wi, out, out_idx, c, only); break;
+        if (P.reduce != RED_NONE) {
+            float* wv = out + 8 * c;
+            int64_t* wi = out_idx ? out_idx + 8 * c : nullptr;
+            switch (P.reduce) {  // uniform: one branch per chunk
+                case RED_SUM: chunk_warps<RED_SUM>(A, cb, n, idx_base, wv, wi); break;
+                case RED_MIN: chunk_warps<RED_MIN>(A, cb, n, idx_base, wv, wi); break;
+                case RED_MAX: chunk_warps<RED_MAX>(A, cb, n, idx_base, wv, wi); break;
+                default: chunk_warps<RED_ARGMAX>(A, cb, n, idx_base, wv, wi); break;
             }
+        }
+        if (BULK) {
+            // Every thread is done with this stage (and, with windows, with
+            // the tiles and temporaries); order its generic accesses before
+            // the next bulk copy into it.
+            fence_proxy_async_smem();
+            if (free_run) {
+                // The counter's read-modify-writes, fenced on both sides, order
+                // every warp's reads of the stage before the refill. The reset
+                // precedes the refill's arrive (a release), which every warp
+                // acquires before it counts this stage again.
+                __syncwarp();
+                if ((tid & 31) == 0) {
+                    __threadfence_block();
+                    if (atomicAdd(&rel[s], 1) == kThreads / 32 - 1) {
+                        __threadfence_block();
+                        rel[s] = 0;
+                        if (c + nst < c1) issue(c + nst, s);
+                    }
+                }
+            } else {
+                __syncthreads();
+                if (tid == 0 && c + nst < c1) issue(c + nst, s);
+            }
+        } else if (!free_run) {
+            __syncthreads();  // the tiles are rewritten by the next chunk
         }
     }
 }
@@ -1437,39 +1453,36 @@ int64_t upper_slots(int64_t m) {
     return total + 1;
 }
 
-// Reduces m partials (v, and vi for ARGMAX) into the caller's value (and
-// index): one k_red_level launch per level of the tree; uv/ui hold the
-// levels between.
+// Reduces m chunk partials (given as their warp partials: v, and vi for
+// ARGMAX) into the caller's value (and index): one k_red_level launch per
+// level of the tree; uv/ui hold the levels between.
 int red_level(int kind, unsigned blocks, const float* v, const int64_t* vi, int64_t m, float* ov,
-              int64_t* oi, bool last, cudaStream_t s) {
+              int64_t* oi, bool last, bool w8, cudaStream_t s) {
+    using namespace tilek;
     sg::before_launch();
     switch (kind) {
-        case tilek::RED_SUM:
-            tilek::k_red_level<tilek::RED_SUM><<<blocks, tilek::kThreads, 0, s>>>(v, vi, m, ov, oi, last);
-            break;
-        case tilek::RED_MIN:
-            tilek::k_red_level<tilek::RED_MIN><<<blocks, tilek::kThreads, 0, s>>>(v, vi, m, ov, oi, last);
-            break;
-        case tilek::RED_MAX:
-            tilek::k_red_level<tilek::RED_MAX><<<blocks, tilek::kThreads, 0, s>>>(v, vi, m, ov, oi, last);
-            break;
-        default:
-            tilek::k_red_level<tilek::RED_ARGMAX><<<blocks, tilek::kThreads, 0, s>>>(v, vi, m, ov, oi,
-                                                                                     last);
+        case RED_SUM: k_red_level<RED_SUM><<<blocks, kThreads, 0, s>>>(v, vi, m, ov, oi, last, w8); break;
+        case RED_MIN: k_red_level<RED_MIN><<<blocks, kThreads, 0, s>>>(v, vi, m, ov, oi, last, w8); break;
+        case RED_MAX: k_red_level<RED_MAX><<<blocks, kThreads, 0, s>>>(v, vi, m, ov, oi, last, w8); break;
+        default: k_red_level<RED_ARGMAX><<<blocks, kThreads, 0, s>>>(v, vi, m, ov, oi, last, w8);
     }
     return sg::launch_status("tile reduce");
 }
 
+// v/vi: the eight warp partials of each of m chunks (the interpreter's
+// output), 8 m entries.
 int finish_levels(int kind, const float* v, const int64_t* vi, int64_t m, float* value,
                   int64_t* index, cudaStream_t s, float* uv, int64_t* ui) {
     const bool am = kind == tilek::RED_ARGMAX;
-    if (m <= 1) return red_level(kind, 1, v, vi, m, value, am ? index : nullptr, true, s);
+    if (m <= 1) return red_level(kind, 1, v, vi, m, value, am ? index : nullptr, true, true, s);
+    bool w8 = true;
     while (m > 1) {
         const int64_t nb = n_partials(m);
         const bool last = nb == 1;
         float* ov = last ? value : uv;
         int64_t* oi = am ? (last ? index : ui) : nullptr;
-        if (int rc = red_level(kind, (unsigned)nb, v, vi, m, ov, oi, last, s)) return rc;
+        if (int rc = red_level(kind, (unsigned)nb, v, vi, m, ov, oi, last, w8, s)) return rc;
+        w8 = false;
         v = ov;
         vi = oi;
         uv += nb;
@@ -1497,16 +1510,15 @@ int reduce_fused(const simtgo_tile_graph* g, int root, int kind, int64_t n, int6
         dev_in.push_back(p);
     }
     const int64_t m = n_partials(n);
-    if (m == 1)  // one chunk: its partial is the result
-        return launch_program(g, L, dev_in, value, n, halo, s, am ? index : nullptr, idx_base);
-    const int64_t slots = m + upper_slots(m);
+    const int64_t slots = 8 * m + upper_slots(m);
     AsyncBuf bv, bi;
     if ((rc = bv.alloc(slots * sizeof(float), s))) return rc;
     if (am && (rc = bi.alloc(slots * sizeof(int64_t), s))) return rc;
     float* pv = (float*)bv.p;
     int64_t* pi = (int64_t*)bi.p;
     if ((rc = launch_program(g, L, dev_in, pv, n, halo, s, pi, idx_base))) return rc;
-    return finish_levels(kind, pv, pi, m, value, index, s, pv + m, am ? pi + m : nullptr);
+    return finish_levels(kind, pv, pi, m, value, index, s, pv + 8 * m,
+                         am ? pi + 8 * m : nullptr);
 }
 
 int check_reduce(simtgo_tile_graph* g, simtgo_tensor t, int32_t kind, const void* value,
@@ -1974,8 +1986,8 @@ int simtgo_tile_reduce_shard(simtgo_tile_graph* g, simtgo_tensor t, int32_t kind
     const bool am = kind == tilek::RED_ARGMAX;
     int64_t s0, per;
     if ((rc = simtgo_tile_shard_range(n_total, nranks, 0, &s0, &per))) return rc;
-    const int64_t C = per / tilek::kChunk;  // chunk slots per rank
-    const int64_t mine = n_partials(len);
+    const int64_t C = 8 * (per / tilek::kChunk);  // warp-partial slots per rank
+    const int64_t mine = 8 * n_partials(len);
     const int64_t m = n_partials(n_total);
     const int64_t slots = C + C * nranks + upper_slots(m);
     AsyncBuf bv, bi;
@@ -2016,8 +2028,8 @@ int simtgo_tile_reduce_shard(simtgo_tile_graph* g, simtgo_tensor t, int32_t kind
     }
     if ((rc = sg::comm_allgather(comm, send_v, recv_v, C * sizeof(float), s))) return rc;
     if (am && (rc = sg::comm_allgather(comm, send_i, recv_i, C * sizeof(int64_t), s))) return rc;
-    // Ranks hold whole chunks in order, so the first m gathered slots are the
-    // partials of the whole signal's chunks.
+    // Ranks hold whole chunks in order, so the first 8 m gathered slots are
+    // the warp partials of the whole signal's chunks.
     return finish_levels(kind, recv_v, recv_i, m, dev_value, dev_index, s,
                          recv_v + C * nranks, am ? recv_i + C * nranks : nullptr);
 }
