@@ -18,7 +18,8 @@ Also reported: the roofline of the FIR kernel (FP32 FMA-bound at 127 taps),
 clocks sampled during the timed region, a CPU baseline (the oracle port on
 the host cores, bounded sample), and at N=1 every kernel's achieved HBM
 GB/s at its workload size ("kernels"), plus, at every N, the sharded
-histogram (with the bins all-reduced) and the sharded tile graph.
+histogram (with the bins all-reduced), the sharded tile graph and the
+sharded tile reductions (block partials all-gathered).
 
 --impl reference times the reference's CPU path (the oracle port of
 gpu.RunCPU's FIR; the reference's own generated FIR.cu stages a 320-sample
