@@ -277,6 +277,16 @@ simtgo_tensor simtgo_tile_sqrt(simtgo_tile_graph* g, simtgo_tensor a);
 simtgo_tensor simtgo_tile_abs(simtgo_tile_graph* g, simtgo_tensor a);
 /* tile/tile.go:135 FIR: h is HOST memory of `taps` floats (copied). */
 simtgo_tensor simtgo_tile_fir(simtgo_tile_graph* g, simtgo_tensor a, const float* h, int32_t taps);
+/* No counterpart in the reference, which rejects a FIR whose input contains
+ * a FIR (tile/tile.go:141-146, pinned by TestChainedWindowRejected) and
+ * lists chained windows as future work (PLAN.md, Phase 6). With allow != 0,
+ * FIRs recorded afterwards on this graph may be chained: each window reads
+ * the one inside it as zero outside [-halo, n), exactly as if the inner one
+ * had been materialised first (MaterializeStepwise gives the same bits). A
+ * sharded run is exact at the shard's edge when halo covers the sum of
+ * taps-1 along the longest chain. The default (0) keeps the reference's
+ * error. */
+int simtgo_tile_allow_chained_windows(simtgo_tile_graph* g, int32_t allow);
 /* tile/tile.go:63 Tensor.Len. -1 for a handle that is not in the graph. */
 int32_t simtgo_tile_len(const simtgo_tile_graph* g, simtgo_tensor t);
 /* tile/tile.go:163 Err: SIMTGO_OK or SIMTGO_EGRAPH; the message is in

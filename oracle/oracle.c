@@ -718,11 +718,9 @@ int oracle_tile_eval(const oracle_tile_node* nodes, int32_t n_nodes, int32_t roo
                 case 5: v[p] = fabsf(ARG(nd->a, p)); break;
                 case 6: v[p] = oracle_hypot(ARG(nd->a, p), ARG(nd->b, p)); break;
                 case 7: {
-                    /* The window exists only at the shard's own positions. */
-                    if (p < halo) {
-                        v[p] = NAN;
-                        break;
-                    }
+                    /* Over the whole span, signal values below the span's
+                     * start (-halo) reading 0: a window read by another
+                     * (chained windows) is read in the halo too. */
                     float acc = 0.0f;
                     for (int32_t k = 0; k < nd->ntaps; k++) {
                         int64_t src = p - k;

@@ -96,7 +96,9 @@ int oracle_histogram_shard(int32_t* bins, int32_t bins_len, const int32_t* x, in
  * every operation is rounded on its own; a FIR tile value at an index before
  * the start of the signal (or of the shard's halo) is 0 (tile/codegen.go:
  * 80-108), and its accumulation is fma(h[k], tile, acc) in k order, as the
- * reference's NVRTC build contracts `v += h[k]*tile[...]`. */
+ * reference's NVRTC build contracts `v += h[k]*tile[...]`. A FIR node's
+ * values exist over the whole span, halo included, so a FIR may read
+ * another (the library's opt-in chained windows). */
 typedef struct oracle_tile_node {
     int32_t kind;
     int32_t a, b;

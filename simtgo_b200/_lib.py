@@ -76,6 +76,7 @@ _SIGS = {
     "simtgo_tile_sqrt": [_vp, _i32],
     "simtgo_tile_abs": [_vp, _i32],
     "simtgo_tile_fir": [_vp, _i32, _vp, _i32],
+    "simtgo_tile_allow_chained_windows": [_vp, _i32],
     "simtgo_tile_len": [_vp, _i32],
     "simtgo_tile_err": [_vp],
     "simtgo_tile_err_string": [_vp],

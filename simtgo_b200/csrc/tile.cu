@@ -65,8 +65,12 @@ constexpr int kMaxTaps = SIMTGO_TILE_MAX_TAPS;
 // Samples a chunk's window reaches below it: taps-1 rounded up to 16 bytes,
 // plus 4 of slack so that the first 16-byte window load stays in the tile.
 __host__ __device__ constexpr int window_reach(int taps) { return (taps - 1 + 3) / 4 * 4 + 4; }
-constexpr int kTileF = kChunk + window_reach(kMaxTaps) + 4;  // staged floats per window node
+// Staged floats of a window's tile: its head, the chunk and 4 of slack.
+__host__ __device__ constexpr int tile_floats(int head) { return kChunk + head + 4; }
 constexpr int kMaxStages = 16;
+// FirDesc.taps flag: a later window's staging reads this window's tile, so
+// the block synchronises after staging it (chained windows).
+constexpr int32_t kSyncAfter = 1 << 8;
 
 // Steps of the accumulator machine. A is the accumulator (the thread's
 // 8 elements), M an operand in shared memory. The lowering emits these one
@@ -112,8 +116,8 @@ static_assert(sizeof(Insn) == 16, "one 16-byte shared load per instruction");
 
 struct FirDesc {
     int32_t start;  // pc of the staging program
-    int32_t taps;
-    int32_t reach;  // window_reach(taps)
+    int32_t taps;   // the taps, | kSyncAfter when a later window reads this one
+    int32_t head;   // positions the tile holds below the chunk (a multiple of 4)
     int32_t tile4;  // float4 offset of the window's tile in shared memory
     float h[kMaxTaps];  // the coefficients travel in the parameter block
 };
@@ -147,6 +151,7 @@ __host__ __device__ constexpr int meta_bytes(int n_code, int n_in, int n_fir) {
 struct Run {
     int32_t sh_in;   // added to F_IN operands: the stage and the run's position
     int32_t sh_st;   // added to STAGE destinations (the run's offset in the tile)
+    int32_t woff4;   // (run position - chunk position) / 4: where FIRACC reads a tile
     uint32_t gm;     // which of the thread's groups take part
     int64_t p0;      // position of the run's element 0
     bool edge;       // some positions of the run lie outside [-halo, n)
@@ -190,7 +195,7 @@ __device__ __forceinline__ float f4_get(const float4& v, int j) {
 }
 
 // The window accumulation for the thread's groups: output j of group k sits
-// at tile index b_k + j, b_k = 4 (t + 256 k) + reach, and takes
+// at tile index b_k + j, b_k = 4 (t + 256 k + woff4) + head, and takes
 // fma(h[i], tile[b_k + j - i], acc) for i = 0 .. taps-1 in order. With
 // W = tile[b_k - i0 - 4 .. b_k - i0 + 3] for taps i0 .. i0+3, the sample of
 // output j at tap i0+u is W[4 + j - u]; the upper half of W is the lower
@@ -208,12 +213,12 @@ __device__ __forceinline__ void fir_step(float (&acc)[4], const float4& lo, cons
             for (int j = 0; j < 4; j++) acc[j] = __fmaf_rn(hv[u], w[4 + j - u], acc[j]);
 }
 
-__device__ __forceinline__ void fir_acc(float4 (&A)[kG], const Ctx& c, int f) {
+__device__ __forceinline__ void fir_acc(float4 (&A)[kG], const Ctx& c, int f, int woff4) {
     const int4 fd = c.fir[f];
-    const int taps = fd.y;
+    const int taps = fd.y & (kSyncAfter - 1);
     const float4* h4 = reinterpret_cast<const float4*>(c.taps_s + f * kMaxTaps);
     // Group k's window float4 at tap i0 (a multiple of 4): tw[k][-i0/4].
-    const float4* tw = c.S + fd.w + threadIdx.x + fd.z / 4;
+    const float4* tw = c.S + fd.w + threadIdx.x + fd.z / 4 + woff4;
     float acc[kG][4];
     float4 hi[kG];
 #pragma unroll
@@ -328,7 +333,7 @@ __device__ __forceinline__ void interpret(const Insn* code, int pc, const Ctx& c
                 for (int k = 0; k < kG; k++) A[k] = f4_abs(A[k]);
                 break;
             case OP_FIRACC:
-                fir_acc(A, c, in.b);
+                fir_acc(A, c, in.b, r.woff4);
                 break;
             default:
                 break;  // OP_END: no operation
@@ -569,16 +574,19 @@ __device__ __forceinline__ ChunkSpan chunk_span(int64_t cb, int hs, int64_t n, i
 }
 
 // Shared memory (float4 units): meta | taps (n_fir x kMaxTaps floats) |
-// tiles (n_fir x kTileF floats) | temporaries (n_tmp x kChunk floats) |
+// tiles (tile_floats(head) floats each) | temporaries (n_tmp x kChunk floats) |
 // stages (nst x n_in x (hs + kChunk) floats, BULK only). Input k of a stage
 // holds positions [cb - hs, cb + kChunk) of the chunk at cb (the part below
 // cb only for the first chunk of the block's range).
 //
 // A block works through a contiguous range of chunks. Window f's tile holds
-// positions [cb - reach, cb + kChunk): the chunk's own positions are staged
+// positions [cb - head, cb + kChunk): the chunk's own positions are staged
 // by one run of the window's program; the head below cb is the previous
-// chunk's last reach positions, copied within the tile, and is computed by
-// a short head run only for the first chunk of the range.
+// chunk's last head positions, copied within the tile, and is computed by
+// a short head run only for the first chunk of the range. head is the
+// window's reach (window_reach(taps)), plus, when later windows read it
+// (chained windows), the largest head among them: their head runs read it
+// that far below the chunk.
 //
 // Bulk-copy mode (BULK): the chunk's inputs travel HBM -> shared memory by
 // cp.async.bulk, one copy per input, in `nst` stages that complete on
@@ -620,7 +628,7 @@ __global__ void __launch_bounds__(kThreads, 3) k_tile(const __grid_constant__ Pr
         code_s[i] = i < P.n_code ? P.code[i] : Insn{OP_END, F_END, 0, 0, 0, 0.0f, 0};
     for (int k = tid; k < P.n_in; k += kThreads) in_s[k] = P.in[k];
     for (int f = tid; f < P.n_fir; f += kThreads)
-        fir_s[f] = make_int4(P.fir[f].start, P.fir[f].taps, P.fir[f].reach, P.fir[f].tile4);
+        fir_s[f] = make_int4(P.fir[f].start, P.fir[f].taps, P.fir[f].head, P.fir[f].tile4);
     for (int f = 0; f < P.n_fir; f++)
         for (int k = tid; k < kMaxTaps; k += kThreads)
             taps_s[f * kMaxTaps + k] = P.fir[f].h[k];  // zero past taps
@@ -704,14 +712,15 @@ __global__ void __launch_bounds__(kThreads, 3) k_tile(const __grid_constant__ Pr
                 const int4 fd = fir_s[j >> 1];
                 const int head4 = fd.z / 4;
                 pc = fd.x;
-                if (!(j & 1)) {  // head: tile [0, reach) = positions [cb - reach, cb)
+                if (!(j & 1)) {  // head: tile [0, head) = positions [cb - head, cb)
                     r.sh_in = in4 + (hs - fd.z) / 4;
                     r.sh_st = 0;
+                    r.woff4 = -head4;
                     r.gm = first && tid < head4 ? 1u : 0u;
                     r.p0 = cb - fd.z;
-                } else {  // the chunk: tile [reach, reach + kChunk)
-                    // Carry the head over: the previous chunk's last reach
-                    // positions sit at tile [kChunk, kChunk + reach). The
+                } else {  // the chunk: tile [head, head + kChunk)
+                    // Carry the head over: the previous chunk's last head
+                    // positions sit at tile [kChunk, kChunk + head). The
                     // thread that copies a float4 is the one whose staging
                     // below overwrites it, so no barrier is needed.
                     if (!first && tid >= kThreads - head4) {
@@ -721,6 +730,7 @@ __global__ void __launch_bounds__(kThreads, 3) k_tile(const __grid_constant__ Pr
                     }
                     r.sh_in = in4 + hs / 4;
                     r.sh_st = head4;
+                    r.woff4 = 0;
                     r.gm = (1u << kG) - 1;
                     r.p0 = cb;
                 }
@@ -728,6 +738,7 @@ __global__ void __launch_bounds__(kThreads, 3) k_tile(const __grid_constant__ Pr
                 pc = P.main_start;
                 r.sh_in = in4 + hs / 4;
                 r.sh_st = 0;
+                r.woff4 = 0;
                 r.gm = (1u << kG) - 1;
                 r.p0 = cb;
             }
@@ -736,7 +747,9 @@ __global__ void __launch_bounds__(kThreads, 3) k_tile(const __grid_constant__ Pr
                 interpret<BULK, true>(code_s, pc, cx, r, A);
             else if (r.gm)
                 interpret<BULK, false>(code_s, pc, cx, r, A);
-            if (j + 1 == 2 * nf) __syncthreads();  // windows staged before main reads them
+            // Windows staged before the main program reads them, and a
+            // window before a later window's staging reads it (chains).
+            if ((j & 1) && (j + 1 == 2 * nf || (fir_s[j >> 1].y & kSyncAfter))) __syncthreads();
         }
         if (P.reduce != RED_NONE) {
             float* wv = out + 8 * c;
@@ -803,6 +816,7 @@ struct Node {
 struct simtgo_tile_graph {
     std::vector<Node> nodes;
     std::string err;
+    bool chained = false;  // FIR of an expression with a FIR accepted (opt-in)
 };
 
 namespace {
@@ -836,6 +850,15 @@ bool contains_fir(const simtgo_tile_graph* g, int id) {
     if (n.a >= 0 && contains_fir(g, n.a)) return true;
     if (n.b >= 0 && contains_fir(g, n.b)) return true;
     return false;
+}
+
+// Whether the expression at id reads window node w directly (not through
+// another window).
+bool reads_window(const simtgo_tile_graph* g, int id, int w) {
+    if (id == w) return true;
+    const Node& n = g->nodes[id];
+    if (n.kind == K_FIR) return false;
+    return (n.a >= 0 && reads_window(g, n.a, w)) || (n.b >= 0 && reads_window(g, n.b, w));
 }
 
 // postorder (tile/codegen.go:135-144): dependencies first, each node once.
@@ -937,6 +960,8 @@ struct Lowered {
     std::vector<int> fir_nodes;      // window node ids, in window order
     std::vector<int> param_of;       // reference parameter index pK of each data input
     int32_t reduce = tilek::RED_NONE;  // the main program's value is reduced, not stored
+    std::vector<int32_t> head;       // each window's head (positions below the chunk)
+    std::vector<char> sync_after;    // a later window's staging reads this window
 };
 
 // Emits one program for the accumulator machine: a window's signal (ending
@@ -973,16 +998,18 @@ struct Gen {
     void push(uint8_t op, uint8_t sp = SP_NONE, int idx = 0, float imm = 0.0f) {
         raw.push_back(LInsn{op, sp, (uint16_t)idx, imm});
     }
+    // A window node is a leaf of every program that reads it (FIRACC of its
+    // staged tile): the main program, and with chained windows a later
+    // window's staging.
     bool leaf(int id) const {
         const Node& n = g->nodes[id];
-        return n.kind == K_INPUT || (main && n.kind == K_FIR);
+        return n.kind == K_INPUT || n.kind == K_FIR;
     }
-    // Counts references inside this program (a window node is a leaf of the
-    // main program).
+    // Counts references inside this program.
     void count(int root) {
         std::vector<int> order;
         std::vector<char> seen(g->nodes.size(), 0);
-        postorder(g, root, order, seen, main);
+        postorder(g, root, order, seen, true);
         for (int id : order) {
             if (leaf(id)) continue;
             const Node& n = g->nodes[id];
@@ -1062,7 +1089,7 @@ struct Gen {
         }
         if (status) return;
         const Node& n = g->nodes[id];
-        if (n.kind == K_FIR) {  // main program only
+        if (n.kind == K_FIR) {
             push(tilek::OP_FIRACC, SP_NONE, fir_index.at(id));
         } else if (n.kind == K_SCALE || n.kind == K_SQRT || n.kind == K_ABS) {
             emit(n.a);
@@ -1146,12 +1173,29 @@ int lower(const simtgo_tile_graph* g, int root, Lowered& L, int32_t reduce = til
         return sg::fail(SIMTGO_ESIZE, "tile: %zu windowed operations; the fused kernel stages at most %d",
                         L.fir_nodes.size(), tilek::kMaxFir);
     std::unordered_map<int, int> fir_index, input_index;
-    for (size_t i = 0; i < L.fir_nodes.size(); i++) fir_index[L.fir_nodes[i]] = (int)i;
+    const int nfw = (int)L.fir_nodes.size();
+    for (int i = 0; i < nfw; i++) fir_index[L.fir_nodes[i]] = i;
+    // Heads: a window read by later windows' staging (chained windows; the
+    // windows are in postorder, so readers come later) reaches below the
+    // chunk by its own reach plus the largest head among its readers.
+    L.head.assign(nfw, 0);
+    L.sync_after.assign(nfw, 0);
+    for (int i = nfw - 1; i >= 0; i--) {
+        const int taps = (int)g->nodes[g->nodes[L.fir_nodes[i]].b].taps.size();
+        int below = 0;
+        for (int j = i + 1; j < nfw; j++)
+            if (reads_window(g, g->nodes[L.fir_nodes[j]].a, L.fir_nodes[i])) {
+                below = std::max(below, L.head[j]);
+                L.sync_after[i] = 1;
+            }
+        L.head[i] = tilek::window_reach(taps) + below;
+    }
+    if (nfw > 0 && *std::max_element(L.head.begin(), L.head.end()) > 4 * tilek::kThreads)
+        return sg::fail(SIMTGO_ESIZE, "tile: chained windows reach more than %d samples below a chunk",
+                        4 * tilek::kThreads);
     int status = 0;
     for (size_t f = 0; f < L.fir_nodes.size() && !status; f++) {
         const int sig = g->nodes[L.fir_nodes[f]].a;
-        if (contains_fir(g, sig))
-            return sg::fail(SIMTGO_EGRAPH, "tile: a windowed operation inside a window");
         L.fir_start.push_back((int32_t)L.code.size());
         Gen gen(g, false, L, input_index, fir_index);
         gen.count(sig);
@@ -1193,6 +1237,13 @@ int lower(const simtgo_tile_graph* g, int root, Lowered& L, int32_t reduce = til
     return 0;
 }
 
+// Float4 offset of window f's tile among the tiles.
+int32_t tile_off4(const Lowered& L, int f) {
+    int32_t off = 0;
+    for (int i = 0; i < f; i++) off += tilek::tile_floats(L.head[i]) / 4;
+    return off;
+}
+
 // The launch's shared-memory layout (float4 offsets) and its program.
 struct Layout {
     int32_t taps4, tiles4, temps4, stages4, sstride, nst;
@@ -1211,9 +1262,9 @@ void build_program(const simtgo_tile_graph* g, const Lowered& L, const Layout& Y
         const Node& fn = g->nodes[L.fir_nodes[f]];
         const std::vector<float>& h = g->nodes[fn.b].taps;
         P.fir[f].start = L.fir_start[f];
-        P.fir[f].taps = (int32_t)h.size();
-        P.fir[f].reach = tilek::window_reach((int)h.size());
-        P.fir[f].tile4 = Y.tiles4 + f * tilek::kTileF / 4;
+        P.fir[f].taps = (int32_t)h.size() | (L.sync_after[f] ? tilek::kSyncAfter : 0);
+        P.fir[f].head = L.head[f];
+        P.fir[f].tile4 = Y.tiles4 + tile_off4(L, f);
         for (size_t k = 0; k < h.size(); k++) P.fir[f].h[k] = h[k];
     }
     // A lowered operand's address: inputs relative to the run's stage
@@ -1223,7 +1274,7 @@ void build_program(const simtgo_tile_graph* g, const Lowered& L, const Layout& Y
         switch (space) {
             case SP_IN: return (uint16_t)(bulk ? idx * Y.sstride / 4 : idx);
             case SP_TMP: return (uint16_t)(Y.temps4 + idx * tilek::kChunk4);
-            case SP_WIN: return (uint16_t)(P.fir[idx].tile4 + P.fir[idx].reach / 4);
+            case SP_WIN: return (uint16_t)(P.fir[idx].tile4 + P.fir[idx].head / 4);
             default: return (uint16_t)idx;
         }
     };
@@ -1277,14 +1328,11 @@ int launch_program(const simtgo_tile_graph* g, const Lowered& L,
     const bool vec = sg::aligned16(out);
     // Samples a chunk's windows reach below it.
     int32_t hs = 0;
-    for (int f = 0; f < n_fir; f++) {
-        const Node& fn = g->nodes[L.fir_nodes[f]];
-        hs = std::max<int32_t>(hs, tilek::window_reach((int)g->nodes[fn.b].taps.size()));
-    }
+    for (int f = 0; f < n_fir; f++) hs = std::max<int32_t>(hs, L.head[f]);
     Layout Y;
     Y.taps4 = tilek::meta_bytes((int)L.code.size(), n_in, n_fir) / 16;
     Y.tiles4 = Y.taps4 + n_fir * tilek::kMaxTaps / 4;
-    Y.temps4 = Y.tiles4 + n_fir * tilek::kTileF / 4;
+    Y.temps4 = Y.tiles4 + tile_off4(L, n_fir);
     Y.stages4 = Y.temps4 + L.n_tmp * tilek::kChunk4;
     Y.sstride = hs + tilek::kChunk;
     const size_t base_smem = (size_t)Y.stages4 * 16;
@@ -1638,7 +1686,7 @@ simtgo_tensor simtgo_tile_fir(simtgo_tile_graph* g, simtgo_tensor a, const float
         latch(g, "FIR: null coefficients");
         return a;
     }
-    if (contains_fir(g, a)) {
+    if (!g->chained && contains_fir(g, a)) {
         latch(g, "FIR: chaining windowed operations is not supported; materialise the first one");
         return a;
     }
@@ -1654,6 +1702,13 @@ simtgo_tensor simtgo_tile_fir(simtgo_tile_graph* g, simtgo_tensor a, const float
     f.a = a;
     f.b = tid;
     return add_node(g, std::move(f));
+}
+
+int simtgo_tile_allow_chained_windows(simtgo_tile_graph* g, int32_t allow) {
+    sg::clear_error();
+    if (!g) return sg::fail(SIMTGO_ENULL, "tile: null graph");
+    g->chained = allow != 0;
+    return 0;
 }
 
 int32_t simtgo_tile_len(const simtgo_tile_graph* g, simtgo_tensor t) {

@@ -60,6 +60,13 @@ class Graph:
         return self._t(self._L.simtgo_tile_input_device(self._h, C.c_void_p(t.data_ptr()),
                                                         t.numel()))
 
+    def AllowChainedWindows(self, allow: bool = True):
+        """No counterpart in the reference (which rejects a FIR of an
+        expression holding a FIR): FIRs recorded afterwards may be chained,
+        each reading the inner one as if it had been materialised first."""
+        check(self._L.simtgo_tile_allow_chained_windows(self._h, 1 if allow else 0))
+        return self
+
     def Err(self):
         """tile/tile.go:163: the first error recorded while building, or None."""
         if self._L.simtgo_tile_err(self._h) == 0:

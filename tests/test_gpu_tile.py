@@ -275,3 +275,60 @@ def test_random_graphs_unaligned_device_inputs(seed):
     rc, want = O.tile_eval(nodes, len(nodes) - 1, n, 0)
     assert rc == 0
     assert_agree(f"unaligned random graph {seed}", out_buf[1:].cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("seed", range(8))
+def test_chained_windows(seed):
+    """Windows of windows (the library's opt-in; the reference rejects
+    them): fused on the device, bit for bit against the oracle's
+    node-by-node evaluation, over one and several chunks per block (heads
+    carried through every window of the chain), and equal to the stepwise
+    path, which materialises each window before the next reads it."""
+    from test_tile_lowering import _chained_graph
+
+    for n in (3001, (1 << 21) + 77):
+        root, nodes = _chained_graph(seed, n, 0)
+        got = root.Materialize()
+        rc, want = O.tile_eval(nodes, len(nodes) - 1, n, 0)
+        assert rc == 0
+        assert_agree(f"chained graph {seed} n={n}", got, want)
+        if n == 3001:
+            step, _ = root.MaterializeStepwise()
+            assert_agree(f"chained graph {seed} stepwise", step, got)
+
+
+@pytest.mark.parametrize("halo", [0, 40, 44])
+def test_chained_windows_shard_halo(halo):
+    """A shard of FIR(Add(FIR(a, h1), a), h2) with taps 17 and 21: with a
+    halo of at least 16 + 20 samples its outputs equal the whole signal's
+    from the shard's first element on; with none, the first shard's."""
+    n_all, start = (1 << 20) + 500, 70000
+    x = normal(n_all, 21)
+    h1 = (np.arange(17, dtype=np.float32) / 60).astype(np.float32)
+    h2 = (np.cos(np.arange(21, dtype=np.float32)) / 9).astype(np.float32)
+    nodes = [{"kind": "input", "data": x}, {"kind": "input", "data": h1},
+             {"kind": "fir", "a": 0, "taps": h1}, {"kind": "add", "a": 2, "b": 0},
+             {"kind": "input", "data": h2}, {"kind": "fir", "a": 3, "taps": h2}]
+    rc, whole = O.tile_eval(nodes, 5, n_all, 0)
+    assert rc == 0
+    s0 = start if halo else 0
+    n = n_all - s0
+    buf = torch.from_numpy(x[s0 - halo:].copy()).cuda()
+    g = tile.New().AllowChainedWindows()
+    a = g.InputDevice(buf[halo:])
+    out = tile.FIR(tile.Add(tile.FIR(a, h1), a), h2)
+    y = torch.empty(n, device="cuda")
+    out.Run(y, halo=halo)
+    np.testing.assert_array_equal(y.cpu().numpy().view(np.uint32),
+                                  whole[s0:].view(np.uint32))
+
+
+def test_chained_windows_reduce():
+    from test_tile_lowering import _chained_graph
+
+    n = (1 << 20) + 3
+    root, nodes = _chained_graph(5, n, 0)
+    rc, want = O.tile_eval(nodes, len(nodes) - 1, n, 0)
+    assert rc == 0
+    got = tile.Sum(root).Materialize()
+    assert np.float32(got).view(np.uint32) == O.tile_reduce(want, "sum")[0].view(np.uint32)

@@ -186,12 +186,15 @@ def test_source_of_an_error_graph_raises():
         out.Source()
 
 
-def _random_graph(seed, n, halo):
+def _random_graph(seed, n, halo, chained=False):
     """A random DAG over the track's seven operations with shared values,
-    x-op-x nodes and up to two windows (none inside another): the tile graph
-    and the oracle's node table, in the same creation order."""
+    x-op-x nodes and up to two windows (none inside another; with chained,
+    up to three, windows of windows allowed): the tile graph and the
+    oracle's node table, in the same creation order."""
     rng = np.random.default_rng(seed)
     g = tile.New()
+    if chained:
+        g.AllowChainedWindows()
     nodes, ts, has_fir, values = [], [], [], []
 
     def add(t, nd, fir):
@@ -210,7 +213,7 @@ def _random_graph(seed, n, halo):
         kind = rng.choice(["scale", "abs", "sqrtabs", "add", "mul", "hypot", "fir"])
         i = pick()
         if kind == "fir":
-            if windows == 2 or has_fir[i]:
+            if windows == (3 if chained else 2) or (has_fir[i] and not chained):
                 kind = "abs"
             else:
                 windows += 1
@@ -237,6 +240,89 @@ def _random_graph(seed, n, halo):
             op = {"add": tile.Add, "mul": tile.Mul, "hypot": tile.Hypot}[kind]
             add(op(ts[i], ts[j]), {"kind": kind, "a": i, "b": j}, has_fir[i] or has_fir[j])
     return ts[values[-1]], nodes
+
+
+def _chained_graph(seed, n, halo):
+    """Two or three windows each reading the one before (chains), sometimes
+    a second window over the same inner one (a diamond), mixed with inputs:
+    the tile graph (chained windows allowed) and the oracle's node table."""
+    rng = np.random.default_rng(seed)
+    g = tile.New().AllowChainedWindows()
+    nodes = []
+
+    def rec(t, nd):
+        assert t.node == len(nodes), (t.node, len(nodes))
+        nodes.append(nd)
+        return t
+
+    def fir(t, h):
+        nodes.append({"kind": "input", "data": h})   # the taps node
+        return rec(tile.FIR(t, h), {"kind": "fir", "a": t.node, "taps": h})
+
+    def binop(name, x, y):
+        op = {"add": tile.Add, "mul": tile.Mul, "hypot": tile.Hypot}[name]
+        return rec(op(x, y), {"kind": name, "a": x.node, "b": y.node})
+
+    ins = []
+    for _ in range(2):
+        d = rng.uniform(-4, 4, n + halo).astype(f32)
+        ins.append(rec(g.Input(d[halo:]), {"kind": "input", "data": d}))
+    a, b = ins
+    cur = binop(str(rng.choice(["add", "mul"])), a, b)
+    wins = []
+    for _ in range(int(rng.integers(2, 4))):
+        h = (rng.uniform(-1, 1, int(rng.integers(1, 20))) / 4).astype(f32)
+        w = fir(cur, h)
+        wins.append(w)
+        pick = int(rng.integers(0, 3))
+        if pick == 0:
+            cur = w
+        elif pick == 1:
+            cur = binop("add", w, a)
+        else:
+            cur = rec(tile.Abs(w), {"kind": "abs", "a": w.node})
+            cur = binop("mul", cur, b)
+    root = cur
+    if rng.random() < 0.5:   # a diamond: another window over the first one
+        h = (rng.uniform(-1, 1, int(rng.integers(1, 12))) / 4).astype(f32)
+        root = binop("add", root, fir(wins[0], h))
+    return root, nodes
+
+
+@pytest.mark.parametrize("seed", range(16))
+def test_chained_windows_listing_matches_oracle(seed):
+    """Windows of windows (the opt-in): each window's program reads the
+    windows inside it (firacc), and the emulated listing equals the oracle's
+    node-by-node evaluation, halo included."""
+    n, halo = 40, (12 if seed % 2 else 0)
+    root, nodes = _chained_graph(seed, n, halo)
+    assert root.g.Err() is None
+    src = root.Source()
+    assert any(b.startswith("window") and "firacc" in b
+               for b in re.split(r"\n(?=window|main)", src)), src
+    src = root.Source()
+    node_of = [int(m) for m in re.findall(r"; in\d+ = node (\d+)", src)]
+    taps = {}
+    for m in re.finditer(r"window (\d+) taps \d+ node (\d+)", src):
+        taps[int(m.group(1))] = nodes[int(m.group(2))]["taps"]
+    got = run_listing(src, [nodes[i]["data"] for i in node_of], n, taps, halo)
+    rc, want = O.tile_eval(nodes, len(nodes) - 1, n, halo)
+    assert rc == 0
+    np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+def test_chained_window_opt_in_only():
+    """The reference's rejection stays the default; the opt-in accepts."""
+    x = np.ones(8, f32)
+    g = tile.New()
+    inner = tile.FIR(g.Input(x), np.ones(3, f32))
+    tile.FIR(inner, np.ones(2, f32))
+    assert "chaining windowed" in str(g.Err())
+    g2 = tile.New().AllowChainedWindows()
+    inner = tile.FIR(g2.Input(x), np.ones(3, f32))
+    out = tile.FIR(tile.Add(inner, inner), np.ones(2, f32))
+    assert g2.Err() is None
+    assert "window 1 taps 2" in out.Source()
 
 
 @pytest.mark.parametrize("seed", range(24))
