@@ -5,7 +5,9 @@ part with the oracle, and exchange what the sharded workloads exchange:
   FIR        nothing on the data path (the halo is part of the shard);
              gathered only to check that the shards tile the whole output;
   Histogram  the 256 partial bins, summed with an all-reduce;
-  tile       nothing (pure split), gathered for the check.
+  tile       nothing (pure split), gathered for the check;
+  reduction  the block partials of each rank's whole 2048-blocks,
+             all-gathered, then the same tree on every rank.
 
 Each result must equal the unsharded oracle run. Also: a rank that fails
 between steps is seen by the other as a collective error within the
@@ -97,6 +99,47 @@ def _worker_workloads(rank, port, q):
         dist.destroy_process_group()
 
 
+def _worker_reduce(rank, port, q):
+    """The sharded tile reduction's exchange: each rank reduces its
+    ShardRange slice (whole 2048-blocks) to block partials, pads them to the
+    per-rank slot count with the identity, all-gathers the slots, and
+    finishes the tree over the first m = ceil(total / 2048) of them."""
+    import oracle_lib as O
+    from simtgo_b200 import tile
+
+    _init(rank, port)
+    try:
+        total = 9 * 2048 + 1234
+        x = np.random.default_rng(12).standard_normal(total).astype(np.float32)
+        x[5000] = 50.0
+        s0, n = tile.ShardRange(total, WORLD, rank)
+        _, per = tile.ShardRange(total, WORLD, 0)
+        slots = per // 2048
+        m = (total + 2047) // 2048
+        ok = {}
+        for kind in ("sum", "min", "max", "argmax"):
+            pv, pi = O.tile_reduce_partials(x[s0:s0 + n], kind, idx_base=s0)
+            ident, _ = O.tile_reduce(np.zeros(0, np.float32), kind)
+            pad_v = np.concatenate([pv, np.full(slots - len(pv), ident, np.float32)])
+            pad_i = np.concatenate([pi, np.full(slots - len(pi), -1, np.int64)])
+            gv = [torch.zeros(slots, dtype=torch.float32) for _ in range(WORLD)]
+            gi = [torch.zeros(slots, dtype=torch.int64) for _ in range(WORLD)]
+            dist.all_gather(gv, torch.from_numpy(pad_v))
+            dist.all_gather(gi, torch.from_numpy(pad_i))
+            allv = torch.cat(gv).numpy()[:m]
+            alli = torch.cat(gi).numpy()[:m]
+            got = O.tile_reduce_levels(allv, alli, kind)
+            want = O.tile_reduce(x, kind)
+            ok[kind] = (got[0].view(np.uint32) == want[0].view(np.uint32)
+                        and (kind != "argmax" or got[1] == want[1] == 5000))
+        flags = [None] * WORLD
+        dist.all_gather_object(flags, ok)
+        if rank == 0:
+            q.put(flags)
+    finally:
+        dist.destroy_process_group()
+
+
 def _worker_dead_peer(rank, port, q):
     _init(rank, port, timeout_s=5)
     t = torch.ones(4)
@@ -131,6 +174,12 @@ def test_sharded_workloads_equal_whole():
     assert fir_ok, "FIR shards do not tile the whole output"
     assert hist_ok, "all-reduced partial bins differ from the whole histogram"
     assert tile_ok, "tile graph shards differ from the whole"
+
+
+def test_sharded_reduction_equals_whole():
+    flags = _run(_worker_reduce)
+    for rank, ok in enumerate(flags):
+        assert all(ok.values()), (rank, ok)
 
 
 def test_dead_peer_is_an_error_not_a_hang():
