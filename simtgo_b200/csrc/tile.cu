@@ -28,7 +28,14 @@
 //    plus a halo of taps-1 (zero outside the signal), staged in shared
 //    memory, then each thread forms fma(h[k], tile, acc) in k order for its
 //    8 outputs, one new 16-byte shared load per group per 4 taps. The staged
-//    signal also serves the main program wherever it uses that node.
+//    signal also serves the main program wherever it uses that node;
+//  * with chained windows (an opt-in; the reference rejects a FIR of an
+//    expression holding a FIR) a window's signal program reads the windows
+//    inside it, which are staged first;
+//  * a reduction of the graph (Sum, Min, Max, ArgMax; the reference has
+//    none) consumes the main program's values in the same pass: each warp
+//    reduces its part of a chunk in a fixed tree to one partial in HBM, and
+//    small level kernels finish the tree.
 // Every operation is rounded on its own (Scale = k*x, Add, Mul, Sqrt
 // correctly rounded, Abs exact, Hypot = gpu.Hypot), so the fused program and
 // the stepwise one (one launch per node, tile/run.go:89) agree bit for bit.
@@ -140,7 +147,7 @@ struct Program {
 // The program as the interpreter reads it: copied once per block from the
 // parameter bank into shared memory, where a warp-uniform word is one
 // broadcast load. Layout: code[code_cap] (the program and one END) |
-// fir[n_fir] (start, taps, reach, tile4) | in[n_in], 16-byte rounded.
+// fir[n_fir] (start, taps | flags, head, tile4) | in[n_in], 16-byte rounded.
 __host__ __device__ constexpr int meta_code_cap(int n_code) { return n_code + 1; }
 __host__ __device__ constexpr int meta_bytes(int n_code, int n_in, int n_fir) {
     return ((meta_code_cap(n_code) * 16 + n_in * 8 + n_fir * 16) + 15) & ~15;
@@ -160,7 +167,7 @@ struct Run {
 struct Ctx {
     float4* S;               // dynamic shared memory
     const float* taps_s;     // n_fir x kMaxTaps coefficients, zero past taps
-    const int4* fir;         // shared (start, taps, reach, tile4)
+    const int4* fir;         // shared (start, taps | flags, head, tile4)
     const float* const* in;  // shared copy of Program::in
     float* out;
     int64_t n, halo;
