@@ -1404,13 +1404,17 @@ int launch_program(const simtgo_tile_graph* g, const Lowered& L,
         cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, tilek::kThreads, Y.smem),
         "cudaOccupancyMaxActiveBlocksPerMultiprocessor(tile)");
     if (rc) return rc;
-    // Eight times the resident blocks, each over a contiguous range of
-    // chunks: a block that finishes early is replaced by the next one, so
-    // SMs that see HBM faster take more of the signal (measured 1-10% faster
-    // than one persistent wave on the two-die B200).
+    // Whole waves of resident blocks, up to eight, each block over a
+    // contiguous range of at least 32 chunks: a block that finishes early is
+    // replaced by the next one, so SMs that see HBM faster take more of the
+    // signal (measured 1-10% faster than one persistent wave on the two-die
+    // B200 at 2^28 elements). Short signals keep one wave: every range starts
+    // with a pipeline fill and, with windows, a head run, and a partial wave
+    // would leave most SMs idle at the end.
     const int64_t chunks = sg::ceil_div(n, tilek::kChunk);
-    const int blocks = (int)std::max<int64_t>(
-        1, std::min<int64_t>(chunks, (int64_t)d->sms * std::max(1, per_sm) * 8));
+    const int64_t resident = (int64_t)d->sms * std::max(1, per_sm);
+    const int64_t waves = std::max<int64_t>(1, std::min<int64_t>(8, chunks / (32 * resident)));
+    const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(chunks, waves * resident));
     sg::before_launch();
     kern<<<blocks, tilek::kThreads, Y.smem, s>>>(P, out, n, halo, vec, in_aligned, hs, Y.stages4,
                                                  Y.nst, sg::watchdog_device_ptr(), out_idx,
