@@ -61,8 +61,16 @@ using namespace sgd;
 namespace tilek {
 
 constexpr int kThreads = 256;
-constexpr int kG = 2;                  // float4 groups per thread
-constexpr int kChunk = kThreads * 4 * kG;  // elements per block iteration
+// Float4 groups per thread (the template parameter G): 2 for graphs with
+// windows or Hypot, 4 (kGWide) for the others, whose dispatch and chunk
+// costs then spread over twice the elements (eight chained Muls measured
+// 0.57 -> 0.76 of HBM; Hypot's registers make it slower there).
+constexpr int kG = 2;
+constexpr int kGWide = 4;
+__host__ __device__ constexpr int chunk_of(int G) { return kThreads * 4 * G; }
+// 2048: the chunk of G = 2 (every window's tile is laid out for it) and the
+// block of the reduction trees, whatever G the interpreter runs with.
+constexpr int kChunk = chunk_of(kG);
 constexpr int kChunk4 = kChunk / 4;
 constexpr int kMaxCode = 1024;
 constexpr int kMaxIn = 32;
@@ -220,16 +228,17 @@ __device__ __forceinline__ void fir_step(float (&acc)[4], const float4& lo, cons
             for (int j = 0; j < 4; j++) acc[j] = __fmaf_rn(hv[u], w[4 + j - u], acc[j]);
 }
 
-__device__ __forceinline__ void fir_acc(float4 (&A)[kG], const Ctx& c, int f, int woff4) {
+template <int G>
+__device__ __forceinline__ void fir_acc(float4 (&A)[G], const Ctx& c, int f, int woff4) {
     const int4 fd = c.fir[f];
     const int taps = fd.y & (kSyncAfter - 1);
     const float4* h4 = reinterpret_cast<const float4*>(c.taps_s + f * kMaxTaps);
     // Group k's window float4 at tap i0 (a multiple of 4): tw[k][-i0/4].
     const float4* tw = c.S + fd.w + threadIdx.x + fd.z / 4 + woff4;
-    float acc[kG][4];
-    float4 hi[kG];
+    float acc[G][4];
+    float4 hi[G];
 #pragma unroll
-    for (int k = 0; k < kG; k++) {
+    for (int k = 0; k < G; k++) {
 #pragma unroll
         for (int j = 0; j < 4; j++) acc[k][j] = 0.0f;
         hi[k] = tw[kThreads * k];
@@ -240,7 +249,7 @@ __device__ __forceinline__ void fir_acc(float4 (&A)[kG], const Ctx& c, int f, in
         const float4 ha = h4[i0 / 4], hb = h4[i0 / 4 + 1];
         const float hva[4] = {ha.x, ha.y, ha.z, ha.w}, hvb[4] = {hb.x, hb.y, hb.z, hb.w};
 #pragma unroll
-        for (int k = 0; k < kG; k++) {
+        for (int k = 0; k < G; k++) {
             const float4 m = tw[kThreads * k - i0 / 4 - 1];
             const float4 lo = tw[kThreads * k - i0 / 4 - 2];
             fir_step<false>(acc[k], m, hi[k], hva, 4);
@@ -254,14 +263,14 @@ __device__ __forceinline__ void fir_acc(float4 (&A)[kG], const Ctx& c, int f, in
         const float hv[4] = {hk.x, hk.y, hk.z, hk.w};
         const int nk = min(4, taps - i0);
 #pragma unroll
-        for (int k = 0; k < kG; k++) {
+        for (int k = 0; k < G; k++) {
             const float4 lo = tw[kThreads * k - i0 / 4 - 1];
             fir_step<true>(acc[k], lo, hi[k], hv, nk);
             hi[k] = lo;
         }
     }
 #pragma unroll
-    for (int k = 0; k < kG; k++) A[k] = make_float4(acc[k][0], acc[k][1], acc[k][2], acc[k][3]);
+    for (int k = 0; k < G; k++) A[k] = make_float4(acc[k][0], acc[k][1], acc[k][2], acc[k][3]);
 }
 
 // Positions p .. p+3 of input b read from HBM (DIRECT mode), 0 outside
@@ -292,12 +301,12 @@ __device__ __forceinline__ float4 mask_outside(float4 v, int64_t p, const Ctx& c
 // next instruction ahead measured slower: it costs more instructions than
 // the shared-load latency it hides.) In DIRECT mode (BULK false) an input
 // operand is read from HBM at the run's positions.
-template <bool BULK, bool FULL>
+template <bool BULK, bool FULL, int G>
 __device__ __forceinline__ void interpret(const Insn* code, int pc, const Ctx& c, const Run& r,
-                                          float4 (&A)[kG]) {
+                                          float4 (&A)[G]) {
     const int t = threadIdx.x;
 #pragma unroll
-    for (int k = 0; k < kG; k++) A[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int k = 0; k < G; k++) A[k] = make_float4(0.f, 0.f, 0.f, 0.f);
     for (;;) {
         const Insn in = code[pc++];
         // Group k of operand M(x) (inactive groups: A itself, nothing is read).
@@ -308,7 +317,7 @@ __device__ __forceinline__ void interpret(const Insn* code, int pc, const Ctx& c
         };
         if (in.flags & F_LOADA) {
 #pragma unroll
-            for (int k = 0; k < kG; k++) A[k] = operand(in.a, in.flags & F_IN_A, k);
+            for (int k = 0; k < G; k++) A[k] = operand(in.a, in.flags & F_IN_A, k);
         }
         // The second operand of a binary operation, read inside its case.
         auto binop = [&](int k) -> float4 {
@@ -317,30 +326,30 @@ __device__ __forceinline__ void interpret(const Insn* code, int pc, const Ctx& c
         switch (in.op) {
             case OP_ADD:
 #pragma unroll
-                for (int k = 0; k < kG; k++) A[k] = f4_add(A[k], binop(k));
+                for (int k = 0; k < G; k++) A[k] = f4_add(A[k], binop(k));
                 break;
             case OP_MUL:
 #pragma unroll
-                for (int k = 0; k < kG; k++) A[k] = f4_mul(A[k], binop(k));
+                for (int k = 0; k < G; k++) A[k] = f4_mul(A[k], binop(k));
                 break;
             case OP_HYPOT:
 #pragma unroll
-                for (int k = 0; k < kG; k++) A[k] = f4_hypot(A[k], binop(k));
+                for (int k = 0; k < G; k++) A[k] = f4_hypot(A[k], binop(k));
                 break;
             case OP_SCALE:
 #pragma unroll
-                for (int k = 0; k < kG; k++) A[k] = f4_scale(in.imm, A[k]);
+                for (int k = 0; k < G; k++) A[k] = f4_scale(in.imm, A[k]);
                 break;
             case OP_SQRT:
 #pragma unroll
-                for (int k = 0; k < kG; k++) A[k] = f4_sqrt(A[k]);
+                for (int k = 0; k < G; k++) A[k] = f4_sqrt(A[k]);
                 break;
             case OP_ABS:
 #pragma unroll
-                for (int k = 0; k < kG; k++) A[k] = f4_abs(A[k]);
+                for (int k = 0; k < G; k++) A[k] = f4_abs(A[k]);
                 break;
             case OP_FIRACC:
-                fir_acc(A, c, in.b, r.woff4);
+                fir_acc<G>(A, c, in.b, r.woff4);
                 break;
             default:
                 break;  // OP_END: no operation
@@ -348,20 +357,20 @@ __device__ __forceinline__ void interpret(const Insn* code, int pc, const Ctx& c
         if (in.flags & (F_STA | F_STAGE | F_STORE | F_END)) {
             if (in.flags & F_STA) {
 #pragma unroll
-                for (int k = 0; k < kG; k++)
+                for (int k = 0; k < G; k++)
                     if (FULL || ((r.gm >> k) & 1)) c.S[in.d + t + kThreads * k] = A[k];
             }
             if (in.flags & F_STAGE) {
                 float4* dst = c.S + c.fir[in.d].w + r.sh_st + t;
 #pragma unroll
-                for (int k = 0; k < kG; k++)
+                for (int k = 0; k < G; k++)
                     if (FULL || ((r.gm >> k) & 1))
                         dst[kThreads * k] =
                             r.edge ? mask_outside(A[k], r.p0 + 4 * (t + kThreads * k), c) : A[k];
             }
             if (in.flags & F_STORE) {
 #pragma unroll
-                for (int k = 0; k < kG; k++) {
+                for (int k = 0; k < G; k++) {
                     const int64_t p = r.p0 + 4 * (t + kThreads * k);
                     if (c.vec && p + 3 < c.n) {
                         st_stream_f4(c.out + p, A[k]);
@@ -395,21 +404,23 @@ __device__ __forceinline__ RVal red_identity() {
     return {__int_as_float((int)0xff800000u), kNoIndex};
 }
 // Go's min and max (NaN wins, -0 < +0); NaN is returned as 0x7fc00000.
+// Branch-free: fminf/fmaxf, then equal values (only zeros of opposite signs
+// differ in bits) combined by OR (min: -0 wins) or AND (max: +0 wins), then
+// NaN.
 __device__ __forceinline__ float go_min(float a, float b) {
-    if (a != a || b != b) return __uint_as_float(kQNaN);
-    if (a < b) return a;
-    if (b < a) return b;
-    return (__float_as_uint(a) & 0x80000000u) ? a : b;
+    float m = fminf(a, b);
+    if (a == b) m = __uint_as_float(__float_as_uint(a) | __float_as_uint(b));
+    return (a != a || b != b) ? __uint_as_float(kQNaN) : m;
 }
 __device__ __forceinline__ float go_max(float a, float b) {
-    if (a != a || b != b) return __uint_as_float(kQNaN);
-    if (a > b) return a;
-    if (b > a) return b;
-    return (__float_as_uint(a) & 0x80000000u) ? b : a;
+    float m = fmaxf(a, b);
+    if (a == b) m = __uint_as_float(__float_as_uint(a) & __float_as_uint(b));
+    return (a != a || b != b) ? __uint_as_float(kQNaN) : m;
 }
 // ARGMAX order: NaN above everything, then value (+0 above -0), then the
 // smaller index. A strict total order on distinct indices, so any tree of
-// pairwise choices finds the same element.
+// pairwise choices finds the same element. (Early returns measured faster
+// here than evaluating every clause and selecting.)
 __device__ __forceinline__ bool am_before(const RVal& a, const RVal& b) {
     const bool na = a.v != a.v, nb = b.v != b.v;
     if (na || nb) return na && nb ? a.i < b.i : na;
@@ -464,28 +475,38 @@ __device__ __forceinline__ RVal red_block8(const float* wv, const int64_t* wi) {
 }
 static_assert(kThreads == 256 && kG == 2, "the reduction tree assumes 8 warps of 2 x float4");
 
-// A chunk's warp partials into wv[warp] (and wi[warp]): A holds the
-// values at positions cb + 4 (t + 256 k) + j; positions >= n take the
-// identity.
-template <int KIND>
-__device__ __forceinline__ void chunk_warps(const float4 (&A)[kG], int64_t cb, int64_t n,
-                                            int64_t idx_base, float* wv, int64_t* wi) {
+// A chunk's warp partials: A holds the values at positions
+// cb + 4 (t + 256 k) + j; positions >= n take the identity. The chunk is
+// G/2 blocks of the reduction tree (2048 positions, groups 2 sb and 2 sb + 1
+// of block sb), the first being block blk0 of the launch; block b's warp w
+// writes out[8 b + w] (and out_i), for the nblk blocks the launch has.
+template <int KIND, int G>
+__device__ __forceinline__ void chunk_warps(const float4 (&A)[G], int64_t cb, int64_t n,
+                                            int64_t idx_base, float* out, int64_t* out_i,
+                                            int64_t blk0, int64_t nblk) {
     const int t = threadIdx.x;
-    const bool full = cb + kChunk <= n;
-    RVal x[8];
 #pragma unroll
-    for (int k = 0; k < kG; k++)
+    for (int sb = 0; sb < G / 2; sb++) {
+        const int64_t b = blk0 + sb;
+        if (b < nblk) {  // uniform over the block
+            const int64_t base = cb + (int64_t)kChunk * sb;
+            const bool full = base + kChunk <= n;
+            RVal x[8];
 #pragma unroll
-        for (int e = 0; e < 4; e++) {
-            const int64_t p = cb + 4 * (t + kThreads * k) + e;
-            x[4 * k + e] = (full || p < n)
-                               ? RVal{f4_get(A[k], e), KIND == RED_ARGMAX ? idx_base + p : 0}
-                               : red_identity<KIND>();
+            for (int k = 0; k < 2; k++)
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    const int64_t p = base + 4 * (t + kThreads * k) + e;
+                    x[4 * k + e] = (full || p < n) ? RVal{f4_get(A[2 * sb + k], e),
+                                                          KIND == RED_ARGMAX ? idx_base + p : 0}
+                                                   : red_identity<KIND>();
+                }
+            const RVal w = red_warp<KIND>(red_thread<KIND>(x));
+            if ((t & 31) == 0) {
+                out[8 * b + (t >> 5)] = w.v;
+                if (KIND == RED_ARGMAX) out_i[8 * b + (t >> 5)] = w.i;
+            }
         }
-    const RVal w = red_warp<KIND>(red_thread<KIND>(x));
-    if ((t & 31) == 0) {
-        wv[t >> 5] = w.v;
-        if (KIND == RED_ARGMAX) wi[t >> 5] = w.i;
     }
 }
 // Partial e of a level: entry e itself, or (warps8, the first level) the
@@ -571,11 +592,11 @@ struct ChunkSpan {
 // range, whose window heads are computed) or without (later chunks carry
 // the heads over from the chunk before).
 __device__ __forceinline__ ChunkSpan chunk_span(int64_t cb, int hs, int64_t n, int64_t halo,
-                                                bool with_halo) {
+                                                bool with_halo, int chunk) {
     ChunkSpan s;
     s.org = cb - hs;
     s.lo = max(with_halo ? s.org : cb, -halo);
-    s.hi = min(cb + (int64_t)kChunk, n);
+    s.hi = min(cb + (int64_t)chunk, n);
     s.len4 = s.hi > s.lo ? ((s.hi - s.lo) & ~int64_t(3)) : 0;
     return s;
 }
@@ -611,13 +632,14 @@ __device__ __forceinline__ ChunkSpan chunk_span(int64_t cb, int hs, int64_t n, i
 // run ahead of each other, and the last of the eight warps to finish with a
 // stage (a shared counter per stage) refills it, instead of thread 0 after a
 // block barrier.
-template <bool BULK>
-__global__ void __launch_bounds__(kThreads, 3) k_tile(const __grid_constant__ Program P,
+template <bool BULK, int G>
+__global__ void __launch_bounds__(kThreads, G == kG ? 3 : 2) k_tile(const __grid_constant__ Program P,
                                                    float* __restrict__ out, int64_t n,
                                                    int64_t halo, bool vec, bool in_vec, int32_t hs,
                                                    int32_t stages4, int32_t nst, uint32_t* wd,
                                                    int64_t* __restrict__ out_idx,
                                                    int64_t idx_base) {
+    constexpr int CH = chunk_of(G), CH4 = CH / 4;
     __shared__ __align__(8) uint64_t bars[kMaxStages];   // stage s loaded
     __shared__ int rel[kMaxStages];  // warps done with stage s (window-free graphs)
     extern __shared__ float4 sm4[];
@@ -626,11 +648,11 @@ __global__ void __launch_bounds__(kThreads, 3) k_tile(const __grid_constant__ Pr
     int4* fir_s = reinterpret_cast<int4*>(code_s + code_cap);
     const float** in_s = reinterpret_cast<const float**>(fir_s + P.n_fir);
     float* taps_s = reinterpret_cast<float*>(sm4) + meta_bytes(P.n_code, P.n_in, P.n_fir) / 4;
-    const int32_t sstride = hs + kChunk;  // floats per staged input
+    const int32_t sstride = hs + CH;  // floats per staged input
     const int32_t stage_floats = P.n_in * sstride;
     float* stages = reinterpret_cast<float*>(sm4 + stages4);
     const int tid = threadIdx.x;
-    const int64_t nchunks = (n + kChunk - 1) / kChunk;
+    const int64_t nchunks = (n + CH - 1) / CH;
     for (int i = tid; i < code_cap; i += kThreads)
         code_s[i] = i < P.n_code ? P.code[i] : Insn{OP_END, F_END, 0, 0, 0, 0.0f, 0};
     for (int k = tid; k < P.n_in; k += kThreads) in_s[k] = P.in[k];
@@ -644,7 +666,7 @@ __global__ void __launch_bounds__(kThreads, 3) k_tile(const __grid_constant__ Pr
     const int64_t c0 = blockIdx.x * per_block;
     const int64_t c1 = min(c0 + per_block, nchunks);
     auto issue = [&](int64_t c, int s) {
-        const ChunkSpan sp = chunk_span(c * kChunk, hs, n, halo, c == c0);
+        const ChunkSpan sp = chunk_span(c * CH, hs, n, halo, c == c0, CH);
         mbar_arrive_expect_tx(&bars[s], (uint32_t)(sp.len4 * 4 * P.n_in));
         if (sp.len4 > 0)
             for (int k = 0; k < P.n_in; k++)
@@ -678,12 +700,12 @@ __global__ void __launch_bounds__(kThreads, 3) k_tile(const __grid_constant__ Pr
     cx.in_vec = in_vec;
     const int nf = P.n_fir;
     const bool free_run = nf == 0;
-    float4 A[kG];  // the last run's values (the main program's, for a reduction)
+    float4 A[G];  // the last run's values (the main program's, for a reduction)
     int it = 0;
     for (int64_t c = c0; c < c1; c++, it++) {
-        const int64_t cb = c * kChunk;
+        const int64_t cb = c * CH;
         const bool first = c == c0;
-        const ChunkSpan sp = chunk_span(cb, hs, n, halo, first);
+        const ChunkSpan sp = chunk_span(cb, hs, n, halo, first, CH);
         int s = 0;
         if (BULK) {
             s = it % nst;
@@ -708,7 +730,7 @@ __global__ void __launch_bounds__(kThreads, 3) k_tile(const __grid_constant__ Pr
             }
         }
         const int32_t in4 = stages4 + s * stage_floats / 4;
-        const bool edge = cb - (int64_t)hs < -halo || cb + kChunk > n;
+        const bool edge = cb - (int64_t)hs < -halo || cb + CH > n;
         // Jobs 2f and 2f+1 stage window f: its head (first chunk only) and
         // the chunk itself; job 2 nf is the main program over the chunk. One
         // loop, so the interpreter is inlined once per form.
@@ -725,20 +747,20 @@ __global__ void __launch_bounds__(kThreads, 3) k_tile(const __grid_constant__ Pr
                     r.woff4 = -head4;
                     r.gm = first && tid < head4 ? 1u : 0u;
                     r.p0 = cb - fd.z;
-                } else {  // the chunk: tile [head, head + kChunk)
+                } else {  // the chunk: tile [head, head + CH)
                     // Carry the head over: the previous chunk's last head
-                    // positions sit at tile [kChunk, kChunk + head). The
+                    // positions sit at tile [CH, CH + head). The
                     // thread that copies a float4 is the one whose staging
                     // below overwrites it, so no barrier is needed.
                     if (!first && tid >= kThreads - head4) {
                         float4* tile = cx.S + fd.w;
                         const int q = tid - (kThreads - head4);
-                        tile[q] = tile[kChunk4 + q];
+                        tile[q] = tile[CH4 + q];
                     }
                     r.sh_in = in4 + hs / 4;
                     r.sh_st = head4;
                     r.woff4 = 0;
-                    r.gm = (1u << kG) - 1;
+                    r.gm = (1u << G) - 1;
                     r.p0 = cb;
                 }
             } else {
@@ -746,26 +768,25 @@ __global__ void __launch_bounds__(kThreads, 3) k_tile(const __grid_constant__ Pr
                 r.sh_in = in4 + hs / 4;
                 r.sh_st = 0;
                 r.woff4 = 0;
-                r.gm = (1u << kG) - 1;
+                r.gm = (1u << G) - 1;
                 r.p0 = cb;
             }
             r.edge = edge;
-            if (r.gm == (1u << kG) - 1)
-                interpret<BULK, true>(code_s, pc, cx, r, A);
+            if (r.gm == (1u << G) - 1)
+                interpret<BULK, true, G>(code_s, pc, cx, r, A);
             else if (r.gm)
-                interpret<BULK, false>(code_s, pc, cx, r, A);
+                interpret<BULK, false, G>(code_s, pc, cx, r, A);
             // Windows staged before the main program reads them, and a
             // window before a later window's staging reads it (chains).
             if ((j & 1) && (j + 1 == 2 * nf || (fir_s[j >> 1].y & kSyncAfter))) __syncthreads();
         }
         if (P.reduce != RED_NONE) {
-            float* wv = out + 8 * c;
-            int64_t* wi = out_idx ? out_idx + 8 * c : nullptr;
+            const int64_t b0 = c * (G / 2), nb = (n + kChunk - 1) / kChunk;
             switch (P.reduce) {  // uniform: one branch per chunk
-                case RED_SUM: chunk_warps<RED_SUM>(A, cb, n, idx_base, wv, wi); break;
-                case RED_MIN: chunk_warps<RED_MIN>(A, cb, n, idx_base, wv, wi); break;
-                case RED_MAX: chunk_warps<RED_MAX>(A, cb, n, idx_base, wv, wi); break;
-                default: chunk_warps<RED_ARGMAX>(A, cb, n, idx_base, wv, wi); break;
+                case RED_SUM: chunk_warps<RED_SUM, G>(A, cb, n, idx_base, out, out_idx, b0, nb); break;
+                case RED_MIN: chunk_warps<RED_MIN, G>(A, cb, n, idx_base, out, out_idx, b0, nb); break;
+                case RED_MAX: chunk_warps<RED_MAX, G>(A, cb, n, idx_base, out, out_idx, b0, nb); break;
+                default: chunk_warps<RED_ARGMAX, G>(A, cb, n, idx_base, out, out_idx, b0, nb); break;
             }
         }
         if (BULK) {
@@ -1254,6 +1275,7 @@ int32_t tile_off4(const Lowered& L, int f) {
 // The launch's shared-memory layout (float4 offsets) and its program.
 struct Layout {
     int32_t taps4, tiles4, temps4, stages4, sstride, nst;
+    int32_t g;  // float4 groups per thread (the interpreter's G); chunk = 1024 g
     size_t smem;
 };
 
@@ -1280,7 +1302,7 @@ void build_program(const simtgo_tile_graph* g, const Lowered& L, const Layout& Y
         *input = space == SP_IN;
         switch (space) {
             case SP_IN: return (uint16_t)(bulk ? idx * Y.sstride / 4 : idx);
-            case SP_TMP: return (uint16_t)(Y.temps4 + idx * tilek::kChunk4);
+            case SP_TMP: return (uint16_t)(Y.temps4 + idx * tilek::chunk_of(Y.g) / 4);
             case SP_WIN: return (uint16_t)(P.fir[idx].tile4 + P.fir[idx].head / 4);
             default: return (uint16_t)idx;
         }
@@ -1307,7 +1329,7 @@ void build_program(const simtgo_tile_graph* g, const Lowered& L, const Layout& Y
         }
         if (fi.sta) {
             in.flags |= tilek::F_STA;
-            in.d = (uint16_t)(Y.temps4 + fi.d_idx * tilek::kChunk4);
+            in.d = (uint16_t)(Y.temps4 + fi.d_idx * tilek::chunk_of(Y.g) / 4);
         }
         if (fi.stage) {
             in.flags |= tilek::F_STAGE;
@@ -1320,8 +1342,8 @@ void build_program(const simtgo_tile_graph* g, const Lowered& L, const Layout& Y
 
 // Launches a lowered program. dev_in[k] = device data of L.in_nodes[k] (halo
 // elements first).
-// For a reduction, out (and out_idx, ARGMAX) receive one partial per chunk
-// and idx_base is the index of element 0.
+// For a reduction, out (and out_idx, ARGMAX) receive eight warp partials per
+// 2048-element block and idx_base is the index of element 0.
 int launch_program(const simtgo_tile_graph* g, const Lowered& L,
                    const std::vector<const float*>& dev_in, float* out, int64_t n, int64_t halo,
                    cudaStream_t s, int64_t* out_idx = nullptr, int64_t idx_base = 0) {
@@ -1337,20 +1359,28 @@ int launch_program(const simtgo_tile_graph* g, const Lowered& L,
     int32_t hs = 0;
     for (int f = 0; f < n_fir; f++) hs = std::max<int32_t>(hs, L.head[f]);
     Layout Y;
+    // Four groups per thread for graphs without windows or Hypot.
+    bool hypot = false;
+    for (const FInsn& fi : L.code) hypot = hypot || fi.op == tilek::OP_HYPOT;
+    Y.g = n_fir == 0 && !hypot ? tilek::kGWide : tilek::kG;
+    const int chunk = tilek::chunk_of(Y.g);
     Y.taps4 = tilek::meta_bytes((int)L.code.size(), n_in, n_fir) / 16;
     Y.tiles4 = Y.taps4 + n_fir * tilek::kMaxTaps / 4;
     Y.temps4 = Y.tiles4 + tile_off4(L, n_fir);
-    Y.stages4 = Y.temps4 + L.n_tmp * tilek::kChunk4;
-    Y.sstride = hs + tilek::kChunk;
+    Y.stages4 = Y.temps4 + L.n_tmp * chunk / 4;
+    Y.sstride = hs + chunk;
     const size_t base_smem = (size_t)Y.stages4 * 16;
     const size_t stage_bytes = (size_t)n_in * Y.sstride * sizeof(float);
-    // Both instantiations may take up to the opt-in maximum of dynamic
+    // Every instantiation may take up to the opt-in maximum of dynamic
     // shared memory (less 1 KB for the static mbarriers).
     const int dyn_max = d->max_smem_optin - 1024;
     static std::atomic<uint64_t> configured{0};
     const uint64_t dev_bit = 1ull << (d->device & 63);
+    using tilek::kG;
+    using tilek::kGWide;
     if (!(configured.load() & dev_bit)) {
-        for (auto k : {tilek::k_tile<true>, tilek::k_tile<false>}) {
+        for (auto k : {tilek::k_tile<true, kG>, tilek::k_tile<false, kG>,
+                       tilek::k_tile<true, kGWide>, tilek::k_tile<false, kGWide>}) {
             rc = sg::cuda_status(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                       dyn_max),
                                  "cudaFuncSetAttribute(tile)");
@@ -1366,7 +1396,9 @@ int launch_program(const simtgo_tile_graph* g, const Lowered& L,
     // from HBM by the interpreter itself (DIRECT).
     int reg_blocks = 0;
     rc = sg::cuda_status(cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-                             &reg_blocks, tilek::k_tile<true>, tilek::kThreads, base_smem),
+                             &reg_blocks,
+                             Y.g == kG ? tilek::k_tile<true, kG> : tilek::k_tile<true, kGWide>,
+                             tilek::kThreads, base_smem),
                          "cudaOccupancyMaxActiveBlocksPerMultiprocessor(tile)");
     if (rc) return rc;
     bool bulk = false;
@@ -1398,7 +1430,8 @@ int launch_program(const simtgo_tile_graph* g, const Lowered& L,
     static thread_local tilek::Program P;
     build_program(g, L, Y, bulk, P);
     for (int k = 0; k < n_in; k++) P.in[k] = dev_in[k];  // element 0; [-halo, 0) precede it
-    auto kern = bulk ? tilek::k_tile<true> : tilek::k_tile<false>;
+    auto kern = Y.g == kG ? (bulk ? tilek::k_tile<true, kG> : tilek::k_tile<false, kG>)
+                          : (bulk ? tilek::k_tile<true, kGWide> : tilek::k_tile<false, kGWide>);
     int per_sm = 0;
     rc = sg::cuda_status(
         cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, tilek::kThreads, Y.smem),
@@ -1411,7 +1444,7 @@ int launch_program(const simtgo_tile_graph* g, const Lowered& L,
     // B200 at 2^28 elements). Short signals keep one wave: every range starts
     // with a pipeline fill and, with windows, a head run, and a partial wave
     // would leave most SMs idle at the end.
-    const int64_t chunks = sg::ceil_div(n, tilek::kChunk);
+    const int64_t chunks = sg::ceil_div(n, (int64_t)chunk);
     const int64_t resident = (int64_t)d->sms * std::max(1, per_sm);
     const int64_t waves = std::max<int64_t>(1, std::min<int64_t>(8, chunks / (32 * resident)));
     const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(chunks, waves * resident));
