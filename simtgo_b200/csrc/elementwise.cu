@@ -8,9 +8,10 @@
 // movement for all of them: blocks of 256 threads take contiguous ranges of
 // 16-byte vector units, each thread issuing the loads of four units before
 // it computes any (64 B of every input stream in flight per thread), with
-// L1-bypassing 128-bit loads and evict-first 128-bit stores. Pointers that are not 16-byte aligned take a scalar variant of the
-// same arithmetic. The arithmetic itself is exact.cuh: the emulator's result,
-// bit for bit. The caller's grid*block still bounds which indices are written.
+// L1-bypassing 128-bit loads and evict-first 128-bit stores. Pointers that
+// are not 16-byte aligned take a scalar variant of the same arithmetic. The
+// arithmetic itself is exact.cuh: the emulator's result, bit for bit. The
+// caller's grid*block still bounds which indices are written.
 #include <algorithm>
 #include <type_traits>
 

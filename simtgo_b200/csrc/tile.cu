@@ -633,12 +633,10 @@ __device__ __forceinline__ ChunkSpan chunk_span(int64_t cb, int hs, int64_t n, i
 // stage (a shared counter per stage) refills it, instead of thread 0 after a
 // block barrier.
 template <bool BULK, int G>
-__global__ void __launch_bounds__(kThreads, G == kG ? 3 : 2) k_tile(const __grid_constant__ Program P,
-                                                   float* __restrict__ out, int64_t n,
-                                                   int64_t halo, bool vec, bool in_vec, int32_t hs,
-                                                   int32_t stages4, int32_t nst, uint32_t* wd,
-                                                   int64_t* __restrict__ out_idx,
-                                                   int64_t idx_base) {
+__global__ void __launch_bounds__(kThreads, G == kG ? 3 : 2)
+    k_tile(const __grid_constant__ Program P, float* __restrict__ out, int64_t n, int64_t halo,
+           bool vec, bool in_vec, int32_t hs, int32_t stages4, int32_t nst, uint32_t* wd,
+           int64_t* __restrict__ out_idx, int64_t idx_base) {
     constexpr int CH = chunk_of(G), CH4 = CH / 4;
     __shared__ __align__(8) uint64_t bars[kMaxStages];   // stage s loaded
     __shared__ int rel[kMaxStages];  // warps done with stage s (window-free graphs)
@@ -782,11 +780,13 @@ __global__ void __launch_bounds__(kThreads, G == kG ? 3 : 2) k_tile(const __grid
         }
         if (P.reduce != RED_NONE) {
             const int64_t b0 = c * (G / 2), nb = (n + kChunk - 1) / kChunk;
+            float* o = out;
+            int64_t* oi = out_idx;
             switch (P.reduce) {  // uniform: one branch per chunk
-                case RED_SUM: chunk_warps<RED_SUM, G>(A, cb, n, idx_base, out, out_idx, b0, nb); break;
-                case RED_MIN: chunk_warps<RED_MIN, G>(A, cb, n, idx_base, out, out_idx, b0, nb); break;
-                case RED_MAX: chunk_warps<RED_MAX, G>(A, cb, n, idx_base, out, out_idx, b0, nb); break;
-                default: chunk_warps<RED_ARGMAX, G>(A, cb, n, idx_base, out, out_idx, b0, nb); break;
+                case RED_SUM: chunk_warps<RED_SUM, G>(A, cb, n, idx_base, o, oi, b0, nb); break;
+                case RED_MIN: chunk_warps<RED_MIN, G>(A, cb, n, idx_base, o, oi, b0, nb); break;
+                case RED_MAX: chunk_warps<RED_MAX, G>(A, cb, n, idx_base, o, oi, b0, nb); break;
+                default: chunk_warps<RED_ARGMAX, G>(A, cb, n, idx_base, o, oi, b0, nb); break;
             }
         }
         if (BULK) {
