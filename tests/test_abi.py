@@ -223,3 +223,36 @@ def test_launch_shared_spelling_refused():
     with pytest.raises(simt.DynamicSharedError) as e:
         plain.launch_shared(1, 32, 8, None, None, None)
     assert not e.value.dynamic
+
+
+def test_tile_reduce_arguments_refused_on_the_host(lib):
+    """The reductions' argument checks run before anything touches a
+    device: an unknown kind, a missing value or ArgMax index, a graph error,
+    a shard range outside the ranks."""
+    g = lib.simtgo_tile_new()
+    try:
+        fake = C.c_void_p(0x1000)   # never dereferenced: every call below is refused first
+        t = lib.simtgo_tile_input_device(g, fake, 64)
+        assert lib.simtgo_tile_reduce(g, t, 9, fake, fake, None) == _lib.EARG
+        assert lib.simtgo_tile_reduce(g, t, -1, fake, fake, None) == _lib.EARG
+        assert lib.simtgo_tile_reduce(g, t, tile.SUM, None, None, None) == _lib.ENULL
+        assert lib.simtgo_tile_reduce(g, t, tile.ARGMAX, fake, None, None) == _lib.ENULL
+        assert lib.simtgo_tile_reduce(g, 99, tile.SUM, fake, None, None) == _lib.EARG
+        v, i = C.c_float(), C.c_int64()
+        assert lib.simtgo_tile_reduce_materialize(g, t, 7, C.byref(v), C.byref(i)) == _lib.EARG
+        s0, n = C.c_int64(), C.c_int64()
+        assert lib.simtgo_tile_shard_range(100, 0, 0, C.byref(s0), C.byref(n)) == _lib.EARG
+        assert lib.simtgo_tile_shard_range(-1, 2, 0, C.byref(s0), C.byref(n)) == _lib.EARG
+        assert lib.simtgo_tile_shard_range(100, 2, 0, None, C.byref(n)) == _lib.ENULL
+        assert lib.simtgo_tile_allow_chained_windows(None, 1) == _lib.ENULL
+    finally:
+        lib.simtgo_tile_free(g)
+    bad = lib.simtgo_tile_new()
+    try:
+        a = lib.simtgo_tile_input_device(bad, C.c_void_p(0x1000), 8)
+        b = lib.simtgo_tile_input_device(bad, C.c_void_p(0x2000), 9)
+        lib.simtgo_tile_add(bad, a, b)   # length mismatch: latched
+        assert lib.simtgo_tile_reduce(bad, a, tile.SUM, C.c_void_p(0x1000), None,
+                                      None) == _lib.EGRAPH
+    finally:
+        lib.simtgo_tile_free(bad)
