@@ -480,6 +480,35 @@ static_assert(kThreads == 256 && kG == 2, "the reduction tree assumes 8 warps of
 // G/2 blocks of the reduction tree (2048 positions, groups 2 sb and 2 sb + 1
 // of block sb), the first being block blk0 of the launch; block b's warp w
 // writes out[8 b + w] (and out_i), for the nblk blocks the launch has.
+// ARGMAX inside one 2048-block: the index travels as a 32-bit offset in
+// the block (the same order as the global index; INT32_MAX for "no
+// element") and is widened once per warp partial.
+struct RV32 {
+    float v;
+    int32_t o;
+};
+__device__ __forceinline__ RV32 am_pick32(const RV32& a, const RV32& b) {
+    const bool na = a.v != a.v, nb = b.v != b.v;
+    if (na || nb) return (na && nb ? a.o < b.o : na) ? a : b;
+    if (a.v > b.v) return a;
+    if (b.v > a.v) return b;
+    const bool sa = __float_as_uint(a.v) >> 31, sb = __float_as_uint(b.v) >> 31;
+    if (sa != sb) return sa ? b : a;
+    return a.o < b.o ? a : b;
+}
+__device__ __forceinline__ RV32 am_warp32(const RV32 (&x)[8]) {
+    RV32 v = am_pick32(am_pick32(am_pick32(x[0], x[1]), am_pick32(x[2], x[3])),
+                       am_pick32(am_pick32(x[4], x[5]), am_pick32(x[6], x[7])));
+#pragma unroll
+    for (int m = 16; m >= 1; m >>= 1) {
+        RV32 o;
+        o.v = __shfl_xor_sync(0xffffffffu, v.v, m);
+        o.o = __shfl_xor_sync(0xffffffffu, v.o, m);
+        v = am_pick32(v, o);
+    }
+    return v;
+}
+
 template <int KIND, int G>
 __device__ __forceinline__ void chunk_warps(const float4 (&A)[G], int64_t cb, int64_t n,
                                             int64_t idx_base, float* out, int64_t* out_i,
@@ -491,20 +520,34 @@ __device__ __forceinline__ void chunk_warps(const float4 (&A)[G], int64_t cb, in
         if (b < nblk) {  // uniform over the block
             const int64_t base = cb + (int64_t)kChunk * sb;
             const bool full = base + kChunk <= n;
-            RVal x[8];
+            if constexpr (KIND == RED_ARGMAX) {
+                RV32 x[8];
 #pragma unroll
-            for (int k = 0; k < 2; k++)
+                for (int k = 0; k < 2; k++)
 #pragma unroll
-                for (int e = 0; e < 4; e++) {
-                    const int64_t p = base + 4 * (t + kThreads * k) + e;
-                    x[4 * k + e] = (full || p < n) ? RVal{f4_get(A[2 * sb + k], e),
-                                                          KIND == RED_ARGMAX ? idx_base + p : 0}
-                                                   : red_identity<KIND>();
+                    for (int e = 0; e < 4; e++) {
+                        const int32_t o = 4 * (t + kThreads * k) + e;
+                        x[4 * k + e] = (full || base + o < n)
+                                           ? RV32{f4_get(A[2 * sb + k], e), o}
+                                           : RV32{__int_as_float((int)0xff800000u), INT32_MAX};
+                    }
+                const RV32 w = am_warp32(x);
+                if ((t & 31) == 0) {
+                    out[8 * b + (t >> 5)] = w.v;
+                    out_i[8 * b + (t >> 5)] = w.o == INT32_MAX ? kNoIndex : idx_base + base + w.o;
                 }
-            const RVal w = red_warp<KIND>(red_thread<KIND>(x));
-            if ((t & 31) == 0) {
-                out[8 * b + (t >> 5)] = w.v;
-                if (KIND == RED_ARGMAX) out_i[8 * b + (t >> 5)] = w.i;
+            } else {
+                RVal x[8];
+#pragma unroll
+                for (int k = 0; k < 2; k++)
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        const int64_t p = base + 4 * (t + kThreads * k) + e;
+                        x[4 * k + e] = (full || p < n) ? RVal{f4_get(A[2 * sb + k], e), 0}
+                                                       : red_identity<KIND>();
+                    }
+                const RVal w = red_warp<KIND>(red_thread<KIND>(x));
+                if ((t & 31) == 0) out[8 * b + (t >> 5)] = w.v;
             }
         }
     }
