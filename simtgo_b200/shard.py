@@ -63,7 +63,18 @@ def histogram_plan(total: int, world: int, rank: int) -> Shard:
     return Shard(rank, lo, hi, lo, 0)
 
 
+def chain_window(taps_along_chain) -> int:
+    """The window one FIR of `taps` would need to reach as far below a
+    position as a chain of FIRs does (each reads the one inside it, the
+    library's opt-in chained windows): 1 + the sum of taps-1 over the chain.
+    Pass it as tile_plan's max_taps for a shard that is exact at its edge."""
+    return 1 + sum(max(0, int(t) - 1) for t in taps_along_chain)
+
+
 def tile_plan(total: int, world: int, rank: int, max_taps: int = 0) -> Shard:
+    """Contiguous element blocks; with a window (FIR) node of at most
+    max_taps taps -- or a chain of them, see chain_window -- each shard's
+    inputs start round_halo(max_taps) samples early."""
     lo, hi = split(total, world, rank)
     halo = min(lo, round_halo(max_taps)) if max_taps > 0 else 0
     return Shard(rank, lo, hi, lo - halo, halo)

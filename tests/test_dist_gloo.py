@@ -200,3 +200,12 @@ def test_fir_plan_halo_alignment():
     assert p.halo == 128 and p.in_lo == p.out_lo - 128 and p.n == 1 << 28
     assert shard.fir_plan(1 << 31, 8, 0, 127).halo == 0
     assert shard.round_halo(31) == 32 and shard.round_halo(1) == 0
+
+
+def test_chain_window_halo():
+    # FIR(Add(FIR(a, 17 taps), a), 21 taps) reaches 16 + 20 samples below.
+    assert shard.chain_window([17, 21]) == 37
+    assert shard.round_halo(shard.chain_window([17, 21])) == 36
+    p = shard.tile_plan(1 << 20, 4, 2, max_taps=shard.chain_window([17, 21]))
+    assert p.halo == 36 and p.in_lo == p.out_lo - 36
+    assert shard.chain_window([1, 1]) == 1 and shard.round_halo(1) == 0
