@@ -401,7 +401,11 @@ int simtgo_tile_shard_range(int64_t n_total, int32_t nranks, int32_t rank, int64
  * partials of its own blocks, an NCCL all-gather assembles every block's
  * partial on every rank, and each rank finishes the same tree: the result
  * equals simtgo_tile_reduce over the whole signal, bit for bit, on every
- * rank; ARGMAX indices are global. Asynchronous on stream. */
+ * rank; ARGMAX indices are global. Asynchronous on stream. As with any NCCL
+ * collective, the ranks must agree: a rank whose arguments are refused
+ * returns before the all-gather, and its peers' all-gather then waits for
+ * it, so a caller validates the split (simtgo_tile_shard_range) on every
+ * rank before calling. */
 int simtgo_tile_reduce_shard(simtgo_tile_graph* g, simtgo_tensor t, int32_t kind, int32_t halo,
                              int64_t n_total, simtgo_comm* comm, float* dev_value,
                              int64_t* dev_index, void* stream);
