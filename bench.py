@@ -706,11 +706,25 @@ def cpu_baseline(args, np, seconds):
         dt = time.perf_counter() - t0
         if dt >= seconds:
             break
-    return {"value": round(done * sample / dt / 1e9, 4), "unit": "Gsamples/s", "cores": threads,
+    value = done * sample / dt / 1e9
+    # One core, for scale: the same code on a smaller sample for ~1 s.
+    O.set_threads(1)
+    one = 1 << 18
+    done1, t1 = 0, time.perf_counter()
+    while True:
+        O.fir_shard(x[: one + TAPS], 0, h, one, fused=False)
+        done1 += 1
+        dt1 = time.perf_counter() - t1
+        if dt1 >= min(1.0, seconds):
+            break
+    O.set_threads(threads)
+    return {"value": round(value, 4), "unit": "Gsamples/s", "cores": threads,
             "kind": "port", "seconds": round(dt, 2),
+            "single_core_value": round(done1 * one / dt1 / 1e9, 4),
             "sample": f"{done} x {sample} outputs x {TAPS} taps of the FIR workload (the oracle "
                       "port of gpu.RunCPU's FIR, -O3 -ffp-contract=off, block-parallel pthreads "
-                      "on every host core)"}
+                      f"on every host core); single_core_value: {done1} x {one} outputs on one "
+                      "thread"}
 
 
 def run_reference(args):
