@@ -338,3 +338,33 @@ def test_random_graph_listing_matches_oracle(seed):
     rc, want = O.tile_eval(nodes, len(nodes) - 1, n, halo)
     assert rc == 0
     np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+def test_chain_of_eight_full_windows():
+    """The deepest chain the kernel stages: eight 64-tap windows each reading
+    the one before (heads of 68 to 544 samples), emulated against the
+    oracle with a halo."""
+    n, halo = 60, 16   # the emulator wants the span longer than the taps
+    rng = np.random.default_rng(8)
+    g = tile.New().AllowChainedWindows()
+    d = rng.uniform(-1, 1, n + halo).astype(f32)
+    cur = g.Input(d[halo:])
+    nodes = [{"kind": "input", "data": d}]
+    for _ in range(8):
+        h = (rng.uniform(-1, 1, 64) / 16).astype(f32)
+        nodes.append({"kind": "input", "data": h})
+        a = cur.node
+        cur = tile.FIR(cur, h)
+        nodes.append({"kind": "fir", "a": a, "taps": h})
+        assert cur.node == len(nodes) - 1
+    assert g.Err() is None
+    src = cur.Source()
+    assert src.count("window ") == 8
+    node_of = [int(m) for m in re.findall(r"; in\d+ = node (\d+)", src)]
+    taps = {}
+    for m in re.finditer(r"window (\d+) taps \d+ node (\d+)", src):
+        taps[int(m.group(1))] = nodes[int(m.group(2))]["taps"]
+    got = run_listing(src, [nodes[i]["data"] for i in node_of], n, taps, halo)
+    rc, want = O.tile_eval(nodes, len(nodes) - 1, n, halo)
+    assert rc == 0
+    np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))
