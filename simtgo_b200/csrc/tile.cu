@@ -54,814 +54,10 @@
 
 #include "common.cuh"
 #include "exact.cuh"
+#include "tile_kernel.cuh"
 #include "tma.cuh"
 
 using namespace sgd;
-
-namespace tilek {
-
-constexpr int kThreads = 256;
-// Float4 groups per thread (the template parameter G): 2 for graphs with
-// windows or Hypot, 4 (kGWide) for the others, whose dispatch and chunk
-// costs then spread over twice the elements (eight chained Muls measured
-// 0.57 -> 0.76 of HBM; Hypot's registers make it slower there).
-constexpr int kG = 2;
-constexpr int kGWide = 4;
-__host__ __device__ constexpr int chunk_of(int G) { return kThreads * 4 * G; }
-// 2048: the chunk of G = 2 (every window's tile is laid out for it) and the
-// block of the reduction trees, whatever G the interpreter runs with.
-constexpr int kChunk = chunk_of(kG);
-constexpr int kChunk4 = kChunk / 4;
-constexpr int kMaxCode = 1024;
-constexpr int kMaxIn = 32;
-constexpr int kMaxFir = 8;
-constexpr int kMaxTmp = 8;
-constexpr int kMaxTaps = SIMTGO_TILE_MAX_TAPS;
-// Samples a chunk's window reaches below it: taps-1 rounded up to 16 bytes,
-// plus 4 of slack so that the first 16-byte window load stays in the tile.
-__host__ __device__ constexpr int window_reach(int taps) { return (taps - 1 + 3) / 4 * 4 + 4; }
-// Staged floats of a window's tile: its head, the chunk and 4 of slack.
-__host__ __device__ constexpr int tile_floats(int head) { return kChunk + head + 4; }
-constexpr int kMaxStages = 16;
-// FirDesc.taps flag: a later window's staging reads this window's tile, so
-// the block synchronises after staging it (chained windows).
-constexpr int32_t kSyncAfter = 1 << 8;
-
-// Steps of the accumulator machine. A is the accumulator (the thread's
-// 8 elements), M an operand in shared memory. The lowering emits these one
-// by one; a device instruction fuses a run of them (below).
-enum Op : uint8_t {
-    OP_END = 0,
-    OP_LDA,     // A = M
-    OP_STA,     // M = A (a temporary)
-    OP_ADD,     // A = A + M
-    OP_MUL,     // A = A * M
-    OP_HYPOT,   // A = hypot(A, M)
-    OP_SCALE,   // A = imm * A
-    OP_SQRT,    // A = sqrt(A)
-    OP_ABS,     // A = |A|
-    OP_FIRACC,  // A = window b accumulated at the thread's positions
-    OP_STAGE,   // window's tile = A (zero outside the signal)
-    OP_STORE,   // out = A
-    OP_KINDS,
-};
-// A device instruction is one dispatch doing, in order: [A = M(a)] if
-// F_LOADA; the operation op (ADD/MUL/HYPOT with operand M(b), SCALE, SQRT,
-// ABS, FIRACC of window b; OP_END: none); [M(d) = A] if F_STA; [tile of
-// window d = A] if F_STAGE; [out = A] if F_STORE; return if F_END.
-constexpr uint8_t F_LOADA = 1;
-constexpr uint8_t F_IN_A = 2;   // M(a) is a staged input: a is relative to the current stage
-constexpr uint8_t F_IN_B = 4;   // M(b) likewise
-constexpr uint8_t F_SELF = 8;   // M(b) is A itself (x op x)
-constexpr uint8_t F_STA = 16;
-constexpr uint8_t F_STAGE = 32;
-constexpr uint8_t F_STORE = 64;
-constexpr uint8_t F_END = 128;
-
-struct Insn {
-    uint8_t op;
-    uint8_t flags;
-    uint16_t a;  // F_LOADA operand: float4 offset in shared memory (or input index, DIRECT)
-    uint16_t b;  // binary operand likewise, or the FIRACC window
-    uint16_t d;  // F_STA temporary (float4 offset) or F_STAGE window
-    float imm;   // SCALE factor
-    uint32_t pad;
-};
-static_assert(sizeof(Insn) == 16, "one 16-byte shared load per instruction");
-
-struct FirDesc {
-    int32_t start;  // pc of the staging program
-    int32_t taps;   // the taps, | kSyncAfter when a later window reads this one
-    int32_t head;   // positions the tile holds below the chunk (a multiple of 4)
-    int32_t tile4;  // float4 offset of the window's tile in shared memory
-    float h[kMaxTaps];  // the coefficients travel in the parameter block
-};
-
-// Reductions (SIMTGO_TILE_SUM ..): the main program's value is reduced
-// instead of stored.
-enum Reduce : int32_t { RED_NONE = -1, RED_SUM = 0, RED_MIN = 1, RED_MAX = 2, RED_ARGMAX = 3 };
-
-struct Program {
-    int32_t main_start;
-    int32_t reduce;  // RED_NONE, or the reduction of the main program's value
-    int32_t n_fir;
-    int32_t n_in;
-    int32_t n_code;
-    FirDesc fir[kMaxFir];
-    const float* in[kMaxIn];  // element 0 of each input; in[k][i] is valid for i in [-halo, n)
-    Insn code[kMaxCode];
-};
-
-// The program as the interpreter reads it: copied once per block from the
-// parameter bank into shared memory, where a warp-uniform word is one
-// broadcast load. Layout: code[code_cap] (the program and one END) |
-// fir[n_fir] (start, taps | flags, head, tile4) | in[n_in], 16-byte rounded.
-__host__ __device__ constexpr int meta_code_cap(int n_code) { return n_code + 1; }
-__host__ __device__ constexpr int meta_bytes(int n_code, int n_in, int n_fir) {
-    return ((meta_code_cap(n_code) * 16 + n_in * 8 + n_fir * 16) + 15) & ~15;
-}
-
-// One run of a program over kChunk (or, for a window's halo, fewer)
-// positions.
-struct Run {
-    int32_t sh_in;   // added to F_IN operands: the stage and the run's position
-    int32_t sh_st;   // added to STAGE destinations (the run's offset in the tile)
-    int32_t woff4;   // (run position - chunk position) / 4: where FIRACC reads a tile
-    uint32_t gm;     // which of the thread's groups take part
-    int64_t p0;      // position of the run's element 0
-    bool edge;       // some positions of the run lie outside [-halo, n)
-};
-
-struct Ctx {
-    float4* S;               // dynamic shared memory
-    const float* taps_s;     // n_fir x kMaxTaps coefficients, zero past taps
-    const int4* fir;         // shared (start, taps | flags, head, tile4)
-    const float* const* in;  // shared copy of Program::in
-    float* out;
-    int64_t n, halo;
-    bool vec;                // out is 16-byte aligned
-    bool in_vec;             // every input is 16-byte aligned
-};
-
-__device__ __forceinline__ float4 f4_add(float4 a, float4 b) {
-    return make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z),
-                       __fadd_rn(a.w, b.w));
-}
-__device__ __forceinline__ float4 f4_mul(float4 a, float4 b) {
-    return make_float4(__fmul_rn(a.x, b.x), __fmul_rn(a.y, b.y), __fmul_rn(a.z, b.z),
-                       __fmul_rn(a.w, b.w));
-}
-__device__ __forceinline__ float4 f4_scale(float k, float4 a) {
-    return make_float4(__fmul_rn(k, a.x), __fmul_rn(k, a.y), __fmul_rn(k, a.z),
-                       __fmul_rn(k, a.w));
-}
-__device__ __forceinline__ float4 f4_sqrt(float4 a) {
-    return make_float4(__fsqrt_rn(a.x), __fsqrt_rn(a.y), __fsqrt_rn(a.z), __fsqrt_rn(a.w));
-}
-__device__ __forceinline__ float4 f4_abs(float4 a) {
-    return make_float4(fabsf(a.x), fabsf(a.y), fabsf(a.z), fabsf(a.w));
-}
-__device__ __forceinline__ float4 f4_hypot(float4 a, float4 b) {
-    return make_float4(hypot_go(a.x, b.x), hypot_go(a.y, b.y), hypot_go(a.z, b.z),
-                       hypot_go(a.w, b.w));
-}
-__device__ __forceinline__ float f4_get(const float4& v, int j) {
-    return j == 0 ? v.x : j == 1 ? v.y : j == 2 ? v.z : v.w;
-}
-
-// The window accumulation for the thread's groups: output j of group k sits
-// at tile index b_k + j, b_k = 4 (t + 256 k + woff4) + head, and takes
-// fma(h[i], tile[b_k + j - i], acc) for i = 0 .. taps-1 in order. With
-// W = tile[b_k - i0 - 4 .. b_k - i0 + 3] for taps i0 .. i0+3, the sample of
-// output j at tap i0+u is W[4 + j - u]; the upper half of W is the lower
-// half of the previous step, so each step loads one new float4 per group.
-// Four taps (hv[0..nk-1]) on the 4 outputs of one group, with
-// w = tile[b - i0 - 4 .. b - i0 + 3] given as its halves lo, hi.
-template <bool PART>
-__device__ __forceinline__ void fir_step(float (&acc)[4], const float4& lo, const float4& hi,
-                                         const float (&hv)[4], int nk) {
-    const float w[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
-#pragma unroll
-    for (int u = 0; u < 4; u++)
-        if (!PART || u < nk)
-#pragma unroll
-            for (int j = 0; j < 4; j++) acc[j] = __fmaf_rn(hv[u], w[4 + j - u], acc[j]);
-}
-
-template <int G>
-__device__ __forceinline__ void fir_acc(float4 (&A)[G], const Ctx& c, int f, int woff4) {
-    const int4 fd = c.fir[f];
-    const int taps = fd.y & (kSyncAfter - 1);
-    const float4* h4 = reinterpret_cast<const float4*>(c.taps_s + f * kMaxTaps);
-    // Group k's window float4 at tap i0 (a multiple of 4): tw[k][-i0/4].
-    const float4* tw = c.S + fd.w + threadIdx.x + fd.z / 4 + woff4;
-    float acc[G][4];
-    float4 hi[G];
-#pragma unroll
-    for (int k = 0; k < G; k++) {
-#pragma unroll
-        for (int j = 0; j < 4; j++) acc[k][j] = 0.0f;
-        hi[k] = tw[kThreads * k];
-    }
-    // Whole steps of 8 taps, two window loads per group, no predicates.
-    int i0 = 0;
-    for (; i0 + 8 <= taps; i0 += 8) {
-        const float4 ha = h4[i0 / 4], hb = h4[i0 / 4 + 1];
-        const float hva[4] = {ha.x, ha.y, ha.z, ha.w}, hvb[4] = {hb.x, hb.y, hb.z, hb.w};
-#pragma unroll
-        for (int k = 0; k < G; k++) {
-            const float4 m = tw[kThreads * k - i0 / 4 - 1];
-            const float4 lo = tw[kThreads * k - i0 / 4 - 2];
-            fir_step<false>(acc[k], m, hi[k], hva, 4);
-            fir_step<false>(acc[k], lo, m, hvb, 4);
-            hi[k] = lo;
-        }
-    }
-    // The last 1-7 taps, 4 at a time.
-    for (; i0 < taps; i0 += 4) {
-        const float4 hk = h4[i0 / 4];
-        const float hv[4] = {hk.x, hk.y, hk.z, hk.w};
-        const int nk = min(4, taps - i0);
-#pragma unroll
-        for (int k = 0; k < G; k++) {
-            const float4 lo = tw[kThreads * k - i0 / 4 - 1];
-            fir_step<true>(acc[k], lo, hi[k], hv, nk);
-            hi[k] = lo;
-        }
-    }
-#pragma unroll
-    for (int k = 0; k < G; k++) A[k] = make_float4(acc[k][0], acc[k][1], acc[k][2], acc[k][3]);
-}
-
-// Positions p .. p+3 of input b read from HBM (DIRECT mode), 0 outside
-// [-halo, n).
-__device__ __forceinline__ float4 gload4(const float* b, int64_t p, const Ctx& c) {
-    if (p >= -c.halo && p + 3 < c.n)
-        return c.in_vec ? ld_stream_f4(b + p) : make_float4(b[p], b[p + 1], b[p + 2], b[p + 3]);
-    float f[4];
-#pragma unroll
-    for (int j = 0; j < 4; j++) f[j] = (p + j >= -c.halo && p + j < c.n) ? b[p + j] : 0.0f;
-    return make_float4(f[0], f[1], f[2], f[3]);
-}
-
-// Zeroes the lanes of v whose positions (p .. p+3) lie outside [-halo, n).
-__device__ __forceinline__ float4 mask_outside(float4 v, int64_t p, const Ctx& c) {
-    if (p >= -c.halo && p + 3 < c.n) return v;
-    float f[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-    for (int j = 0; j < 4; j++)
-        if (!(p + j >= -c.halo && p + j < c.n)) f[j] = 0.0f;
-    return make_float4(f[0], f[1], f[2], f[3]);
-}
-
-// Runs the program from pc until an instruction with F_END, leaving the
-// last value in A (which a reduction consumes). Inlined into
-// k_tile twice: FULL for runs where all of the thread's groups take part
-// (the chunk), and the general form for a window's head run. (Loading the
-// next instruction ahead measured slower: it costs more instructions than
-// the shared-load latency it hides.) In DIRECT mode (BULK false) an input
-// operand is read from HBM at the run's positions.
-template <bool BULK, bool FULL, int G>
-__device__ __forceinline__ void interpret(const Insn* code, int pc, const Ctx& c, const Run& r,
-                                          float4 (&A)[G]) {
-    const int t = threadIdx.x;
-#pragma unroll
-    for (int k = 0; k < G; k++) A[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (;;) {
-        const Insn in = code[pc++];
-        // Group k of operand M(x) (inactive groups: A itself, nothing is read).
-        auto operand = [&](int x, bool input, int k) -> float4 {
-            if (!FULL && !((r.gm >> k) & 1)) return A[k];
-            if (!BULK && input) return gload4(c.in[x], r.p0 + 4 * (t + kThreads * k), c);
-            return c.S[x + (input ? r.sh_in : 0) + t + kThreads * k];
-        };
-        if (in.flags & F_LOADA) {
-#pragma unroll
-            for (int k = 0; k < G; k++) A[k] = operand(in.a, in.flags & F_IN_A, k);
-        }
-        // The second operand of a binary operation, read inside its case.
-        auto binop = [&](int k) -> float4 {
-            return (in.flags & F_SELF) ? A[k] : operand(in.b, in.flags & F_IN_B, k);
-        };
-        switch (in.op) {
-            case OP_ADD:
-#pragma unroll
-                for (int k = 0; k < G; k++) A[k] = f4_add(A[k], binop(k));
-                break;
-            case OP_MUL:
-#pragma unroll
-                for (int k = 0; k < G; k++) A[k] = f4_mul(A[k], binop(k));
-                break;
-            case OP_HYPOT:
-#pragma unroll
-                for (int k = 0; k < G; k++) A[k] = f4_hypot(A[k], binop(k));
-                break;
-            case OP_SCALE:
-#pragma unroll
-                for (int k = 0; k < G; k++) A[k] = f4_scale(in.imm, A[k]);
-                break;
-            case OP_SQRT:
-#pragma unroll
-                for (int k = 0; k < G; k++) A[k] = f4_sqrt(A[k]);
-                break;
-            case OP_ABS:
-#pragma unroll
-                for (int k = 0; k < G; k++) A[k] = f4_abs(A[k]);
-                break;
-            case OP_FIRACC:
-                fir_acc<G>(A, c, in.b, r.woff4);
-                break;
-            default:
-                break;  // OP_END: no operation
-        }
-        if (in.flags & (F_STA | F_STAGE | F_STORE | F_END)) {
-            if (in.flags & F_STA) {
-#pragma unroll
-                for (int k = 0; k < G; k++)
-                    if (FULL || ((r.gm >> k) & 1)) c.S[in.d + t + kThreads * k] = A[k];
-            }
-            if (in.flags & F_STAGE) {
-                float4* dst = c.S + c.fir[in.d].w + r.sh_st + t;
-#pragma unroll
-                for (int k = 0; k < G; k++)
-                    if (FULL || ((r.gm >> k) & 1))
-                        dst[kThreads * k] =
-                            r.edge ? mask_outside(A[k], r.p0 + 4 * (t + kThreads * k), c) : A[k];
-            }
-            if (in.flags & F_STORE) {
-#pragma unroll
-                for (int k = 0; k < G; k++) {
-                    const int64_t p = r.p0 + 4 * (t + kThreads * k);
-                    if (c.vec && p + 3 < c.n) {
-                        st_stream_f4(c.out + p, A[k]);
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < 4; j++)
-                            if (p + j < c.n) c.out[p + j] = f4_get(A[k], j);
-                    }
-                }
-            }
-            if (in.flags & F_END) return;
-        }
-    }
-}
-
-// ---- reductions ---------------------------------------------------------------
-// A value and, for ARGMAX, its index. The empty identity of ARGMAX is
-// (-inf, INT64_MAX): any element beats it. Every step is a template on the
-// reduction, so a chunk's reduction is straight-line code.
-struct RVal {
-    float v;
-    int64_t i;
-};
-constexpr int64_t kNoIndex = INT64_MAX;
-constexpr uint32_t kQNaN = 0x7fc00000u;
-
-template <int KIND>
-__device__ __forceinline__ RVal red_identity() {
-    if (KIND == RED_SUM) return {0.0f, 0};
-    if (KIND == RED_MIN) return {__int_as_float(0x7f800000), 0};
-    return {__int_as_float((int)0xff800000u), kNoIndex};
-}
-// Go's min and max (NaN wins, -0 < +0); NaN is returned as 0x7fc00000.
-// Branch-free: fminf/fmaxf, then equal values (only zeros of opposite signs
-// differ in bits) combined by OR (min: -0 wins) or AND (max: +0 wins), then
-// NaN.
-__device__ __forceinline__ float go_min(float a, float b) {
-    float m = fminf(a, b);
-    if (a == b) m = __uint_as_float(__float_as_uint(a) | __float_as_uint(b));
-    return (a != a || b != b) ? __uint_as_float(kQNaN) : m;
-}
-__device__ __forceinline__ float go_max(float a, float b) {
-    float m = fmaxf(a, b);
-    if (a == b) m = __uint_as_float(__float_as_uint(a) & __float_as_uint(b));
-    return (a != a || b != b) ? __uint_as_float(kQNaN) : m;
-}
-// ARGMAX order: NaN above everything, then value (+0 above -0), then the
-// smaller index. A strict total order on distinct indices, so any tree of
-// pairwise choices finds the same element. (Early returns measured faster
-// here than evaluating every clause and selecting.)
-__device__ __forceinline__ bool am_before(const RVal& a, const RVal& b) {
-    const bool na = a.v != a.v, nb = b.v != b.v;
-    if (na || nb) return na && nb ? a.i < b.i : na;
-    if (a.v > b.v) return true;
-    if (b.v > a.v) return false;
-    const bool sa = __float_as_uint(a.v) >> 31, sb = __float_as_uint(b.v) >> 31;
-    if (sa != sb) return !sa;
-    return a.i < b.i;
-}
-template <int KIND>
-__device__ __forceinline__ RVal red2(const RVal& a, const RVal& b) {
-    if (KIND == RED_SUM) return {__fadd_rn(a.v, b.v), 0};
-    if (KIND == RED_MIN) return {go_min(a.v, b.v), 0};
-    if (KIND == RED_MAX) return {go_max(a.v, b.v), 0};
-    return am_before(a, b) ? a : b;
-}
-// The caller's result: a NaN sum as 0x7fc00000 (NaN payloads differ by
-// platform), ARGMAX's empty index as -1.
-template <int KIND>
-__device__ __forceinline__ RVal red_final(RVal r) {
-    if (KIND == RED_SUM && r.v != r.v) r.v = __uint_as_float(kQNaN);
-    if (KIND == RED_ARGMAX && r.i == kNoIndex) r.i = -1;
-    return r;
-}
-// A thread's eight values: x[0..3] its group at 4t, x[4..7] at 1024 + 4t.
-template <int KIND>
-__device__ __forceinline__ RVal red_thread(const RVal (&x)[8]) {
-    return red2<KIND>(red2<KIND>(red2<KIND>(x[0], x[1]), red2<KIND>(x[2], x[3])),
-                      red2<KIND>(red2<KIND>(x[4], x[5]), red2<KIND>(x[6], x[7])));
-}
-// Butterfly over the warp: every lane ends with the same value (each step
-// combines a commutative pair).
-template <int KIND>
-__device__ __forceinline__ RVal red_warp(RVal v) {
-#pragma unroll
-    for (int m = 16; m >= 1; m >>= 1) {
-        RVal o;
-        o.v = __shfl_xor_sync(0xffffffffu, v.v, m);
-        o.i = KIND == RED_ARGMAX ? __shfl_xor_sync(0xffffffffu, v.i, m) : 0;
-        v = red2<KIND>(v, o);
-    }
-    return v;
-}
-// The eight warps of a block, as ((w0 w1)(w2 w3))((w4 w5)(w6 w7)).
-template <int KIND>
-__device__ __forceinline__ RVal red_block8(const float* wv, const int64_t* wi) {
-    RVal w[8];
-#pragma unroll
-    for (int k = 0; k < 8; k++) w[k] = {wv[k], KIND == RED_ARGMAX ? wi[k] : 0};
-    return red2<KIND>(red2<KIND>(red2<KIND>(w[0], w[1]), red2<KIND>(w[2], w[3])),
-                      red2<KIND>(red2<KIND>(w[4], w[5]), red2<KIND>(w[6], w[7])));
-}
-static_assert(kThreads == 256 && kG == 2, "the reduction tree assumes 8 warps of 2 x float4");
-
-// A chunk's warp partials: A holds the values at positions
-// cb + 4 (t + 256 k) + j; positions >= n take the identity. The chunk is
-// G/2 blocks of the reduction tree (2048 positions, groups 2 sb and 2 sb + 1
-// of block sb), the first being block blk0 of the launch; block b's warp w
-// writes out[8 b + w] (and out_i), for the nblk blocks the launch has.
-// ARGMAX inside one 2048-block: the index travels as a 32-bit offset in
-// the block (the same order as the global index; INT32_MAX for "no
-// element") and is widened once per warp partial.
-struct RV32 {
-    float v;
-    int32_t o;
-};
-__device__ __forceinline__ RV32 am_pick32(const RV32& a, const RV32& b) {
-    const bool na = a.v != a.v, nb = b.v != b.v;
-    if (na || nb) return (na && nb ? a.o < b.o : na) ? a : b;
-    if (a.v > b.v) return a;
-    if (b.v > a.v) return b;
-    const bool sa = __float_as_uint(a.v) >> 31, sb = __float_as_uint(b.v) >> 31;
-    if (sa != sb) return sa ? b : a;
-    return a.o < b.o ? a : b;
-}
-__device__ __forceinline__ RV32 am_warp32(const RV32 (&x)[8]) {
-    RV32 v = am_pick32(am_pick32(am_pick32(x[0], x[1]), am_pick32(x[2], x[3])),
-                       am_pick32(am_pick32(x[4], x[5]), am_pick32(x[6], x[7])));
-#pragma unroll
-    for (int m = 16; m >= 1; m >>= 1) {
-        RV32 o;
-        o.v = __shfl_xor_sync(0xffffffffu, v.v, m);
-        o.o = __shfl_xor_sync(0xffffffffu, v.o, m);
-        v = am_pick32(v, o);
-    }
-    return v;
-}
-
-template <int KIND, int G>
-__device__ __forceinline__ void chunk_warps(const float4 (&A)[G], int64_t cb, int64_t n,
-                                            int64_t idx_base, float* out, int64_t* out_i,
-                                            int64_t blk0, int64_t nblk) {
-    const int t = threadIdx.x;
-#pragma unroll
-    for (int sb = 0; sb < G / 2; sb++) {
-        const int64_t b = blk0 + sb;
-        if (b < nblk) {  // uniform over the block
-            const int64_t base = cb + (int64_t)kChunk * sb;
-            const bool full = base + kChunk <= n;
-            if constexpr (KIND == RED_ARGMAX) {
-                RV32 x[8];
-#pragma unroll
-                for (int k = 0; k < 2; k++)
-#pragma unroll
-                    for (int e = 0; e < 4; e++) {
-                        const int32_t o = 4 * (t + kThreads * k) + e;
-                        x[4 * k + e] = (full || base + o < n)
-                                           ? RV32{f4_get(A[2 * sb + k], e), o}
-                                           : RV32{__int_as_float((int)0xff800000u), INT32_MAX};
-                    }
-                const RV32 w = am_warp32(x);
-                if ((t & 31) == 0) {
-                    out[8 * b + (t >> 5)] = w.v;
-                    out_i[8 * b + (t >> 5)] = w.o == INT32_MAX ? kNoIndex : idx_base + base + w.o;
-                }
-            } else {
-                RVal x[8];
-#pragma unroll
-                for (int k = 0; k < 2; k++)
-#pragma unroll
-                    for (int e = 0; e < 4; e++) {
-                        const int64_t p = base + 4 * (t + kThreads * k) + e;
-                        x[4 * k + e] = (full || p < n) ? RVal{f4_get(A[2 * sb + k], e), 0}
-                                                       : red_identity<KIND>();
-                    }
-                const RVal w = red_warp<KIND>(red_thread<KIND>(x));
-                if ((t & 31) == 0) out[8 * b + (t >> 5)] = w.v;
-            }
-        }
-    }
-}
-// Partial e of a level: entry e itself, or (warps8, the first level) the
-// eight warp partials of chunk e combined.
-template <int KIND>
-__device__ __forceinline__ RVal red_entry(const float* v, const int64_t* vi, int64_t e,
-                                          bool warps8) {
-    if (warps8) return red_block8<KIND>(v + 8 * e, KIND == RED_ARGMAX ? vi + 8 * e : nullptr);
-    return {v[e], KIND == RED_ARGMAX ? vi[e] : 0};
-}
-
-// One level of the reduction tree over m partials (value, index): block b
-// reduces partials [kChunk b, kChunk b + kChunk) with the tree above into
-// ov[b] (and oi[b]). With m = 0 one block writes the identity; with m = 1
-// the partial is the result itself. `last`: the caller's result
-// (red_final).
-template <int KIND>
-__global__ void __launch_bounds__(kThreads) k_red_level(const float* __restrict__ v,
-                                                        const int64_t* __restrict__ vi, int64_t m,
-                                                        float* ov, int64_t* oi, bool last,
-                                                        bool warps8) {
-    __shared__ float wv[8];
-    __shared__ int64_t wi[8];
-    const int t = threadIdx.x;
-    if (m == 1) {  // no identity is added to a lone partial
-        if (blockIdx.x == 0 && t == 0) {
-            RVal b = red_entry<KIND>(v, vi, 0, warps8);
-            if (last) b = red_final<KIND>(b);
-            ov[0] = b.v;
-            if (KIND == RED_ARGMAX) oi[0] = b.i;
-        }
-        return;
-    }
-    const int64_t base = (int64_t)blockIdx.x * kChunk;
-    RVal x[8];
-#pragma unroll
-    for (int k = 0; k < kG; k++)
-#pragma unroll
-        for (int j = 0; j < 4; j++) {
-            const int64_t e = base + 4 * (t + kThreads * k) + j;
-            x[4 * k + j] = e < m ? red_entry<KIND>(v, vi, e, warps8) : red_identity<KIND>();
-        }
-    const RVal r = red_warp<KIND>(red_thread<KIND>(x));
-    if ((t & 31) == 0) {
-        wv[t >> 5] = r.v;
-        wi[t >> 5] = r.i;
-    }
-    __syncthreads();
-    if (t == 0) {
-        RVal b = red_block8<KIND>(wv, wi);
-        if (last) b = red_final<KIND>(b);
-        ov[blockIdx.x] = b.v;
-        if (KIND == RED_ARGMAX) oi[blockIdx.x] = b.i;
-    }
-}
-
-// Partials [from, to) set to the identity (a rank's slots past its own
-// chunks in the sharded reduction's all-gather).
-template <int KIND>
-__global__ void k_red_fill(float* v, int64_t* vi, int64_t from, int64_t to) {
-    const RVal id = red_identity<KIND>();
-    for (int64_t e = from + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < to;
-         e += (int64_t)gridDim.x * blockDim.x) {
-        v[e] = id.v;
-        if (vi) vi[e] = id.i;
-    }
-}
-
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,
-                                         uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-            smem_u32(dst)),
-        "l"(src), "r"(bytes), "r"(smem_u32(bar))
-        : "memory");
-}
-
-struct ChunkSpan {
-    int64_t org, lo, len4, hi;  // buffer origin, copied [lo, lo+len4), valid [lo, hi)
-};
-
-// The input span a chunk needs: with its halo (the first chunk of a block's
-// range, whose window heads are computed) or without (later chunks carry
-// the heads over from the chunk before).
-__device__ __forceinline__ ChunkSpan chunk_span(int64_t cb, int hs, int64_t n, int64_t halo,
-                                                bool with_halo, int chunk) {
-    ChunkSpan s;
-    s.org = cb - hs;
-    s.lo = max(with_halo ? s.org : cb, -halo);
-    s.hi = min(cb + (int64_t)chunk, n);
-    s.len4 = s.hi > s.lo ? ((s.hi - s.lo) & ~int64_t(3)) : 0;
-    return s;
-}
-
-// Shared memory (float4 units): meta | taps (n_fir x kMaxTaps floats) |
-// tiles (tile_floats(head) floats each) | temporaries (n_tmp x kChunk floats) |
-// stages (nst x n_in x (hs + kChunk) floats, BULK only). Input k of a stage
-// holds positions [cb - hs, cb + kChunk) of the chunk at cb (the part below
-// cb only for the first chunk of the block's range).
-//
-// A block works through a contiguous range of chunks. Window f's tile holds
-// positions [cb - head, cb + kChunk): the chunk's own positions are staged
-// by one run of the window's program; the head below cb is the previous
-// chunk's last head positions, copied within the tile, and is computed by
-// a short head run only for the first chunk of the range. head is the
-// window's reach (window_reach(taps)), plus, when later windows read it
-// (chained windows), the largest head among them: their head runs read it
-// that far below the chunk.
-//
-// Bulk-copy mode (BULK): the chunk's inputs travel HBM -> shared memory by
-// cp.async.bulk, one copy per input, in `nst` stages that complete on
-// per-stage mbarriers, so nst-1 chunks stream in while one is interpreted.
-// Requires every input 16-byte aligned and halo = 0 mod 4. Otherwise
-// (DIRECT) the interpreter reads input operands from HBM itself.
-//
-// A reduction (P.reduce) writes no output array: each warp's values of
-// chunk c (its index in the launch) are reduced (red_thread, red_warp) into
-// out[8 c + warp] and, for ARGMAX, out_idx[8 c + warp]; idx_base + p is the
-// index of position p. The level kernels combine the eight warps.
-//
-// A graph without windows has no shared value that one thread writes and
-// another reads (temporaries and staged operands are per thread): its warps
-// run ahead of each other, and the last of the eight warps to finish with a
-// stage (a shared counter per stage) refills it, instead of thread 0 after a
-// block barrier.
-template <bool BULK, int G>
-__global__ void __launch_bounds__(kThreads, G == kG ? 3 : 2)
-    k_tile(const __grid_constant__ Program P, float* __restrict__ out, int64_t n, int64_t halo,
-           bool vec, bool in_vec, int32_t hs, int32_t stages4, int32_t nst, uint32_t* wd,
-           int64_t* __restrict__ out_idx, int64_t idx_base) {
-    constexpr int CH = chunk_of(G), CH4 = CH / 4;
-    __shared__ __align__(8) uint64_t bars[kMaxStages];   // stage s loaded
-    __shared__ int rel[kMaxStages];  // warps done with stage s (window-free graphs)
-    extern __shared__ float4 sm4[];
-    const int code_cap = meta_code_cap(P.n_code);
-    Insn* code_s = reinterpret_cast<Insn*>(sm4);
-    int4* fir_s = reinterpret_cast<int4*>(code_s + code_cap);
-    const float** in_s = reinterpret_cast<const float**>(fir_s + P.n_fir);
-    float* taps_s = reinterpret_cast<float*>(sm4) + meta_bytes(P.n_code, P.n_in, P.n_fir) / 4;
-    const int32_t sstride = hs + CH;  // floats per staged input
-    const int32_t stage_floats = P.n_in * sstride;
-    float* stages = reinterpret_cast<float*>(sm4 + stages4);
-    const int tid = threadIdx.x;
-    const int64_t nchunks = (n + CH - 1) / CH;
-    for (int i = tid; i < code_cap; i += kThreads)
-        code_s[i] = i < P.n_code ? P.code[i] : Insn{OP_END, F_END, 0, 0, 0, 0.0f, 0};
-    for (int k = tid; k < P.n_in; k += kThreads) in_s[k] = P.in[k];
-    for (int f = tid; f < P.n_fir; f += kThreads)
-        fir_s[f] = make_int4(P.fir[f].start, P.fir[f].taps, P.fir[f].head, P.fir[f].tile4);
-    for (int f = 0; f < P.n_fir; f++)
-        for (int k = tid; k < kMaxTaps; k += kThreads)
-            taps_s[f * kMaxTaps + k] = P.fir[f].h[k];  // zero past taps
-
-    const int64_t per_block = (nchunks + gridDim.x - 1) / gridDim.x;
-    const int64_t c0 = blockIdx.x * per_block;
-    const int64_t c1 = min(c0 + per_block, nchunks);
-    auto issue = [&](int64_t c, int s) {
-        const ChunkSpan sp = chunk_span(c * CH, hs, n, halo, c == c0, CH);
-        mbar_arrive_expect_tx(&bars[s], (uint32_t)(sp.len4 * 4 * P.n_in));
-        if (sp.len4 > 0)
-            for (int k = 0; k < P.n_in; k++)
-                bulk_g2s(stages + s * stage_floats + k * sstride + (sp.lo - sp.org),
-                         in_s[k] + sp.lo, (uint32_t)(sp.len4 * 4), &bars[s]);
-    };
-    if (BULK) {
-        if (tid == 0) {
-            for (int s = 0; s < nst; s++) {
-                mbar_init(&bars[s], 1);
-                rel[s] = 0;
-            }
-            fence_mbar_init();
-        }
-        __syncthreads();
-        if (tid == 0)
-            for (int s = 0; s < nst; s++)
-                if (c0 + s < c1) issue(c0 + s, s);
-    }
-    __syncthreads();
-
-    Ctx cx;
-    cx.S = sm4;
-    cx.taps_s = taps_s;
-    cx.fir = fir_s;
-    cx.in = in_s;
-    cx.out = out;
-    cx.n = n;
-    cx.halo = halo;
-    cx.vec = vec;
-    cx.in_vec = in_vec;
-    const int nf = P.n_fir;
-    const bool free_run = nf == 0;
-    float4 A[G];  // the last run's values (the main program's, for a reduction)
-    int it = 0;
-    for (int64_t c = c0; c < c1; c++, it++) {
-        const int64_t cb = c * CH;
-        const bool first = c == c0;
-        const ChunkSpan sp = chunk_span(cb, hs, n, halo, first, CH);
-        int s = 0;
-        if (BULK) {
-            s = it % nst;
-            if (!mbar_wait(&bars[s], (uint32_t)((it / nst) & 1), wd)) {
-                // Gave up (the watchdog is raised): let the block's other
-                // copies in flight land, each wait bounded, before exiting.
-                for (int j = 1; j < nst && c + j < c1; j++)
-                    mbar_wait(&bars[(it + j) % nst], (uint32_t)(((it + j) / nst) & 1), wd);
-                return;
-            }
-            float* buf = stages + s * stage_floats;
-            // The last 0-3 samples of a ragged signal are not a whole 16-byte
-            // unit: plain loads.
-            const int64_t tail = sp.hi - (sp.lo + sp.len4);
-            if (tail > 0) {  // uniform over the block
-                if (tid < P.n_in * 4) {
-                    const int k = tid / 4, e = tid % 4;
-                    const int64_t pos = sp.lo + sp.len4 + e;
-                    if (e < tail) buf[k * sstride + (pos - sp.org)] = in_s[k][pos];
-                }
-                __syncthreads();
-            }
-        }
-        const int32_t in4 = stages4 + s * stage_floats / 4;
-        const bool edge = cb - (int64_t)hs < -halo || cb + CH > n;
-        // Jobs 2f and 2f+1 stage window f: its head (first chunk only) and
-        // the chunk itself; job 2 nf is the main program over the chunk. One
-        // loop, so the interpreter is inlined once per form.
-        for (int j = 0; j <= 2 * nf; j++) {
-            Run r;
-            int pc;
-            if (j < 2 * nf) {
-                const int4 fd = fir_s[j >> 1];
-                const int head4 = fd.z / 4;
-                pc = fd.x;
-                if (!(j & 1)) {  // head: tile [0, head) = positions [cb - head, cb)
-                    r.sh_in = in4 + (hs - fd.z) / 4;
-                    r.sh_st = 0;
-                    r.woff4 = -head4;
-                    r.gm = first && tid < head4 ? 1u : 0u;
-                    r.p0 = cb - fd.z;
-                } else {  // the chunk: tile [head, head + CH)
-                    // Carry the head over: the previous chunk's last head
-                    // positions sit at tile [CH, CH + head). The
-                    // thread that copies a float4 is the one whose staging
-                    // below overwrites it, so no barrier is needed.
-                    if (!first && tid >= kThreads - head4) {
-                        float4* tile = cx.S + fd.w;
-                        const int q = tid - (kThreads - head4);
-                        tile[q] = tile[CH4 + q];
-                    }
-                    r.sh_in = in4 + hs / 4;
-                    r.sh_st = head4;
-                    r.woff4 = 0;
-                    r.gm = (1u << G) - 1;
-                    r.p0 = cb;
-                }
-            } else {
-                pc = P.main_start;
-                r.sh_in = in4 + hs / 4;
-                r.sh_st = 0;
-                r.woff4 = 0;
-                r.gm = (1u << G) - 1;
-                r.p0 = cb;
-            }
-            r.edge = edge;
-            if (r.gm == (1u << G) - 1)
-                interpret<BULK, true, G>(code_s, pc, cx, r, A);
-            else if (r.gm)
-                interpret<BULK, false, G>(code_s, pc, cx, r, A);
-            // Windows staged before the main program reads them, and a
-            // window before a later window's staging reads it (chains).
-            if ((j & 1) && (j + 1 == 2 * nf || (fir_s[j >> 1].y & kSyncAfter))) __syncthreads();
-        }
-        if (P.reduce != RED_NONE) {
-            const int64_t b0 = c * (G / 2), nb = (n + kChunk - 1) / kChunk;
-            float* o = out;
-            int64_t* oi = out_idx;
-            switch (P.reduce) {  // uniform: one branch per chunk
-                case RED_SUM: chunk_warps<RED_SUM, G>(A, cb, n, idx_base, o, oi, b0, nb); break;
-                case RED_MIN: chunk_warps<RED_MIN, G>(A, cb, n, idx_base, o, oi, b0, nb); break;
-                case RED_MAX: chunk_warps<RED_MAX, G>(A, cb, n, idx_base, o, oi, b0, nb); break;
-                default: chunk_warps<RED_ARGMAX, G>(A, cb, n, idx_base, o, oi, b0, nb); break;
-            }
-        }
-        if (BULK) {
-            // Every thread is done with this stage (and, with windows, with
-            // the tiles and temporaries); order its generic accesses before
-            // the next bulk copy into it.
-            fence_proxy_async_smem();
-            if (free_run) {
-                // The counter's read-modify-writes, fenced on both sides, order
-                // every warp's reads of the stage before the refill. The reset
-                // precedes the refill's arrive (a release), which every warp
-                // acquires before it counts this stage again.
-                __syncwarp();
-                if ((tid & 31) == 0) {
-                    __threadfence_block();
-                    if (atomicAdd(&rel[s], 1) == kThreads / 32 - 1) {
-                        __threadfence_block();
-                        rel[s] = 0;
-                        if (c + nst < c1) issue(c + nst, s);
-                    }
-                }
-            } else {
-                __syncthreads();
-                if (tid == 0 && c + nst < c1) issue(c + nst, s);
-            }
-        } else if (!free_run) {
-            __syncthreads();  // the tiles are rewritten by the next chunk
-        }
-    }
-}
-
-}  // namespace tilek
 
 // ============================================================================
 // Host side: the recorded graph (tile/tile.go) and its lowering.
