@@ -343,7 +343,8 @@ int simtgo_tile_run_shard(simtgo_tile_graph* g, simtgo_tensor t, float* dev_out,
  * intermediate nodes need more (each node's length rounded up to 64 floats,
  * summed over the nodes other than t) is refused with SIMTGO_ESIZE. The
  * first call on a device resolves the array's device address (once per
- * device, with that device current). Every call uses the same array and
+ * device, with that device current), so it should come before any stream
+ * capture begins on that device. Every call uses the same array and
  * leaves its values there; each node's region is written in full before it
  * is read, so nothing needs clearing. Calls that overlap on the GPU (two
  * streams, or two host threads) race on the array. Asynchronous on stream;

@@ -1445,6 +1445,12 @@ extern "C" int simtgo_tile_run_stepwise_noalloc(simtgo_tile_graph* g, simtgo_ten
                         (long long)used, (long long)kNoAllocFloats);
     float* scratch = nullptr;
     if ((rc = stepwise_scratch(&scratch))) return rc;
+    if (g->nodes[t].kind == K_INPUT) {
+        // The root is an input: its values are copied to dev_out by the same
+        // one-node program simtgo_tile_run launches (after the same alias check).
+        auto resolve = [&](int nid) -> const float* { return g->nodes[nid].dev; };
+        return run_fused(g, t, dev_out, out_len, 0, (cudaStream_t)stream, resolve, true);
+    }
     auto value = [&](int id) -> const float* {
         return g->nodes[id].kind == K_INPUT ? g->nodes[id].dev : scratch + region[id];
     };
@@ -1453,7 +1459,7 @@ extern "C" int simtgo_tile_run_stepwise_noalloc(simtgo_tile_graph* g, simtgo_ten
         if (nd.kind == K_INPUT) continue;
         simtgo_tile_graph one;
         const int a = simtgo_tile_input_device(&one, value(nd.a), g->nodes[nd.a].n);
-        int r;
+        int r = a;
         if (nd.kind == K_FIR) {
             const Node& tp = g->nodes[nd.b];
             r = simtgo_tile_fir(&one, a, tp.taps.data(), (int32_t)tp.taps.size());
@@ -1469,6 +1475,11 @@ extern "C" int simtgo_tile_run_stepwise_noalloc(simtgo_tile_graph* g, simtgo_ten
                 : nd.kind == K_MUL ? simtgo_tile_mul(&one, a, b)
                                    : simtgo_tile_hypot(&one, a, b);
         }
+        // A step the one-node graph refused comes back as its recorded error,
+        // never as a node index.
+        if (r < 0 || !one.err.empty())
+            return sg::fail(SIMTGO_EGRAPH, "tile: step for node %d: %s", id,
+                            one.err.empty() ? "refused" : one.err.c_str());
         float* target = id == t ? dev_out : scratch + region[id];
         auto resolve = [&](int nid) -> const float* { return one.nodes[nid].dev; };
         rc = run_fused(&one, r, target, nd.n, 0, (cudaStream_t)stream, resolve, true);

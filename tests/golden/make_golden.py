@@ -2,14 +2,15 @@
 
 Each case feeds seeded inputs to the REFERENCE's own generated kernels
 (kernels/prebuilt/*.cu of CWBudde/simtgo) compiled for the host by
-oracle/Makefile (`make -C oracle ref`, which reads /root/reference) and
+oracle/Makefile (`make -C oracle ref`, which reads the reference tree named
+by the SIMTGO_REFERENCE environment variable) and
 stores inputs, launch geometry and outputs. The reference publishes no
 numeric golden vectors, so these pin the oracle to the reference's code; the
 shapes and special values follow the reference's own parity tests
 (simt/parity_test.go, simt/shared_parity_cuda_test.go,
 simt/warp_parity_cuda_test.go).
 
-Run here (needs the reference tree):  python tests/golden/make_golden.py
+Run with the reference tree:  SIMTGO_REFERENCE=<tree> python tests/golden/make_golden.py
 The .npz files are committed; the GPU tests only read them.
 """
 from __future__ import annotations

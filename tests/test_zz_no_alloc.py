@@ -78,6 +78,20 @@ def test_matches_existing_entry_on_consecutive_calls():
     same("third call, first graph again", run_noalloc(L, g1, o1, n1), want1)
 
 
+def test_input_root_and_single_step_match_existing_entry():
+    # A graph whose root is one of its device inputs has no step to run; the
+    # output must still receive the input's values, as simtgo_tile_run gives.
+    L = _lib.load()
+    n = 50021
+    rng = np.random.default_rng(4)
+    g = tile.New()
+    a = g.InputDevice(dev(rng.uniform(-4, 4, n)))
+    same("input root", run_noalloc(L, g, a, n), run_existing(L, g, a, n))
+    s = tile.Scale(a, -1.5)
+    same("Scale of an input", run_noalloc(L, g, s, n), run_existing(L, g, s, n))
+    same("input root again", run_noalloc(L, g, a, n), run_existing(L, g, a, n))
+
+
 def test_refuses_what_does_not_fit():
     L = _lib.load()
     # 7 intermediate nodes of 1M floats each: 7M floats > the 4M-float scratch.
