@@ -67,15 +67,21 @@ def fir_taps():
         seed += 1000
 
 
-def signal(torch, g0, n, device):
+def signal(torch, g0, n, device, piece=1 << 26):
     """Samples g0 .. g0+n-1 of one long uniform[-1,1) signal, as a function
-    of the global index, so every shard sees the same halo values."""
-    g = torch.arange(g0, g0 + n, dtype=torch.int64, device=device)
-    h = (g * 0x9E3779B1 + 0x7F4A7C15) & 0xFFFFFFFF
-    h = (h ^ (h >> 15)) * 0x2C1B3C6D & 0xFFFFFFFF
-    h = h ^ (h >> 12)
-    out = ((h & 0xFFFFFF).to(torch.float32) * (2.0 / 16777216.0) - 1.0)
-    out[g < 0] = 0.0
+    of the global index, so every shard sees the same halo values. Filled
+    in pieces so that a 2^31-sample signal needs no more temporary memory
+    than a 2^26-sample one."""
+    out = torch.empty(n, dtype=torch.float32, device=device)
+    for o in range(0, n, piece):
+        m = min(piece, n - o)
+        g = torch.arange(g0 + o, g0 + o + m, dtype=torch.int64, device=device)
+        h = (g * 0x9E3779B1 + 0x7F4A7C15) & 0xFFFFFFFF
+        h = (h ^ (h >> 15)) * 0x2C1B3C6D & 0xFFFFFFFF
+        h = h ^ (h >> 12)
+        v = out[o:o + m]
+        v.copy_((h & 0xFFFFFF).to(torch.float32) * (2.0 / 16777216.0) - 1.0)
+        v[g < 0] = 0.0
     return out
 
 
@@ -232,8 +238,9 @@ def run_ours(args):
     value = world * n * args.steps / (ms_max * 1e-3) / 1e9
     launch_ms = ms / args.steps
 
-    # Parity spot check of this rank's shard against the oracle (512 outputs).
-    spot = spot_check(np, x[: halo + 512].cpu().numpy() if rank == 0 else None, y, h, halo)
+    # Parity of this rank's whole shard against the oracle (outside the
+    # timed region; the oracle on this rank's share of the host cores).
+    spot = shard_parity(np, x, y, h, halo, world)
 
     # ---- e2e: host buffers through the C ABI ----------------------------------
     # simtgo_FIR_shard_host streams the pinned host shard through the GPU in
@@ -271,6 +278,8 @@ def run_ours(args):
     barrier()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1))
     e2e_value = world * n * e2e_steps / (e2e_ms * 1e-3) / 1e9
+    ceiling = copy_ceiling(torch, xh, yh, h2d_bytes, dev, barrier, max_over_ranks, events,
+                           e2e_steps)
     del xh, yh
 
     # ---- roofline of the FIR kernel ---------------------------------------------
@@ -281,22 +290,25 @@ def run_ours(args):
     fp32_peak = sms.value * 128 * 2 * sm_mhz * 1e6 / 1e12
     hbm_gbs = (8.0 * n + 4.0 * halo) / (launch_ms * 1e-3) / 1e9
     traffic = ncu_traffic("FIR_shard_127")
+    # At 127 taps the kernel is bound by FP32 FMA issue, not HBM (2*taps
+    # FLOPs per 8 bytes): the headline fraction is of the FP32 peak (no
+    # measured figure exists for it: SMs x 128 lanes x 2 x the sampled
+    # clock); the HBM fraction is the sub-record.
     roofline = {
-        "bound": "hbm",
-        "achieved": round(hbm_gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
-        "frac": round(hbm_gbs / peaks["hbm_gbs"], 4),
-        "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs, copy burst)",
-        "algorithmic_bytes_per_launch": int(8 * n + 4 * halo),
+        "bound": "fp32",
+        "achieved": round(achieved_tflops, 2), "peak": round(fp32_peak, 2), "unit": "TFLOP/s",
+        "frac": round(achieved_tflops / fp32_peak, 4),
+        "peak_source": f"derived: {sms.value} SMs x 128 FP32 lanes x 2 FLOP x {sm_mhz:.0f} MHz "
+                       "(the SM clock sampled during the timed region)",
+        "algorithmic_flops_per_launch": int(flops),
         "traffic": None if traffic is None else int(traffic * n),
+        "traffic_note": "DRAM bytes per launch (ncu dram__bytes_read+write per output x outputs)",
         "kernel_ms": round(launch_ms, 4),
-        # At 127 taps the kernel is bound by FP32 FMA issue, not HBM: 2*taps
-        # FLOPs per 8 bytes. Its fraction of the FP32 peak (no measured
-        # figure exists for it: SMs x 128 lanes x 2 x the sampled clock).
-        "fp32": {
-            "achieved_tflops": round(achieved_tflops, 2), "peak_tflops": round(fp32_peak, 2),
-            "frac": round(achieved_tflops / fp32_peak, 4),
-            "peak_basis": f"{sms.value} SMs x 128 FP32 lanes x 2 FLOP x {sm_mhz:.0f} MHz "
-                          "(the SM clock sampled during the timed region)",
+        "hbm": {
+            "achieved": round(hbm_gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+            "frac": round(hbm_gbs / peaks["hbm_gbs"], 4),
+            "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs, copy burst)",
+            "algorithmic_bytes_per_launch": int(8 * n + 4 * halo),
         },
     }
 
@@ -304,6 +316,8 @@ def run_ours(args):
     sharded = {}
     del x, y
     torch.cuda.empty_cache()
+    sharded["fir_strong"] = bench_fir_strong(args, torch, L, dev, sp, rank, world, h, barrier,
+                                             max_over_ranks, events)
     sharded["histogram_allreduce"] = bench_histogram(args, torch, L, dev, sp, rank, world,
                                                      barrier, max_over_ranks, events)
     sharded["tile_graph"] = bench_tile(args, torch, np, L, dev, sp, rank, world, barrier,
@@ -312,8 +326,10 @@ def run_ours(args):
                                                max_over_ranks, events)
 
     kernels = None
+    chain = None
     cpu = None
     if world == 1 and not args.skip_kernels:
+        chain = bench_signal_chain(args, torch, np, L, dev, sp, events, peaks)
         kernels = bench_kernels(args, torch, np, L, dev, sp, events, peaks)
     if rank == 0 and world == 1 and not args.skip_cpu:
         cpu = cpu_baseline(args, np, seconds=args.cpu_seconds)
@@ -338,13 +354,17 @@ def run_ours(args):
                 "steps": e2e_steps,
                 "path": "simtgo_FIR_shard_host on pinned host buffers: 2^22-output chunks on "
                         "three streams, uploads, kernels and downloads overlapping; bytes summed "
-                        "over ranks"},
+                        "over ranks",
+                "copy_ceiling": ceiling,
+                "frac_of_copy_ceiling": (round(e2e_value / ceiling["gsamples_per_s"], 4)
+                                         if ceiling else None)},
         "gpu_launches": args.steps,
         "gpu_launches_note": "simtgo_FIR_shard kernels per rank inside the timed region",
         "roofline": roofline,
         "clocks": clocks,
         "cpu_baseline": cpu,
-        "parity_spot_check": spot,
+        "parity": spot,
+        "signal_chain": chain,
         "sharded": sharded,
         "kernels": kernels,
     }
@@ -355,18 +375,183 @@ def run_ours(args):
         print(json.dumps(line), flush=True)
 
 
-def spot_check(np, x_host, y, h, halo):
-    """512 outputs of rank 0's shard against the oracle's fma order."""
-    if x_host is None:
-        return None
+def oracle_module(world):
+    """The oracle (test infrastructure: the checker, never the measured
+    path) with this rank's share of the host cores."""
     sys.path.insert(0, str(ROOT / "tests"))
     import oracle_lib as O
 
-    yh = y[:512].cpu().numpy()
-    rc, want = O.fir_shard(np.ascontiguousarray(x_host[: halo + 512]), halo,
-                           h.cpu().numpy(), 512)
-    return {"outputs": 512, "bit_exact": bool(rc == 0 and np.array_equal(
-        yh.view(np.uint32), want.view(np.uint32)))}
+    O.set_threads(max(1, (os.cpu_count() or 1) // world))
+    return O
+
+
+def shard_parity(np, x, y, h, halo, world):
+    """This rank's whole FIR shard against the oracle's fma order, bit for
+    bit (every output, not a sample)."""
+    O = oracle_module(world)
+    xh = x.cpu().numpy()
+    got = y.cpu().numpy()
+    rc, want = O.fir_shard(xh, halo, h.cpu().numpy(), got.size)
+    bad = int(np.count_nonzero(got.view(np.uint32) != want.view(np.uint32))) if rc == 0 else -1
+    return {"fir_shard": {"outputs": int(got.size), "bit_exact": rc == 0 and bad == 0,
+                          "mismatches": bad,
+                          "check": "every output of this rank's shard against the oracle "
+                                   "(device fma order), outside the timed region"}}
+
+
+def copy_ceiling(torch, xh, yh, h2d_bytes, dev, barrier, max_over_ranks, events, steps):
+    """What the host link allows for the e2e step: the same bytes as the
+    host-memory FIR moves (h2d_bytes up, the outputs down), as pinned
+    copies in 2^22-element pieces on two streams (one per direction) so that
+    both directions overlap, with no kernel; Gsamples/s of the same n."""
+    n = yh.numel()
+    up = max(1, h2d_bytes // 4)
+    xd = torch.empty(min(up, xh.numel()), dtype=torch.float32, device=dev)
+    yd = torch.empty(n, dtype=torch.float32, device=dev)
+    s_up, s_dn = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    piece = 1 << 22
+    cur = torch.cuda.current_stream(dev)
+
+    def step():
+        s_up.wait_stream(cur)
+        s_dn.wait_stream(cur)
+        with torch.cuda.stream(s_up):
+            for o in range(0, xd.numel(), piece):
+                xd[o:o + piece].copy_(xh[o:o + piece], non_blocking=True)
+        with torch.cuda.stream(s_dn):
+            for o in range(0, n, piece):
+                yh[o:o + piece].copy_(yd[o:o + piece], non_blocking=True)
+        cur.wait_stream(s_up)
+        cur.wait_stream(s_dn)
+
+    step()
+    barrier()
+    e0, e1 = events()
+    e0.record(cur)
+    for _ in range(steps):
+        step()
+    e1.record(cur)
+    e1.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1) / steps)
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    return {"ms_per_step": round(ms, 4),
+            "gsamples_per_s": round(world * n / (ms * 1e-3) / 1e9, 3),
+            "h2d_gbs": round(xd.numel() * 4 / (ms * 1e-3) / 1e9, 1),
+            "d2h_gbs": round(n * 4 / (ms * 1e-3) / 1e9, 1),
+            "how": "pinned host<->device copies of the e2e step's bytes, 2^22-element pieces, "
+                   "one stream per direction, no kernel"}
+
+
+def bench_fir_strong(args, torch, L, dev, sp, rank, world, h, barrier, max_over_ranks, events):
+    """Strong scaling: the whole 2^31-sample, 127-tap signal split over the
+    ranks (2^31 outputs on one GPU: 16 GiB of input and output)."""
+    from simtgo_b200 import _lib, shard
+
+    total = 1 << args.fir_strong_log2
+    plan = shard.fir_plan(total, world, rank, TAPS)
+    n, halo = plan.n, plan.halo
+    x = signal(torch, plan.in_lo, plan.in_len, dev)
+    y = torch.empty(n, dtype=torch.float32, device=dev)
+
+    def step():
+        rc = L.simtgo_FIR_shard(P(y.data_ptr()), n, P(x.data_ptr()), x.numel(), halo,
+                                P(h.data_ptr()), TAPS, sp)
+        if rc:
+            _lib.check(rc)
+
+    steps = max(5, min(args.steps, 20))
+    barrier()
+    ms = max_over_ranks(timed(step, steps, args.warmup, torch.cuda.current_stream(), events))
+    del x, y
+    torch.cuda.empty_cache()
+    return {"total_samples": total, "taps": TAPS, "ms_per_step": round(ms, 4),
+            "gsamples_per_s": round(total / (ms * 1e-3) / 1e9, 3), "scaling": "strong",
+            "steps": steps,
+            "workload": f"one 2^{args.fir_strong_log2}-sample signal, {TAPS} taps, split over "
+                        f"{world} GPU(s), each shard with its 126 preceding samples"}
+
+
+def bench_signal_chain(args, torch, np, L, dev, sp, events, peaks):
+    """The signal chain on 2^28 interleaved N(0,1) complex samples:
+    MagnitudeFast(scale 3) -> Softclip(0.5) -> Quantize(step 0.25, seed
+    0x9e3779b9) -> WarpReduceSum of the Softclip output; one step = the
+    four launches, with CUDA events between the stages. The first 2^20
+    elements of every stage are checked against the oracle afterwards."""
+    from simtgo_b200 import _lib
+
+    n = 1 << args.chain_log2
+    gen = torch.Generator(device=dev).manual_seed(11)
+    z = torch.randn(2 * n, device=dev, generator=gen)
+    mag = torch.empty(n, device=dev)
+    soft = torch.empty(n, device=dev)
+    code = torch.empty(n, dtype=torch.int32, device=dev)
+    energy = torch.empty(n, dtype=torch.int64, device=dev)
+    clipped = torch.empty(n, dtype=torch.uint8, device=dev)
+    sums = torch.empty(n // 32, device=dev)
+    G, W = (n + 255) // 256, (n + 127) // 128
+    stages = [
+        ("MagnitudeFast_interleaved", 12.0, lambda: L.simtgo_MagnitudeFast_interleaved(
+            P(mag.data_ptr()), n, P(z.data_ptr()), 2 * n, 3.0, G, 256, sp)),
+        ("Softclip", 8.0, lambda: L.simtgo_Softclip(P(soft.data_ptr()), n, P(mag.data_ptr()), n,
+                                                    0.5, G, 256, sp)),
+        ("Quantize", 17.0, lambda: L.simtgo_Quantize(
+            P(code.data_ptr()), n, P(energy.data_ptr()), n, P(clipped.data_ptr()), n,
+            P(soft.data_ptr()), n, 0.25, 0x9E3779B9, G, 256, sp)),
+        ("WarpReduceSum", 4.125, lambda: L.simtgo_WarpReduceSum(
+            P(sums.data_ptr()), n // 32, P(soft.data_ptr()), n, W, 128, sp)),
+    ]
+    stream = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        for _, _, f in stages:
+            _lib.check(f())
+    torch.cuda.synchronize()
+    steps = max(5, min(args.steps, 20))
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(len(stages) + 1)]
+          for _ in range(steps)]
+    for k in range(steps):
+        ev[k][0].record(stream)
+        for j, (_, _, f) in enumerate(stages):
+            rc = f()
+            if rc:
+                _lib.check(rc)
+            ev[k][j + 1].record(stream)
+    ev[-1][-1].synchronize()
+    hbm = peaks["hbm_gbs"]
+    res = {"elements": n, "steps": steps, "stages": {}}
+    total_ms = sum(ev[k][0].elapsed_time(ev[k][-1]) for k in range(steps)) / steps
+    for j, (name, bpe, _) in enumerate(stages):
+        ms = sum(ev[k][j].elapsed_time(ev[k][j + 1]) for k in range(steps)) / steps
+        gbs = bpe * n / (ms * 1e-3) / 1e9
+        res["stages"][name] = {"ms": round(ms, 4), "gbs": round(gbs, 1),
+                               "frac_hbm": round(gbs / hbm, 4), "bytes_per_element": bpe}
+    bpe = sum(b for _, b, _ in stages)
+    gbs = bpe * n / (total_ms * 1e-3) / 1e9
+    res.update({"ms": round(total_ms, 4), "gbs": round(gbs, 1), "frac_hbm": round(gbs / hbm, 4),
+                "bytes_per_element": bpe,
+                "gelements_per_s": round(n / (total_ms * 1e-3) / 1e9, 3)})
+    # Parity of the first 2^20 elements of every stage (oracle, outside timing).
+    O = oracle_module(1)
+    m = min(n, 1 << 20)
+    g = (m + 255) // 256
+    zs = z[: 2 * m].cpu().numpy()
+    ok = {}
+    rc, w_mag = O.magnitudefast_interleaved(zs, 3.0, g, 256)
+    ok["MagnitudeFast_interleaved"] = rc == 0 and np.array_equal(
+        mag[:m].cpu().numpy().view(np.uint32), w_mag.view(np.uint32))
+    rc, w_soft = O.softclip(w_mag, 0.5, g, 256)
+    ok["Softclip"] = rc == 0 and np.array_equal(soft[:m].cpu().numpy().view(np.uint32),
+                                                 w_soft.view(np.uint32))
+    rc, wc, we, wk = O.quantize(w_soft, 0.25, 0x9E3779B9, g, 256)
+    ok["Quantize"] = (rc == 0 and np.array_equal(code[:m].cpu().numpy(), wc)
+                      and np.array_equal(energy[:m].cpu().numpy(), we)
+                      and np.array_equal(clipped[:m].cpu().numpy(), wk))
+    rc, ws = O.warpreducesum(w_soft, m // 32, (m + 127) // 128)
+    ok["WarpReduceSum"] = rc == 0 and np.array_equal(sums[: m // 32].cpu().numpy().view(np.uint32),
+                                                      ws.view(np.uint32))
+    res["parity_first_2^20"] = {k: bool(v) for k, v in ok.items()}
+    del z, mag, soft, code, energy, clipped, sums
+    torch.cuda.empty_cache()
+    return res
 
 
 def in_turn(fns):
@@ -500,6 +685,23 @@ def bench_tile(args, torch, np, L, dev, sp, rank, world, barrier, max_over_ranks
            "gbs": round(16.0 * total / (ms * 1e-3) / 1e9, 1),
            "gelements_per_s": round(total / (ms * 1e-3) / 1e9, 2),
            "scaling": "strong", "bytes_per_element": 16}
+    # Parity: this rank's first 2^22 outputs (and its halo) against the
+    # oracle's node-by-node evaluation, outside the timed region.
+    O = oracle_module(world)
+    m = min(n, 1 << 22)
+    host = [t[: halo + m].cpu().numpy() for t in ins]
+    taps = np.full(31, 1 / 31, np.float32)
+    nodes = [{"kind": "input", "data": host[0]}, {"kind": "input", "data": host[1]},
+             {"kind": "input", "data": host[2]}, {"kind": "scale", "a": 0, "scale": 0.5},
+             {"kind": "abs", "a": 1}, {"kind": "sqrt", "a": 4}, {"kind": "mul", "a": 3, "b": 5},
+             {"kind": "add", "a": 6, "b": 2}, {"kind": "input", "data": taps},
+             {"kind": "fir", "a": 3, "taps": taps}, {"kind": "hypot", "a": 7, "b": 9},
+             {"kind": "mul", "a": 10, "b": 4}]
+    rc, want = O.tile_eval(nodes, 11, m, halo)
+    got = out[:m].cpu().numpy()
+    res["parity"] = {"outputs": m, "bit_exact": bool(rc == 0 and np.array_equal(
+        got.view(np.uint32), want.view(np.uint32))),
+        "check": "this rank's first outputs against the oracle, outside the timed region"}
     if world == 1:
         # Other graphs over the same inputs: what the interpreter costs per
         # kind of node (the twelve-node graph is compute-heavy: a 31-tap
@@ -788,6 +990,9 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--soak-s", type=float, default=1.5)
     ap.add_argument("--tile-log2", type=int, default=28)
+    ap.add_argument("--fir-strong-log2", type=int, default=31,
+                    help="samples of the strong-scaling FIR signal (31 = the 2^31 x 127 workload)")
+    ap.add_argument("--chain-log2", type=int, default=28)
     ap.add_argument("--kernels-log2", type=int, default=28,
                     help="elements per kernel in the per-kernel table (20..28; 28 = the workloads)")
     ap.add_argument("--skip-kernels", action="store_true")

@@ -265,6 +265,36 @@ def tile_eval(nodes, root, n, halo=0):
     return rc, out
 
 
+def tile_eval_chunked(nodes, root, n, reach, chunk=1 << 22, threads=None):
+    """tile_eval over n elements as independent chunks evaluated in parallel
+    (the ctypes call releases the GIL): chunk c takes its inputs from
+    [c0 - h, c0 + len) with h = min(reach, c0), so every window of the graph
+    (reach = the most samples any output reads below itself) sees the same
+    values as in one whole evaluation. Input nodes whose data has n elements
+    are sliced; the others (taps) are passed whole."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    out = np.empty(n, np.float32)
+    starts = list(range(0, n, chunk))
+
+    def one(c0):
+        h = min(reach, c0)
+        cn = min(chunk, n - c0)
+        sub = []
+        for nd in nodes:
+            d = nd.get("data")
+            if nd["kind"] == "input" and d is not None and len(d) == n:
+                nd = dict(nd, data=d[c0 - h: c0 + cn])
+            sub.append(nd)
+        rc, o = tile_eval(sub, root, cn, h)
+        assert rc == 0, rc
+        out[c0: c0 + cn] = o
+
+    with ThreadPoolExecutor(threads or os.cpu_count() or 1) as ex:
+        list(ex.map(one, starts))
+    return out
+
+
 TILE_REDUCE = {"sum": 0, "min": 1, "max": 2, "argmax": 3}
 
 
