@@ -5,8 +5,9 @@
 // order and rounding of the reference's device code, where nvcc contracts
 // `acc += h[k] * tile[...]` (kernels/prebuilt/FIR.cu:24-27).
 //
-// B200 design. A 256-thread block produces 5120 consecutive outputs; thread
-// t owns 20 consecutive outputs, so every sample it loads from shared memory
+// B200 design. A 256-thread block produces 5120 consecutive outputs (a
+// 64-thread block, 1280, for short signals, so that they spread over every
+// SM); thread t owns 20 consecutive outputs, so every sample it loads from shared memory
 // feeds up to 20 fused multiply-adds from registers (the reference does one
 // output per thread, with one shared load and one global tap load per
 // multiply-add):
@@ -25,6 +26,7 @@
 //    1-D bulk store (cp.async.bulk shared -> global).
 // At 127 taps the kernel is bound by FP32 FMA issue, not by HBM.
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 
 #include "common.cuh"
@@ -34,8 +36,13 @@ using namespace sgd;
 
 namespace {
 
-constexpr int kThreads = 256;
-constexpr int kMinBlocks = 4;  // blocks per SM the register budget is sized for
+// Threads per block: kWide for long signals, kNarrow for signals with
+// fewer than four waves of wide tiles (a 2^20-sample signal is 205 wide
+// tiles on 148 SMs, but 820 narrow ones). Both are sized for a 64-register
+// budget: 4 wide or 16 narrow blocks per SM.
+constexpr int kWide = 256;
+constexpr int kNarrow = 64;
+__host__ __device__ constexpr int min_blocks(int nt) { return 1024 / nt; }
 // Outputs per thread: lane windows are 4*kPerThread bytes apart, so
 // kPerThread/4 must be odd for the 8 lanes of a 16-byte load phase to hit 8
 // different bank groups. 20 (with 4 blocks per SM) measured fastest of
@@ -43,7 +50,7 @@ constexpr int kMinBlocks = 4;  // blocks per SM the register budget is sized for
 // share the register file, not only on reuse.
 constexpr int kPerThread = 20;
 static_assert(kPerThread % 4 == 0 && (kPerThread / 4) % 2 == 1, "lane stride must be odd x 16 B");
-constexpr int kTileOut = kThreads * kPerThread;  // outputs per tile
+__host__ __device__ constexpr int tile_out(int nt) { return nt * kPerThread; }  // outputs per tile
 constexpr int kChunk = 8;                        // taps per register chunk
 constexpr int kWin4 = (kPerThread + 10 + 3) / 4;  // window float4s: kPerThread + 7 + SH floats
 
@@ -134,9 +141,10 @@ __device__ __forceinline__ void fir_chunk_tail(const float* __restrict__ w, cons
 struct Span {
     int64_t A, c0, c1;  // buffer origin; [c0, c1) arrives by bulk copy
 };
+template <int NT>
 __device__ __forceinline__ Span tile_span(int64_t t, const FirGeom& g, bool bulk_in) {
     Span s;
-    s.A = t * kTileOut + g.halo - g.D;
+    s.A = t * tile_out(NT) + g.halo - g.D;
     s.c0 = max(s.A, (int64_t)0);
     const int64_t end = min(s.A + g.tile, g.x_len);
     s.c1 = bulk_in && end > s.c0 ? s.c0 + ((end - s.c0) & ~int64_t(3)) : s.c0;
@@ -150,12 +158,13 @@ __device__ __forceinline__ Span tile_span(int64_t t, const FirGeom& g, bool bulk
 // outputs has read it. The launch gives every tile its own block, which
 // measured faster on B200: four resident blocks per SM overlap one block's
 // load with the others' FMAs without the per-tile drain.
-template <int SH>
-__global__ void __launch_bounds__(kThreads, kMinBlocks) k_fir(float* __restrict__ y,
+template <int SH, int NT>
+__global__ void __launch_bounds__(NT, min_blocks(NT)) k_fir(float* __restrict__ y,
                                                       const float* __restrict__ x,
                                                       const float* __restrict__ h, FirGeom g,
                                                       int64_t ntiles, bool bulk_in, bool bulk_out,
                                                       uint32_t* wd) {
+    constexpr int kTileOut = tile_out(NT);
     __shared__ __align__(8) uint64_t bars[2];
     extern __shared__ float4 dyn4[];
     float* const buf0 = reinterpret_cast<float*>(dyn4);
@@ -164,13 +173,13 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks) k_fir(float* __restrict_
     const int tid = threadIdx.x;
 
     auto issue = [&](int64_t t, int b) {
-        const Span s = tile_span(t, g, bulk_in);
+        const Span s = tile_span<NT>(t, g, bulk_in);
         mbar_arrive_expect_tx(&bars[b], (uint32_t)((s.c1 - s.c0) * 4));
         if (s.c1 > s.c0)
             bulk_load((b ? buf1 : buf0) + (s.c0 - s.A), x + s.c0, (uint32_t)((s.c1 - s.c0) * 4),
                       &bars[b]);
     };
-    for (int k = tid; k < g.taps_pad; k += kThreads) hs[k] = k < g.taps ? h[k] : 0.0f;
+    for (int k = tid; k < g.taps_pad; k += NT) hs[k] = k < g.taps ? h[k] : 0.0f;
     if (bulk_in && tid == 0) {
         mbar_init(&bars[0], 1);
         mbar_init(&bars[1], 1);
@@ -185,12 +194,12 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks) k_fir(float* __restrict_
     for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x, it++) {
         const int b = it & 1;
         float* tile = b ? buf1 : buf0;
-        const Span s = tile_span(t, g, bulk_in);
+        const Span s = tile_span<NT>(t, g, bulk_in);
         // The threads fill what the bulk copy does not: samples before x
         // (zeros), and from c1 on (a ragged last 1-3 samples, zeros past x,
         // or everything when x is not 16-byte aligned).
-        for (int64_t i = tid; i < s.c0 - s.A; i += kThreads) tile[i] = 0.0f;
-        for (int64_t i = (s.c1 - s.A) + tid; i < g.tile; i += kThreads) {
+        for (int64_t i = tid; i < s.c0 - s.A; i += NT) tile[i] = 0.0f;
+        for (int64_t i = (s.c1 - s.A) + tid; i < g.tile; i += NT) {
             const int64_t p = s.A + i;
             tile[i] = (p >= 0 && p < g.x_len) ? x[p] : 0.0f;
         }
@@ -228,7 +237,7 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks) k_fir(float* __restrict_
             }
         } else {
             const int64_t n = min((int64_t)kTileOut, g.y_len - ob);
-            for (int64_t i = tid; i < n; i += kThreads) y[ob + i] = tile[i];
+            for (int64_t i = tid; i < n; i += NT) y[ob + i] = tile[i];
             fence_proxy_async_smem();
             __syncthreads();
         }
@@ -241,12 +250,37 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks) k_fir(float* __restrict_
 using FirKernel = void (*)(float*, const float*, const float*, FirGeom, int64_t, bool, bool,
                            uint32_t*);
 
+template <int NT>
+constexpr FirKernel kFirKernels[4] = {k_fir<0, NT>, k_fir<1, NT>, k_fir<2, NT>, k_fir<3, NT>};
+
+// Each kernel may take the opt-in maximum of dynamic shared memory less 1 KB
+// (its static mbarriers); set once per device (a bit per device, for the
+// eight kernels).
+int fir_dyn_max(const sg::DevInfo* d) { return d->max_smem_optin - 1024; }
+std::atomic<uint64_t> g_fir_configured[8];
+
+int fir_configure(const sg::DevInfo* d, int slot, FirKernel kern) {
+    const uint64_t bit = 1ull << (d->device & 63);
+    if (g_fir_configured[slot].load(std::memory_order_acquire) & bit) return 0;
+    const int rc = sg::cuda_status(cudaFuncSetAttribute(kern,
+                                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                        fir_dyn_max(d)),
+                                   "cudaFuncSetAttribute(FIR)");
+    if (rc == 0) g_fir_configured[slot].fetch_or(bit, std::memory_order_acq_rel);
+    return rc;
+}
+
 int launch_fir(const char* K, float* y, int64_t y_len, const float* x, int64_t x_len,
                int64_t halo, const float* h, int32_t taps, void* stream) {
     const sg::DevInfo* d;
     int rc;
     if ((rc = sg::current_device(&d))) return rc;
     if (y_len <= 0) return 0;
+    // Narrow blocks while wide ones would make fewer than four waves.
+    const int64_t wide_waves =
+        sg::ceil_div(y_len, (int64_t)tile_out(kWide)) / ((int64_t)d->sms * min_blocks(kWide));
+    const bool narrow = wide_waves < 4;
+    const int nt = narrow ? kNarrow : kWide;
     FirGeom g;
     g.y_len = y_len;
     g.x_len = x_len;
@@ -258,35 +292,24 @@ int launch_fir(const char* K, float* y, int64_t y_len, const float* x, int64_t x
     g.D = (int32_t)(taps + 6 + m);
     // The window loads of the last thread reach a few floats past the last
     // sample its outputs use (whole 16-byte loads): 8 floats of slack.
-    g.tile = (int32_t)sg::ceil_div(g.D + kTileOut + 8, 4) * 4;
+    g.tile = (int32_t)sg::ceil_div(g.D + tile_out(nt) + 8, 4) * 4;
     const int sh = (g.D - 7) % 4;
 
-    static const FirKernel kernels[4] = {k_fir<0>, k_fir<1>, k_fir<2>, k_fir<3>};
-    const FirKernel kern = kernels[sh];
+    const FirKernel kern = narrow ? kFirKernels<kNarrow>[sh] : kFirKernels<kWide>[sh];
     const size_t smem = (size_t)(2 * g.tile + g.taps_pad) * sizeof(float);
-    if (smem > (size_t)d->max_smem_optin)
+    if (smem > (size_t)fir_dyn_max(d))
         return sg::fail(SIMTGO_ESIZE, "%s: %d taps need %zu bytes of shared memory", K, taps,
                         smem);
-    rc = sg::cuda_status(
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
-        "cudaFuncSetAttribute(FIR)");
-    if (rc) return rc;
-    int per_sm = 0;
-    rc = sg::cuda_status(
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem),
-        "cudaOccupancyMaxActiveBlocksPerMultiprocessor(FIR)");
-    if (rc) return rc;
-    const int64_t ntiles = sg::ceil_div(y_len, kTileOut);
-    const int64_t resident = (int64_t)d->sms * std::max(1, per_sm);
+    if ((rc = fir_configure(d, (narrow ? 4 : 0) + sh, kern))) return rc;
+    const int64_t ntiles = sg::ceil_div(y_len, (int64_t)tile_out(nt));
     // One tile per block measured faster than a persistent grid (the
     // hardware starts the next block's load while this one computes), so
     // the grid covers every tile; the loop in k_fir also serves a grid that
     // does not.
-    (void)resident;
-    const int blocks = (int)ntiles;
     if (ntiles > 0x7fffffffLL) return sg::fail(SIMTGO_ESIZE, "%s: y_len too large", K);
+    const int blocks = (int)ntiles;
     sg::before_launch();
-    kern<<<blocks, kThreads, smem, (cudaStream_t)stream>>>(
+    kern<<<blocks, nt, smem, (cudaStream_t)stream>>>(
         y, x, h, g, ntiles, sg::aligned16(x), sg::aligned16(y), sg::watchdog_device_ptr());
     return sg::launch_status(K);
 }
