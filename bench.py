@@ -633,6 +633,20 @@ def bench_histogram(args, torch, L, dev, sp, rank, world, barrier, max_over_rank
 
     ms, ok = run(L.simtgo_Histogram_allreduce)
     ms_f, ok_f = run(L.simtgo_Histogram_allreduce_fused)
+    # Where the fused step's time goes: the zeroing launch alone, and this
+    # rank's count alone (the local kernel, no exchange); the rest of the
+    # step is the exchange tail and the ranks' skew.
+    stream = torch.cuda.current_stream()
+    barrier()
+    ms_zero = max_over_ranks(timed(lambda: bins.zero_(), args.steps, args.warmup, stream, events))
+
+    def count():
+        rc = L.simtgo_Histogram_shard(P(bins.data_ptr()), 256, P(x.data_ptr()), n, sp)
+        if rc:
+            _lib.check(rc)
+
+    barrier()
+    ms_count = max_over_ranks(timed(count, args.steps, args.warmup, stream, events))
     barrier()
     _lib.check(L.simtgo_comm_destroy(comm))
     return {"samples_total": total, "ms_per_step": round(ms, 4),
@@ -645,7 +659,12 @@ def bench_histogram(args, torch, L, dev, sp, rank, world, barrier, max_over_rank
                       "bins_sum_ok": ok_f,
                       "step": "zero bins; one kernel: local histogram, then its last block "
                               "stores the bins to every rank over NVLink and sums the "
-                              "ranks' slots (simtgo_Histogram_allreduce_fused)"}}
+                              "ranks' slots (simtgo_Histogram_allreduce_fused)"},
+            "breakdown": {"zero_ms": round(ms_zero, 4), "local_count_ms": round(ms_count, 4),
+                          "exchange_and_skew_ms": round(ms_f - ms_zero - ms_count, 4),
+                          "samples_per_rank": n,
+                          "how": "each part timed alone with CUDA events, max over ranks; the "
+                                 "exchange is the fused step less the other two"}}
 
 
 def twelve(tile, g, a, b, c, h):

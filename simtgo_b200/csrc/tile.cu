@@ -801,12 +801,11 @@ int red_level(int kind, unsigned blocks, const float* v, const int64_t* vi, int6
 }
 
 // v/vi: the eight warp partials of each of m chunks (the interpreter's
-// output), 8 m entries.
+// output), 8 m entries; or, with w8 false, one partial per chunk.
 int finish_levels(int kind, const float* v, const int64_t* vi, int64_t m, float* value,
-                  int64_t* index, cudaStream_t s, float* uv, int64_t* ui) {
+                  int64_t* index, cudaStream_t s, float* uv, int64_t* ui, bool w8 = true) {
     const bool am = kind == tilek::RED_ARGMAX;
-    if (m <= 1) return red_level(kind, 1, v, vi, m, value, am ? index : nullptr, true, true, s);
-    bool w8 = true;
+    if (m <= 1) return red_level(kind, 1, v, vi, m, value, am ? index : nullptr, true, w8, s);
     while (m > 1) {
         const int64_t nb = n_partials(m);
         const bool last = nb == 1;
@@ -823,14 +822,105 @@ int finish_levels(int kind, const float* v, const int64_t* vi, int64_t m, float*
     return 0;
 }
 
-// The fused reduction of root over n elements (inputs resolved by
-// `resolve`, halo preceding samples) into value/index; idx_base is the
-// index of element 0.
+// The reduction's value as a chain of steps on one input (the streaming
+// path, tilek::k_red_direct): every node from the root down is Scale, Sqrt,
+// Abs, or Add/Mul/Hypot with both operands the same node, ending at one
+// device input. False for anything else (windows, two inputs, more than
+// kMaxSteps steps).
+bool direct_chain(const simtgo_tile_graph* g, int root, tilek::Chain& ch, int& input) {
+    int ops[tilek::kMaxSteps];
+    float imm[tilek::kMaxSteps];
+    int k = 0;
+    for (int id = root;;) {
+        const Node& nd = g->nodes[id];
+        if (nd.kind == K_INPUT) {
+            if (nd.is_taps) return false;
+            input = id;
+            break;
+        }
+        if (k == tilek::kMaxSteps) return false;
+        imm[k] = 0.0f;
+        switch (nd.kind) {
+            case K_SCALE: ops[k] = tilek::OP_SCALE; imm[k] = nd.scale; break;
+            case K_SQRT: ops[k] = tilek::OP_SQRT; break;
+            case K_ABS: ops[k] = tilek::OP_ABS; break;
+            case K_ADD: ops[k] = tilek::OP_ADD; break;
+            case K_MUL: ops[k] = tilek::OP_MUL; break;
+            case K_HYPOT: ops[k] = tilek::OP_HYPOT; break;
+            default: return false;  // a window
+        }
+        if ((nd.kind == K_ADD || nd.kind == K_MUL || nd.kind == K_HYPOT) && nd.b != nd.a)
+            return false;
+        k++;
+        id = nd.a;
+    }
+    ch.n = k;
+    for (int i = 0; i < k; i++) {  // the input's step first
+        ch.op[i] = ops[k - 1 - i];
+        ch.imm[i] = imm[k - 1 - i];
+    }
+    return true;
+}
+
+// Resident blocks per SM of k_red_direct<kind> (the same on every B200),
+// found once.
+int direct_blocks_per_sm(int kind, int* out) {
+    static std::atomic<int> cache[4];
+    int v = cache[kind & 3].load(std::memory_order_relaxed);
+    if (v == 0) {
+        using namespace tilek;
+        cudaError_t e;
+        switch (kind) {
+            case RED_SUM: e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, k_red_direct<RED_SUM>, kThreads, 0); break;
+            case RED_MIN: e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, k_red_direct<RED_MIN>, kThreads, 0); break;
+            case RED_MAX: e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, k_red_direct<RED_MAX>, kThreads, 0); break;
+            default: e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, k_red_direct<RED_ARGMAX>, kThreads, 0);
+        }
+        if (e != cudaSuccess)
+            return sg::cuda_status(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor(tile reduce)");
+        v = std::max(1, v);
+        cache[kind & 3].store(v, std::memory_order_relaxed);
+    }
+    *out = v;
+    return 0;
+}
+
+// The eight warp partials of every 2048-element block of root's value over
+// n elements (inputs resolved by `resolve`, halo preceding samples) into
+// pv/pi, 8 ceil(n/2048) entries; idx_base is the index of element 0. A
+// chain of steps on one aligned input streams through k_red_direct; any
+// other graph runs the interpreter. Both write the same bits.
 template <class Resolve>
-int reduce_fused(const simtgo_tile_graph* g, int root, int kind, int64_t n, int64_t halo,
-                 int64_t idx_base, cudaStream_t s, Resolve resolve, float* value, int64_t* index) {
-    const bool am = kind == tilek::RED_ARGMAX;
-    if (n == 0) return finish_levels(kind, nullptr, nullptr, 0, value, index, s, nullptr, nullptr);
+int launch_partials(const simtgo_tile_graph* g, int root, int kind, int64_t n, int64_t halo,
+                    int64_t idx_base, cudaStream_t s, Resolve resolve, float* pv, int64_t* pi) {
+    tilek::Chain ch;
+    int input = -1;
+    if (direct_chain(g, root, ch, input)) {
+        const float* x = resolve(input);
+        if (!x) return sg::fail(SIMTGO_EARG, "tile: input node %d has no device data", input);
+        if (sg::aligned16(x)) {
+            const sg::DevInfo* d;
+            int rc;
+            if ((rc = sg::current_device(&d))) return rc;
+            const int64_t nblk = n_partials(n);
+            // One wave of resident blocks, each over a contiguous range of
+            // 2048-blocks.
+            int ps;
+            if ((rc = direct_blocks_per_sm(kind, &ps))) return rc;
+            const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(nblk, (int64_t)d->sms * ps));
+            const int64_t per = (nblk + grid - 1) / grid;
+            const unsigned blocks = (unsigned)((nblk + per - 1) / per);
+            sg::before_launch();
+            using namespace tilek;
+            switch (kind) {
+                case RED_SUM: k_red_direct<RED_SUM><<<blocks, kThreads, 0, s>>>(x, n, idx_base, ch, pv, pi, nblk, per); break;
+                case RED_MIN: k_red_direct<RED_MIN><<<blocks, kThreads, 0, s>>>(x, n, idx_base, ch, pv, pi, nblk, per); break;
+                case RED_MAX: k_red_direct<RED_MAX><<<blocks, kThreads, 0, s>>>(x, n, idx_base, ch, pv, pi, nblk, per); break;
+                default: k_red_direct<RED_ARGMAX><<<blocks, kThreads, 0, s>>>(x, n, idx_base, ch, pv, pi, nblk, per);
+            }
+            return sg::launch_status("tile reduce (streaming)");
+        }
+    }
     Lowered L;
     int rc = lower(g, root, L, kind);
     if (rc) return rc;
@@ -840,6 +930,18 @@ int reduce_fused(const simtgo_tile_graph* g, int root, int kind, int64_t n, int6
         if (!p) return sg::fail(SIMTGO_EARG, "tile: input node %d has no device data", id);
         dev_in.push_back(p);
     }
+    return launch_program(g, L, dev_in, pv, n, halo, s, pi, idx_base);
+}
+
+// The fused reduction of root over n elements (inputs resolved by
+// `resolve`, halo preceding samples) into value/index; idx_base is the
+// index of element 0.
+template <class Resolve>
+int reduce_fused(const simtgo_tile_graph* g, int root, int kind, int64_t n, int64_t halo,
+                 int64_t idx_base, cudaStream_t s, Resolve resolve, float* value, int64_t* index) {
+    const bool am = kind == tilek::RED_ARGMAX;
+    if (n == 0) return finish_levels(kind, nullptr, nullptr, 0, value, index, s, nullptr, nullptr);
+    int rc;
     const int64_t m = n_partials(n);
     const int64_t slots = 8 * m + upper_slots(m);
     AsyncBuf bv, bi;
@@ -847,7 +949,7 @@ int reduce_fused(const simtgo_tile_graph* g, int root, int kind, int64_t n, int6
     if (am && (rc = bi.alloc(slots * sizeof(int64_t), s))) return rc;
     float* pv = (float*)bv.p;
     int64_t* pi = (int64_t*)bi.p;
-    if ((rc = launch_program(g, L, dev_in, pv, n, halo, s, pi, idx_base))) return rc;
+    if ((rc = launch_partials(g, root, kind, n, halo, idx_base, s, resolve, pv, pi))) return rc;
     return finish_levels(kind, pv, pi, m, value, index, s, pv + 8 * m,
                          am ? pi + 8 * m : nullptr);
 }
@@ -1324,52 +1426,54 @@ int simtgo_tile_reduce_shard(simtgo_tile_graph* g, simtgo_tensor t, int32_t kind
     const bool am = kind == tilek::RED_ARGMAX;
     int64_t s0, per;
     if ((rc = simtgo_tile_shard_range(n_total, nranks, 0, &s0, &per))) return rc;
-    const int64_t C = 8 * (per / tilek::kChunk);  // warp-partial slots per rank
-    const int64_t mine = 8 * n_partials(len);
+    // Each rank folds its chunks' eight warp partials into one partial per
+    // chunk (the first level's own first step) before the exchange, so the
+    // all-gather moves one float (and one index) per 2048 elements.
+    // Chunk-partial slots per rank: rank 0 holds the most chunks (whole ones,
+    // unless it holds the entire signal).
+    const int64_t C = n_partials(per);
+    const int64_t mine = n_partials(len);
     const int64_t m = n_partials(n_total);
-    const int64_t slots = C + C * nranks + upper_slots(m);
+    const int64_t slots = 8 * mine + C + C * nranks + upper_slots(m);
     AsyncBuf bv, bi;
     if ((rc = bv.alloc(slots * sizeof(float), s))) return rc;
     if (am && (rc = bi.alloc(slots * sizeof(int64_t), s))) return rc;
-    float* send_v = (float*)bv.p;
+    float* warp_v = (float*)bv.p;
+    float* send_v = warp_v + 8 * mine;
     float* recv_v = send_v + C;
-    int64_t* send_i = am ? (int64_t*)bi.p : nullptr;
+    int64_t* warp_i = am ? (int64_t*)bi.p : nullptr;
+    int64_t* send_i = am ? warp_i + 8 * mine : nullptr;
     int64_t* recv_i = am ? send_i + C : nullptr;
+    using namespace tilek;
     if (len > 0) {
-        Lowered L;
-        if ((rc = lower(g, t, L, kind))) return rc;
-        std::vector<const float*> dev_in;
-        for (int id : L.in_nodes) {
-            const float* p = resolve(id);
-            if (!p) return sg::fail(SIMTGO_EARG, "tile: input node %d has no device data", id);
-            dev_in.push_back(p);
+        if ((rc = launch_partials(g, t, kind, len, halo, start, s, resolve, warp_v, warp_i)))
+            return rc;
+        const unsigned fb = (unsigned)std::min<int64_t>(sg::ceil_div(mine, (int64_t)kThreads), 1024);
+        sg::before_launch();
+        switch (kind) {
+            case RED_SUM: k_red_w8<RED_SUM><<<fb, kThreads, 0, s>>>(warp_v, warp_i, mine, send_v, send_i); break;
+            case RED_MIN: k_red_w8<RED_MIN><<<fb, kThreads, 0, s>>>(warp_v, warp_i, mine, send_v, send_i); break;
+            case RED_MAX: k_red_w8<RED_MAX><<<fb, kThreads, 0, s>>>(warp_v, warp_i, mine, send_v, send_i); break;
+            default: k_red_w8<RED_ARGMAX><<<fb, kThreads, 0, s>>>(warp_v, warp_i, mine, send_v, send_i);
         }
-        if ((rc = launch_program(g, L, dev_in, send_v, len, halo, s, send_i, start))) return rc;
+        if ((rc = sg::launch_status("tile reduce"))) return rc;
     }
     if (mine < C) {
         sg::before_launch();
         switch (kind) {
-            case tilek::RED_SUM:
-                tilek::k_red_fill<tilek::RED_SUM><<<1, tilek::kThreads, 0, s>>>(send_v, send_i, mine, C);
-                break;
-            case tilek::RED_MIN:
-                tilek::k_red_fill<tilek::RED_MIN><<<1, tilek::kThreads, 0, s>>>(send_v, send_i, mine, C);
-                break;
-            case tilek::RED_MAX:
-                tilek::k_red_fill<tilek::RED_MAX><<<1, tilek::kThreads, 0, s>>>(send_v, send_i, mine, C);
-                break;
-            default:
-                tilek::k_red_fill<tilek::RED_ARGMAX><<<1, tilek::kThreads, 0, s>>>(send_v, send_i, mine,
-                                                                                  C);
+            case RED_SUM: k_red_fill<RED_SUM><<<1, kThreads, 0, s>>>(send_v, send_i, mine, C); break;
+            case RED_MIN: k_red_fill<RED_MIN><<<1, kThreads, 0, s>>>(send_v, send_i, mine, C); break;
+            case RED_MAX: k_red_fill<RED_MAX><<<1, kThreads, 0, s>>>(send_v, send_i, mine, C); break;
+            default: k_red_fill<RED_ARGMAX><<<1, kThreads, 0, s>>>(send_v, send_i, mine, C);
         }
         if ((rc = sg::launch_status("tile reduce"))) return rc;
     }
     if ((rc = sg::comm_allgather(comm, send_v, recv_v, C * sizeof(float), s))) return rc;
     if (am && (rc = sg::comm_allgather(comm, send_i, recv_i, C * sizeof(int64_t), s))) return rc;
-    // Ranks hold whole chunks in order, so the first 8 m gathered slots are
-    // the warp partials of the whole signal's chunks.
-    return finish_levels(kind, recv_v, recv_i, m, dev_value, dev_index, s,
-                         recv_v + C * nranks, am ? recv_i + C * nranks : nullptr);
+    // Ranks hold whole chunks in order, so the first m gathered slots are
+    // the partials of the whole signal's chunks.
+    return finish_levels(kind, recv_v, recv_i, m, dev_value, dev_index, s, recv_v + C * nranks,
+                         am ? recv_i + C * nranks : nullptr, false);
 }
 
 }  // extern "C"

@@ -442,26 +442,57 @@ struct RV32 {
     float v;
     int32_t o;
 };
-__device__ __forceinline__ RV32 am_pick32(const RV32& a, const RV32& b) {
-    const bool na = a.v != a.v, nb = b.v != b.v;
-    if (na || nb) return (na && nb ? a.o < b.o : na) ? a : b;
-    if (a.v > b.v) return a;
-    if (b.v > a.v) return b;
-    const bool sa = __float_as_uint(a.v) >> 31, sb = __float_as_uint(b.v) >> 31;
-    if (sa != sb) return sa ? b : a;
-    return a.o < b.o ? a : b;
+// The ARGMAX order as one unsigned key per value: every NaN above
+// everything, then the value's order with +0 above -0 (the float's bits
+// made monotonic). Ties of the key (the same value, or two NaNs) go to the
+// smaller offset, so pairwise choices by (key, offset) choose exactly as
+// am_before does.
+__device__ __forceinline__ uint32_t am_key(float v) {
+    const uint32_t u = __float_as_uint(v);
+    return v != v ? 0xffffffffu : ((u >> 31) ? ~u : (u | 0x80000000u));
 }
+// A thread's eight values (offsets increasing with the index into x, so the
+// left of each pair keeps a tie), then the warp butterfly on (key, offset);
+// every lane ends with the warp's choice. The value comes back from the key
+// (its bits, -0 included), or for a NaN from the lane that holds it.
 __device__ __forceinline__ RV32 am_warp32(const RV32 (&x)[8]) {
-    RV32 v = am_pick32(am_pick32(am_pick32(x[0], x[1]), am_pick32(x[2], x[3])),
-                       am_pick32(am_pick32(x[4], x[5]), am_pick32(x[6], x[7])));
+    uint32_t k[8];
+    int32_t o[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        k[i] = am_key(x[i].v);
+        o[i] = x[i].o;
+    }
+#pragma unroll
+    for (int w = 1; w < 8; w *= 2)
+#pragma unroll
+        for (int i = 0; i < 8; i += 2 * w)
+            if (k[i + w] > k[i]) {
+                k[i] = k[i + w];
+                o[i] = o[i + w];
+            }
+    uint32_t K = k[0];
+    int32_t O = o[0];
 #pragma unroll
     for (int m = 16; m >= 1; m >>= 1) {
-        RV32 o;
-        o.v = __shfl_xor_sync(0xffffffffu, v.v, m);
-        o.o = __shfl_xor_sync(0xffffffffu, v.o, m);
-        v = am_pick32(v, o);
+        const uint32_t k2 = __shfl_xor_sync(0xffffffffu, K, m);
+        const int32_t o2 = __shfl_xor_sync(0xffffffffu, O, m);
+        if (k2 > K || (k2 == K && o2 < O)) {
+            K = k2;
+            O = o2;
+        }
     }
-    return v;
+    float v;
+    if (K != 0xffffffffu) {
+        v = __uint_as_float((K >> 31) ? (K & 0x7fffffffu) : ~K);
+    } else {  // a NaN: its own bits, from the lane whose values hold offset O
+        float c = x[0].v;
+#pragma unroll
+        for (int i = 1; i < 8; i++)
+            if (x[i].o == O) c = x[i].v;
+        v = __shfl_sync(0xffffffffu, c, (O >> 2) & 31);
+    }
+    return {v, O};
 }
 
 template <int KIND, int G>
@@ -474,7 +505,7 @@ __device__ __forceinline__ void chunk_warps(const float4 (&A)[G], int64_t cb, in
         const int64_t b = blk0 + sb;
         if (b < nblk) {  // uniform over the block
             const int64_t base = cb + (int64_t)kChunk * sb;
-            const bool full = base + kChunk <= n;
+            const bool full = base + kChunk <= n;  // uniform: no value past n
             if constexpr (KIND == RED_ARGMAX) {
                 RV32 x[8];
 #pragma unroll
@@ -482,10 +513,14 @@ __device__ __forceinline__ void chunk_warps(const float4 (&A)[G], int64_t cb, in
 #pragma unroll
                     for (int e = 0; e < 4; e++) {
                         const int32_t o = 4 * (t + kThreads * k) + e;
-                        x[4 * k + e] = (full || base + o < n)
-                                           ? RV32{f4_get(A[2 * sb + k], e), o}
-                                           : RV32{__int_as_float((int)0xff800000u), INT32_MAX};
+                        x[4 * k + e] = RV32{f4_get(A[2 * sb + k], e), o};
                     }
+                if (!full) {
+#pragma unroll
+                    for (int i = 0; i < 8; i++)
+                        if (base + x[i].o >= n)
+                            x[i] = RV32{__int_as_float((int)0xff800000u), INT32_MAX};
+                }
                 const RV32 w = am_warp32(x);
                 if ((t & 31) == 0) {
                     out[8 * b + (t >> 5)] = w.v;
@@ -496,11 +531,15 @@ __device__ __forceinline__ void chunk_warps(const float4 (&A)[G], int64_t cb, in
 #pragma unroll
                 for (int k = 0; k < 2; k++)
 #pragma unroll
-                    for (int e = 0; e < 4; e++) {
-                        const int64_t p = base + 4 * (t + kThreads * k) + e;
-                        x[4 * k + e] = (full || p < n) ? RVal{f4_get(A[2 * sb + k], e), 0}
-                                                       : red_identity<KIND>();
-                    }
+                    for (int e = 0; e < 4; e++) x[4 * k + e] = RVal{f4_get(A[2 * sb + k], e), 0};
+                if (!full) {
+#pragma unroll
+                    for (int k = 0; k < 2; k++)
+#pragma unroll
+                        for (int e = 0; e < 4; e++)
+                            if (base + 4 * (t + kThreads * k) + e >= n)
+                                x[4 * k + e] = red_identity<KIND>();
+                }
                 const RVal w = red_warp<KIND>(red_thread<KIND>(x));
                 if ((t & 31) == 0) out[8 * b + (t >> 5)] = w.v;
             }
@@ -570,6 +609,120 @@ __global__ void k_red_fill(float* v, int64_t* vi, int64_t from, int64_t to) {
          e += (int64_t)gridDim.x * blockDim.x) {
         v[e] = id.v;
         if (vi) vi[e] = id.i;
+    }
+}
+
+// ---- the streaming reduction -------------------------------------------------
+// A reduction whose value is a chain of steps on ONE input (Scale, Sqrt, Abs,
+// and Add, Mul or Hypot of a value with itself) needs neither shared operands
+// nor the interpreter: each thread loads its two float4 groups of a
+// 2048-element block straight from HBM, applies the steps to all eight
+// values, and the block's warps reduce them with the chunk tree
+// (chunk_warps) into the same warp partials the interpreter writes.
+constexpr int kMaxSteps = 8;
+struct Chain {
+    int32_t n;               // steps
+    int32_t op[kMaxSteps];   // OP_SCALE, OP_SQRT, OP_ABS, OP_ADD, OP_MUL, OP_HYPOT (x op x)
+    float imm[kMaxSteps];    // OP_SCALE's factor
+};
+
+template <int G>
+__device__ __forceinline__ void apply_chain(const Chain& ch, float4 (&A)[G]) {
+    for (int s = 0; s < ch.n; s++) {
+        const float k = ch.imm[s];
+        switch (ch.op[s]) {  // uniform: one branch per step for all the thread's values
+            case OP_SCALE:
+#pragma unroll
+                for (int j = 0; j < G; j++) A[j] = f4_scale(k, A[j]);
+                break;
+            case OP_SQRT:
+#pragma unroll
+                for (int j = 0; j < G; j++) A[j] = f4_sqrt(A[j]);
+                break;
+            case OP_ABS:
+#pragma unroll
+                for (int j = 0; j < G; j++) A[j] = f4_abs(A[j]);
+                break;
+            case OP_ADD:
+#pragma unroll
+                for (int j = 0; j < G; j++) A[j] = f4_add(A[j], A[j]);
+                break;
+            case OP_MUL:
+#pragma unroll
+                for (int j = 0; j < G; j++) A[j] = f4_mul(A[j], A[j]);
+                break;
+            default:
+#pragma unroll
+                for (int j = 0; j < G; j++) A[j] = f4_hypot(A[j], A[j]);
+                break;
+        }
+    }
+}
+
+// Block b's values for this thread: positions b*kChunk + 4 (t + 256 k) + j;
+// positions at or past n read as 0 (the tree replaces them by the identity).
+__device__ __forceinline__ void load_block2(const float* __restrict__ x, int64_t n, int64_t b,
+                                            float4 (&V)[2]) {
+    const float* q = x + b * kChunk + 4 * threadIdx.x;
+    if ((b + 1) * kChunk <= n) {  // uniform: a whole block
+        V[0] = ld_stream_f4(q);
+        V[1] = ld_stream_f4(q + 4 * kThreads);
+        return;
+    }
+#pragma unroll
+    for (int k = 0; k < 2; k++) {
+        const int64_t p = b * kChunk + 4 * (threadIdx.x + kThreads * k);
+        if (p + 3 < n) {
+            V[k] = ld_stream_f4(x + p);
+        } else {
+            float f[4];
+#pragma unroll
+            for (int j = 0; j < 4; j++) f[j] = p + j < n ? x[p + j] : 0.0f;
+            V[k] = make_float4(f[0], f[1], f[2], f[3]);
+        }
+    }
+}
+
+// Blocks [blockIdx.x * per, +per) of the nblk 2048-element blocks of x (16-byte
+// aligned; idx_base + p is the index of position p). Each thread keeps
+// kDirectDepth blocks' loads in flight (a ring of registers): the loads of
+// block b + kDirectDepth go out as block b is reduced, so an SM has about
+// 100 KB of reads outstanding, what HBM's latency needs at full bandwidth.
+constexpr int kDirectDepth = 2;
+template <int KIND>
+__global__ void __launch_bounds__(kThreads) k_red_direct(const float* __restrict__ x, int64_t n,
+                                                         int64_t idx_base, const Chain ch,
+                                                         float* __restrict__ out,
+                                                         int64_t* __restrict__ out_i,
+                                                         int64_t nblk, int64_t per) {
+    const int64_t b0 = (int64_t)blockIdx.x * per;
+    const int64_t b1 = min(b0 + per, nblk);
+    float4 R[kDirectDepth][2];
+#pragma unroll
+    for (int j = 0; j < kDirectDepth; j++)
+        if (b0 + j < b1) load_block2(x, n, b0 + j, R[j]);
+    for (int64_t b = b0; b < b1; b += kDirectDepth) {
+#pragma unroll
+        for (int j = 0; j < kDirectDepth; j++) {
+            if (b + j < b1) {  // uniform over the block
+                apply_chain<2>(ch, R[j]);
+                chunk_warps<KIND, 2>(R[j], (b + j) * kChunk, n, idx_base, out, out_i, b + j, nblk);
+                if (b + j + kDirectDepth < b1) load_block2(x, n, b + j + kDirectDepth, R[j]);
+            }
+        }
+    }
+}
+
+// Chunk e's partial from its eight warp partials, ((w0 w1)(w2 w3))((w4 w5)(w6
+// w7)) as the first level computes it: ov[e] (and oi[e]) for e < m.
+template <int KIND>
+__global__ void k_red_w8(const float* __restrict__ v, const int64_t* __restrict__ vi, int64_t m,
+                         float* __restrict__ ov, int64_t* __restrict__ oi) {
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < m;
+         e += (int64_t)gridDim.x * blockDim.x) {
+        const RVal r = red_block8<KIND>(v + 8 * e, KIND == RED_ARGMAX ? vi + 8 * e : nullptr);
+        ov[e] = r.v;
+        if (KIND == RED_ARGMAX) oi[e] = r.i;
     }
 }
 

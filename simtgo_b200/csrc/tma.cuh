@@ -3,7 +3,7 @@
 // driver entry point so the library needs no link against libcuda) and
 // device-side mbarrier / cp.async.bulk.tensor wrappers in inline PTX.
 //
-// No load here uses .multicast::cluster: every tensor map covers this GPU's
+// No load here is a cluster-multicast load: every tensor map covers this GPU's
 // own memory and every CTA fetches its own tiles.
 #pragma once
 #include <cuda.h>
