@@ -161,7 +161,9 @@ const char* simtgo_version(void) { return "simtgo_b200 0.1.0 (sm_100a)"; }
 
 int simtgo_shutdown(void) {
     sg::clear_error();
-    return sg::fir_host_release();
+    const int rc = sg::fir_host_release();
+    const int rc2 = sg::tile_pool_release();
+    return rc ? rc : rc2;
 }
 
 int simtgo_device_info(int32_t* sm_count, int32_t* cc_major, int32_t* cc_minor) {

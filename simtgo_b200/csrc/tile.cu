@@ -760,6 +760,56 @@ int run_fused(const simtgo_tile_graph* g, int root, float* out, int64_t n, int64
 
 // Stream-ordered device scratch, released on its stream when it goes out of
 // scope (after everything enqueued before).
+// The reductions' stream-ordered scratch comes from a pool of the library's
+// own per device, which keeps up to 1 GiB of freed memory mapped (the
+// default pool returns it at every synchronisation, and mapping it again
+// costs more than a 2^28-element reduction).
+std::mutex g_pool_mu;
+cudaMemPool_t g_pool[64];
+
+int scratch_pool(cudaMemPool_t* out) {
+    int dev = -1;
+    int rc = sg::cuda_status(cudaGetDevice(&dev), "cudaGetDevice");
+    if (rc) return rc;
+    if (dev < 0 || dev >= 64) return sg::fail(SIMTGO_EDEVICE, "device %d out of range", dev);
+    std::lock_guard<std::mutex> lk(g_pool_mu);
+    if (!g_pool[dev]) {
+        cudaMemPoolProps props = {};
+        props.allocType = cudaMemAllocationTypePinned;
+        props.location.type = cudaMemLocationTypeDevice;
+        props.location.id = dev;
+        cudaMemPool_t pool;
+        if ((rc = sg::cuda_status(cudaMemPoolCreate(&pool, &props), "cudaMemPoolCreate")))
+            return rc;
+        uint64_t keep = 1ull << 30;
+        if ((rc = sg::cuda_status(
+                 cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep),
+                 "cudaMemPoolSetAttribute"))) {
+            cudaMemPoolDestroy(pool);
+            return rc;
+        }
+        g_pool[dev] = pool;
+    }
+    *out = g_pool[dev];
+    return 0;
+}
+
+}  // namespace
+
+namespace sg {
+int tile_pool_release() {
+    std::lock_guard<std::mutex> lk(g_pool_mu);
+    for (int dev = 0; dev < 64; dev++)
+        if (g_pool[dev]) {
+            const int rc = cuda_status(cudaMemPoolTrimTo(g_pool[dev], 0), "cudaMemPoolTrimTo");
+            if (rc) return rc;
+        }
+    return 0;
+}
+}  // namespace sg
+
+namespace {
+
 struct AsyncBuf {
     void* p = nullptr;
     cudaStream_t s = 0;
@@ -768,8 +818,10 @@ struct AsyncBuf {
     }
     int alloc(size_t bytes, cudaStream_t st) {
         s = st;
-        return sg::cuda_status(cudaMallocAsync(&p, std::max<size_t>(bytes, 16), st),
-                               "cudaMallocAsync");
+        cudaMemPool_t pool;
+        if (int rc = scratch_pool(&pool)) return rc;
+        return sg::cuda_status(cudaMallocFromPoolAsync(&p, std::max<size_t>(bytes, 16), pool, st),
+                               "cudaMallocFromPoolAsync");
     }
 };
 
@@ -824,7 +876,7 @@ int finish_levels(int kind, const float* v, const int64_t* vi, int64_t m, float*
 
 // The reduction's value as a chain of steps on one input (the streaming
 // path, tilek::k_red_direct): every node from the root down is Scale, Sqrt,
-// Abs, or Add/Mul/Hypot with both operands the same node, ending at one
+// Abs, or Add/Mul with both operands the same node, ending at one
 // device input. False for anything else (windows, two inputs, more than
 // kMaxSteps steps).
 bool direct_chain(const simtgo_tile_graph* g, int root, tilek::Chain& ch, int& input) {
@@ -846,10 +898,9 @@ bool direct_chain(const simtgo_tile_graph* g, int root, tilek::Chain& ch, int& i
             case K_ABS: ops[k] = tilek::OP_ABS; break;
             case K_ADD: ops[k] = tilek::OP_ADD; break;
             case K_MUL: ops[k] = tilek::OP_MUL; break;
-            case K_HYPOT: ops[k] = tilek::OP_HYPOT; break;
-            default: return false;  // a window
+            default: return false;  // a window, or Hypot (its float64 registers would slow the rest)
         }
-        if ((nd.kind == K_ADD || nd.kind == K_MUL || nd.kind == K_HYPOT) && nd.b != nd.a)
+        if ((nd.kind == K_ADD || nd.kind == K_MUL) && nd.b != nd.a)
             return false;
         k++;
         id = nd.a;
@@ -885,31 +936,52 @@ int direct_blocks_per_sm(int kind, int* out) {
     return 0;
 }
 
-// The eight warp partials of every 2048-element block of root's value over
-// n elements (inputs resolved by `resolve`, halo preceding samples) into
-// pv/pi, 8 ceil(n/2048) entries; idx_base is the index of element 0. A
-// chain of steps on one aligned input streams through k_red_direct; any
-// other graph runs the interpreter. Both write the same bits.
+// Folds the eight warp partials of each of m chunks (wv/wi, 8 m entries)
+// into the chunk partials pv/pi (m entries).
+int fold_warps(int kind, const float* wv, const int64_t* wi, int64_t m, float* pv, int64_t* pi,
+               cudaStream_t s) {
+    using namespace tilek;
+    if (m <= 0) return 0;
+    const unsigned fb = (unsigned)std::min<int64_t>(sg::ceil_div(m, (int64_t)kThreads), 1024);
+    sg::before_launch();
+    switch (kind) {
+        case RED_SUM: k_red_w8<RED_SUM><<<fb, kThreads, 0, s>>>(wv, wi, m, pv, pi); break;
+        case RED_MIN: k_red_w8<RED_MIN><<<fb, kThreads, 0, s>>>(wv, wi, m, pv, pi); break;
+        case RED_MAX: k_red_w8<RED_MAX><<<fb, kThreads, 0, s>>>(wv, wi, m, pv, pi); break;
+        default: k_red_w8<RED_ARGMAX><<<fb, kThreads, 0, s>>>(wv, wi, m, pv, pi);
+    }
+    return sg::launch_status("tile reduce");
+}
+
+// The partial of every 2048-element chunk of root's value over n elements
+// (inputs resolved by `resolve`, halo preceding samples) into pv/pi,
+// ceil(n/2048) entries; idx_base is the index of element 0. A chain of steps
+// on one aligned input streams through k_red_direct (one warp per chunk);
+// any other graph runs the interpreter, whose eight warp partials per chunk
+// (in wv/wi, 8 ceil(n/2048) entries of scratch) are then folded. Both give
+// the same bits: the same trees in the same order.
 template <class Resolve>
 int launch_partials(const simtgo_tile_graph* g, int root, int kind, int64_t n, int64_t halo,
-                    int64_t idx_base, cudaStream_t s, Resolve resolve, float* pv, int64_t* pi) {
+                    int64_t idx_base, cudaStream_t s, Resolve resolve, float* pv, int64_t* pi,
+                    float* wv, int64_t* wi) {
     tilek::Chain ch;
     int input = -1;
+    int rc;
+    const int64_t nblk = n_partials(n);
     if (direct_chain(g, root, ch, input)) {
         const float* x = resolve(input);
         if (!x) return sg::fail(SIMTGO_EARG, "tile: input node %d has no device data", input);
         if (sg::aligned16(x)) {
             const sg::DevInfo* d;
-            int rc;
             if ((rc = sg::current_device(&d))) return rc;
-            const int64_t nblk = n_partials(n);
-            // One wave of resident blocks, each over a contiguous range of
-            // 2048-blocks.
+            // One wave of resident blocks; each warp takes a contiguous
+            // range of chunks.
             int ps;
             if ((rc = direct_blocks_per_sm(kind, &ps))) return rc;
-            const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(nblk, (int64_t)d->sms * ps));
-            const int64_t per = (nblk + grid - 1) / grid;
-            const unsigned blocks = (unsigned)((nblk + per - 1) / per);
+            const int64_t warps = (int64_t)d->sms * ps * (tilek::kThreads / 32);
+            const int64_t per = sg::ceil_div(nblk, std::min<int64_t>(nblk, warps));
+            const int64_t used = sg::ceil_div(nblk, per);
+            const unsigned blocks = (unsigned)sg::ceil_div(used, (int64_t)(tilek::kThreads / 32));
             sg::before_launch();
             using namespace tilek;
             switch (kind) {
@@ -922,15 +994,15 @@ int launch_partials(const simtgo_tile_graph* g, int root, int kind, int64_t n, i
         }
     }
     Lowered L;
-    int rc = lower(g, root, L, kind);
-    if (rc) return rc;
+    if ((rc = lower(g, root, L, kind))) return rc;
     std::vector<const float*> dev_in;
     for (int id : L.in_nodes) {
         const float* p = resolve(id);
         if (!p) return sg::fail(SIMTGO_EARG, "tile: input node %d has no device data", id);
         dev_in.push_back(p);
     }
-    return launch_program(g, L, dev_in, pv, n, halo, s, pi, idx_base);
+    if ((rc = launch_program(g, L, dev_in, wv, n, halo, s, wi, idx_base))) return rc;
+    return fold_warps(kind, wv, wi, nblk, pv, pi, s);
 }
 
 // The fused reduction of root over n elements (inputs resolved by
@@ -943,15 +1015,21 @@ int reduce_fused(const simtgo_tile_graph* g, int root, int kind, int64_t n, int6
     if (n == 0) return finish_levels(kind, nullptr, nullptr, 0, value, index, s, nullptr, nullptr);
     int rc;
     const int64_t m = n_partials(n);
-    const int64_t slots = 8 * m + upper_slots(m);
+    // m chunk partials, the levels above them, and 8 m warp partials of
+    // scratch for the interpreter's path.
+    const int64_t slots = m + upper_slots(m) + 8 * m;
     AsyncBuf bv, bi;
     if ((rc = bv.alloc(slots * sizeof(float), s))) return rc;
     if (am && (rc = bi.alloc(slots * sizeof(int64_t), s))) return rc;
     float* pv = (float*)bv.p;
     int64_t* pi = (int64_t*)bi.p;
-    if ((rc = launch_partials(g, root, kind, n, halo, idx_base, s, resolve, pv, pi))) return rc;
-    return finish_levels(kind, pv, pi, m, value, index, s, pv + 8 * m,
-                         am ? pi + 8 * m : nullptr);
+    float* uv = pv + m;
+    int64_t* ui = am ? pi + m : nullptr;
+    float* wv = uv + upper_slots(m);
+    int64_t* wi = am ? ui + upper_slots(m) : nullptr;
+    if ((rc = launch_partials(g, root, kind, n, halo, idx_base, s, resolve, pv, pi, wv, wi)))
+        return rc;
+    return finish_levels(kind, pv, pi, m, value, index, s, uv, ui, false);
 }
 
 int check_reduce(simtgo_tile_graph* g, simtgo_tensor t, int32_t kind, const void* value,
@@ -1426,38 +1504,27 @@ int simtgo_tile_reduce_shard(simtgo_tile_graph* g, simtgo_tensor t, int32_t kind
     const bool am = kind == tilek::RED_ARGMAX;
     int64_t s0, per;
     if ((rc = simtgo_tile_shard_range(n_total, nranks, 0, &s0, &per))) return rc;
-    // Each rank folds its chunks' eight warp partials into one partial per
-    // chunk (the first level's own first step) before the exchange, so the
+    // Each rank exchanges one partial per chunk (launch_partials), so the
     // all-gather moves one float (and one index) per 2048 elements.
     // Chunk-partial slots per rank: rank 0 holds the most chunks (whole ones,
     // unless it holds the entire signal).
     const int64_t C = n_partials(per);
     const int64_t mine = n_partials(len);
     const int64_t m = n_partials(n_total);
-    const int64_t slots = 8 * mine + C + C * nranks + upper_slots(m);
+    const int64_t slots = C + C * nranks + upper_slots(m) + 8 * mine;
     AsyncBuf bv, bi;
     if ((rc = bv.alloc(slots * sizeof(float), s))) return rc;
     if (am && (rc = bi.alloc(slots * sizeof(int64_t), s))) return rc;
-    float* warp_v = (float*)bv.p;
-    float* send_v = warp_v + 8 * mine;
+    float* send_v = (float*)bv.p;
     float* recv_v = send_v + C;
-    int64_t* warp_i = am ? (int64_t*)bi.p : nullptr;
-    int64_t* send_i = am ? warp_i + 8 * mine : nullptr;
+    float* warp_v = recv_v + C * nranks + upper_slots(m);
+    int64_t* send_i = am ? (int64_t*)bi.p : nullptr;
     int64_t* recv_i = am ? send_i + C : nullptr;
+    int64_t* warp_i = am ? recv_i + C * nranks + upper_slots(m) : nullptr;
     using namespace tilek;
-    if (len > 0) {
-        if ((rc = launch_partials(g, t, kind, len, halo, start, s, resolve, warp_v, warp_i)))
-            return rc;
-        const unsigned fb = (unsigned)std::min<int64_t>(sg::ceil_div(mine, (int64_t)kThreads), 1024);
-        sg::before_launch();
-        switch (kind) {
-            case RED_SUM: k_red_w8<RED_SUM><<<fb, kThreads, 0, s>>>(warp_v, warp_i, mine, send_v, send_i); break;
-            case RED_MIN: k_red_w8<RED_MIN><<<fb, kThreads, 0, s>>>(warp_v, warp_i, mine, send_v, send_i); break;
-            case RED_MAX: k_red_w8<RED_MAX><<<fb, kThreads, 0, s>>>(warp_v, warp_i, mine, send_v, send_i); break;
-            default: k_red_w8<RED_ARGMAX><<<fb, kThreads, 0, s>>>(warp_v, warp_i, mine, send_v, send_i);
-        }
-        if ((rc = sg::launch_status("tile reduce"))) return rc;
-    }
+    if (len > 0 && (rc = launch_partials(g, t, kind, len, halo, start, s, resolve, send_v, send_i,
+                                         warp_v, warp_i)))
+        return rc;
     if (mine < C) {
         sg::before_launch();
         switch (kind) {

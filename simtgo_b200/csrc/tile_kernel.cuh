@@ -614,20 +614,23 @@ __global__ void k_red_fill(float* v, int64_t* vi, int64_t from, int64_t to) {
 
 // ---- the streaming reduction -------------------------------------------------
 // A reduction whose value is a chain of steps on ONE input (Scale, Sqrt, Abs,
-// and Add, Mul or Hypot of a value with itself) needs neither shared operands
-// nor the interpreter: each thread loads its two float4 groups of a
-// 2048-element block straight from HBM, applies the steps to all eight
-// values, and the block's warps reduce them with the chunk tree
-// (chunk_warps) into the same warp partials the interpreter writes.
+// and Add or Mul of a value with itself) needs neither shared operands
+// nor the interpreter. One warp takes a whole 2048-element block: the eight
+// rows that warps 0..7 of the interpreter's block hold (lane l of row w: the
+// four positions 4 (32 w + l) and the four 1024 later) come straight from
+// HBM, one after another, each reduced by the same thread and butterfly
+// trees; the eight row results combine as ((w0 w1)(w2 w3))((w4 w5)(w6 w7)),
+// the first level's own step, into the chunk's partial. No block barrier.
 constexpr int kMaxSteps = 8;
 struct Chain {
     int32_t n;               // steps
-    int32_t op[kMaxSteps];   // OP_SCALE, OP_SQRT, OP_ABS, OP_ADD, OP_MUL, OP_HYPOT (x op x)
+    int32_t op[kMaxSteps];   // OP_SCALE, OP_SQRT, OP_ABS, OP_ADD, OP_MUL (x op x)
     float imm[kMaxSteps];    // OP_SCALE's factor
 };
 
 template <int G>
 __device__ __forceinline__ void apply_chain(const Chain& ch, float4 (&A)[G]) {
+    static_assert(G == 2, "the streaming reduction holds two groups per row");
     for (int s = 0; s < ch.n; s++) {
         const float k = ch.imm[s];
         switch (ch.op[s]) {  // uniform: one branch per step for all the thread's values
@@ -647,67 +650,171 @@ __device__ __forceinline__ void apply_chain(const Chain& ch, float4 (&A)[G]) {
 #pragma unroll
                 for (int j = 0; j < G; j++) A[j] = f4_add(A[j], A[j]);
                 break;
-            case OP_MUL:
+            default:  // OP_MUL
 #pragma unroll
                 for (int j = 0; j < G; j++) A[j] = f4_mul(A[j], A[j]);
-                break;
-            default:
-#pragma unroll
-                for (int j = 0; j < G; j++) A[j] = f4_hypot(A[j], A[j]);
                 break;
         }
     }
 }
 
-// Block b's values for this thread: positions b*kChunk + 4 (t + 256 k) + j;
-// positions at or past n read as 0 (the tree replaces them by the identity).
-__device__ __forceinline__ void load_block2(const float* __restrict__ x, int64_t n, int64_t b,
-                                            float4 (&V)[2]) {
-    const float* q = x + b * kChunk + 4 * threadIdx.x;
+// Row w of block b for this lane: positions b*kChunk + 4 (32 w + lane) + j
+// and 1024 later; positions at or past n read as 0 (the trees put the
+// identity there).
+__device__ __forceinline__ void load_row(const float* __restrict__ x, int64_t n, int64_t b, int w,
+                                         int lane, float4 (&V)[2]) {
+    const int64_t p0 = b * kChunk + 4 * (32 * w + lane);
     if ((b + 1) * kChunk <= n) {  // uniform: a whole block
-        V[0] = ld_stream_f4(q);
-        V[1] = ld_stream_f4(q + 4 * kThreads);
+        V[0] = ld_stream_f4(x + p0);
+        V[1] = ld_stream_f4(x + p0 + 4 * kThreads);
         return;
     }
 #pragma unroll
     for (int k = 0; k < 2; k++) {
-        const int64_t p = b * kChunk + 4 * (threadIdx.x + kThreads * k);
-        if (p + 3 < n) {
-            V[k] = ld_stream_f4(x + p);
-        } else {
-            float f[4];
+        float f[4];
 #pragma unroll
-            for (int j = 0; j < 4; j++) f[j] = p + j < n ? x[p + j] : 0.0f;
-            V[k] = make_float4(f[0], f[1], f[2], f[3]);
+        for (int j = 0; j < 4; j++) {
+            const int64_t p = p0 + 4 * kThreads * k + j;
+            f[j] = p < n ? x[p] : 0.0f;
         }
+        V[k] = make_float4(f[0], f[1], f[2], f[3]);
     }
 }
 
-// Blocks [blockIdx.x * per, +per) of the nblk 2048-element blocks of x (16-byte
-// aligned; idx_base + p is the index of position p). Each thread keeps
-// kDirectDepth blocks' loads in flight (a ring of registers): the loads of
-// block b + kDirectDepth go out as block b is reduced, so an SM has about
-// 100 KB of reads outstanding, what HBM's latency needs at full bandwidth.
-constexpr int kDirectDepth = 2;
+// A row's eight values of a SUM/MIN/MAX reduction through the thread tree;
+// values at positions past n are the identity.
+template <int KIND>
+__device__ __forceinline__ float row_thread(const float4 (&V)[2], int64_t p0, int64_t n, bool full) {
+    RVal x[8];
+#pragma unroll
+    for (int k = 0; k < 2; k++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) x[4 * k + j] = RVal{f4_get(V[k], j), 0};
+    if (!full) {
+#pragma unroll
+        for (int k = 0; k < 2; k++)
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+                if (p0 + 4 * kThreads * k + j >= n) x[4 * k + j] = red_identity<KIND>();
+    }
+    return red_thread<KIND>(x).v;
+}
+
+// A row's ARGMAX: the thread's eight values (their keys' maximum and the
+// first of them that has it: offsets grow with the index, so the first is
+// the smallest offset), then the warp's largest key and the smallest offset
+// among the lanes holding it (two warp reductions), and the value from the
+// lane that holds it (its bits, NaN payloads included). (K, O, v) is the
+// same on every lane.
+__device__ __forceinline__ void row_argmax(const float4 (&V)[2], int w, int lane, int64_t cb,
+                                           int64_t n, bool full, uint32_t& K, int32_t& O,
+                                           float& v) {
+    uint32_t k[8];
+    float x[8];
+#pragma unroll
+    for (int c = 0; c < 2; c++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int i = 4 * c + j;
+            x[i] = f4_get(V[c], j);
+            k[i] = am_key(x[i]);
+        }
+    const int32_t o0 = 4 * (32 * w + lane);  // offset of x[0]; x[4 + j] is 1024 later
+    if (!full) {
+#pragma unroll
+        for (int i = 0; i < 8; i++)
+            if (cb + o0 + (i >> 2) * 4 * kThreads + (i & 3) >= n) k[i] = 0;  // below any value
+    }
+    uint32_t mk = k[0];
+#pragma unroll
+    for (int i = 1; i < 8; i++) mk = max(mk, k[i]);
+    int32_t ob = INT32_MAX;
+    float vb = 0.0f;
+#pragma unroll
+    for (int i = 7; i >= 0; i--)
+        if (k[i] == mk && mk != 0) {
+            ob = o0 + (i >> 2) * 4 * kThreads + (i & 3);
+            vb = x[i];
+        }
+    K = __reduce_max_sync(0xffffffffu, mk);
+    O = (int32_t)__reduce_min_sync(0xffffffffu, mk == K ? (uint32_t)ob : 0xffffffffu);
+    v = __shfl_sync(0xffffffffu, vb, (O >> 2) & 31);
+    if (K == 0) {  // every position past n: the identity
+        O = INT32_MAX;
+        v = __int_as_float((int)0xff800000u);
+    }
+}
+
+// One warp per block b in [gw * per, +per) of the nblk 2048-element blocks of
+// x (16-byte aligned), gw its index in the grid; out[b] (and, ARGMAX,
+// out_i[b] = idx_base + the position) receive the chunk partials. Rows
+// stream through a ring of four register slots, three rows ahead of the
+// one being reduced.
 template <int KIND>
 __global__ void __launch_bounds__(kThreads) k_red_direct(const float* __restrict__ x, int64_t n,
                                                          int64_t idx_base, const Chain ch,
                                                          float* __restrict__ out,
                                                          int64_t* __restrict__ out_i,
                                                          int64_t nblk, int64_t per) {
-    const int64_t b0 = (int64_t)blockIdx.x * per;
+    const int lane = threadIdx.x & 31;
+    const int64_t gw = ((int64_t)blockIdx.x * kThreads + threadIdx.x) >> 5;
+    const int64_t b0 = gw * per;
     const int64_t b1 = min(b0 + per, nblk);
-    float4 R[kDirectDepth][2];
+    if (b0 >= b1) return;
+    float4 R[4][2];  // row w of a block lives in slot w % 4
 #pragma unroll
-    for (int j = 0; j < kDirectDepth; j++)
-        if (b0 + j < b1) load_block2(x, n, b0 + j, R[j]);
-    for (int64_t b = b0; b < b1; b += kDirectDepth) {
+    for (int w = 0; w < 3; w++) load_row(x, n, b0, w, lane, R[w]);
+    for (int64_t b = b0; b < b1; b++) {
+        const int64_t cb = b * kChunk;
+        const bool full = cb + kChunk <= n;
+        uint32_t bK = 0;
+        int32_t bO = INT32_MAX;
+        float bv = __int_as_float((int)0xff800000u);
+        float acc01 = 0.0f, acc0123 = 0.0f, acc45 = 0.0f, w0 = 0.0f, w4 = 0.0f, w6 = 0.0f;
+        auto r2 = [](float a, float c) { return red2<KIND>(RVal{a, 0}, RVal{c, 0}).v; };
 #pragma unroll
-        for (int j = 0; j < kDirectDepth; j++) {
-            if (b + j < b1) {  // uniform over the block
-                apply_chain<2>(ch, R[j]);
-                chunk_warps<KIND, 2>(R[j], (b + j) * kChunk, n, idx_base, out, out_i, b + j, nblk);
-                if (b + j + kDirectDepth < b1) load_block2(x, n, b + j + kDirectDepth, R[j]);
+        for (int w = 0; w < 8; w++) {
+            // Row w + 3 (of this block or the next) into the slot row w - 1 left.
+            if (w + 3 < 8)
+                load_row(x, n, b, w + 3, lane, R[(w + 3) & 3]);
+            else if (b + 1 < b1)
+                load_row(x, n, b + 1, w + 3 - 8, lane, R[(w + 3) & 3]);
+            float4 (&cur)[2] = R[w & 3];
+            apply_chain<2>(ch, cur);
+            if constexpr (KIND == RED_ARGMAX) {
+                uint32_t K;
+                int32_t O;
+                float v;
+                row_argmax(cur, w, lane, cb, n, full, K, O, v);
+                if (K > bK || (K == bK && O < bO)) {
+                    bK = K;
+                    bO = O;
+                    bv = v;
+                }
+            } else {
+                float r = row_thread<KIND>(cur, cb + 4 * (32 * w + lane), n, full);
+#pragma unroll
+                for (int m = 16; m >= 1; m >>= 1) r = r2(r, __shfl_xor_sync(0xffffffffu, r, m));
+                // ((w0 w1)(w2 w3))((w4 w5)(w6 w7)), as the rows arrive.
+                switch (w) {
+                    case 0: w0 = r; break;
+                    case 1: acc01 = r2(w0, r); break;
+                    case 2: w0 = r; break;
+                    case 3: acc0123 = r2(acc01, r2(w0, r)); break;
+                    case 4: w4 = r; break;
+                    case 5: acc45 = r2(w4, r); break;
+                    case 6: w6 = r; break;
+                    default: {
+                        const float total = r2(acc0123, r2(acc45, r2(w6, r)));
+                        if (lane == 0) out[b] = total;
+                    }
+                }
+            }
+        }
+        if constexpr (KIND == RED_ARGMAX) {
+            if (lane == 0) {
+                out[b] = bv;
+                out_i[b] = bO == INT32_MAX ? kNoIndex : idx_base + cb + bO;
             }
         }
     }
