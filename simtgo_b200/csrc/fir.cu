@@ -5,25 +5,26 @@
 // order and rounding of the reference's device code, where nvcc contracts
 // `acc += h[k] * tile[...]` (kernels/prebuilt/FIR.cu:24-27).
 //
-// B200 design. A 256-thread block produces 5120 consecutive outputs (a
-// 64-thread block, 1280, for short signals, so that they spread over every
-// SM); thread t owns 20 consecutive outputs, so every sample it loads from shared memory
+// B200 design. Each warp produces 640 consecutive outputs on its own: lane l
+// owns 20 consecutive outputs, so every sample it loads from shared memory
 // feeds up to 20 fused multiply-adds from registers (the reference does one
 // output per thread, with one shared load and one global tap load per
 // multiply-add):
-//  * the block's signal span (its outputs plus the taps-1 halo) arrives by
-//    one 1-D bulk copy (cp.async.bulk, TMA) into a LINEAR shared tile;
-//  * 20 outputs per thread put lane t's window 80 bytes after lane t-1's
+//  * the warp's signal span (its outputs plus the taps-1 halo) arrives by
+//    one 1-D bulk copy (cp.async.bulk, TMA) into a LINEAR shared tile of the
+//    warp's own, completing on the warp's own mbarrier, so no instruction
+//    waits for more than one warp (no block barrier);
+//  * 20 outputs per lane put lane l's window 80 bytes after lane l-1's
 //    (5 x 16 B, odd), so the eight lanes of each 16-byte load phase hit
 //    eight different bank groups: conflict-free without any swizzle or
 //    padding, and every window load is base + a compile-time offset;
-//  * per chunk of 8 taps a thread issues eight 16-byte shared loads (the 27
+//  * per chunk of 8 taps a lane issues eight 16-byte shared loads (the 27
 //    samples its outputs need, aligned down) and two broadcast tap loads,
 //    then 20 x 8 FFMA with every operand in a register;
 //  * the window's alignment within a 16-byte chunk, (D - 7) mod 4, is the
-//    same for every block and chunk, so it is a template parameter;
-//  * the outputs are staged back into the same shared tile and leave by one
-//    1-D bulk store (cp.async.bulk shared -> global).
+//    same for every warp and chunk, so it is a template parameter;
+//  * the outputs leave from registers as 16-byte streaming stores.
+// Blocks hold 8 warps (2 for short signals, so that they spread over every SM).
 // At 127 taps the kernel is bound by FP32 FMA issue, not by HBM.
 #include <algorithm>
 #include <atomic>
@@ -73,19 +74,6 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
         : "memory");
 }
 
-__device__ __forceinline__ void bulk_store(void* dst, const void* src, uint32_t bytes) {
-    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst),
-                 "r"(smem_u32(src)), "r"(bytes)
-                 : "memory");
-    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-}
-
-// Waits until every bulk store of this thread has finished reading shared
-// memory (the CTA may then exit or reuse it).
-__device__ __forceinline__ void bulk_store_drain() {
-    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
-}
-
 // Loads the window of one chunk: wv[i] = w[i], i < 4*kWin4, w 16-byte aligned.
 __device__ __forceinline__ void load_window(const float* __restrict__ w, float (&wv)[4 * kWin4]) {
 #pragma unroll
@@ -132,119 +120,74 @@ __device__ __forceinline__ void fir_chunk_tail(const float* __restrict__ w, cons
         }
 }
 
-// Tile t = outputs [ob, ob + kTileOut), ob = kTileOut t. Its shared buffer holds
-// samples [A, A + tile) of x (x-index = j + halo for output j),
-// A = ob + halo - D, zero outside [0, x_len). Output ob + 20i + r at tap k
-// reads buffer index D + 20i + r - k, with D = taps + 6 + ((halo - taps - 6)
-// mod 4), so A is a multiple of 4 (16-byte aligned when x is) and the window
-// of the last, partial chunk (up to 7 taps past the end) stays inside.
-struct Span {
-    int64_t A, c0, c1;  // buffer origin; [c0, c1) arrives by bulk copy
-};
-template <int NT>
-__device__ __forceinline__ Span tile_span(int64_t t, const FirGeom& g, bool bulk_in) {
-    Span s;
-    s.A = t * tile_out(NT) + g.halo - g.D;
-    s.c0 = max(s.A, (int64_t)0);
-    const int64_t end = min(s.A + g.tile, g.x_len);
-    s.c1 = bulk_in && end > s.c0 ? s.c0 + ((end - s.c0) & ~int64_t(3)) : s.c0;
-    return s;
-}
+// Warp tile t = outputs [ob, ob + kWarpOut), ob = kWarpOut t. The warp's
+// shared tile holds samples [A, A + tile) of x (x-index = j + halo for
+// output j), A = ob + halo - D, zero outside [0, x_len). Output ob + 20 l + r
+// at tap k reads tile index D + 20 l + r - k, with D = taps + 6 + ((halo -
+// taps - 6) mod 4), so A is a multiple of 4 (16-byte aligned when x is) and
+// the window of the last, partial chunk (up to 7 taps past the end) stays
+// inside.
+constexpr int kWarpOut = 32 * kPerThread;
 
-// Each block walks tiles blockIdx.x, +gridDim.x, ... with two shared
-// buffers: with fewer blocks than tiles, tile i+1's signal span streams in
-// (one bulk copy, completing on that buffer's mbarrier) while tile i is
-// computed, and a buffer is refilled (tile i+2) once the bulk store of its
-// outputs has read it. The launch gives every tile its own block, which
-// measured faster on B200: four resident blocks per SM overlap one block's
-// load with the others' FMAs without the per-tile drain.
 template <int SH, int NT>
 __global__ void __launch_bounds__(NT, min_blocks(NT)) k_fir(float* __restrict__ y,
-                                                      const float* __restrict__ x,
-                                                      const float* __restrict__ h, FirGeom g,
-                                                      int64_t ntiles, bool bulk_in, bool bulk_out,
-                                                      uint32_t* wd) {
-    constexpr int kTileOut = tile_out(NT);
-    __shared__ __align__(8) uint64_t bars[2];
+                                                            const float* __restrict__ x,
+                                                            const float* __restrict__ h, FirGeom g,
+                                                            int64_t nwt, bool bulk_in,
+                                                            bool vec_out, uint32_t* wd) {
+    __shared__ __align__(8) uint64_t bars[NT / 32];
     extern __shared__ float4 dyn4[];
-    float* const buf0 = reinterpret_cast<float*>(dyn4);
-    float* const buf1 = buf0 + g.tile;
-    float* hs = buf1 + g.tile;
-    const int tid = threadIdx.x;
-
-    auto issue = [&](int64_t t, int b) {
-        const Span s = tile_span<NT>(t, g, bulk_in);
-        mbar_arrive_expect_tx(&bars[b], (uint32_t)((s.c1 - s.c0) * 4));
-        if (s.c1 > s.c0)
-            bulk_load((b ? buf1 : buf0) + (s.c0 - s.A), x + s.c0, (uint32_t)((s.c1 - s.c0) * 4),
-                      &bars[b]);
-    };
-    for (int k = tid; k < g.taps_pad; k += NT) hs[k] = k < g.taps ? h[k] : 0.0f;
-    if (bulk_in && tid == 0) {
-        mbar_init(&bars[0], 1);
-        mbar_init(&bars[1], 1);
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    const int64_t t = (int64_t)blockIdx.x * (NT / 32) + wid;
+    if (t >= nwt) return;
+    // The warp's region: its copy of the taps, then its signal tile.
+    float* const hs = reinterpret_cast<float*>(dyn4) + wid * (g.taps_pad + g.tile);
+    float* const tile = hs + g.taps_pad;
+    uint64_t* const bar = &bars[wid];
+    const int64_t A = t * kWarpOut + g.halo - g.D;
+    // [c0, c1) arrives by bulk copy; the lanes fill the rest: samples before
+    // x (zeros), and from c1 on (a ragged last 1-3 samples, zeros past x, or
+    // everything when x is not 16-byte aligned).
+    const int64_t c0 = max(A, (int64_t)0);
+    const int64_t end = min(A + g.tile, g.x_len);
+    const int64_t c1 = bulk_in && end > c0 ? c0 + ((end - c0) & ~int64_t(3)) : c0;
+    if (c1 > c0 && lane == 0) {
+        mbar_init(bar, 1);
         fence_mbar_init();
+        mbar_arrive_expect_tx(bar, (uint32_t)((c1 - c0) * 4));
+        bulk_load(tile + (c0 - A), x + c0, (uint32_t)((c1 - c0) * 4), bar);
     }
-    __syncthreads();
-    if (bulk_in && tid == 0)
-        for (int b = 0; b < 2; b++)
-            if (blockIdx.x + (int64_t)b * gridDim.x < ntiles) issue(blockIdx.x + (int64_t)b * gridDim.x, b);
+    for (int k = lane; k < g.taps_pad; k += 32) hs[k] = k < g.taps ? h[k] : 0.0f;
+    for (int64_t i = lane; i < c0 - A; i += 32) tile[i] = 0.0f;
+    for (int64_t i = (c1 - A) + lane; i < g.tile; i += 32) {
+        const int64_t p = A + i;
+        tile[i] = (p >= 0 && p < g.x_len) ? x[p] : 0.0f;
+    }
+    __syncwarp();  // the barrier's initialisation and the lanes' fills
+    // Gave up waiting (the watchdog is raised): nothing else is in flight.
+    if (c1 > c0 && !mbar_wait(bar, 0, wd)) return;
+    __syncwarp();
 
-    int it = 0;
-    for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x, it++) {
-        const int b = it & 1;
-        float* tile = b ? buf1 : buf0;
-        const Span s = tile_span<NT>(t, g, bulk_in);
-        // The threads fill what the bulk copy does not: samples before x
-        // (zeros), and from c1 on (a ragged last 1-3 samples, zeros past x,
-        // or everything when x is not 16-byte aligned).
-        for (int64_t i = tid; i < s.c0 - s.A; i += NT) tile[i] = 0.0f;
-        for (int64_t i = (s.c1 - s.A) + tid; i < g.tile; i += NT) {
-            const int64_t p = s.A + i;
-            tile[i] = (p >= 0 && p < g.x_len) ? x[p] : 0.0f;
-        }
-        if (bulk_in && !mbar_wait(&bars[b], (uint32_t)((it >> 1) & 1), wd)) {
-            // Gave up (the watchdog is raised): the other buffer's copy, if
-            // one is in flight, lands (bounded wait) before the block exits.
-            if (t + gridDim.x < ntiles) mbar_wait(&bars[b ^ 1], (uint32_t)(((it + 1) >> 1) & 1), wd);
-            return;
-        }
-        __syncthreads();
-
-        float acc[kPerThread];
+    float acc[kPerThread];
 #pragma unroll
-        for (int r = 0; r < kPerThread; r++) acc[r] = 0.0f;
-        // Window start at chunk k0: D - 7 - SH + 20 tid - k0 (a multiple of 4).
-        const float* w = tile + (g.D - 7 - SH) + kPerThread * tid;
-        int k0 = 0;
-        for (; k0 + kChunk <= g.taps; k0 += kChunk) fir_chunk<SH>(w - k0, hs + k0, acc);
-        if (k0 < g.taps) fir_chunk_tail<SH>(w - k0, hs + k0, g.taps - k0, acc);
+    for (int r = 0; r < kPerThread; r++) acc[r] = 0.0f;
+    // Window start at chunk k0: D - 7 - SH + 20 lane - k0 (a multiple of 4).
+    const float* w = tile + (g.D - 7 - SH) + kPerThread * lane;
+    int k0 = 0;
+    for (; k0 + kChunk <= g.taps; k0 += kChunk) fir_chunk<SH>(w - k0, hs + k0, acc);
+    if (k0 < g.taps) fir_chunk_tail<SH>(w - k0, hs + k0, g.taps - k0, acc);
 
-        __syncthreads();  // every window read of this buffer is done
-        float* o = tile + kPerThread * tid;
+    const int64_t ob = t * kWarpOut + kPerThread * lane;
+    if (vec_out && (t + 1) * kWarpOut <= g.y_len) {
 #pragma unroll
         for (int c = 0; c < kPerThread / 4; c++)
-            *reinterpret_cast<float4*>(o + 4 * c) =
-                make_float4(acc[4 * c], acc[4 * c + 1], acc[4 * c + 2], acc[4 * c + 3]);
-        const int64_t ob = t * kTileOut;
-        const bool whole = ob + kTileOut <= g.y_len;
-        fence_proxy_async_smem();  // this buffer's generic accesses, before async ones
-        __syncthreads();
-        if (bulk_out && whole) {
-            if (tid == 0) {
-                bulk_store(y + ob, tile, kTileOut * 4u);
-                bulk_store_drain();
-            }
-        } else {
-            const int64_t n = min((int64_t)kTileOut, g.y_len - ob);
-            for (int64_t i = tid; i < n; i += NT) y[ob + i] = tile[i];
-            fence_proxy_async_smem();
-            __syncthreads();
-        }
-        if (bulk_in && tid == 0 && t + 2 * (int64_t)gridDim.x < ntiles)
-            issue(t + 2 * (int64_t)gridDim.x, b);
+            st_stream_f4(y + ob + 4 * c,
+                         make_float4(acc[4 * c], acc[4 * c + 1], acc[4 * c + 2], acc[4 * c + 3]));
+    } else {
+#pragma unroll
+        for (int r = 0; r < kPerThread; r++)
+            if (ob + r < g.y_len) y[ob + r] = acc[r];
     }
-    if (bulk_out && tid == 0) bulk_store_drain();
 }
 
 using FirKernel = void (*)(float*, const float*, const float*, FirGeom, int64_t, bool, bool,
@@ -287,30 +230,26 @@ int launch_fir(const char* K, float* y, int64_t y_len, const float* x, int64_t x
     g.halo = halo;
     g.taps = taps;
     g.taps_pad = (int32_t)sg::ceil_div(std::max(taps, 1), kChunk) * kChunk;
-    // ob is a multiple of 4, so D (and with it SH) is the same for every block.
+    // ob is a multiple of 4, so D (and with it SH) is the same for every warp.
     const int64_t m = (((halo - taps - 6) % 4) + 4) % 4;
     g.D = (int32_t)(taps + 6 + m);
-    // The window loads of the last thread reach a few floats past the last
+    // The window loads of the last lane reach a few floats past the last
     // sample its outputs use (whole 16-byte loads): 8 floats of slack.
-    g.tile = (int32_t)sg::ceil_div(g.D + tile_out(nt) + 8, 4) * 4;
+    g.tile = (int32_t)sg::ceil_div(g.D + kWarpOut + 8, 4) * 4;
     const int sh = (g.D - 7) % 4;
 
     const FirKernel kern = narrow ? kFirKernels<kNarrow>[sh] : kFirKernels<kWide>[sh];
-    const size_t smem = (size_t)(2 * g.tile + g.taps_pad) * sizeof(float);
+    const size_t smem = (size_t)(nt / 32) * (g.tile + g.taps_pad) * sizeof(float);
     if (smem > (size_t)fir_dyn_max(d))
         return sg::fail(SIMTGO_ESIZE, "%s: %d taps need %zu bytes of shared memory", K, taps,
                         smem);
     if ((rc = fir_configure(d, (narrow ? 4 : 0) + sh, kern))) return rc;
-    const int64_t ntiles = sg::ceil_div(y_len, (int64_t)tile_out(nt));
-    // One tile per block measured faster than a persistent grid (the
-    // hardware starts the next block's load while this one computes), so
-    // the grid covers every tile; the loop in k_fir also serves a grid that
-    // does not.
-    if (ntiles > 0x7fffffffLL) return sg::fail(SIMTGO_ESIZE, "%s: y_len too large", K);
-    const int blocks = (int)ntiles;
+    const int64_t nwt = sg::ceil_div(y_len, (int64_t)kWarpOut);
+    const int64_t blocks = sg::ceil_div(nwt, (int64_t)(nt / 32));
+    if (blocks > 0x7fffffffLL) return sg::fail(SIMTGO_ESIZE, "%s: y_len too large", K);
     sg::before_launch();
-    kern<<<blocks, nt, smem, (cudaStream_t)stream>>>(
-        y, x, h, g, ntiles, sg::aligned16(x), sg::aligned16(y), sg::watchdog_device_ptr());
+    kern<<<(unsigned)blocks, nt, smem, (cudaStream_t)stream>>>(
+        y, x, h, g, nwt, sg::aligned16(x), sg::aligned16(y), sg::watchdog_device_ptr());
     return sg::launch_status(K);
 }
 
