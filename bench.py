@@ -618,9 +618,10 @@ def bench_histogram(args, torch, L, dev, sp, rank, world, barrier, max_over_rank
     bins = torch.zeros(256, dtype=torch.int32, device=dev)
     comm = make_comm(torch, L, dev, rank, world)
 
-    def run(fn):
+    def run(fn, zero=True):
         def step():
-            bins.zero_()
+            if zero:
+                bins.zero_()
             rc = fn(comm, P(bins.data_ptr()), 256, P(x.data_ptr()), n, sp)
             if rc:
                 _lib.check(rc)
@@ -632,10 +633,11 @@ def bench_histogram(args, torch, L, dev, sp, rank, world, barrier, max_over_rank
         return ms, int(bins.sum().item()) == total
 
     ms, ok = run(L.simtgo_Histogram_allreduce)
-    ms_f, ok_f = run(L.simtgo_Histogram_allreduce_fused)
-    # Where the fused step's time goes: the zeroing launch alone, and this
-    # rank's count alone (the local kernel, no exchange); the rest of the
-    # step is the exchange tail and the ranks' skew.
+    ms_f, ok_f = run(L.simtgo_Histogram_allreduce_fused_overwrite, zero=False)
+    # Where the steps' time goes: the zeroing launch alone (the NCCL step's
+    # first part), and this rank's count alone (the local kernel, no
+    # exchange); the rest of the fused step is the exchange tail and the
+    # ranks' skew.
     stream = torch.cuda.current_stream()
     barrier()
     ms_zero = max_over_ranks(timed(lambda: bins.zero_(), args.steps, args.warmup, stream, events))
@@ -657,14 +659,15 @@ def bench_histogram(args, torch, L, dev, sp, rank, world, barrier, max_over_rank
             "fused": {"ms_per_step": round(ms_f, 4),
                       "gsamples_per_s": round(total / (ms_f * 1e-3) / 1e9, 2),
                       "bins_sum_ok": ok_f,
-                      "step": "zero bins; one kernel: local histogram, then its last block "
-                              "stores the bins to every rank over NVLink and sums the "
-                              "ranks' slots (simtgo_Histogram_allreduce_fused)"},
+                      "step": "one kernel: local histogram, then its last block stores the "
+                              "counts to every rank over NVLink and sums the ranks' slots "
+                              "into bins (simtgo_Histogram_allreduce_fused_overwrite: no "
+                              "zeroing launch)"},
             "breakdown": {"zero_ms": round(ms_zero, 4), "local_count_ms": round(ms_count, 4),
-                          "exchange_and_skew_ms": round(ms_f - ms_zero - ms_count, 4),
+                          "fused_exchange_and_skew_ms": round(ms_f - ms_count, 4),
                           "samples_per_rank": n,
                           "how": "each part timed alone with CUDA events, max over ranks; the "
-                                 "exchange is the fused step less the other two"}}
+                                 "fused step's exchange is its time less the local count"}}
 
 
 def twelve(tile, g, a, b, c, h):
@@ -894,18 +897,38 @@ def bench_kernels(args, torch, np, L, dev, sp, events, peaks):
                                                       T // 16, 16, 16, sp), steps, warm, stream,
                            events), 8.0 * T * T, T * T, "elements")
     # FIR of the 2^20-sample, 31-tap case: 32 signals filtered in turn
-    # (256 MB), so each launch starts with its 8 MB out of L2.
+    # (256 MB), so each launch starts with its 8 MB out of L2. A launch is a
+    # few microseconds, less than a host-side call from Python, so the 32
+    # launches are captured once in a CUDA graph and the graph is replayed:
+    # the time is the device's, per launch.
     n20 = 1 << 20
     h31 = torch.rand(31, device=dev, generator=gen)
     h31 /= h31.sum()
     sig = [(torch.empty(n20, device=dev), torch.randn(n20, device=dev, generator=gen))
            for _ in range(32)]
-    rec("FIR_31taps_2^20", timed(in_turn([
-        (lambda y=y, x=x: L.simtgo_FIR(P(y.data_ptr()), n20, P(x.data_ptr()), n20,
-                                       P(h31.data_ptr()), 31, n20 // 256, 256, sp))
-        for y, x in sig]), steps, warm, stream, events), 8.0 * n20, n20,
-        "outputs (32 signals in turn, 256 MB: inputs larger than L2, no flush)")
-    del sig
+
+    def fir20(y, x, s):
+        rc = L.simtgo_FIR(P(y.data_ptr()), n20, P(x.data_ptr()), n20, P(h31.data_ptr()), 31,
+                          n20 // 256, 256, P(s))
+        if rc:
+            from simtgo_b200 import _lib
+            _lib.check(rc)
+
+    for y, x in sig:
+        fir20(y, x, stream.cuda_stream)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    cap = torch.cuda.Stream(dev)
+    cap.wait_stream(stream)
+    with torch.cuda.graph(graph, stream=cap, capture_error_mode="thread_local"):
+        for y, x in sig:
+            fir20(y, x, cap.cuda_stream)
+    torch.cuda.synchronize()
+    rec("FIR_31taps_2^20", timed(graph.replay, max(3, steps // 4), 2, stream, events) / len(sig),
+        8.0 * n20, n20,
+        "outputs (32 signals in turn, 256 MB: inputs larger than L2, no flush; the 32 "
+        "launches replayed as one CUDA graph, time per launch)")
+    del graph, sig
     return out
 
 

@@ -248,6 +248,14 @@ int simtgo_Histogram_allreduce(simtgo_comm* comm, int32_t* bins, int32_t bins_le
  * as SIMTGO_EDEVICE. */
 int simtgo_Histogram_allreduce_fused(simtgo_comm* comm, int32_t* bins, int32_t bins_len,
                                      const int32_t* x, int64_t x_len, void* stream);
+/* No counterpart in the reference (which adds into bins, as the entry above
+ * does): the same exchange with the incoming bins read as zero, so that
+ * every rank ends with the counts of the whole input without zeroing bins
+ * first -- the zeroing launch of a repeated sharded histogram folded into
+ * the kernel. Same limits, collective order and bounded wait. */
+int simtgo_Histogram_allreduce_fused_overwrite(simtgo_comm* comm, int32_t* bins,
+                                               int32_t bins_len, const int32_t* x, int64_t x_len,
+                                               void* stream);
 
 /* ---- the tile track (package tile) -------------------------------------- */
 

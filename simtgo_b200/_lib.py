@@ -65,6 +65,7 @@ _SIGS = {
     "simtgo_comm_allreduce_i32": [_vp, _vp, _i32, _vp],
     "simtgo_Histogram_allreduce": [_vp, _vp, _i32, _vp, _i64, _vp],
     "simtgo_Histogram_allreduce_fused": [_vp, _vp, _i32, _vp, _i64, _vp],
+    "simtgo_Histogram_allreduce_fused_overwrite": [_vp, _vp, _i32, _vp, _i64, _vp],
     "simtgo_tile_new": [],
     "simtgo_tile_free": [_vp],
     "simtgo_tile_input": [_vp, _vp, _i32],

@@ -96,7 +96,7 @@ __host__ __device__ constexpr size_t p2p_flags_offset(int nranks) {
 __global__ void __launch_bounds__(kHistThreads) k_hist_allreduce(
     int* __restrict__ bins, int bins_len, const int* __restrict__ x, int64_t m, bool vec,
     int* part, char* const* __restrict__ peers, char* mine, int rank, int nranks, uint32_t epoch,
-    uint32_t* wd) {
+    bool overwrite, uint32_t* wd) {
     __shared__ int sh[kHistWarps][kHistBins];
     __shared__ int last, failed;
     for (int k = threadIdx.x; k < kHistWarps * kHistBins; k += blockDim.x) (&sh[0][0])[k] = 0;
@@ -123,10 +123,10 @@ __global__ void __launch_bounds__(kHistThreads) k_hist_allreduce(
     if (!last) return;
     __threadfence();
     const int par = (int)(epoch & 1u);
-    // This rank's bins (the caller's plus its counts) into its slot on
-    // every rank, over NVLink for the peers.
+    // This rank's bins (the caller's plus its counts, or with overwrite its
+    // counts alone) into its slot on every rank, over NVLink for the peers.
     for (int k = threadIdx.x; k < bins_len; k += blockDim.x) {
-        const int v = bins[k] + (k < kHistBins ? __ldcg(part + k) : 0);
+        const int v = (overwrite ? 0 : bins[k]) + (k < kHistBins ? __ldcg(part + k) : 0);
         for (int r = 0; r < nranks; r++)
             reinterpret_cast<int*>(peers[r])[((size_t)par * nranks + rank) * kP2PCap + k] = v;
     }
@@ -319,9 +319,12 @@ int simtgo_Histogram_allreduce(simtgo_comm* comm, int32_t* bins, int32_t bins_le
     return simtgo_comm_allreduce_i32(comm, bins, bins_len, stream);
 }
 
-int simtgo_Histogram_allreduce_fused(simtgo_comm* comm, int32_t* bins, int32_t bins_len,
-                                     const int32_t* x, int64_t x_len, void* stream) {
-    const char* K = "Histogram_allreduce_fused";
+}  // extern "C"
+
+namespace {
+
+int hist_allreduce_fused(const char* K, simtgo_comm* comm, int32_t* bins, int32_t bins_len,
+                         const int32_t* x, int64_t x_len, bool overwrite, void* stream) {
     sg::clear_error();
     int rc;
     if (!comm) return sg::fail(SIMTGO_ECOMM, "%s: null communicator", K);
@@ -347,8 +350,25 @@ int simtgo_Histogram_allreduce_fused(simtgo_comm* comm, int32_t* bins, int32_t b
     sg::before_launch();
     k_hist_allreduce<<<blocks, kHistThreads, 0, s>>>(
         bins, bins_len, x, x_len, sg::aligned16(x), comm->part, comm->d_peer, comm->xb,
-        comm->rank, comm->nranks, comm->epoch, sg::watchdog_device_ptr());
+        comm->rank, comm->nranks, comm->epoch, overwrite, sg::watchdog_device_ptr());
     return sg::launch_status(K);
+}
+
+}  // namespace
+
+extern "C" {
+
+int simtgo_Histogram_allreduce_fused(simtgo_comm* comm, int32_t* bins, int32_t bins_len,
+                                     const int32_t* x, int64_t x_len, void* stream) {
+    return hist_allreduce_fused("Histogram_allreduce_fused", comm, bins, bins_len, x, x_len,
+                                false, stream);
+}
+
+int simtgo_Histogram_allreduce_fused_overwrite(simtgo_comm* comm, int32_t* bins,
+                                               int32_t bins_len, const int32_t* x, int64_t x_len,
+                                               void* stream) {
+    return hist_allreduce_fused("Histogram_allreduce_fused_overwrite", comm, bins, bins_len, x,
+                                x_len, true, stream);
 }
 
 }  // extern "C"

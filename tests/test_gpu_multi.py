@@ -56,6 +56,13 @@ def _child(rank, uid, mode, q, bar):
                                                 xs.numel(), None))
                     _lib.check(L.simtgo_stream_sync(None))
                     out[(name, call)] = b.cpu().numpy()
+            # The overwrite form: the starting values are ignored.
+            for call in range(3):
+                b = t.full((300,), 1000 + rank + call, dtype=t.int32, device="cuda")
+                _lib.check(L.simtgo_Histogram_allreduce_fused_overwrite(
+                    comm, P(b.data_ptr()), 300, P(xs.data_ptr()), xs.numel(), None))
+                _lib.check(L.simtgo_stream_sync(None))
+                out[("overwrite", call)] = b.cpu().numpy()
         elif mode == "reduce":  # the tile reductions over shards with a halo
             from simtgo_b200 import tile
 
@@ -139,6 +146,10 @@ def test_fused_and_nccl_agree_with_the_whole():
             for name in ("simtgo_Histogram_allreduce", "simtgo_Histogram_allreduce_fused"):
                 np.testing.assert_array_equal(res[rank][(name, call)], want.astype(np.int32),
                                               err_msg=f"{name} call {call} rank {rank}")
+            over = np.zeros(300, np.int64)
+            over[:256] = counts
+            np.testing.assert_array_equal(res[rank][("overwrite", call)], over.astype(np.int32),
+                                          err_msg=f"overwrite call {call} rank {rank}")
 
 
 def test_absent_rank_times_out_with_a_status():

@@ -190,6 +190,13 @@ def test_histogram_allreduce_fused_single_rank(bins_len):
                                                           P(xd.data_ptr()), n, None))
             _lib.check(L.simtgo_stream_sync(None))
             assert_equal(f"call {call}", b.cpu().numpy(), want)
+            # The overwrite form counts into bins whatever they held.
+            b = torch.from_numpy(bins0).cuda()
+            _lib.check(L.simtgo_Histogram_allreduce_fused_overwrite(
+                comm, P(b.data_ptr()), bins_len, P(xd.data_ptr()), n, None))
+            _lib.check(L.simtgo_stream_sync(None))
+            rc, fresh = O.histogram_shard(x, bins_len)
+            assert_equal(f"overwrite call {call}", b.cpu().numpy(), fresh)
         big = torch.zeros(4097, dtype=torch.int32, device="cuda")
         assert L.simtgo_Histogram_allreduce_fused(comm, P(big.data_ptr()), 4097,
                                                   P(xd.data_ptr()), n, None) == _lib.ESIZE
