@@ -68,6 +68,36 @@ __device__ __forceinline__ float hypot_go(float x, float y) {
     return __double2float_rn(g1);
 }
 
+// Four gpu.Hypot values at once, bit for bit as hypot_go: the fast path of
+// all four first, with no branch between them, so that their float64 chains
+// interleave (one value's chain is about nine dependent float64 steps), then
+// hypot_go_exact for the rare values the fast path cannot decide.
+__device__ __forceinline__ float4 hypot_go4(float4 x, float4 y) {
+    const float xs[4] = {x.x, x.y, x.z, x.w}, ys[4] = {y.x, y.y, y.z, y.w};
+    float r[4];
+    bool slow[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const float p = fmaxf(fabsf(xs[i]), fabsf(ys[i]));
+        const double dx = (double)xs[i], dy = (double)ys[i];
+        const double s = fma(dx, dx, __dmul_rn(dy, dy));
+        const double r0 = (double)rsqrtf(__double2float_rn(s));
+        const double g0 = __dmul_rn(s, r0);
+        const double g1 = fma(0.5 * r0, fma(-g0, g0, s), g0);
+        const int32_t low =
+            (int32_t)((unsigned long long)__double_as_longlong(g1) & 0x1fffffffull) - 0x10000000;
+        // NaN fails both range comparisons.
+        slow[i] = !(p >= 0x1p-60f && p <= 0x1p60f) || (low >= -4096 && low <= 4096);
+        r[i] = __double2float_rn(g1);
+    }
+    if (slow[0] || slow[1] || slow[2] || slow[3]) {
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+            if (slow[i]) r[i] = hypot_go_exact(xs[i], ys[i]);
+    }
+    return make_float4(r[0], r[1], r[2], r[3]);
+}
+
 // kernels/softclip.go:11-23.
 __device__ __forceinline__ float softclip_go(float v, float t) {
     const float a = fabsf(v);

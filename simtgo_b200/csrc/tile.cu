@@ -505,9 +505,9 @@ int lower(const simtgo_tile_graph* g, int root, Lowered& L, int32_t reduce = til
 }
 
 // Float4 offset of window f's tile among the tiles.
-int32_t tile_off4(const Lowered& L, int f) {
+int32_t tile_off4(const Lowered& L, int f, int chunk) {
     int32_t off = 0;
-    for (int i = 0; i < f; i++) off += tilek::tile_floats(L.head[i]) / 4;
+    for (int i = 0; i < f; i++) off += tilek::tile_floats(L.head[i], chunk) / 4;
     return off;
 }
 
@@ -532,7 +532,7 @@ void build_program(const simtgo_tile_graph* g, const Lowered& L, const Layout& Y
         P.fir[f].start = L.fir_start[f];
         P.fir[f].taps = (int32_t)h.size() | (L.sync_after[f] ? tilek::kSyncAfter : 0);
         P.fir[f].head = L.head[f];
-        P.fir[f].tile4 = Y.tiles4 + tile_off4(L, f);
+        P.fir[f].tile4 = Y.tiles4 + tile_off4(L, f, tilek::chunk_of(Y.g));
         for (size_t k = 0; k < h.size(); k++) P.fir[f].h[k] = h[k];
     }
     // A lowered operand's address: inputs relative to the run's stage
@@ -598,14 +598,29 @@ int launch_program(const simtgo_tile_graph* g, const Lowered& L,
     int32_t hs = 0;
     for (int f = 0; f < n_fir; f++) hs = std::max<int32_t>(hs, L.head[f]);
     Layout Y;
-    // Four groups per thread for graphs without windows or Hypot.
+    // Four groups per thread (4096-element chunks: each dispatch and each
+    // chunk's pipeline spread over twice the elements) for graphs without
+    // Hypot (its float64 registers make it slower there) whose four-group
+    // layout, with two input stages, still leaves room for two blocks per
+    // SM; two groups otherwise. A 31-tap window over one input measured
+    // 1.00 -> 0.85 ms at 2^28; three inputs and a window fit one block per
+    // SM with four groups, and ran 1.5 times slower.
     bool hypot = false;
     for (const FInsn& fi : L.code) hypot = hypot || fi.op == tilek::OP_HYPOT;
-    Y.g = n_fir == 0 && !hypot ? tilek::kGWide : tilek::kG;
+    auto smem_for = [&](int g) {
+        const int ch = tilek::chunk_of(g);
+        const size_t fixed = (size_t)tilek::meta_bytes((int)L.code.size(), n_in, n_fir) +
+                             (size_t)n_fir * tilek::kMaxTaps * 4 + (size_t)tile_off4(L, n_fir, ch) * 16 +
+                             (size_t)L.n_tmp * ch * 4;
+        return fixed + 2 * (size_t)n_in * (hs + ch) * sizeof(float);
+    };
+    Y.g = !hypot && (n_fir == 0 || smem_for(tilek::kGWide) <= (size_t)d->smem_per_sm / 2 - 2048)
+              ? tilek::kGWide
+              : tilek::kG;
     const int chunk = tilek::chunk_of(Y.g);
     Y.taps4 = tilek::meta_bytes((int)L.code.size(), n_in, n_fir) / 16;
     Y.tiles4 = Y.taps4 + n_fir * tilek::kMaxTaps / 4;
-    Y.temps4 = Y.tiles4 + tile_off4(L, n_fir);
+    Y.temps4 = Y.tiles4 + tile_off4(L, n_fir, chunk);
     Y.stages4 = Y.temps4 + L.n_tmp * chunk / 4;
     Y.sstride = hs + chunk;
     const size_t base_smem = (size_t)Y.stages4 * 16;

@@ -16,15 +16,17 @@ using namespace sgd;
 namespace tilek {
 
 constexpr int kThreads = 256;
-// Float4 groups per thread (the template parameter G): 2 for graphs with
-// windows or Hypot, 4 (kGWide) for the others, whose dispatch and chunk
-// costs then spread over twice the elements (eight chained Muls measured
-// 0.57 -> 0.76 of HBM; Hypot's registers make it slower there).
+// Float4 groups per thread (the template parameter G): 4 (kGWide) for
+// graphs without Hypot whose layout still fits two blocks per SM, whose
+// dispatch and chunk costs then spread over twice the elements (eight
+// chained Muls measured 0.57 -> 0.76 of HBM); 2 otherwise (Hypot's
+// registers make it slower with four; windows over several inputs need
+// too much shared memory). A window's tile holds one chunk of either size.
 constexpr int kG = 2;
 constexpr int kGWide = 4;
 __host__ __device__ constexpr int chunk_of(int G) { return kThreads * 4 * G; }
-// 2048: the chunk of G = 2 (every window's tile is laid out for it) and the
-// block of the reduction trees, whatever G the interpreter runs with.
+// 2048: the chunk of G = 2 and the block of the reduction trees, whatever G
+// the interpreter runs with.
 constexpr int kChunk = chunk_of(kG);
 constexpr int kChunk4 = kChunk / 4;
 constexpr int kMaxCode = 1024;
@@ -36,7 +38,7 @@ constexpr int kMaxTaps = SIMTGO_TILE_MAX_TAPS;
 // plus 4 of slack so that the first 16-byte window load stays in the tile.
 __host__ __device__ constexpr int window_reach(int taps) { return (taps - 1 + 3) / 4 * 4 + 4; }
 // Staged floats of a window's tile: its head, the chunk and 4 of slack.
-__host__ __device__ constexpr int tile_floats(int head) { return kChunk + head + 4; }
+__host__ __device__ constexpr int tile_floats(int head, int chunk = kChunk) { return chunk + head + 4; }
 constexpr int kMaxStages = 16;
 // FirDesc.taps flag: a later window's staging reads this window's tile, so
 // the block synchronises after staging it (chained windows).
@@ -156,10 +158,7 @@ __device__ __forceinline__ float4 f4_sqrt(float4 a) {
 __device__ __forceinline__ float4 f4_abs(float4 a) {
     return make_float4(fabsf(a.x), fabsf(a.y), fabsf(a.z), fabsf(a.w));
 }
-__device__ __forceinline__ float4 f4_hypot(float4 a, float4 b) {
-    return make_float4(hypot_go(a.x, b.x), hypot_go(a.y, b.y), hypot_go(a.z, b.z),
-                       hypot_go(a.w, b.w));
-}
+__device__ __forceinline__ float4 f4_hypot(float4 a, float4 b) { return hypot_go4(a, b); }
 __device__ __forceinline__ float f4_get(const float4& v, int j) {
     return j == 0 ? v.x : j == 1 ? v.y : j == 2 ? v.z : v.w;
 }
