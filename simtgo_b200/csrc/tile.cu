@@ -599,12 +599,14 @@ int launch_program(const simtgo_tile_graph* g, const Lowered& L,
     for (int f = 0; f < n_fir; f++) hs = std::max<int32_t>(hs, L.head[f]);
     Layout Y;
     // Four groups per thread (4096-element chunks: each dispatch and each
-    // chunk's pipeline spread over twice the elements) for graphs without
-    // Hypot (its float64 registers make it slower there) whose four-group
-    // layout, with two input stages, still leaves room for two blocks per
-    // SM; two groups otherwise. A 31-tap window over one input measured
-    // 1.00 -> 0.85 ms at 2^28; three inputs and a window fit one block per
-    // SM with four groups, and ran 1.5 times slower.
+    // chunk's pipeline spread over twice the elements) whenever the
+    // four-group layout with one input stage leaves room for two blocks per
+    // SM; two groups otherwise. A graph with windows may then run with a
+    // single stage per block: its next chunk's inputs stream in while the
+    // SM's other block computes (measured at 2^28: the twelve-node graph
+    // 1.82 -> 1.71 ms, a 31-tap window over one input 1.00 -> 0.85 ms; with
+    // two stages required, three inputs and a window fit one block per SM
+    // and ran 2.90 ms).
     bool hypot = false;
     for (const FInsn& fi : L.code) hypot = hypot || fi.op == tilek::OP_HYPOT;
     auto smem_for = [&](int g) {
@@ -612,11 +614,12 @@ int launch_program(const simtgo_tile_graph* g, const Lowered& L,
         const size_t fixed = (size_t)tilek::meta_bytes((int)L.code.size(), n_in, n_fir) +
                              (size_t)n_fir * tilek::kMaxTaps * 4 + (size_t)tile_off4(L, n_fir, ch) * 16 +
                              (size_t)L.n_tmp * ch * 4;
-        return fixed + 2 * (size_t)n_in * (hs + ch) * sizeof(float);
+        return fixed + 1 * (size_t)n_in * (hs + ch) * sizeof(float);
     };
-    Y.g = !hypot && (n_fir == 0 || smem_for(tilek::kGWide) <= (size_t)d->smem_per_sm / 2 - 2048)
+    Y.g = (n_fir == 0 || smem_for(tilek::kGWide) <= (size_t)d->smem_per_sm / 2 - 2048)
               ? tilek::kGWide
               : tilek::kG;
+    const int min_st = Y.g == tilek::kGWide && n_fir > 0 ? 1 : 2;  // input stages per block
     const int chunk = tilek::chunk_of(Y.g);
     Y.taps4 = tilek::meta_bytes((int)L.code.size(), n_in, n_fir) / 16;
     Y.tiles4 = Y.taps4 + n_fir * tilek::kMaxTaps / 4;
@@ -664,8 +667,8 @@ int launch_program(const simtgo_tile_graph* g, const Lowered& L,
                 std::min<int64_t>(dyn_max, d->smem_per_sm / per_sm - 2048);
             const int64_t fit = (share - (int64_t)base_smem) / (int64_t)stage_bytes;
             const int nst = (int)std::min<int64_t>(fit, tilek::kMaxStages);
-            if (nst < 2) continue;
-            const int64_t inflight = (int64_t)per_sm * (nst - 1) * (int64_t)stage_bytes;
+            if (nst < min_st) continue;
+            const int64_t inflight = (int64_t)per_sm * std::max(1, nst - 1) * (int64_t)stage_bytes;
             if (inflight > best_inflight) {
                 best_inflight = inflight;
                 Y.nst = nst;
@@ -675,7 +678,7 @@ int launch_program(const simtgo_tile_graph* g, const Lowered& L,
                 break;
             }
         }
-        bulk = Y.nst >= 2;
+        bulk = Y.nst >= min_st;
     }
     Y.smem = bulk ? base_smem + Y.nst * stage_bytes : base_smem;
     if (Y.smem > (size_t)dyn_max)

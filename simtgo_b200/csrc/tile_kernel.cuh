@@ -17,11 +17,10 @@ namespace tilek {
 
 constexpr int kThreads = 256;
 // Float4 groups per thread (the template parameter G): 4 (kGWide) for
-// graphs without Hypot whose layout still fits two blocks per SM, whose
+// graphs whose four-group layout still fits two blocks per SM, whose
 // dispatch and chunk costs then spread over twice the elements (eight
-// chained Muls measured 0.57 -> 0.76 of HBM); 2 otherwise (Hypot's
-// registers make it slower with four; windows over several inputs need
-// too much shared memory). A window's tile holds one chunk of either size.
+// chained Muls measured 0.57 -> 0.76 of HBM); 2 otherwise. A window's tile
+// holds one chunk of either size.
 constexpr int kG = 2;
 constexpr int kGWide = 4;
 __host__ __device__ constexpr int chunk_of(int G) { return kThreads * 4 * G; }
@@ -875,8 +874,10 @@ __device__ __forceinline__ ChunkSpan chunk_span(int64_t cb, int hs, int64_t n, i
 //
 // Bulk-copy mode (BULK): the chunk's inputs travel HBM -> shared memory by
 // cp.async.bulk, one copy per input, in `nst` stages that complete on
-// per-stage mbarriers, so nst-1 chunks stream in while one is interpreted.
-// Requires every input 16-byte aligned and halo = 0 mod 4. Otherwise
+// per-stage mbarriers, so nst-1 chunks stream in while one is interpreted
+// (with nst = 1, a four-group window graph's, the next chunk streams in
+// while the SM's other block computes). Requires every input 16-byte
+// aligned and halo = 0 mod 4. Otherwise
 // (DIRECT) the interpreter reads input operands from HBM itself.
 //
 // A reduction (P.reduce) writes no output array: each warp's values of
