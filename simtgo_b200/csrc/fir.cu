@@ -42,23 +42,31 @@ using namespace sgd;
 namespace {
 
 // Threads per block: kWide for long signals, kNarrow for signals with
-// fewer than four waves of wide tiles (a 2^20-sample signal is 205 wide
-// tiles on 148 SMs, but 820 narrow ones). Both are sized for a 64-register
-// budget: 4 wide or 16 narrow blocks per SM.
+// fewer than four waves of wide blocks (a 2^20-sample signal fills 205 wide
+// blocks of 5120 outputs on 148 SMs, but 1366 narrow ones of 768). Both
+// are sized for a 64-register budget: 4 wide or 16 narrow blocks per SM.
 constexpr int kWide = 256;
 constexpr int kNarrow = 64;
 __host__ __device__ constexpr int min_blocks(int nt) { return 1024 / nt; }
-// Outputs per thread: lane windows are 4*kPerThread bytes apart, so
-// kPerThread/4 must be odd for the 8 lanes of a 16-byte load phase to hit 8
-// different bank groups. 20 (with 4 blocks per SM) measured fastest of
+// Outputs per lane (KPT): lane windows are 4*KPT bytes apart, so KPT/4 must
+// be odd for the 8 lanes of a 16-byte load phase to hit 8 different bank
+// groups. 20 for long signals (with 4 blocks per SM it measured fastest of
 // 20/28/36/44: the FFMA rate depends on how the accumulators and the window
-// share the register file, not only on reuse.
-constexpr int kPerThread = 20;
-static_assert(kPerThread % 4 == 0 && (kPerThread / 4) % 2 == 1, "lane stride must be odd x 16 B");
-__host__ __device__ constexpr int tile_out(int nt) { return nt * kPerThread; }  // outputs per tile
-constexpr int kChunk = 8;                        // taps per register chunk
-constexpr int kWin4 = (kPerThread + 10 + 3) / 4;  // window float4s: kPerThread + 7 + SH floats
-static_assert(kWin4 == 8, "the register ring holds the eight float4s of a chunk's window");
+// share the register file, not only on reuse); 12 for signals under one
+// wave of wide blocks, whose launches are too short for their warps'
+// load-compute-store chains to overlap: more, shorter chains (a 2^20-sample,
+// 31-tap launch 4.50 -> 4.07 us; at 2^22 samples 20 per lane stays ahead).
+constexpr int kKptLong = 20;
+constexpr int kKptShort = 12;
+__host__ __device__ constexpr bool kpt_ok(int kpt) { return kpt % 4 == 0 && (kpt / 4) % 2 == 1; }
+static_assert(kpt_ok(kKptLong) && kpt_ok(kKptShort), "lane stride must be odd x 16 B");
+constexpr int kChunk = 8;  // taps per register chunk
+// A chunk's window, KPT + 7 + SH floats, in float4s: the register ring's size.
+__host__ __device__ constexpr int ring_of(int kpt) { return (kpt + 10 + 3) / 4; }
+static_assert(ring_of(kKptLong) == 8 && ring_of(kKptShort) == 6, "ring sizes");
+// Ring slot of window float4 q (q may be negative).
+__host__ __device__ constexpr int ring_slot(int q, int ring) { return ((q % ring) + ring) % ring; }
+__host__ __device__ constexpr int tile_out(int nt) { return nt * kKptLong; }  // outputs per wide block
 
 struct FirGeom {
     int64_t y_len;   // outputs of this launch
@@ -82,30 +90,31 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
 // NC whole chunks (8 NC taps), and with TAIL a last chunk of nk < 8 taps,
 // from one register window: chunk c's window float4 i is w4[i - 2c] (w4 = w
 // as float4, the window of chunk 0; output r at tap u of a chunk reads its
-// float SH + 7 + r - u), kept in ring slot (i - 2c) & 7, so each chunk after
-// the first loads only its two new float4s.
-template <int SH, int NC, bool TAIL = false>
+// float SH + 7 + r - u), kept in ring slot (i - 2c) mod RING, so each chunk
+// after the first loads only its two new float4s.
+template <int SH, int NC, bool TAIL, int KPT>
 __device__ __forceinline__ void fir_ring(const float* __restrict__ w, const float* hs,
-                                         float (&acc)[kPerThread], int nk = 0) {
+                                         float (&acc)[KPT], int nk = 0) {
+    constexpr int RING = ring_of(KPT);
     const float4* w4 = reinterpret_cast<const float4*>(w);
-    float4 R[8];
+    float4 R[RING];
 #pragma unroll
-    for (int q = 0; q < 8; q++) R[q] = w4[q];
+    for (int q = 0; q < RING; q++) R[q] = w4[q];
 #pragma unroll
     for (int c = 0; c < NC; c++) {
         if (c > 0) {
-            R[(16 - 2 * c) & 7] = w4[-2 * c];
-            R[(17 - 2 * c) & 7] = w4[1 - 2 * c];
+            R[ring_slot(-2 * c, RING)] = w4[-2 * c];
+            R[ring_slot(1 - 2 * c, RING)] = w4[1 - 2 * c];
         }
         const float4 ha = *reinterpret_cast<const float4*>(hs + 8 * c);
         const float4 hb = *reinterpret_cast<const float4*>(hs + 8 * c + 4);
         const float hv[kChunk] = {ha.x, ha.y, ha.z, ha.w, hb.x, hb.y, hb.z, hb.w};
 #pragma unroll
-        for (int r = 0; r < kPerThread; r++)
+        for (int r = 0; r < KPT; r++)
 #pragma unroll
             for (int u = 0; u < kChunk; u++) {
                 const int j = SH + 7 + r - u;
-                const float4& q = R[((j >> 2) - 2 * c + 16) & 7];
+                const float4& q = R[ring_slot((j >> 2) - 2 * c, RING)];
                 const float s = (j & 3) == 0 ? q.x : (j & 3) == 1 ? q.y : (j & 3) == 2 ? q.z : q.w;
                 acc[r] = __fmaf_rn(hv[u], s, acc[r]);
             }
@@ -113,8 +122,8 @@ __device__ __forceinline__ void fir_ring(const float* __restrict__ w, const floa
     if (TAIL) {  // chunk NC, with nk < 8 taps (the taps past them are zero padding)
         constexpr int c = NC;
         if (c > 0) {
-            R[(16 - 2 * c) & 7] = w4[-2 * c];
-            R[(17 - 2 * c) & 7] = w4[1 - 2 * c];
+            R[ring_slot(-2 * c, RING)] = w4[-2 * c];
+            R[ring_slot(1 - 2 * c, RING)] = w4[1 - 2 * c];
         }
         const float4 ha = *reinterpret_cast<const float4*>(hs + 8 * c);
         const float4 hb = *reinterpret_cast<const float4*>(hs + 8 * c + 4);
@@ -123,9 +132,9 @@ __device__ __forceinline__ void fir_ring(const float* __restrict__ w, const floa
         for (int u = 0; u < kChunk - 1; u++)
             if (u < nk) {
 #pragma unroll
-                for (int r = 0; r < kPerThread; r++) {
+                for (int r = 0; r < KPT; r++) {
                     const int j = SH + 7 + r - u;
-                    const float4& q = R[((j >> 2) - 2 * c + 16) & 7];
+                    const float4& q = R[ring_slot((j >> 2) - 2 * c, RING)];
                     const float s = (j & 3) == 0 ? q.x : (j & 3) == 1 ? q.y : (j & 3) == 2 ? q.z : q.w;
                     acc[r] = __fmaf_rn(hv[u], s, acc[r]);
                 }
@@ -133,25 +142,28 @@ __device__ __forceinline__ void fir_ring(const float* __restrict__ w, const floa
     }
 }
 
-// Warp tile t = outputs [ob, ob + kWarpOut), ob = kWarpOut t. The warp's
-// shared tile holds samples [A, A + tile) of x (x-index = j + halo for
-// output j), A = ob + halo - D, zero outside [0, x_len). Output ob + 20 l + r
-// at tap k reads tile index D + 20 l + r - k, with D = taps + 6 + ((halo -
-// taps - 6) mod 4), so A is a multiple of 4 (16-byte aligned when x is) and
-// the window of the last, partial chunk (up to 7 taps past the end) stays
-// inside.
-constexpr int kWarpOut = 32 * kPerThread;
+// Warp tile t = outputs [ob, ob + 32 KPT), ob = 32 KPT t. The warp's shared
+// tile holds samples [A, A + tile) of x (x-index = j + halo for output j),
+// A = ob + halo - D, zero outside [0, x_len). Output ob + KPT l + r at tap k
+// reads tile index D + KPT l + r - k, with D = taps + 6 + ((halo - taps - 6)
+// mod 4), so A is a multiple of 4 (16-byte aligned when x is) and the window
+// of the last, partial chunk (up to 7 taps past the end) stays inside.
+__host__ __device__ constexpr int warp_out(int kpt) { return 32 * kpt; }
 
-template <int SH, int NT>
+template <int SH, int NT, int KPT>
 __global__ void __launch_bounds__(NT, min_blocks(NT)) k_fir(float* __restrict__ y,
                                                             const float* __restrict__ x,
                                                             const float* __restrict__ h, FirGeom g,
                                                             int64_t nwt, bool bulk_in,
                                                             bool vec_out, uint32_t* wd) {
+    constexpr int kWarpOut = warp_out(KPT);
     __shared__ __align__(8) uint64_t bars[NT / 32];
     extern __shared__ float4 dyn4[];
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     const int64_t t = (int64_t)blockIdx.x * (NT / 32) + wid;
+    // Programmatic dependent launch: wait for the grids this one depends on
+    // (their writes visible) before touching memory.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     if (t >= nwt) return;
     // The warp's region: its copy of the taps, then its signal tile.
     float* const hs = reinterpret_cast<float*>(dyn4) + wid * (g.taps_pad + g.tile);
@@ -181,39 +193,45 @@ __global__ void __launch_bounds__(NT, min_blocks(NT)) k_fir(float* __restrict__ 
     if (c1 > c0 && !mbar_wait(bar, 0, wd)) return;
     __syncwarp();
 
-    float acc[kPerThread];
+    float acc[KPT];
 #pragma unroll
-    for (int r = 0; r < kPerThread; r++) acc[r] = 0.0f;
-    // Window start at chunk k0: D - 7 - SH + 20 lane - k0 (a multiple of 4).
-    const float* w = tile + (g.D - 7 - SH) + kPerThread * lane;
+    for (int r = 0; r < KPT; r++) acc[r] = 0.0f;
+    // Window start at chunk k0: D - 7 - SH + KPT lane - k0 (a multiple of 4).
+    const float* w = tile + (g.D - 7 - SH) + KPT * lane;
     int k0 = 0;
-    for (; k0 + 4 * kChunk <= g.taps; k0 += 4 * kChunk) fir_ring<SH, 4>(w - k0, hs + k0, acc);
+    for (; k0 + 4 * kChunk <= g.taps; k0 += 4 * kChunk)
+        fir_ring<SH, 4, false, KPT>(w - k0, hs + k0, acc);
     const int nk = (g.taps - k0) % kChunk;
     if (nk) {
         switch ((g.taps - k0) / kChunk) {
-            case 3: fir_ring<SH, 3, true>(w - k0, hs + k0, acc, nk); break;
-            case 2: fir_ring<SH, 2, true>(w - k0, hs + k0, acc, nk); break;
-            case 1: fir_ring<SH, 1, true>(w - k0, hs + k0, acc, nk); break;
-            default: fir_ring<SH, 0, true>(w - k0, hs + k0, acc, nk); break;
+            case 3: fir_ring<SH, 3, true, KPT>(w - k0, hs + k0, acc, nk); break;
+            case 2: fir_ring<SH, 2, true, KPT>(w - k0, hs + k0, acc, nk); break;
+            case 1: fir_ring<SH, 1, true, KPT>(w - k0, hs + k0, acc, nk); break;
+            default: fir_ring<SH, 0, true, KPT>(w - k0, hs + k0, acc, nk); break;
         }
     } else {
         switch ((g.taps - k0) / kChunk) {
-            case 3: fir_ring<SH, 3>(w - k0, hs + k0, acc); break;
-            case 2: fir_ring<SH, 2>(w - k0, hs + k0, acc); break;
-            case 1: fir_ring<SH, 1>(w - k0, hs + k0, acc); break;
+            case 3: fir_ring<SH, 3, false, KPT>(w - k0, hs + k0, acc); break;
+            case 2: fir_ring<SH, 2, false, KPT>(w - k0, hs + k0, acc); break;
+            case 1: fir_ring<SH, 1, false, KPT>(w - k0, hs + k0, acc); break;
             default: break;
         }
     }
 
-    const int64_t ob = t * kWarpOut + kPerThread * lane;
+    // Let the next grid start launching once every block is this far: its
+    // blocks take the SMs as this grid's finish (launched before the FMAs,
+    // they held SM slots through the whole of a short launch: 2^20 samples
+    // x 31 taps 4.1 -> 4.8 us per launch; released here, 3.9 us).
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const int64_t ob = t * kWarpOut + KPT * lane;
     if (vec_out && (t + 1) * kWarpOut <= g.y_len) {
 #pragma unroll
-        for (int c = 0; c < kPerThread / 4; c++)
+        for (int c = 0; c < KPT / 4; c++)
             st_stream_f4(y + ob + 4 * c,
                          make_float4(acc[4 * c], acc[4 * c + 1], acc[4 * c + 2], acc[4 * c + 3]));
     } else {
 #pragma unroll
-        for (int r = 0; r < kPerThread; r++)
+        for (int r = 0; r < KPT; r++)
             if (ob + r < g.y_len) y[ob + r] = acc[r];
     }
 }
@@ -221,14 +239,15 @@ __global__ void __launch_bounds__(NT, min_blocks(NT)) k_fir(float* __restrict__ 
 using FirKernel = void (*)(float*, const float*, const float*, FirGeom, int64_t, bool, bool,
                            uint32_t*);
 
-template <int NT>
-constexpr FirKernel kFirKernels[4] = {k_fir<0, NT>, k_fir<1, NT>, k_fir<2, NT>, k_fir<3, NT>};
+template <int NT, int KPT>
+constexpr FirKernel kFirKernels[4] = {k_fir<0, NT, KPT>, k_fir<1, NT, KPT>, k_fir<2, NT, KPT>,
+                                      k_fir<3, NT, KPT>};
 
 // Each kernel may take the opt-in maximum of dynamic shared memory less 1 KB
 // (its static mbarriers); set once per device (a bit per device, for the
-// eight kernels).
+// twelve kernels).
 int fir_dyn_max(const sg::DevInfo* d) { return d->max_smem_optin - 1024; }
-std::atomic<uint64_t> g_fir_configured[8];
+std::atomic<uint64_t> g_fir_configured[12];
 
 int fir_configure(const sg::DevInfo* d, int slot, FirKernel kern) {
     const uint64_t bit = 1ull << (d->device & 63);
@@ -251,7 +270,9 @@ int launch_fir(const char* K, float* y, int64_t y_len, const float* x, int64_t x
     const int64_t wide_waves =
         sg::ceil_div(y_len, (int64_t)tile_out(kWide)) / ((int64_t)d->sms * min_blocks(kWide));
     const bool narrow = wide_waves < 4;
+    const bool short_chains = wide_waves < 1;  // 12 outputs per lane
     const int nt = narrow ? kNarrow : kWide;
+    const int kpt = short_chains ? kKptShort : kKptLong;
     FirGeom g;
     g.y_len = y_len;
     g.x_len = x_len;
@@ -263,22 +284,37 @@ int launch_fir(const char* K, float* y, int64_t y_len, const float* x, int64_t x
     g.D = (int32_t)(taps + 6 + m);
     // The window loads of the last lane reach a few floats past the last
     // sample its outputs use (whole 16-byte loads): 8 floats of slack.
-    g.tile = (int32_t)sg::ceil_div(g.D + kWarpOut + 8, 4) * 4;
+    g.tile = (int32_t)sg::ceil_div(g.D + warp_out(kpt) + 8, 4) * 4;
     const int sh = (g.D - 7) % 4;
 
-    const FirKernel kern = narrow ? kFirKernels<kNarrow>[sh] : kFirKernels<kWide>[sh];
+    const FirKernel kern = short_chains ? kFirKernels<kNarrow, kKptShort>[sh]
+                           : narrow     ? kFirKernels<kNarrow, kKptLong>[sh]
+                                        : kFirKernels<kWide, kKptLong>[sh];
     const size_t smem = (size_t)(nt / 32) * (g.tile + g.taps_pad) * sizeof(float);
     if (smem > (size_t)fir_dyn_max(d))
         return sg::fail(SIMTGO_ESIZE, "%s: %d taps need %zu bytes of shared memory", K, taps,
                         smem);
-    if ((rc = fir_configure(d, (narrow ? 4 : 0) + sh, kern))) return rc;
-    const int64_t nwt = sg::ceil_div(y_len, (int64_t)kWarpOut);
+    if ((rc = fir_configure(d, (short_chains ? 8 : narrow ? 4 : 0) + sh, kern))) return rc;
+    const int64_t nwt = sg::ceil_div(y_len, (int64_t)warp_out(kpt));
     const int64_t blocks = sg::ceil_div(nwt, (int64_t)(nt / 32));
     if (blocks > 0x7fffffffLL) return sg::fail(SIMTGO_ESIZE, "%s: y_len too large", K);
     sg::before_launch();
-    kern<<<(unsigned)blocks, nt, smem, (cudaStream_t)stream>>>(
-        y, x, h, g, nwt, sg::aligned16(x), sg::aligned16(y), sg::watchdog_device_ptr());
-    return sg::launch_status(K);
+    // Launched with programmatic stream serialisation (PDL): a launch that
+    // follows another kernel on the stream starts while that one drains,
+    // and waits in griddepcontrol.wait before touching memory.
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)blocks);
+    cfg.blockDim = dim3(nt);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = (cudaStream_t)stream;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return sg::cuda_status(cudaLaunchKernelEx(&cfg, kern, y, x, h, g, nwt, sg::aligned16(x),
+                                              sg::aligned16(y), sg::watchdog_device_ptr()),
+                           K);
 }
 
 // ---- the shard from host memory ----------------------------------------------
