@@ -189,25 +189,25 @@ __device__ __forceinline__ void fir_acc(float4 (&A)[G], const Ctx& c, int f, int
     // Group k's window float4 at tap i0 (a multiple of 4): tw[k][-i0/4].
     const float4* tw = c.S + fd.w + threadIdx.x + fd.z / 4 + woff4;
     float acc[G][4];
-    float4 hi[G];
 #pragma unroll
-    for (int k = 0; k < G; k++) {
+    for (int k = 0; k < G; k++)
 #pragma unroll
         for (int j = 0; j < 4; j++) acc[k][j] = 0.0f;
-        hi[k] = tw[kThreads * k];
-    }
-    // Whole steps of 8 taps, two window loads per group, no predicates.
+    // Whole steps of 8 taps, three window loads per group, no predicates.
+    // No window value is carried from one step to the next: a carried float4
+    // costs four register moves per step, a third load one shared load
+    // (measured at 2^28: a 31-tap window 0.781 -> 0.775 ms).
     int i0 = 0;
     for (; i0 + 8 <= taps; i0 += 8) {
         const float4 ha = h4[i0 / 4], hb = h4[i0 / 4 + 1];
         const float hva[4] = {ha.x, ha.y, ha.z, ha.w}, hvb[4] = {hb.x, hb.y, hb.z, hb.w};
 #pragma unroll
         for (int k = 0; k < G; k++) {
+            const float4 hi = tw[kThreads * k - i0 / 4];
             const float4 m = tw[kThreads * k - i0 / 4 - 1];
             const float4 lo = tw[kThreads * k - i0 / 4 - 2];
-            fir_step<false>(acc[k], m, hi[k], hva, 4);
+            fir_step<false>(acc[k], m, hi, hva, 4);
             fir_step<false>(acc[k], lo, m, hvb, 4);
-            hi[k] = lo;
         }
     }
     // The last 1-7 taps, 4 at a time.
@@ -217,9 +217,9 @@ __device__ __forceinline__ void fir_acc(float4 (&A)[G], const Ctx& c, int f, int
         const int nk = min(4, taps - i0);
 #pragma unroll
         for (int k = 0; k < G; k++) {
+            const float4 hi = tw[kThreads * k - i0 / 4];
             const float4 lo = tw[kThreads * k - i0 / 4 - 1];
-            fir_step<true>(acc[k], lo, hi[k], hv, nk);
-            hi[k] = lo;
+            fir_step<true>(acc[k], lo, hi, hv, nk);
         }
     }
 #pragma unroll
@@ -258,8 +258,12 @@ template <bool BULK, bool FULL, int G>
 __device__ __forceinline__ void interpret(const Insn* code, int pc, const Ctx& c, const Run& r,
                                           float4 (&A)[G]) {
     const int t = threadIdx.x;
+    // Every program's first step writes A (LDA or FIRACC); a head run's
+    // inactive groups read A as their own operand, so it starts defined.
+    if (!FULL) {
 #pragma unroll
-    for (int k = 0; k < G; k++) A[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int k = 0; k < G; k++) A[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
     for (;;) {
         const Insn in = code[pc++];
         // Group k of operand M(x) (inactive groups: A itself, nothing is read).
@@ -321,7 +325,13 @@ __device__ __forceinline__ void interpret(const Insn* code, int pc, const Ctx& c
                         dst[kThreads * k] =
                             r.edge ? mask_outside(A[k], r.p0 + 4 * (t + kThreads * k), c) : A[k];
             }
-            if (in.flags & F_STORE) {
+            // A run inside [0, n) with a 16-byte aligned output stores its
+            // float4s unchecked; the rest element by element.
+            if ((in.flags & F_STORE) && !r.edge && c.vec) {
+                float* o = c.out + r.p0 + 4 * t;
+#pragma unroll
+                for (int k = 0; k < G; k++) st_stream_f4(o + 4 * kThreads * k, A[k]);
+            } else if (in.flags & F_STORE) {
 #pragma unroll
                 for (int k = 0; k < G; k++) {
                     const int64_t p = r.p0 + 4 * (t + kThreads * k);
@@ -957,36 +967,39 @@ __global__ void __launch_bounds__(kThreads, G == kG ? 3 : 2)
     const int nf = P.n_fir;
     const bool free_run = nf == 0;
     float4 A[G];  // the last run's values (the main program's, for a reduction)
-    int it = 0;
-    for (int64_t c = c0; c < c1; c++, it++) {
+    int s = 0;           // this chunk's stage
+    uint32_t phase = 0;  // the parity its mbarrier completes next
+    for (int64_t c = c0; c < c1; c++) {
         const int64_t cb = c * CH;
         const bool first = c == c0;
-        const ChunkSpan sp = chunk_span(cb, hs, n, halo, first, CH);
-        int s = 0;
+        const bool edge = cb - (int64_t)hs < -halo || cb + CH > n;
         if (BULK) {
-            s = it % nst;
-            if (!mbar_wait(&bars[s], (uint32_t)((it / nst) & 1), wd)) {
+            if (!mbar_wait(&bars[s], phase, wd)) {
                 // Gave up (the watchdog is raised): let the block's other
                 // copies in flight land, each wait bounded, before exiting.
-                for (int j = 1; j < nst && c + j < c1; j++)
-                    mbar_wait(&bars[(it + j) % nst], (uint32_t)(((it + j) / nst) & 1), wd);
+                for (int j = 1; j < nst && c + j < c1; j++) {
+                    const int s2 = s + j;
+                    mbar_wait(&bars[s2 < nst ? s2 : s2 - nst], s2 < nst ? phase : phase ^ 1u, wd);
+                }
                 return;
             }
-            float* buf = stages + s * stage_floats;
-            // The last 0-3 samples of a ragged signal are not a whole 16-byte
-            // unit: plain loads.
-            const int64_t tail = sp.hi - (sp.lo + sp.len4);
-            if (tail > 0) {  // uniform over the block
-                if (tid < P.n_in * 4) {
-                    const int k = tid / 4, e = tid % 4;
-                    const int64_t pos = sp.lo + sp.len4 + e;
-                    if (e < tail) buf[k * sstride + (pos - sp.org)] = in_s[k][pos];
+            if (edge) {  // only a chunk at either end of the signal has a ragged span
+                const ChunkSpan sp = chunk_span(cb, hs, n, halo, first, CH);
+                float* buf = stages + s * stage_floats;
+                // The last 0-3 samples of a ragged signal are not a whole
+                // 16-byte unit: plain loads.
+                const int64_t tail = sp.hi - (sp.lo + sp.len4);
+                if (tail > 0) {  // uniform over the block
+                    if (tid < P.n_in * 4) {
+                        const int k = tid / 4, e = tid % 4;
+                        const int64_t pos = sp.lo + sp.len4 + e;
+                        if (e < tail) buf[k * sstride + (pos - sp.org)] = in_s[k][pos];
+                    }
+                    __syncthreads();
                 }
-                __syncthreads();
             }
         }
-        const int32_t in4 = stages4 + s * stage_floats / 4;
-        const bool edge = cb - (int64_t)hs < -halo || cb + CH > n;
+        const int32_t in4 = stages4 + s * (stage_floats / 4);
         // Jobs 2f and 2f+1 stage window f: its head (first chunk only) and
         // the chunk itself; job 2 nf is the main program over the chunk. One
         // loop, so the interpreter is inlined once per form.
@@ -1072,6 +1085,10 @@ __global__ void __launch_bounds__(kThreads, G == kG ? 3 : 2)
             }
         } else if (!free_run) {
             __syncthreads();  // the tiles are rewritten by the next chunk
+        }
+        if (BULK && ++s == nst) {
+            s = 0;
+            phase ^= 1u;
         }
     }
 }

@@ -223,6 +223,59 @@ def test_input_only_and_unaligned():
     assert_agree("unaligned device inputs", out.cpu().numpy(), want)
 
 
+def test_hypot_wide_range():
+    """The fused kernel's four-wide Hypot over exponents across the whole
+    float32 range and both signs -- the fast path's domain edge (2^-60,
+    2^60), zeros, subnormals, overflow, infinities and NaN -- bit for bit
+    against the oracle's gpu.Hypot (kernels/kernels.go:29)."""
+    rng = np.random.default_rng(16)
+    n = (1 << 20) + 13
+    e1 = rng.integers(-150, 128, n).astype(np.float64)
+    e2 = np.clip(e1 + rng.integers(-40, 40, n), -150, 127)
+    sx, sy = rng.choice([-1.0, 1.0], n), rng.choice([-1.0, 1.0], n)
+    with np.errstate(over="ignore"):
+        x = (sx * rng.uniform(1, 2, n) * np.exp2(e1)).astype(np.float32)
+        y = (sy * rng.uniform(1, 2, n) * np.exp2(e2)).astype(np.float32)
+    x[:14] = [3, 0, -5, 1e-45, 3.4e38, 2.0 ** -60, np.inf, np.nan, -0.0, 2.0 ** 60, 1.0, -np.inf,
+              2.0 ** -61, 1e-40]
+    y[:14] = [4, 0, 12, 1e-45, 3.4e38, 2.0 ** 60, np.nan, 1.0, 7.0, 2.0 ** -61, 0.0, np.nan,
+              2.0 ** -61, 2.0 ** -59]
+    rc, want = O.magnitude(x, y, (n + 255) // 256, 256)
+    assert rc == 0
+    g = tile.New()
+    tx, ty = torch.from_numpy(x).cuda(), torch.from_numpy(y).cuda()
+    out = torch.empty(n, dtype=torch.float32, device="cuda")
+    tile.Hypot(g.InputDevice(tx), g.InputDevice(ty)).Run(out)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()
+    assert_agree("tile Hypot, wide range", got, want)
+    assert got[0] == 5 and got[2] == 13 and got[10] == 1
+
+
+def test_sqrt_every_float32():
+    """The fused kernel's Sqrt over all 2^32 float32 bit patterns, in sixteen
+    runs of 2^28, bit for bit against the correctly rounded float32 square
+    root (gpu.Sqrt is float32(math.Sqrt(float64(x))), gpu/math.go:11-17, and
+    that double rounding is exact for square roots); NaN agrees with NaN."""
+    run = 1 << 28
+    x = torch.empty(run, dtype=torch.float32, device="cuda")
+    out = torch.empty(run, dtype=torch.float32, device="cuda")
+    g = tile.New()
+    root = tile.Sqrt(g.InputDevice(x))
+    for r in range(16):
+        bits = np.arange(r * run, (r + 1) * run, dtype=np.uint64).astype(np.uint32)
+        xs = bits.view(np.float32)
+        x.copy_(torch.from_numpy(xs))
+        root.Run(out)
+        got = out.cpu().numpy()
+        with np.errstate(invalid="ignore"):
+            want = np.sqrt(xs)
+        bad = (got.view(np.uint32) != want.view(np.uint32)) & ~(np.isnan(got) & np.isnan(want))
+        assert not bad.any(), (
+            f"sqrt({xs[bad][0]!r} = {bits[bad][0]:#010x}): got {got[bad][0]!r}, want "
+            f"{want[bad][0]!r}; {int(bad.sum())} of {run} in run {r} differ")
+
+
 @pytest.mark.parametrize("seed", range(16))
 def test_random_graphs(seed):
     """Random DAGs over the seven operations (shared values, x-op-x nodes,
