@@ -131,6 +131,9 @@ var (
 	TileErrString             func(g uintptr) string
 	TileProgramSize           func(g uintptr, t int32, nInstructions *int32, nInputs *int32, nWindows *int32) int32
 	TileSource                func(g uintptr, t int32, buf unsafe.Pointer, capacity int32) int32
+	TileSetJIT                func(mode int32) int32
+	TileJITInfo               func(mode *int32, available *int32, compiled *int64, launches *int64) int32
+	TileJITSource             func(g uintptr, t int32, reduce int32, groups int32, bulk int32, compile int32, buf unsafe.Pointer, capacity int32) int32
 	TileMaterialize           func(g uintptr, t int32, hostOut unsafe.Pointer, outLen int32) int32
 	TileMaterializeStepwise   func(g uintptr, t int32, hostOut unsafe.Pointer, outLen int32, launches *int32) int32
 	TileRun                   func(g uintptr, t int32, devOut uintptr, outLen int32, stream uintptr) int32
@@ -216,6 +219,9 @@ func bind(h uintptr) {
 	purego.RegisterLibFunc(&TileErrString, h, "simtgo_tile_err_string")
 	purego.RegisterLibFunc(&TileProgramSize, h, "simtgo_tile_program_size")
 	purego.RegisterLibFunc(&TileSource, h, "simtgo_tile_source")
+	purego.RegisterLibFunc(&TileSetJIT, h, "simtgo_tile_set_jit")
+	purego.RegisterLibFunc(&TileJITInfo, h, "simtgo_tile_jit_info")
+	purego.RegisterLibFunc(&TileJITSource, h, "simtgo_tile_jit_source")
 	purego.RegisterLibFunc(&TileMaterialize, h, "simtgo_tile_materialize")
 	purego.RegisterLibFunc(&TileMaterializeStepwise, h, "simtgo_tile_materialize_stepwise")
 	purego.RegisterLibFunc(&TileRun, h, "simtgo_tile_run")

@@ -315,6 +315,32 @@ int simtgo_tile_program_size(simtgo_tile_graph* g, simtgo_tensor t, int32_t* n_i
  * negative status. */
 int32_t simtgo_tile_source(simtgo_tile_graph* g, simtgo_tensor t, char* buf, int32_t cap);
 
+/* Specialised kernels (tile/run.go:38 run -> internal/jit/jit.go Load: the
+ * reference compiles each distinct graph with NVRTC and caches the result).
+ * Every launch of a fused program (materialise, run, shards, reductions,
+ * stepwise steps) runs the program's own specialised kernel: the lowered
+ * program compiled in as constants (NVRTC, sm_100a, on first use of each
+ * distinct program per device, then cached for the life of the process),
+ * computing the same bits as the interpreter it replaces. Mode 0: the
+ * interpreter only; 1 (the default, or SIMTGO_TILE_JIT=1 in the environment
+ * before the first tile launch): specialise, or interpret when libnvrtc
+ * cannot be opened; 2: specialise or fail with SIMTGO_EDEVICE. A first launch
+ * of a new program compiles (about a second) before it enqueues, so make it
+ * before any stream capture. */
+int simtgo_tile_set_jit(int32_t mode);
+/* The mode, whether libnvrtc could be opened, and how many programs were
+ * compiled and specialised launches made in this process. Any pointer may
+ * be NULL. */
+int simtgo_tile_jit_info(int32_t* mode, int32_t* available, int64_t* compiled,
+                         int64_t* launches);
+/* The specialised kernel's source for t (reduce: -1 or a SIMTGO_TILE_*
+ * reduction) with `groups` (2 or 4) float4 groups per thread and bulk-copied
+ * (bulk != 0) or directly read inputs, written like simtgo_tile_source; with
+ * compile != 0 it is compiled too (no GPU needed) and a failure returned. */
+int32_t simtgo_tile_jit_source(simtgo_tile_graph* g, simtgo_tensor t, int32_t reduce,
+                               int32_t groups, int32_t bulk, int32_t compile, char* buf,
+                               int32_t cap);
+
 /* tile/run.go:20 Materialize: upload host inputs, run the one fused kernel,
  * download into host_out (out_len == Len(t)), free what the call allocated.
  * Synchronous. */
@@ -356,8 +382,10 @@ int simtgo_tile_run_shard(simtgo_tile_graph* g, simtgo_tensor t, float* dev_out,
  * capture begins on that device. Every call uses the same array and
  * leaves its values there; each node's region is written in full before it
  * is read, so nothing needs clearing. Calls that overlap on the GPU (two
- * streams, or two host threads) race on the array. Asynchronous on stream;
- * the result equals simtgo_tile_run's bit for bit. */
+ * streams, or two host threads) race on the array. Its steps always run in
+ * the precompiled interpreter, never in a specialised kernel (loading one
+ * allocates device memory for its code). Asynchronous on stream; the
+ * result equals simtgo_tile_run's bit for bit. */
 #define SIMTGO_TILE_NOALLOC_SCRATCH_FLOATS (1 << 22)
 int simtgo_tile_run_stepwise_noalloc(simtgo_tile_graph* g, simtgo_tensor t, float* dev_out,
                                      int32_t out_len, void* stream);

@@ -5,7 +5,10 @@
 
 Each csrc/*.cu is compiled to simtgo_b200/_build/<name>.o (in parallel, only
 when it or a header changed), then linked with -ldl into
-simtgo_b200/libsimtgo_b200.so. The library links the CUDA runtime
+simtgo_b200/libsimtgo_b200.so. The device headers a tile graph's specialised
+kernel is compiled from at run time (tile_jit.cu, NVRTC) are written into
+_build/rtc_headers.inc as string literals first, so they travel inside the
+library. The library links the CUDA runtime
 statically, so it needs only libcuda.so.1 at run time.
 """
 from __future__ import annotations
@@ -25,12 +28,14 @@ LIB = PKG / "libsimtgo_b200.so"
 NVCC = os.environ.get("NVCC", "nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "--fmad=false", "-Xcompiler", "-fPIC",
-         "-Xcompiler", "-Wall", "-I", str(ROOT / "include"), "--expt-relaxed-constexpr",
+         "-Xcompiler", "-Wall", "-I", str(ROOT / "include"), "-I", str(BUILD),
+         "--expt-relaxed-constexpr",
          "-Xptxas", "-warn-spills"]
 
 
 def _headers():
-    return sorted(list(CSRC.glob("*.cuh")) + list((ROOT / "include").glob("*.h")))
+    return sorted(list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.h")) +
+                  list((ROOT / "include").glob("*.h")))
 
 
 def _compile(src: pathlib.Path, force: bool, verbose: bool) -> pathlib.Path:
@@ -49,8 +54,38 @@ def _compile(src: pathlib.Path, force: bool, verbose: bool) -> pathlib.Path:
     return obj
 
 
+# The headers NVRTC needs for a specialised tile kernel, by the names
+# tile_kernel.cuh includes them under.
+RTC_HEADERS = ["tile_kernel.cuh", "common.cuh", "exact.cuh", "tma.cuh"]
+RTC_INC = BUILD / "rtc_headers.inc"
+_DELIM = "SIMTGO_RTC"
+
+
+def _write_rtc_headers(force: bool) -> None:
+    srcs = [CSRC / h for h in RTC_HEADERS]
+    if not force and RTC_INC.exists() and RTC_INC.stat().st_mtime >= max(
+            p.stat().st_mtime for p in srcs):
+        return
+    out = ["// Written by simtgo_b200/build.py from csrc/: the device headers of a",
+           "// specialised tile kernel, for NVRTC. Do not edit.",
+           f"const int kRtcHeaderCount = {len(srcs)};",
+           "const char* const kRtcHeaderNames[] = {" + ", ".join(f'"{h}"' for h in RTC_HEADERS)
+           + "};",
+           "const char* const kRtcHeaderSources[] = {"]
+    for p in srcs:
+        text = p.read_text()
+        if f"){_DELIM}" in text:
+            raise RuntimeError(f"{p.name} contains the raw-string delimiter")
+        out.append(f'R"{_DELIM}({text}){_DELIM}",')
+    out.append("};")
+    tmp = RTC_INC.with_suffix(".tmp")
+    tmp.write_text("\n".join(out) + "\n")
+    os.replace(tmp, RTC_INC)
+
+
 def build(force: bool = False, verbose: bool = False) -> pathlib.Path:
     BUILD.mkdir(exist_ok=True)
+    _write_rtc_headers(force)
     sources = sorted(CSRC.glob("*.cu"))
     with cf.ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 1)) as ex:
         objs = list(ex.map(lambda s: _compile(s, force, verbose), sources))

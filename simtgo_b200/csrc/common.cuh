@@ -4,6 +4,10 @@
 // 128-bit streaming load/store helpers the memory-bound kernels share.
 #pragma once
 
+// Under run-time compilation (a tile graph's specialised kernel, tile_jit.cu)
+// only the device helpers below are compiled; the JIT's prelude supplies the
+// integer types.
+#ifndef __CUDACC_RTC__
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -79,6 +83,7 @@ inline void before_launch() { (void)cudaGetLastError(); }
 int launch_status(const char* kernel);
 
 }  // namespace sg
+#endif  // __CUDACC_RTC__
 
 // ---- device helpers ----------------------------------------------------------
 namespace sgd {

@@ -6,8 +6,10 @@
 // (gpu/math.go:11-17). Everything here therefore uses the _rn intrinsics
 // explicitly; the library is also compiled with --fmad=false.
 #pragma once
+#ifndef __CUDACC_RTC__
 #include <cuda_runtime.h>
 #include <stdint.h>
+#endif
 
 namespace sgd {
 

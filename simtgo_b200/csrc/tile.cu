@@ -54,6 +54,7 @@
 
 #include "common.cuh"
 #include "exact.cuh"
+#include "tile_jit.h"
 #include "tile_kernel.cuh"
 #include "tma.cuh"
 
@@ -518,6 +519,18 @@ struct Layout {
     size_t smem;
 };
 
+// The float4 offsets of the layout's parts for Y.g groups per thread; hs
+// is the samples a chunk's windows reach below it.
+void set_offsets(const Lowered& L, int32_t hs, Layout& Y) {
+    const int n_in = (int)L.in_nodes.size(), n_fir = (int)L.fir_nodes.size();
+    const int chunk = tilek::chunk_of(Y.g);
+    Y.taps4 = tilek::meta_bytes((int)L.code.size(), n_in, n_fir) / 16;
+    Y.tiles4 = Y.taps4 + n_fir * tilek::kMaxTaps / 4;
+    Y.temps4 = Y.tiles4 + tile_off4(L, n_fir, chunk);
+    Y.stages4 = Y.temps4 + L.n_tmp * chunk / 4;
+    Y.sstride = hs + chunk;
+}
+
 void build_program(const simtgo_tile_graph* g, const Lowered& L, const Layout& Y, bool bulk,
                    tilek::Program& P) {
     memset(&P, 0, sizeof P);
@@ -585,7 +598,8 @@ void build_program(const simtgo_tile_graph* g, const Lowered& L, const Layout& Y
 // 2048-element block and idx_base is the index of element 0.
 int launch_program(const simtgo_tile_graph* g, const Lowered& L,
                    const std::vector<const float*>& dev_in, float* out, int64_t n, int64_t halo,
-                   cudaStream_t s, int64_t* out_idx = nullptr, int64_t idx_base = 0) {
+                   cudaStream_t s, int64_t* out_idx = nullptr, int64_t idx_base = 0,
+                   bool jit_ok = true) {
     const sg::DevInfo* d;
     int rc;
     if ((rc = sg::current_device(&d))) return rc;
@@ -620,12 +634,7 @@ int launch_program(const simtgo_tile_graph* g, const Lowered& L,
               ? tilek::kGWide
               : tilek::kG;
     const int min_st = Y.g == tilek::kGWide && n_fir > 0 ? 1 : 2;  // input stages per block
-    const int chunk = tilek::chunk_of(Y.g);
-    Y.taps4 = tilek::meta_bytes((int)L.code.size(), n_in, n_fir) / 16;
-    Y.tiles4 = Y.taps4 + n_fir * tilek::kMaxTaps / 4;
-    Y.temps4 = Y.tiles4 + tile_off4(L, n_fir, chunk);
-    Y.stages4 = Y.temps4 + L.n_tmp * chunk / 4;
-    Y.sstride = hs + chunk;
+    set_offsets(L, hs, Y);
     const size_t base_smem = (size_t)Y.stages4 * 16;
     const size_t stage_bytes = (size_t)n_in * Y.sstride * sizeof(float);
     // Every instantiation may take up to the opt-in maximum of dynamic
@@ -651,16 +660,30 @@ int launch_program(const simtgo_tile_graph* g, const Lowered& L,
     // latency x bandwidth per SM), else the most bytes in flight. With
     // unaligned inputs, or fewer than two stages' room, the inputs are read
     // from HBM by the interpreter itself (DIRECT).
+    //
+    // The program runs in its specialised kernel (tile_jit.cu: this
+    // program's instructions compiled in as constants) when run-time
+    // compilation is on, else in the interpreter; the choice of stages
+    // follows the registers of the kernel that runs.
+    const bool bulk_cand = in_aligned && halo % 4 == 0 && n_in > 0;
+    static thread_local tilek::Program P;
+    build_program(g, L, Y, bulk_cand, P);
+    CUfunction spec = nullptr;
+    if (jit_ok && (rc = tilejit::get(P, bulk_cand, Y.g, dyn_max, &spec))) return rc;
     int reg_blocks = 0;
-    rc = sg::cuda_status(cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-                             &reg_blocks,
-                             Y.g == kG ? tilek::k_tile<true, kG> : tilek::k_tile<true, kGWide>,
-                             tilek::kThreads, base_smem),
-                         "cudaOccupancyMaxActiveBlocksPerMultiprocessor(tile)");
+    if (spec) {
+        rc = tilejit::occupancy(spec, base_smem, &reg_blocks);
+    } else {
+        rc = sg::cuda_status(
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+                &reg_blocks, Y.g == kG ? tilek::k_tile<true, kG> : tilek::k_tile<true, kGWide>,
+                tilek::kThreads, base_smem),
+            "cudaOccupancyMaxActiveBlocksPerMultiprocessor(tile)");
+    }
     if (rc) return rc;
     bool bulk = false;
     Y.nst = 0;
-    if (in_aligned && halo % 4 == 0 && n_in > 0) {
+    if (bulk_cand) {
         int64_t best_inflight = -1;
         for (int per_sm = std::max(1, reg_blocks); per_sm >= 1; per_sm--) {
             const int64_t share =
@@ -684,15 +707,21 @@ int launch_program(const simtgo_tile_graph* g, const Lowered& L,
     if (Y.smem > (size_t)dyn_max)
         return sg::fail(SIMTGO_ESIZE, "tile: the program needs %zu bytes of shared memory (max %d)",
                         Y.smem, dyn_max);
-    static thread_local tilek::Program P;
-    build_program(g, L, Y, bulk, P);
+    if (bulk != bulk_cand) {  // no room for the stages after all: DIRECT addressing
+        build_program(g, L, Y, bulk, P);
+        spec = nullptr;
+        if (jit_ok && (rc = tilejit::get(P, bulk, Y.g, dyn_max, &spec))) return rc;
+    }
     for (int k = 0; k < n_in; k++) P.in[k] = dev_in[k];  // element 0; [-halo, 0) precede it
     auto kern = Y.g == kG ? (bulk ? tilek::k_tile<true, kG> : tilek::k_tile<false, kG>)
                           : (bulk ? tilek::k_tile<true, kGWide> : tilek::k_tile<false, kGWide>);
     int per_sm = 0;
-    rc = sg::cuda_status(
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, tilek::kThreads, Y.smem),
-        "cudaOccupancyMaxActiveBlocksPerMultiprocessor(tile)");
+    if (spec)
+        rc = tilejit::occupancy(spec, Y.smem, &per_sm);
+    else
+        rc = sg::cuda_status(
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, tilek::kThreads, Y.smem),
+            "cudaOccupancyMaxActiveBlocksPerMultiprocessor(tile)");
     if (rc) return rc;
     // Whole waves of resident blocks, up to eight, each block over a
     // contiguous range of at least 32 chunks: a block that finishes early is
@@ -701,14 +730,20 @@ int launch_program(const simtgo_tile_graph* g, const Lowered& L,
     // B200 at 2^28 elements). Short signals keep one wave: every range starts
     // with a pipeline fill and, with windows, a head run, and a partial wave
     // would leave most SMs idle at the end.
-    const int64_t chunks = sg::ceil_div(n, (int64_t)chunk);
+    const int64_t chunks = sg::ceil_div(n, (int64_t)tilek::chunk_of(Y.g));
     const int64_t resident = (int64_t)d->sms * std::max(1, per_sm);
     const int64_t waves = std::max<int64_t>(1, std::min<int64_t>(8, chunks / (32 * resident)));
     const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(chunks, waves * resident));
     sg::before_launch();
+    uint32_t* wd = sg::watchdog_device_ptr();
+    if (spec) {
+        bool out_vec = vec, in_vec = in_aligned;
+        void* args[] = {&P, &out, &n, &halo, &out_vec, &in_vec, &hs,
+                        &Y.stages4, &Y.nst, &wd, &out_idx, &idx_base};
+        return tilejit::launch(spec, blocks, Y.smem, s, args);
+    }
     kern<<<blocks, tilek::kThreads, Y.smem, s>>>(P, out, n, halo, vec, in_aligned, hs, Y.stages4,
-                                                 Y.nst, sg::watchdog_device_ptr(), out_idx,
-                                                 idx_base);
+                                                 Y.nst, wd, out_idx, idx_base);
     return sg::launch_status("tile");
 }
 
@@ -757,10 +792,11 @@ int check_out_alias(const Lowered& L, const simtgo_tile_graph* g, const float* o
 }
 
 // Runs the fused program for root with inputs resolved by `resolve`
-// (node id -> device pointer).
+// (node id -> device pointer). jit_ok false keeps it on the interpreter
+// (loading a specialised kernel's module allocates device memory).
 template <class Resolve>
 int run_fused(const simtgo_tile_graph* g, int root, float* out, int64_t n, int64_t halo,
-              cudaStream_t s, Resolve resolve, bool check_alias) {
+              cudaStream_t s, Resolve resolve, bool check_alias, bool jit_ok = true) {
     Lowered L;
     int rc = lower(g, root, L);
     if (rc) return rc;
@@ -771,7 +807,7 @@ int run_fused(const simtgo_tile_graph* g, int root, float* out, int64_t n, int64
         dev_in.push_back(p);
     }
     if (check_alias && (rc = check_out_alias(L, g, out, n, dev_in, halo))) return rc;
-    return launch_program(g, L, dev_in, out, n, halo, s);
+    return launch_program(g, L, dev_in, out, n, halo, s, nullptr, 0, jit_ok);
 }
 
 // ---- reductions ----------------------------------------------------------------
@@ -1220,6 +1256,42 @@ int simtgo_tile_program_size(simtgo_tile_graph* g, simtgo_tensor t, int32_t* n_i
     return 0;
 }
 
+// The specialised kernel's source for t (reduced by `reduce`, or -1) with
+// `groups` float4 groups per thread and bulk or DIRECT input addressing,
+// into buf like simtgo_tile_source; with compile != 0 it is also compiled
+// (no GPU needed) and a compilation error is returned.
+int32_t simtgo_tile_jit_source(simtgo_tile_graph* g, simtgo_tensor t, int32_t reduce,
+                               int32_t groups, int32_t bulk, int32_t compile, char* buf,
+                               int32_t cap) {
+    sg::clear_error();
+    if (!g) return sg::fail(SIMTGO_ENULL, "tile: null graph");
+    if (!g->err.empty()) return sg::fail(SIMTGO_EGRAPH, "%s", g->err.c_str());
+    if (!valid(g, t)) return sg::fail(SIMTGO_EARG, "tile: unknown tensor %d", t);
+    if (groups != tilek::kG && groups != tilek::kGWide)
+        return sg::fail(SIMTGO_EARG, "tile: %d groups per thread is not %d or %d", (int)groups,
+                        tilek::kG, tilek::kGWide);
+    if (reduce < -1 || reduce > SIMTGO_TILE_ARGMAX)
+        return sg::fail(SIMTGO_EARG, "tile: unknown reduction %d", (int)reduce);
+    Lowered L;
+    int rc = lower(g, t, L, reduce);
+    if (rc) return rc;
+    int32_t hs = 0;
+    for (size_t f = 0; f < L.fir_nodes.size(); f++) hs = std::max<int32_t>(hs, L.head[f]);
+    Layout Y{};
+    Y.g = groups;
+    set_offsets(L, hs, Y);
+    static thread_local tilek::Program P;
+    build_program(g, L, Y, bulk != 0, P);
+    if (compile && (rc = tilejit::compile_only(P, bulk != 0, groups))) return rc;
+    const std::string s = tilejit::spec_source(P, bulk != 0, groups);
+    if (buf && cap > 0) {
+        const size_t n = std::min<size_t>(s.size(), (size_t)cap - 1);
+        memcpy(buf, s.data(), n);
+        buf[n] = 0;
+    }
+    return (int32_t)s.size() + 1;
+}
+
 // The listing of a lowered program, one device instruction per line:
 //   "window <f> taps <T> node <id>" / "main" section headers, then
 //   "<pc> <step> | <step> ...", the steps the instruction fuses, in order:
@@ -1638,7 +1710,7 @@ extern "C" int simtgo_tile_run_stepwise_noalloc(simtgo_tile_graph* g, simtgo_ten
         // The root is an input: its values are copied to dev_out by the same
         // one-node program simtgo_tile_run launches (after the same alias check).
         auto resolve = [&](int nid) -> const float* { return g->nodes[nid].dev; };
-        return run_fused(g, t, dev_out, out_len, 0, (cudaStream_t)stream, resolve, true);
+        return run_fused(g, t, dev_out, out_len, 0, (cudaStream_t)stream, resolve, true, false);
     }
     auto value = [&](int id) -> const float* {
         return g->nodes[id].kind == K_INPUT ? g->nodes[id].dev : scratch + region[id];
@@ -1671,7 +1743,7 @@ extern "C" int simtgo_tile_run_stepwise_noalloc(simtgo_tile_graph* g, simtgo_ten
                             one.err.empty() ? "refused" : one.err.c_str());
         float* target = id == t ? dev_out : scratch + region[id];
         auto resolve = [&](int nid) -> const float* { return one.nodes[nid].dev; };
-        rc = run_fused(&one, r, target, nd.n, 0, (cudaStream_t)stream, resolve, true);
+        rc = run_fused(&one, r, target, nd.n, 0, (cudaStream_t)stream, resolve, true, false);
         if (rc) return rc;
     }
     return 0;

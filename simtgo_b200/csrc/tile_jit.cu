@@ -1,0 +1,325 @@
+// tile_jit.cu -- a tile graph's specialised kernel: the lowered program
+// (tile.cu) written out as compile-time constants, compiled for sm_100a at
+// run time by NVRTC and cached per device and program.
+//
+// The reference compiles every distinct graph with NVRTC (tile/run.go:40,
+// kernels cached by source). Here the compiled code is not a new rendering
+// of the graph: it is tile_kernel.cuh's own kernel body, tile_body<BULK, G,
+// S>, instantiated with a struct S that holds the program's instructions and
+// window descriptors as constants (interpret_s), so every instruction's
+// decode, dispatch and operand addressing folds away and the windows' taps
+// are parameter-bank operands, while each value is computed by the same
+// device functions in the same order as the interpreter: the two produce
+// the same bits. The device headers travel inside the library (rtc_headers.inc,
+// written by build.py); NVRTC is opened with dlopen on first use and the
+// module loaded through the runtime's driver entry points, so the library
+// links against neither.
+//
+// Modes (simtgo_tile_set_jit, or SIMTGO_TILE_JIT in the environment at the
+// first tile launch): 0 = the interpreter only; 1 (default) = specialise
+// every program, falling back to the interpreter when NVRTC cannot be opened;
+// 2 = specialise or fail. A program whose compilation fails is an error in
+// modes 1 and 2 (it is a bug, not a missing dependency).
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <atomic>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+
+#include "common.cuh"
+#include "tile_kernel.cuh"
+#include "tile_jit.h"
+
+namespace {
+
+#include "rtc_headers.inc"  // kRtcHeaderNames[], kRtcHeaderSources[], kRtcHeaderCount
+
+// ---- NVRTC, opened on first use ----------------------------------------------
+typedef int nvrtcResult_t;
+typedef struct _nvrtcProgram* nvrtcProgram_t;
+struct Nvrtc {
+    nvrtcResult_t (*create)(nvrtcProgram_t*, const char*, const char*, int, const char* const*,
+                            const char* const*);
+    nvrtcResult_t (*compile)(nvrtcProgram_t, int, const char* const*);
+    nvrtcResult_t (*log_size)(nvrtcProgram_t, size_t*);
+    nvrtcResult_t (*log)(nvrtcProgram_t, char*);
+    nvrtcResult_t (*cubin_size)(nvrtcProgram_t, size_t*);
+    nvrtcResult_t (*cubin)(nvrtcProgram_t, char*);
+    nvrtcResult_t (*destroy)(nvrtcProgram_t*);
+    const char* (*err)(nvrtcResult_t);
+    bool ok = false;
+    std::string why;
+};
+
+Nvrtc g_rtc;
+std::once_flag g_rtc_once;
+
+void open_nvrtc() {
+    void* h = dlopen("libnvrtc.so.12", RTLD_NOW | RTLD_LOCAL);
+    if (!h) h = dlopen("libnvrtc.so", RTLD_NOW | RTLD_LOCAL);
+    if (!h) {
+        const char* e = dlerror();
+        g_rtc.why = std::string("libnvrtc.so.12 could not be opened: ") + (e ? e : "?");
+        return;
+    }
+    bool all = true;
+    auto sym = [&](const char* name) {
+        void* p = dlsym(h, name);
+        all = all && p;
+        return p;
+    };
+    g_rtc.create = (decltype(g_rtc.create))sym("nvrtcCreateProgram");
+    g_rtc.compile = (decltype(g_rtc.compile))sym("nvrtcCompileProgram");
+    g_rtc.log_size = (decltype(g_rtc.log_size))sym("nvrtcGetProgramLogSize");
+    g_rtc.log = (decltype(g_rtc.log))sym("nvrtcGetProgramLog");
+    g_rtc.cubin_size = (decltype(g_rtc.cubin_size))sym("nvrtcGetCUBINSize");
+    g_rtc.cubin = (decltype(g_rtc.cubin))sym("nvrtcGetCUBIN");
+    g_rtc.destroy = (decltype(g_rtc.destroy))sym("nvrtcDestroyProgram");
+    g_rtc.err = (decltype(g_rtc.err))sym("nvrtcGetErrorString");
+    if (!all) {
+        g_rtc.why = "libnvrtc.so.12 lacks an entry point this library needs";
+        return;
+    }
+    g_rtc.ok = true;
+}
+
+// ---- driver entry points ------------------------------------------------------
+struct Drv {
+    CUresult (*load)(CUmodule*, const void*);
+    CUresult (*get_fn)(CUfunction*, CUmodule, const char*);
+    CUresult (*set_attr)(CUfunction, CUfunction_attribute, int);
+    CUresult (*launch)(CUfunction, unsigned, unsigned, unsigned, unsigned, unsigned, unsigned,
+                       unsigned, CUstream, void**, void**);
+    CUresult (*occupancy)(int*, CUfunction, int, size_t);
+    CUresult (*err)(CUresult, const char**);
+    bool ok = false;
+};
+Drv g_drv;
+std::once_flag g_drv_once;
+
+void open_driver() {
+    bool all = true;
+    auto ep = [&](const char* name) {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint(name, &fn, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            fn = nullptr;
+        all = all && fn;
+        return fn;
+    };
+    g_drv.load = (decltype(g_drv.load))ep("cuModuleLoadData");
+    g_drv.get_fn = (decltype(g_drv.get_fn))ep("cuModuleGetFunction");
+    g_drv.set_attr = (decltype(g_drv.set_attr))ep("cuFuncSetAttribute");
+    g_drv.launch = (decltype(g_drv.launch))ep("cuLaunchKernel");
+    g_drv.occupancy = (decltype(g_drv.occupancy))ep("cuOccupancyMaxActiveBlocksPerMultiprocessor");
+    g_drv.err = (decltype(g_drv.err))ep("cuGetErrorString");
+    g_drv.ok = all;
+}
+
+int drv_status(CUresult r, const char* what) {
+    if (r == CUDA_SUCCESS) return 0;
+    const char* s = nullptr;
+    if (g_drv.err) g_drv.err(r, &s);
+    return sg::fail(SIMTGO_EDEVICE, "tile: %s failed: %s (CUresult %d)", what, s ? s : "?",
+                    (int)r);
+}
+
+// ---- mode and counters --------------------------------------------------------
+std::atomic<int> g_mode{-1};
+std::atomic<int64_t> g_compiled{0}, g_launches{0};
+
+int mode() {
+    int m = g_mode.load();
+    if (m < 0) {
+        const char* e = getenv("SIMTGO_TILE_JIT");
+        int v = 1;
+        if (e && (e[0] == '0' || e[0] == '1' || e[0] == '2') && e[1] == 0) v = e[0] - '0';
+        int expect = -1;
+        g_mode.compare_exchange_strong(expect, v);
+        m = g_mode.load();
+    }
+    return m;
+}
+
+// The prelude every specialised source starts with: NVRTC has no C library
+// headers, so the integer types and limits the device headers use come from
+// here, and CUtensorMap (only named by tma.cuh's device helpers) is an
+// opaque 128-byte type.
+const char* kPrelude =
+    "typedef signed char int8_t; typedef short int16_t; typedef int int32_t;\n"
+    "typedef long long int64_t; typedef unsigned char uint8_t;\n"
+    "typedef unsigned short uint16_t; typedef unsigned int uint32_t;\n"
+    "typedef unsigned long long uint64_t; typedef unsigned long long uintptr_t;\n"
+    "#define INT32_MAX 2147483647\n"
+    "#define INT32_MIN (-2147483647 - 1)\n"
+    "#define INT64_MAX 9223372036854775807LL\n"
+    "struct alignas(64) CUtensorMap { unsigned long long opaque[16]; };\n";
+
+struct Entry {
+    CUmodule mod = nullptr;
+    CUfunction fn = nullptr;
+};
+std::mutex g_mu;
+std::unordered_map<std::string, Entry> g_cache;  // key: device | source
+
+int compile_source(const std::string& src, std::string* cubin) {
+    nvrtcProgram_t prog = nullptr;
+    nvrtcResult_t r = g_rtc.create(&prog, src.c_str(), "tile_spec.cu", kRtcHeaderCount,
+                                   kRtcHeaderSources, kRtcHeaderNames);
+    if (r) return sg::fail(SIMTGO_EDEVICE, "tile: nvrtcCreateProgram: %s", g_rtc.err(r));
+    const std::string taps = "-DSIMTGO_TILE_MAX_TAPS=" + std::to_string(SIMTGO_TILE_MAX_TAPS);
+    const char* opts[] = {"-arch=sm_100a", "-std=c++17", "--fmad=false", taps.c_str()};
+    r = g_rtc.compile(prog, 4, opts);
+    if (r) {
+        size_t n = 0;
+        g_rtc.log_size(prog, &n);
+        std::string log(n, '\0');
+        if (n) g_rtc.log(prog, &log[0]);
+        g_rtc.destroy(&prog);
+        if (log.size() > 1500) log.resize(1500);
+        return sg::fail(SIMTGO_EDEVICE, "tile: run-time compilation of the graph's kernel failed: "
+                                        "%s\n%s",
+                        g_rtc.err(r), log.c_str());
+    }
+    size_t n = 0;
+    g_rtc.cubin_size(prog, &n);
+    cubin->assign(n, '\0');
+    if (n) g_rtc.cubin(prog, &(*cubin)[0]);
+    g_rtc.destroy(&prog);
+    return 0;
+}
+
+}  // namespace
+
+namespace tilejit {
+
+std::string spec_source(const tilek::Program& P, bool bulk, int g) {
+    std::string s;
+    char line[1024];
+    s += kPrelude;
+    s += "#include \"tile_kernel.cuh\"\n";
+    s += "struct Spec {\n";
+    snprintf(line, sizeof line,
+             "  static constexpr int n_fir = %d, main_start = %d, reduce = %d;\n", P.n_fir,
+             P.main_start, P.reduce);
+    s += line;
+    s += "  static constexpr tilek::FirC fir[] = {";
+    if (P.n_fir == 0) s += "{0, 0, 0, 0}";
+    for (int f = 0; f < P.n_fir; f++) {
+        snprintf(line, sizeof line, "%s{%d, %d, %d, %d}", f ? ", " : "", P.fir[f].start,
+                 P.fir[f].taps, P.fir[f].head, P.fir[f].tile4);
+        s += line;
+    }
+    s += "};\n  static constexpr tilek::Insn code[] = {\n";
+    for (int pc = 0; pc < P.n_code; pc++) {
+        const tilek::Insn& in = P.code[pc];
+        snprintf(line, sizeof line, "    {%u, %u, %u, %u, %u, 0.0f, 0u},\n", (unsigned)in.op,
+                 (unsigned)in.flags, (unsigned)in.a, (unsigned)in.b, (unsigned)in.d);
+        s += line;
+    }
+    s += "  };\n};\n";
+    snprintf(line, sizeof line,
+             "extern \"C\" __global__ void __launch_bounds__(%d, %d)\n"
+             "k_tile_spec(const __grid_constant__ tilek::Program P, float* __restrict__ out,\n"
+             "            int64_t n, int64_t halo, bool vec, bool in_vec, int32_t hs,\n"
+             "            int32_t stages4, int32_t nst, uint32_t* wd,\n"
+             "            int64_t* __restrict__ out_idx, int64_t idx_base) {\n",
+             tilek::kThreads, g == tilek::kG ? 3 : 2);
+    s += line;
+    snprintf(line, sizeof line,
+             "  tilek::tile_body<%s, %d, Spec>(P, out, n, halo, vec, in_vec, hs, stages4, nst, wd,\n"
+             "                                 out_idx, idx_base);\n}\n",
+             bulk ? "true" : "false", g);
+    s += line;
+    return s;
+}
+
+int get(const tilek::Program& P, bool bulk, int g, int dyn_max, CUfunction* out) {
+    *out = nullptr;
+    const int m = mode();
+    if (m == 0) return 0;
+    std::call_once(g_rtc_once, open_nvrtc);
+    std::call_once(g_drv_once, open_driver);
+    if (!g_rtc.ok || !g_drv.ok) {
+        if (m == 1) return 0;
+        return sg::fail(SIMTGO_EDEVICE, "tile: specialised kernels are required but %s",
+                        !g_rtc.ok ? g_rtc.why.c_str()
+                                  : "the driver's module entry points are not available");
+    }
+    int dev = -1;
+    int rc = sg::cuda_status(cudaGetDevice(&dev), "cudaGetDevice");
+    if (rc) return rc;
+    const std::string src = spec_source(P, bulk, g);
+    const std::string key = std::to_string(dev) + "|" + src;
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto it = g_cache.find(key);
+    if (it != g_cache.end()) {
+        *out = it->second.fn;
+        return 0;
+    }
+    std::string cubin;
+    if ((rc = compile_source(src, &cubin))) return rc;
+    Entry e;
+    if ((rc = drv_status(g_drv.load(&e.mod, cubin.data()), "cuModuleLoadData"))) return rc;
+    if ((rc = drv_status(g_drv.get_fn(&e.fn, e.mod, "k_tile_spec"), "cuModuleGetFunction")))
+        return rc;
+    if ((rc = drv_status(
+             g_drv.set_attr(e.fn, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, dyn_max),
+             "cuFuncSetAttribute")))
+        return rc;
+    g_cache.emplace(key, e);
+    g_compiled.fetch_add(1);
+    *out = e.fn;
+    return 0;
+}
+
+int compile_only(const tilek::Program& P, bool bulk, int g) {
+    std::call_once(g_rtc_once, open_nvrtc);
+    if (!g_rtc.ok) return sg::fail(SIMTGO_EDEVICE, "tile: %s", g_rtc.why.c_str());
+    std::string cubin;
+    return compile_source(spec_source(P, bulk, g), &cubin);
+}
+
+int occupancy(CUfunction fn, size_t smem, int* blocks) {
+    return drv_status(g_drv.occupancy(blocks, fn, tilek::kThreads, smem),
+                      "cuOccupancyMaxActiveBlocksPerMultiprocessor(tile)");
+}
+
+int launch(CUfunction fn, int blocks, size_t smem, cudaStream_t s, void** args) {
+    g_launches.fetch_add(1);
+    return drv_status(g_drv.launch(fn, blocks, 1, 1, tilek::kThreads, 1, 1, (unsigned)smem,
+                                   (CUstream)s, args, nullptr),
+                      "cuLaunchKernel(tile)");
+}
+
+}  // namespace tilejit
+
+extern "C" {
+
+int simtgo_tile_set_jit(int32_t m) {
+    sg::clear_error();
+    if (m < 0 || m > 2)
+        return sg::fail(SIMTGO_EARG, "tile: JIT mode %d is not 0 (off), 1 (on) or 2 (required)",
+                        (int)m);
+    g_mode.store(m);
+    return 0;
+}
+
+int simtgo_tile_jit_info(int32_t* m, int32_t* available, int64_t* compiled, int64_t* launches) {
+    sg::clear_error();
+    std::call_once(g_rtc_once, open_nvrtc);
+    if (m) *m = mode();
+    if (available) *available = g_rtc.ok ? 1 : 0;
+    if (compiled) *compiled = g_compiled.load();
+    if (launches) *launches = g_launches.load();
+    return 0;
+}
+
+}  // extern "C"

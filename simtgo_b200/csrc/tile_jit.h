@@ -1,0 +1,32 @@
+// tile_jit.h -- host interface of tile_jit.cu (a tile graph's specialised
+// kernel, compiled at run time) for tile.cu.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <string>
+
+#include "tile_kernel.cuh"
+
+namespace tilejit {
+
+// The source of the specialised kernel for program P (instructions and
+// window descriptors as constants; inputs, taps and SCALE factors stay in
+// the parameter block).
+std::string spec_source(const tilek::Program& P, bool bulk, int g);
+
+// The compiled kernel for P on the current device (compiled and cached on
+// first use, its dynamic shared memory limit set to dyn_max), or nullptr
+// with 0 when specialisation is off or (mode 1) NVRTC is unavailable.
+int get(const tilek::Program& P, bool bulk, int g, int dyn_max, CUfunction* out);
+
+// Resident blocks per SM of fn at kThreads threads and smem bytes.
+int occupancy(CUfunction fn, size_t smem, int* blocks);
+
+// Launches fn (the k_tile parameter list in args) on stream s.
+int launch(CUfunction fn, int blocks, size_t smem, cudaStream_t s, void** args);
+
+// Compiles the specialised source of P without loading it (no GPU needed).
+int compile_only(const tilek::Program& P, bool bulk, int g);
+
+}  // namespace tilejit

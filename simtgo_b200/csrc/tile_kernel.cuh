@@ -5,7 +5,9 @@
 // k_red_level / k_red_fill (the levels of a reduction above its chunks).
 // tile.cu's header describes the design; this file is its device code.
 #pragma once
+#ifndef __CUDACC_RTC__
 #include <stdint.h>
+#endif
 
 #include "common.cuh"
 #include "exact.cuh"
@@ -181,46 +183,85 @@ __device__ __forceinline__ void fir_step(float (&acc)[4], const float4& lo, cons
             for (int j = 0; j < 4; j++) acc[j] = __fmaf_rn(hv[u], w[4 + j - u], acc[j]);
 }
 
+// Eight taps i0 .. i0+7 (hva, hvb) on the G groups of the thread, whose
+// window float4 at tap i0 (a multiple of 4) is tw[256 k - i0/4]: three
+// window loads per group, no predicates. No window value is carried from
+// one step to the next: a carried float4 costs four register moves per
+// step, a third load one shared load (measured at 2^28: a 31-tap window
+// 0.781 -> 0.775 ms).
+template <int G>
+__device__ __forceinline__ void fir_step8(float (&acc)[G][4], const float4* tw, int i0,
+                                          const float (&hva)[4], const float (&hvb)[4]) {
+#pragma unroll
+    for (int k = 0; k < G; k++) {
+        const float4 hi = tw[kThreads * k - i0 / 4];
+        const float4 m = tw[kThreads * k - i0 / 4 - 1];
+        const float4 lo = tw[kThreads * k - i0 / 4 - 2];
+        fir_step<false>(acc[k], m, hi, hva, 4);
+        fir_step<false>(acc[k], lo, m, hvb, 4);
+    }
+}
+// The last 1-7 taps, 4 (nk <= 4 of them) at a time.
+template <int G>
+__device__ __forceinline__ void fir_step4(float (&acc)[G][4], const float4* tw, int i0,
+                                          const float (&hv)[4], int nk) {
+#pragma unroll
+    for (int k = 0; k < G; k++) {
+        const float4 hi = tw[kThreads * k - i0 / 4];
+        const float4 lo = tw[kThreads * k - i0 / 4 - 1];
+        fir_step<true>(acc[k], lo, hi, hv, nk);
+    }
+}
+
+// Window f accumulated at the thread's positions, its descriptor and taps
+// read from shared memory (the interpreter).
 template <int G>
 __device__ __forceinline__ void fir_acc(float4 (&A)[G], const Ctx& c, int f, int woff4) {
     const int4 fd = c.fir[f];
     const int taps = fd.y & (kSyncAfter - 1);
     const float4* h4 = reinterpret_cast<const float4*>(c.taps_s + f * kMaxTaps);
-    // Group k's window float4 at tap i0 (a multiple of 4): tw[k][-i0/4].
     const float4* tw = c.S + fd.w + threadIdx.x + fd.z / 4 + woff4;
     float acc[G][4];
 #pragma unroll
     for (int k = 0; k < G; k++)
 #pragma unroll
         for (int j = 0; j < 4; j++) acc[k][j] = 0.0f;
-    // Whole steps of 8 taps, three window loads per group, no predicates.
-    // No window value is carried from one step to the next: a carried float4
-    // costs four register moves per step, a third load one shared load
-    // (measured at 2^28: a 31-tap window 0.781 -> 0.775 ms).
     int i0 = 0;
     for (; i0 + 8 <= taps; i0 += 8) {
         const float4 ha = h4[i0 / 4], hb = h4[i0 / 4 + 1];
         const float hva[4] = {ha.x, ha.y, ha.z, ha.w}, hvb[4] = {hb.x, hb.y, hb.z, hb.w};
-#pragma unroll
-        for (int k = 0; k < G; k++) {
-            const float4 hi = tw[kThreads * k - i0 / 4];
-            const float4 m = tw[kThreads * k - i0 / 4 - 1];
-            const float4 lo = tw[kThreads * k - i0 / 4 - 2];
-            fir_step<false>(acc[k], m, hi, hva, 4);
-            fir_step<false>(acc[k], lo, m, hvb, 4);
-        }
+        fir_step8<G>(acc, tw, i0, hva, hvb);
     }
-    // The last 1-7 taps, 4 at a time.
     for (; i0 < taps; i0 += 4) {
         const float4 hk = h4[i0 / 4];
         const float hv[4] = {hk.x, hk.y, hk.z, hk.w};
-        const int nk = min(4, taps - i0);
+        fir_step4<G>(acc, tw, i0, hv, min(4, taps - i0));
+    }
 #pragma unroll
-        for (int k = 0; k < G; k++) {
-            const float4 hi = tw[kThreads * k - i0 / 4];
-            const float4 lo = tw[kThreads * k - i0 / 4 - 1];
-            fir_step<true>(acc[k], lo, hi, hv, nk);
-        }
+    for (int k = 0; k < G; k++) A[k] = make_float4(acc[k][0], acc[k][1], acc[k][2], acc[k][3]);
+}
+
+// The same accumulation with TAPS and the tile's place compile-time
+// constants (a graph's specialised kernel): both loops unroll completely
+// and the taps h[] are read from the kernel's parameter block, where each
+// is an operand of its FMAs.
+template <int G, int TAPS>
+__device__ __forceinline__ void fir_acc_static(float4 (&A)[G], const float4* tw, const float* h) {
+    float acc[G][4];
+#pragma unroll
+    for (int k = 0; k < G; k++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) acc[k][j] = 0.0f;
+#pragma unroll
+    for (int i0 = 0; i0 + 8 <= TAPS; i0 += 8) {
+        const float hva[4] = {h[i0], h[i0 + 1], h[i0 + 2], h[i0 + 3]};
+        const float hvb[4] = {h[i0 + 4], h[i0 + 5], h[i0 + 6], h[i0 + 7]};
+        fir_step8<G>(acc, tw, i0, hva, hvb);
+    }
+#pragma unroll
+    for (int i0 = TAPS / 8 * 8; i0 < TAPS; i0 += 4) {
+        const float hv[4] = {h[i0], h[i0 + 1], h[i0 + 2], h[i0 + 3]};
+        fir_step4<G>(acc, tw, i0, hv, TAPS - i0 < 4 ? TAPS - i0 : 4);
     }
 #pragma unroll
     for (int k = 0; k < G; k++) A[k] = make_float4(acc[k][0], acc[k][1], acc[k][2], acc[k][3]);
@@ -247,13 +288,119 @@ __device__ __forceinline__ float4 mask_outside(float4 v, int64_t p, const Ctx& c
     return make_float4(f[0], f[1], f[2], f[3]);
 }
 
+// One instruction of a run (the order of its parts is the format's: load,
+// operation, temporary, window tile, output). The hooks give what depends
+// on where the program lives: hk.win(in, c, r, A) accumulates the window
+// the instruction names (OP_FIRACC), hk.tile_of(in, c) is the float4
+// offset of the tile it stages (F_STAGE), hk.imm(in) the SCALE factor. The
+// interpreter's hooks read the program in shared memory, a graph's
+// specialised kernel's are compile-time constants and its parameter block.
+// In DIRECT mode (BULK false) an input operand is read from HBM at the
+// run's positions. Returns true at the program's last instruction.
+template <bool BULK, bool FULL, int G, class Hooks>
+__device__ __forceinline__ bool exec(const Insn& in, const Hooks& hk, const Ctx& c, const Run& r,
+                                     float4 (&A)[G], const int t) {
+    // Group k of operand M(x) (inactive groups: A itself, nothing is read).
+    auto operand = [&](int x, bool input, int k) -> float4 {
+        if (!FULL && !((r.gm >> k) & 1)) return A[k];
+        if (!BULK && input) return gload4(c.in[x], r.p0 + 4 * (t + kThreads * k), c);
+        return c.S[x + (input ? r.sh_in : 0) + t + kThreads * k];
+    };
+    if (in.flags & F_LOADA) {
+#pragma unroll
+        for (int k = 0; k < G; k++) A[k] = operand(in.a, in.flags & F_IN_A, k);
+    }
+    // The second operand of a binary operation, read inside its case.
+    auto binop = [&](int k) -> float4 {
+        return (in.flags & F_SELF) ? A[k] : operand(in.b, in.flags & F_IN_B, k);
+    };
+    switch (in.op) {
+        case OP_ADD:
+#pragma unroll
+            for (int k = 0; k < G; k++) A[k] = f4_add(A[k], binop(k));
+            break;
+        case OP_MUL:
+#pragma unroll
+            for (int k = 0; k < G; k++) A[k] = f4_mul(A[k], binop(k));
+            break;
+        case OP_HYPOT:
+#pragma unroll
+            for (int k = 0; k < G; k++) A[k] = f4_hypot(A[k], binop(k));
+            break;
+        case OP_SCALE:
+#pragma unroll
+            for (int k = 0; k < G; k++) A[k] = f4_scale(hk.imm(in), A[k]);
+            break;
+        case OP_SQRT:
+#pragma unroll
+            for (int k = 0; k < G; k++) A[k] = f4_sqrt(A[k]);
+            break;
+        case OP_ABS:
+#pragma unroll
+            for (int k = 0; k < G; k++) A[k] = f4_abs(A[k]);
+            break;
+        case OP_FIRACC:
+            hk.win(in, c, r, A);
+            break;
+        default:
+            break;  // OP_END: no operation
+    }
+    if (in.flags & (F_STA | F_STAGE | F_STORE | F_END)) {
+        if (in.flags & F_STA) {
+#pragma unroll
+            for (int k = 0; k < G; k++)
+                if (FULL || ((r.gm >> k) & 1)) c.S[in.d + t + kThreads * k] = A[k];
+        }
+        if (in.flags & F_STAGE) {
+            float4* dst = c.S + hk.tile_of(in, c) + r.sh_st + t;
+#pragma unroll
+            for (int k = 0; k < G; k++)
+                if (FULL || ((r.gm >> k) & 1))
+                    dst[kThreads * k] =
+                        r.edge ? mask_outside(A[k], r.p0 + 4 * (t + kThreads * k), c) : A[k];
+        }
+        // A run inside [0, n) with a 16-byte aligned output stores its
+        // float4s unchecked; the rest element by element.
+        if ((in.flags & F_STORE) && !r.edge && c.vec) {
+            float* o = c.out + r.p0 + 4 * t;
+#pragma unroll
+            for (int k = 0; k < G; k++) st_stream_f4(o + 4 * kThreads * k, A[k]);
+        } else if (in.flags & F_STORE) {
+#pragma unroll
+            for (int k = 0; k < G; k++) {
+                const int64_t p = r.p0 + 4 * (t + kThreads * k);
+                if (c.vec && p + 3 < c.n) {
+                    st_stream_f4(c.out + p, A[k]);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 4; j++)
+                        if (p + j < c.n) c.out[p + j] = f4_get(A[k], j);
+                }
+            }
+        }
+        if (in.flags & F_END) return true;
+    }
+    return false;
+}
+
+template <int G>
+struct InterpHooks {
+    __device__ __forceinline__ float imm(const Insn& in) const { return in.imm; }
+    __device__ __forceinline__ void win(const Insn& in, const Ctx& c, const Run& r,
+                                        float4 (&A)[G]) const {
+        fir_acc<G>(A, c, in.b, r.woff4);
+    }
+    __device__ __forceinline__ int tile_of(const Insn& in, const Ctx& c) const {
+        return c.fir[in.d].w;
+    }
+};
+
 // Runs the program from pc until an instruction with F_END, leaving the
 // last value in A (which a reduction consumes). Inlined into
 // k_tile twice: FULL for runs where all of the thread's groups take part
 // (the chunk), and the general form for a window's head run. (Loading the
 // next instruction ahead measured slower: it costs more instructions than
-// the shared-load latency it hides.) In DIRECT mode (BULK false) an input
-// operand is read from HBM at the run's positions.
+// the shared-load latency it hides.)
 template <bool BULK, bool FULL, int G>
 __device__ __forceinline__ void interpret(const Insn* code, int pc, const Ctx& c, const Run& r,
                                           float4 (&A)[G]) {
@@ -266,87 +413,49 @@ __device__ __forceinline__ void interpret(const Insn* code, int pc, const Ctx& c
     }
     for (;;) {
         const Insn in = code[pc++];
-        // Group k of operand M(x) (inactive groups: A itself, nothing is read).
-        auto operand = [&](int x, bool input, int k) -> float4 {
-            if (!FULL && !((r.gm >> k) & 1)) return A[k];
-            if (!BULK && input) return gload4(c.in[x], r.p0 + 4 * (t + kThreads * k), c);
-            return c.S[x + (input ? r.sh_in : 0) + t + kThreads * k];
-        };
-        if (in.flags & F_LOADA) {
-#pragma unroll
-            for (int k = 0; k < G; k++) A[k] = operand(in.a, in.flags & F_IN_A, k);
-        }
-        // The second operand of a binary operation, read inside its case.
-        auto binop = [&](int k) -> float4 {
-            return (in.flags & F_SELF) ? A[k] : operand(in.b, in.flags & F_IN_B, k);
-        };
-        switch (in.op) {
-            case OP_ADD:
-#pragma unroll
-                for (int k = 0; k < G; k++) A[k] = f4_add(A[k], binop(k));
-                break;
-            case OP_MUL:
-#pragma unroll
-                for (int k = 0; k < G; k++) A[k] = f4_mul(A[k], binop(k));
-                break;
-            case OP_HYPOT:
-#pragma unroll
-                for (int k = 0; k < G; k++) A[k] = f4_hypot(A[k], binop(k));
-                break;
-            case OP_SCALE:
-#pragma unroll
-                for (int k = 0; k < G; k++) A[k] = f4_scale(in.imm, A[k]);
-                break;
-            case OP_SQRT:
-#pragma unroll
-                for (int k = 0; k < G; k++) A[k] = f4_sqrt(A[k]);
-                break;
-            case OP_ABS:
-#pragma unroll
-                for (int k = 0; k < G; k++) A[k] = f4_abs(A[k]);
-                break;
-            case OP_FIRACC:
-                fir_acc<G>(A, c, in.b, r.woff4);
-                break;
-            default:
-                break;  // OP_END: no operation
-        }
-        if (in.flags & (F_STA | F_STAGE | F_STORE | F_END)) {
-            if (in.flags & F_STA) {
-#pragma unroll
-                for (int k = 0; k < G; k++)
-                    if (FULL || ((r.gm >> k) & 1)) c.S[in.d + t + kThreads * k] = A[k];
-            }
-            if (in.flags & F_STAGE) {
-                float4* dst = c.S + c.fir[in.d].w + r.sh_st + t;
-#pragma unroll
-                for (int k = 0; k < G; k++)
-                    if (FULL || ((r.gm >> k) & 1))
-                        dst[kThreads * k] =
-                            r.edge ? mask_outside(A[k], r.p0 + 4 * (t + kThreads * k), c) : A[k];
-            }
-            // A run inside [0, n) with a 16-byte aligned output stores its
-            // float4s unchecked; the rest element by element.
-            if ((in.flags & F_STORE) && !r.edge && c.vec) {
-                float* o = c.out + r.p0 + 4 * t;
-#pragma unroll
-                for (int k = 0; k < G; k++) st_stream_f4(o + 4 * kThreads * k, A[k]);
-            } else if (in.flags & F_STORE) {
-#pragma unroll
-                for (int k = 0; k < G; k++) {
-                    const int64_t p = r.p0 + 4 * (t + kThreads * k);
-                    if (c.vec && p + 3 < c.n) {
-                        st_stream_f4(c.out + p, A[k]);
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < 4; j++)
-                            if (p + j < c.n) c.out[p + j] = f4_get(A[k], j);
-                    }
-                }
-            }
-            if (in.flags & F_END) return;
-        }
+        if (exec<BULK, FULL, G>(in, InterpHooks<G>{}, c, r, A, t)) return;
     }
+}
+
+// ---- a graph's specialised kernel ------------------------------------------------
+// The same program with every instruction and window descriptor a
+// compile-time constant: a generated struct S (one per distinct program,
+// compiled at run time for sm_100a) supplies
+//   static constexpr Insn code[];       the program (imm unused: SCALE
+//                                       factors come from the parameter block)
+//   static constexpr FirC fir[];        per window (at least one entry)
+//   static constexpr int n_fir, main_start, reduce;
+// and exec() runs each instruction with its operation, flags and
+// addresses folded, so nothing is decoded or dispatched at run time, and a
+// window's taps are parameter-bank operands of its FMAs. The arithmetic is
+// exec()'s and fir_acc_core()'s, the interpreter's own: both produce the
+// same bits.
+struct FirC {
+    int32_t start, taps, head, tile4;  // as FirDesc (taps | kSyncAfter)
+};
+
+template <int G, int PC, int TAPS, int WTILE, int DTILE>
+struct StaticHooks {
+    const Program& P;
+    __device__ __forceinline__ float imm(const Insn&) const { return P.code[PC].imm; }
+    __device__ __forceinline__ void win(const Insn& in, const Ctx& c, const Run& r,
+                                        float4 (&A)[G]) const {
+        fir_acc_static<G, TAPS>(A, c.S + WTILE + threadIdx.x + r.woff4, P.fir[in.b].h);
+    }
+    __device__ __forceinline__ int tile_of(const Insn&, const Ctx&) const { return DTILE; }
+};
+
+template <class S, int PC, bool BULK, bool FULL, int G>
+__device__ __forceinline__ void interpret_s(const Program& P, const Ctx& c, const Run& r,
+                                            float4 (&A)[G]) {
+    constexpr Insn in = S::code[PC];
+    constexpr int FW = in.op == OP_FIRACC ? in.b : 0;
+    constexpr int TAPS = S::fir[FW].taps & (kSyncAfter - 1);
+    constexpr int WTILE = S::fir[FW].tile4 + S::fir[FW].head / 4;
+    constexpr int DTILE = (in.flags & F_STAGE) ? S::fir[in.d].tile4 : 0;
+    (void)exec<BULK, FULL, G>(in, StaticHooks<G, PC, TAPS, WTILE, DTILE>{P}, c, r, A,
+                              (int)threadIdx.x);
+    if constexpr (!(in.flags & F_END)) interpret_s<S, PC + 1, BULK, FULL, G>(P, c, r, A);
 }
 
 // ---- reductions ---------------------------------------------------------------
@@ -900,11 +1009,81 @@ __device__ __forceinline__ ChunkSpan chunk_span(int64_t cb, int hs, int64_t n, i
 // run ahead of each other, and the last of the eight warps to finish with a
 // stage (a shared counter per stage) refills it, instead of thread 0 after a
 // block barrier.
-template <bool BULK, int G>
-__global__ void __launch_bounds__(kThreads, G == kG ? 3 : 2)
-    k_tile(const __grid_constant__ Program P, float* __restrict__ out, int64_t n, int64_t halo,
-           bool vec, bool in_vec, int32_t hs, int32_t stages4, int32_t nst, uint32_t* wd,
-           int64_t* __restrict__ out_idx, int64_t idx_base) {
+//
+// tile_body is the kernel's code for both forms: S = Interp runs the
+// program from shared memory (k_tile), any other S is a graph's generated
+// struct (interpret_s above) and the body is that graph's kernel.
+struct Interp {};
+template <class S>
+struct is_interp {
+    static constexpr bool value = false;
+};
+template <>
+struct is_interp<Interp> {
+    static constexpr bool value = true;
+};
+
+// A specialised kernel's jobs for one chunk, J = 2f (window f's head run,
+// first chunk of a range only), 2f + 1 (window f over the chunk), 2 n_fir
+// (the main program): the interpreter's job loop with every descriptor a
+// constant.
+template <class S, int PC, bool BULK, bool FULL, int G>
+__device__ __forceinline__ void run_s(const Program& P, const Ctx& c, const Run& r,
+                                      float4 (&A)[G]) {
+    if (!FULL) {
+#pragma unroll
+        for (int k = 0; k < G; k++) A[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    interpret_s<S, PC, BULK, FULL, G>(P, c, r, A);
+}
+template <class S, int J, bool BULK, int G>
+__device__ __forceinline__ void jobs_s(const Program& P, const Ctx& cx, int32_t in4, int32_t hs,
+                                       int64_t cb, bool first, bool edge, float4 (&A)[G]) {
+    constexpr int NF = S::n_fir;
+    const int tid = threadIdx.x;
+    Run r;
+    r.edge = edge;
+    if constexpr (J < 2 * NF) {
+        constexpr FirC fd = S::fir[J >> 1];
+        constexpr int head4 = fd.head / 4;
+        if constexpr (!(J & 1)) {
+            r.sh_in = in4 + (hs - fd.head) / 4;
+            r.sh_st = 0;
+            r.woff4 = -head4;
+            r.gm = first && tid < head4 ? 1u : 0u;
+            r.p0 = cb - fd.head;
+            if (r.gm) run_s<S, fd.start, BULK, false, G>(P, cx, r, A);
+        } else {
+            if (!first && tid >= kThreads - head4) {
+                float4* tile = cx.S + fd.tile4;
+                const int q = tid - (kThreads - head4);
+                tile[q] = tile[chunk_of(G) / 4 + q];
+            }
+            r.sh_in = in4 + hs / 4;
+            r.sh_st = head4;
+            r.woff4 = 0;
+            r.gm = (1u << G) - 1;
+            r.p0 = cb;
+            run_s<S, fd.start, BULK, true, G>(P, cx, r, A);
+            if constexpr (J + 1 == 2 * NF || (fd.taps & kSyncAfter)) __syncthreads();
+        }
+        jobs_s<S, J + 1, BULK, G>(P, cx, in4, hs, cb, first, edge, A);
+    } else {
+        r.sh_in = in4 + hs / 4;
+        r.sh_st = 0;
+        r.woff4 = 0;
+        r.gm = (1u << G) - 1;
+        r.p0 = cb;
+        run_s<S, S::main_start, BULK, true, G>(P, cx, r, A);
+    }
+}
+
+template <bool BULK, int G, class S>
+__device__ __forceinline__ void tile_body(const Program& P, float* __restrict__ out, int64_t n,
+                                          int64_t halo, bool vec, bool in_vec, int32_t hs,
+                                          int32_t stages4, int32_t nst, uint32_t* wd,
+                                          int64_t* __restrict__ out_idx, int64_t idx_base) {
+    constexpr bool SPEC = !is_interp<S>::value;
     constexpr int CH = chunk_of(G), CH4 = CH / 4;
     __shared__ __align__(8) uint64_t bars[kMaxStages];   // stage s loaded
     __shared__ int rel[kMaxStages];  // warps done with stage s (window-free graphs)
@@ -919,14 +1098,18 @@ __global__ void __launch_bounds__(kThreads, G == kG ? 3 : 2)
     float* stages = reinterpret_cast<float*>(sm4 + stages4);
     const int tid = threadIdx.x;
     const int64_t nchunks = (n + CH - 1) / CH;
-    for (int i = tid; i < code_cap; i += kThreads)
-        code_s[i] = i < P.n_code ? P.code[i] : Insn{OP_END, F_END, 0, 0, 0, 0.0f, 0};
+    // The program and its windows in shared memory (a specialised kernel
+    // has them as constants and reads its taps from the parameter block).
+    if constexpr (!SPEC) {
+        for (int i = tid; i < code_cap; i += kThreads)
+            code_s[i] = i < P.n_code ? P.code[i] : Insn{OP_END, F_END, 0, 0, 0, 0.0f, 0};
+        for (int f = tid; f < P.n_fir; f += kThreads)
+            fir_s[f] = make_int4(P.fir[f].start, P.fir[f].taps, P.fir[f].head, P.fir[f].tile4);
+        for (int f = 0; f < P.n_fir; f++)
+            for (int k = tid; k < kMaxTaps; k += kThreads)
+                taps_s[f * kMaxTaps + k] = P.fir[f].h[k];  // zero past taps
+    }
     for (int k = tid; k < P.n_in; k += kThreads) in_s[k] = P.in[k];
-    for (int f = tid; f < P.n_fir; f += kThreads)
-        fir_s[f] = make_int4(P.fir[f].start, P.fir[f].taps, P.fir[f].head, P.fir[f].tile4);
-    for (int f = 0; f < P.n_fir; f++)
-        for (int k = tid; k < kMaxTaps; k += kThreads)
-            taps_s[f * kMaxTaps + k] = P.fir[f].h[k];  // zero past taps
 
     const int64_t per_block = (nchunks + gridDim.x - 1) / gridDim.x;
     const int64_t c0 = blockIdx.x * per_block;
@@ -964,7 +1147,19 @@ __global__ void __launch_bounds__(kThreads, G == kG ? 3 : 2)
     cx.halo = halo;
     cx.vec = vec;
     cx.in_vec = in_vec;
-    const int nf = P.n_fir;
+    int nf;
+    if constexpr (SPEC)
+        nf = S::n_fir;
+    else
+        nf = P.n_fir;
+    // The reduction, read where it is used (a parameter-bank operand for
+    // the interpreter, a constant for a specialised kernel).
+    auto reduce_kind = [&]() -> int {
+        if constexpr (SPEC)
+            return S::reduce;
+        else
+            return P.reduce;
+    };
     const bool free_run = nf == 0;
     float4 A[G];  // the last run's values (the main program's, for a reduction)
     int s = 0;           // this chunk's stage
@@ -1000,60 +1195,64 @@ __global__ void __launch_bounds__(kThreads, G == kG ? 3 : 2)
             }
         }
         const int32_t in4 = stages4 + s * (stage_floats / 4);
-        // Jobs 2f and 2f+1 stage window f: its head (first chunk only) and
-        // the chunk itself; job 2 nf is the main program over the chunk. One
-        // loop, so the interpreter is inlined once per form.
-        for (int j = 0; j <= 2 * nf; j++) {
-            Run r;
-            int pc;
-            if (j < 2 * nf) {
-                const int4 fd = fir_s[j >> 1];
-                const int head4 = fd.z / 4;
-                pc = fd.x;
-                if (!(j & 1)) {  // head: tile [0, head) = positions [cb - head, cb)
-                    r.sh_in = in4 + (hs - fd.z) / 4;
-                    r.sh_st = 0;
-                    r.woff4 = -head4;
-                    r.gm = first && tid < head4 ? 1u : 0u;
-                    r.p0 = cb - fd.z;
-                } else {  // the chunk: tile [head, head + CH)
-                    // Carry the head over: the previous chunk's last head
-                    // positions sit at tile [CH, CH + head). The
-                    // thread that copies a float4 is the one whose staging
-                    // below overwrites it, so no barrier is needed.
-                    if (!first && tid >= kThreads - head4) {
-                        float4* tile = cx.S + fd.w;
-                        const int q = tid - (kThreads - head4);
-                        tile[q] = tile[CH4 + q];
+        if constexpr (SPEC) {
+            jobs_s<S, 0, BULK, G>(P, cx, in4, hs, cb, first, edge, A);
+        } else {
+            // Jobs 2f and 2f+1 stage window f: its head (first chunk only) and
+            // the chunk itself; job 2 nf is the main program over the chunk. One
+            // loop, so the interpreter is inlined once per form.
+            for (int j = 0; j <= 2 * nf; j++) {
+                Run r;
+                int pc;
+                if (j < 2 * nf) {
+                    const int4 fd = fir_s[j >> 1];
+                    const int head4 = fd.z / 4;
+                    pc = fd.x;
+                    if (!(j & 1)) {  // head: tile [0, head) = positions [cb - head, cb)
+                        r.sh_in = in4 + (hs - fd.z) / 4;
+                        r.sh_st = 0;
+                        r.woff4 = -head4;
+                        r.gm = first && tid < head4 ? 1u : 0u;
+                        r.p0 = cb - fd.z;
+                    } else {  // the chunk: tile [head, head + CH)
+                        // Carry the head over: the previous chunk's last head
+                        // positions sit at tile [CH, CH + head). The
+                        // thread that copies a float4 is the one whose staging
+                        // below overwrites it, so no barrier is needed.
+                        if (!first && tid >= kThreads - head4) {
+                            float4* tile = cx.S + fd.w;
+                            const int q = tid - (kThreads - head4);
+                            tile[q] = tile[CH4 + q];
+                        }
+                        r.sh_in = in4 + hs / 4;
+                        r.sh_st = head4;
+                        r.woff4 = 0;
+                        r.gm = (1u << G) - 1;
+                        r.p0 = cb;
                     }
+                } else {
+                    pc = P.main_start;
                     r.sh_in = in4 + hs / 4;
-                    r.sh_st = head4;
+                    r.sh_st = 0;
                     r.woff4 = 0;
                     r.gm = (1u << G) - 1;
                     r.p0 = cb;
                 }
-            } else {
-                pc = P.main_start;
-                r.sh_in = in4 + hs / 4;
-                r.sh_st = 0;
-                r.woff4 = 0;
-                r.gm = (1u << G) - 1;
-                r.p0 = cb;
+                r.edge = edge;
+                if (r.gm == (1u << G) - 1)
+                    interpret<BULK, true, G>(code_s, pc, cx, r, A);
+                else if (r.gm)
+                    interpret<BULK, false, G>(code_s, pc, cx, r, A);
+                // Windows staged before the main program reads them, and a
+                // window before a later window's staging reads it (chains).
+                if ((j & 1) && (j + 1 == 2 * nf || (fir_s[j >> 1].y & kSyncAfter))) __syncthreads();
             }
-            r.edge = edge;
-            if (r.gm == (1u << G) - 1)
-                interpret<BULK, true, G>(code_s, pc, cx, r, A);
-            else if (r.gm)
-                interpret<BULK, false, G>(code_s, pc, cx, r, A);
-            // Windows staged before the main program reads them, and a
-            // window before a later window's staging reads it (chains).
-            if ((j & 1) && (j + 1 == 2 * nf || (fir_s[j >> 1].y & kSyncAfter))) __syncthreads();
         }
-        if (P.reduce != RED_NONE) {
+        if (reduce_kind() != RED_NONE) {
             const int64_t b0 = c * (G / 2), nb = (n + kChunk - 1) / kChunk;
             float* o = out;
             int64_t* oi = out_idx;
-            switch (P.reduce) {  // uniform: one branch per chunk
+            switch (reduce_kind()) {  // uniform: one branch per chunk
                 case RED_SUM: chunk_warps<RED_SUM, G>(A, cb, n, idx_base, o, oi, b0, nb); break;
                 case RED_MIN: chunk_warps<RED_MIN, G>(A, cb, n, idx_base, o, oi, b0, nb); break;
                 case RED_MAX: chunk_warps<RED_MAX, G>(A, cb, n, idx_base, o, oi, b0, nb); break;
@@ -1091,6 +1290,15 @@ __global__ void __launch_bounds__(kThreads, G == kG ? 3 : 2)
             phase ^= 1u;
         }
     }
+}
+
+template <bool BULK, int G>
+__global__ void __launch_bounds__(kThreads, G == kG ? 3 : 2)
+    k_tile(const __grid_constant__ Program P, float* __restrict__ out, int64_t n, int64_t halo,
+           bool vec, bool in_vec, int32_t hs, int32_t stages4, int32_t nst, uint32_t* wd,
+           int64_t* __restrict__ out_idx, int64_t idx_base) {
+    tile_body<BULK, G, Interp>(P, out, n, halo, vec, in_vec, hs, stages4, nst, wd, out_idx,
+                               idx_base);
 }
 
 }  // namespace tilek

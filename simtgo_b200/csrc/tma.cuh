@@ -6,12 +6,15 @@
 // No load here is a cluster-multicast load: every tensor map covers this GPU's
 // own memory and every CTA fetches its own tiles.
 #pragma once
+#ifndef __CUDACC_RTC__  // run-time compilation (tile_jit.cu) brings its own prelude
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#endif
 
 #include "common.cuh"
 
+#ifndef __CUDACC_RTC__
 namespace sg {
 
 // Encodes a 2-D tiled map over a row-major array of `rows` rows of `inner`
@@ -22,6 +25,7 @@ int tma_encode_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base,
                   CUtensorMapSwizzle swizzle);
 
 }  // namespace sg
+#endif
 
 namespace sgd {
 

@@ -101,6 +101,21 @@ class Tensor:
         L.simtgo_tile_source(g, self.node, buf, need)
         return buf.value.decode()
 
+    def JITSource(self, reduce: int = -1, groups: int = 4, bulk: bool = True,
+                  compile: bool = False) -> str:
+        """The source of this tensor's specialised kernel (the lowered
+        program as compile-time constants, tile_jit.cu) for `groups` float4
+        groups per thread and bulk-copied or directly read inputs; with
+        compile=True NVRTC also compiles it (no GPU needed) and a failure
+        raises."""
+        L, g = self.g._L, self.g._h
+        need = L.simtgo_tile_jit_source(g, self.node, reduce, groups, int(bulk), int(compile),
+                                        None, 0)
+        check(need if need < 0 else 0)
+        buf = C.create_string_buffer(need)
+        L.simtgo_tile_jit_source(g, self.node, reduce, groups, int(bulk), 0, buf, need)
+        return buf.value.decode()
+
     def Materialize(self) -> np.ndarray:
         out = np.empty(max(self.Len(), 0), np.float32)
         check(self.g._L.simtgo_tile_materialize(self.g._h, self.node,
@@ -178,6 +193,21 @@ def Max(t: Tensor) -> Reduction:
 
 def ArgMax(t: Tensor) -> Reduction:
     return Reduction(t, ARGMAX)
+
+
+def SetJIT(mode: int) -> None:
+    """How fused programs run: 0 the interpreter only, 1 (default) each
+    program's specialised kernel when libnvrtc can be opened, 2 the
+    specialised kernel or an error (simtgo_tile_set_jit)."""
+    check(_lib.load().simtgo_tile_set_jit(mode))
+
+
+def JITInfo():
+    """(mode, NVRTC available, programs compiled, specialised launches)."""
+    m, a = C.c_int32(), C.c_int32()
+    c, n = C.c_int64(), C.c_int64()
+    check(_lib.load().simtgo_tile_jit_info(C.byref(m), C.byref(a), C.byref(c), C.byref(n)))
+    return m.value, bool(a.value), c.value, n.value
 
 
 def ShardRange(n_total: int, nranks: int, rank: int):

@@ -1,0 +1,154 @@
+"""GPU parity of the tile track's specialised kernels (each program compiled
+in as constants, tile_jit.cu) against the interpreter they replace and the
+oracle, bit for bit: random graphs in every layout the launcher picks (bulk
+and direct inputs, two and four groups per thread), windows carried across
+chunks, shards with a halo, chained windows and the four reductions. The
+other tile tests run in the default mode, which is the specialised path;
+here each case runs in both modes."""
+import numpy as np
+import pytest
+
+import oracle_lib as O
+from tolerance import assert_agree
+
+torch = pytest.importorskip("torch")
+from simtgo_b200 import tile  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+KINDS = {"sum": tile.Sum, "min": tile.Min, "max": tile.Max, "argmax": tile.ArgMax}
+
+
+@pytest.fixture(autouse=True)
+def restore_mode():
+    mode = tile.JITInfo()[0]
+    yield
+    tile.SetJIT(mode)
+
+
+def both(fn):
+    """fn() with the interpreter (mode 0) and with the specialised kernel
+    required (mode 2); checks that the second ran specialised launches."""
+    tile.SetJIT(0)
+    a = fn()
+    tile.SetJIT(2)
+    before = tile.JITInfo()[3]
+    b = fn()
+    assert tile.JITInfo()[3] > before, "no specialised kernel was launched"
+    return a, b
+
+
+def bits(x):
+    return np.asarray(x, np.float32).view(np.uint32)
+
+
+def test_nvrtc_is_there():
+    mode, available, _, _ = tile.JITInfo()
+    assert available, "libnvrtc could not be opened: tile programs would run interpreted"
+
+
+@pytest.mark.parametrize("seed", range(8))
+def test_random_graphs_both_modes(seed):
+    from test_tile_lowering import _random_graph
+
+    for n in (3001, (1 << 21) + 77):
+        root, nodes = _random_graph(seed, n, 0)
+        interp, spec = both(root.Materialize)
+        assert np.array_equal(bits(interp), bits(spec)), f"seed {seed} n={n}"
+        rc, want = O.tile_eval(nodes, len(nodes) - 1, n, 0)
+        assert rc == 0
+        assert_agree(f"specialised random graph {seed} n={n}", spec, want)
+
+
+@pytest.mark.parametrize("seed", [3, 11])
+def test_unaligned_device_inputs_both_modes(seed):
+    """Inputs and output 4 bytes past a 16-byte boundary: the direct form
+    (inputs read from HBM by the kernel itself)."""
+    from test_tile_lowering import _random_graph
+
+    n = (1 << 20) + 5
+    root, nodes = _random_graph(seed, n, 0)
+    g = tile.New()
+    keep, ids = [], {}
+    for i, nd in enumerate(nodes):
+        if nd["kind"] == "input" and not any(m.get("taps") is nd["data"] for m in nodes):
+            buf = torch.empty(len(nd["data"]) + 1, device="cuda")
+            buf[1:].copy_(torch.from_numpy(nd["data"]))
+            keep.append(buf)
+            ids[i] = g.InputDevice(buf[1:])
+        elif nd["kind"] == "input":
+            ids[i] = None
+        elif nd["kind"] == "fir":
+            ids[i] = tile.FIR(ids[nd["a"]], nd["taps"])
+        elif nd["kind"] == "scale":
+            ids[i] = tile.Scale(ids[nd["a"]], nd["scale"])
+        elif nd["kind"] in ("abs", "sqrt"):
+            ids[i] = {"abs": tile.Abs, "sqrt": tile.Sqrt}[nd["kind"]](ids[nd["a"]])
+        else:
+            op = {"add": tile.Add, "mul": tile.Mul, "hypot": tile.Hypot}[nd["kind"]]
+            ids[i] = op(ids[nd["a"]], ids[nd["b"]])
+    last = ids[len(nodes) - 1]
+
+    def run():
+        out = torch.empty(n + 1, device="cuda")
+        last.Run(out[1:])
+        torch.cuda.synchronize()
+        return out[1:].cpu().numpy()
+
+    interp, spec = both(run)
+    assert np.array_equal(bits(interp), bits(spec))
+    rc, want = O.tile_eval(nodes, len(nodes) - 1, n, 0)
+    assert rc == 0
+    assert_agree(f"specialised unaligned graph {seed}", spec, want)
+
+
+@pytest.mark.parametrize("halo", [0, 32, 40])
+def test_shard_halo_both_modes(halo):
+    """The twelve-node graph on a shard whose device inputs carry `halo`
+    preceding samples (bulk copies for halo % 4 == 0, several chunks per
+    block): the same slice of the whole signal in both modes."""
+    from test_abi import twelve_node_graph
+
+    n_total, start, n = 3 << 20, 1 << 20, (1 << 20) + 3
+    rng = np.random.default_rng(12)
+    full = [rng.uniform(-4, 4, n_total).astype(np.float32) for _ in range(3)]
+    g = tile.New()
+    keep = [torch.from_numpy(x[start - halo:start + n].copy()).cuda() for x in full]
+    root = twelve_node_graph(g, *[g.InputDevice(t[halo:]) for t in keep],
+                             np.full(31, 1 / 31, np.float32))
+
+    def run():
+        out = torch.empty(n, device="cuda")
+        root.Run(out, halo=halo)
+        torch.cuda.synchronize()
+        return out.cpu().numpy()
+
+    interp, spec = both(run)
+    assert np.array_equal(bits(interp), bits(spec))
+
+
+@pytest.mark.parametrize("seed", [0, 4])
+def test_chained_windows_both_modes(seed):
+    from test_tile_lowering import _chained_graph
+
+    n = (1 << 20) + 333
+    root, nodes = _chained_graph(seed, n, 0)
+    interp, spec = both(root.Materialize)
+    assert np.array_equal(bits(interp), bits(spec))
+    rc, want = O.tile_eval(nodes, len(nodes) - 1, n, 0)
+    assert rc == 0
+    assert_agree(f"specialised chained windows {seed}", spec, want)
+
+
+@pytest.mark.parametrize("kind", list(KINDS))
+def test_reductions_both_modes(kind):
+    from test_tile_lowering import _random_graph
+
+    n = 3 * 4096 + 1001
+    root, nodes = _random_graph(2, n, 0)
+    def run():
+        r = KINDS[kind](root).Materialize()
+        return r if isinstance(r, tuple) else (None, r)   # (index, value)
+
+    interp, spec = both(run)
+    assert interp[0] == spec[0] and bits(interp[1]) == bits(spec[1]), (kind, interp, spec)

@@ -1,0 +1,88 @@
+"""A tile graph's specialised kernel on the CPU: its source is the lowered
+program as compile-time constants (one entry per device instruction, one
+descriptor per window), and NVRTC compiles it for sm_100a without a GPU for
+every form the launcher can choose (two or four groups per thread, bulk or
+direct inputs, a reduction, chained windows). The reference compiles each
+graph with NVRTC the same way (tile/run.go:38-41)."""
+import re
+
+import numpy as np
+import pytest
+
+from simtgo_b200 import tile
+from simtgo_b200._lib import SimtgoError
+from test_tile_lowering import _chained_graph, _random_graph
+
+f32 = np.float32
+
+
+def _available():
+    return tile.JITInfo()[1]
+
+
+needs_nvrtc = pytest.mark.skipif(not _available(), reason="libnvrtc cannot be opened")
+
+
+def twelve(n=4099):
+    rng = np.random.default_rng(6)
+    g = tile.New()
+    a, b, c = (g.Input(rng.uniform(-4, 4, n).astype(f32)) for _ in range(3))
+    s = tile.Scale(a, 0.5)
+    ab = tile.Abs(b)
+    h = np.full(31, 1 / 31, f32)
+    return tile.Mul(tile.Hypot(tile.Add(tile.Mul(s, tile.Sqrt(ab)), c), tile.FIR(s, h)), ab)
+
+
+def test_source_holds_the_program():
+    t = twelve()
+    n_insn, n_in, n_win = t.ProgramSize()
+    src = t.JITSource(groups=4, bulk=True)
+    code = src.split("code[] = {", 1)[1].split("};", 1)[0]
+    assert len(re.findall(r"\{\d+, \d+, \d+, \d+, \d+, 0\.0f, 0u\}", code)) == n_insn
+    fir = src.split("fir[] = {", 1)[1].split("};", 1)[0]
+    assert fir.count("{") == n_win == 1
+    assert ", 31, " in fir  # the window's taps
+    assert "tile_body<true, 4, Spec>" in src
+    assert "tile_body<false, 2, Spec>" in t.JITSource(groups=2, bulk=False)
+    # SCALE factors and tap values are not in the source: they stay in the
+    # parameter block, so graphs that differ only in them share a kernel.
+    assert "0.5" not in src and "0.0322" not in src
+
+
+def test_arguments_refused():
+    t = twelve()
+    with pytest.raises(SimtgoError):
+        t.JITSource(groups=3)
+    with pytest.raises(SimtgoError):
+        t.JITSource(reduce=7)
+    with pytest.raises(SimtgoError):
+        tile.SetJIT(3)
+    mode = tile.JITInfo()[0]
+    tile.SetJIT(0)
+    assert tile.JITInfo()[0] == 0
+    tile.SetJIT(mode)
+
+
+@needs_nvrtc
+@pytest.mark.parametrize("groups,bulk", [(4, True), (2, True), (4, False), (2, False)])
+def test_twelve_node_compiles(groups, bulk):
+    twelve().JITSource(groups=groups, bulk=bulk, compile=True)
+
+
+@needs_nvrtc
+@pytest.mark.parametrize("reduce", [0, 3])
+def test_reduction_compiles(reduce):
+    twelve().JITSource(reduce=reduce, groups=4, compile=True)
+
+
+@needs_nvrtc
+@pytest.mark.parametrize("seed", [0, 1, 2])
+def test_random_graphs_compile(seed):
+    root, _ = _random_graph(seed, 3001, 0)
+    root.JITSource(groups=4 if seed % 2 else 2, bulk=seed != 2, compile=True)
+
+
+@needs_nvrtc
+def test_chained_windows_compile():
+    root, _ = _chained_graph(1, 3001, 0)
+    root.JITSource(groups=2, bulk=True, compile=True)
