@@ -519,6 +519,10 @@ struct Layout {
     size_t smem;
 };
 
+// Floats per thread a specialised kernel may hold its temporaries in
+// (registers); programs with more keep them in shared memory.
+constexpr int kTmpRegFloats = 32;
+
 // The float4 offsets of the layout's parts for Y.g groups per thread; hs
 // is the samples a chunk's windows reach below it.
 void set_offsets(const Lowered& L, int32_t hs, Layout& Y) {
@@ -621,20 +625,36 @@ int launch_program(const simtgo_tile_graph* g, const Lowered& L,
     // 1.82 -> 1.71 ms, a 31-tap window over one input 1.00 -> 0.85 ms; with
     // two stages required, three inputs and a window fit one block per SM
     // and ran 2.90 ms).
-    bool hypot = false;
-    for (const FInsn& fi : L.code) hypot = hypot || fi.op == tilek::OP_HYPOT;
-    auto smem_for = [&](int g) {
+    //
+    // A specialised kernel keeps the program's temporaries in registers
+    // when they take at most kTmpRegFloats per thread (each is the thread's
+    // G float4 groups), and then reserves no shared memory for them.
+    const bool jit_on = jit_ok && tilejit::available();
+    auto tmp_regs = [&](int g) {
+        return jit_on && L.n_tmp > 0 && L.n_tmp * g * 4 <= kTmpRegFloats;
+    };
+    // A specialised kernel with windows takes four groups only when two
+    // input stages still fit two blocks per SM (double-buffered chunks
+    // matter more once dispatch costs nothing: the twelve-node graph at 2^28
+    // measured 0.88 ms with two groups, three blocks and two stages per SM,
+    // against 1.08 ms with four groups and one stage; a 31-tap window over
+    // one input keeps four groups, 0.43 ms).
+    auto smem_for = [&](int g, int stages) {
         const int ch = tilek::chunk_of(g);
         const size_t fixed = (size_t)tilek::meta_bytes((int)L.code.size(), n_in, n_fir) +
                              (size_t)n_fir * tilek::kMaxTaps * 4 + (size_t)tile_off4(L, n_fir, ch) * 16 +
-                             (size_t)L.n_tmp * ch * 4;
-        return fixed + 1 * (size_t)n_in * (hs + ch) * sizeof(float);
+                             (tmp_regs(g) ? 0 : (size_t)L.n_tmp * ch * 4);
+        return fixed + stages * (size_t)n_in * (hs + ch) * sizeof(float);
     };
-    Y.g = (n_fir == 0 || smem_for(tilek::kGWide) <= (size_t)d->smem_per_sm / 2 - 2048)
+    const int wide_stages = jit_on ? 2 : 1;
+    Y.g = (n_fir == 0 ||
+           smem_for(tilek::kGWide, wide_stages) <= (size_t)d->smem_per_sm / 2 - 2048)
               ? tilek::kGWide
               : tilek::kG;
-    const int min_st = Y.g == tilek::kGWide && n_fir > 0 ? 1 : 2;  // input stages per block
+    // Input stages per block.
+    const int min_st = Y.g == tilek::kGWide && n_fir > 0 && !jit_on ? 1 : 2;
     set_offsets(L, hs, Y);
+    if (tmp_regs(Y.g)) Y.stages4 = Y.temps4;
     const size_t base_smem = (size_t)Y.stages4 * 16;
     const size_t stage_bytes = (size_t)n_in * Y.sstride * sizeof(float);
     // Every instantiation may take up to the opt-in maximum of dynamic
@@ -669,7 +689,9 @@ int launch_program(const simtgo_tile_graph* g, const Lowered& L,
     static thread_local tilek::Program P;
     build_program(g, L, Y, bulk_cand, P);
     CUfunction spec = nullptr;
-    if (jit_ok && (rc = tilejit::get(P, bulk_cand, Y.g, dyn_max, &spec))) return rc;
+    tilejit::Form form{bulk_cand, Y.g, tmp_regs(Y.g), Y.temps4, L.n_tmp};
+    if (jit_on && (rc = tilejit::get(P, form, dyn_max, &spec))) return rc;
+    if (!spec && tmp_regs(Y.g)) return sg::fail(SIMTGO_EDEVICE, "tile: no specialised kernel");
     int reg_blocks = 0;
     if (spec) {
         rc = tilejit::occupancy(spec, base_smem, &reg_blocks);
@@ -710,7 +732,8 @@ int launch_program(const simtgo_tile_graph* g, const Lowered& L,
     if (bulk != bulk_cand) {  // no room for the stages after all: DIRECT addressing
         build_program(g, L, Y, bulk, P);
         spec = nullptr;
-        if (jit_ok && (rc = tilejit::get(P, bulk, Y.g, dyn_max, &spec))) return rc;
+        form.bulk = bulk;
+        if (jit_on && (rc = tilejit::get(P, form, dyn_max, &spec))) return rc;
     }
     for (int k = 0; k < n_in; k++) P.in[k] = dev_in[k];  // element 0; [-halo, 0) precede it
     auto kern = Y.g == kG ? (bulk ? tilek::k_tile<true, kG> : tilek::k_tile<false, kG>)
@@ -1282,8 +1305,11 @@ int32_t simtgo_tile_jit_source(simtgo_tile_graph* g, simtgo_tensor t, int32_t re
     set_offsets(L, hs, Y);
     static thread_local tilek::Program P;
     build_program(g, L, Y, bulk != 0, P);
-    if (compile && (rc = tilejit::compile_only(P, bulk != 0, groups))) return rc;
-    const std::string s = tilejit::spec_source(P, bulk != 0, groups);
+    const tilejit::Form form{bulk != 0, (int)groups,
+                             L.n_tmp > 0 && L.n_tmp * groups * 4 <= kTmpRegFloats, Y.temps4,
+                             L.n_tmp};
+    if (compile && (rc = tilejit::compile_only(P, form))) return rc;
+    const std::string s = tilejit::spec_source(P, form);
     if (buf && cap > 0) {
         const size_t n = std::min<size_t>(s.size(), (size_t)cap - 1);
         memcpy(buf, s.data(), n);

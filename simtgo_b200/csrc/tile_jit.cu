@@ -200,15 +200,19 @@ int compile_source(const std::string& src, std::string* cubin) {
 
 namespace tilejit {
 
-std::string spec_source(const tilek::Program& P, bool bulk, int g) {
+std::string spec_source(const tilek::Program& P, const Form& f) {
+    const bool bulk = f.bulk;
+    const int g = f.g;
     std::string s;
     char line[1024];
     s += kPrelude;
     s += "#include \"tile_kernel.cuh\"\n";
     s += "struct Spec {\n";
     snprintf(line, sizeof line,
-             "  static constexpr int n_fir = %d, main_start = %d, reduce = %d;\n", P.n_fir,
-             P.main_start, P.reduce);
+             "  static constexpr int n_fir = %d, main_start = %d, reduce = %d;\n"
+             "  static constexpr int temps4 = %d, n_tmp = %d;\n"
+             "  static constexpr bool tmp_regs = %s;\n",
+             P.n_fir, P.main_start, P.reduce, f.temps4, f.n_tmp, f.tmp_regs ? "true" : "false");
     s += line;
     s += "  static constexpr tilek::FirC fir[] = {";
     if (P.n_fir == 0) s += "{0, 0, 0, 0}";
@@ -241,7 +245,7 @@ std::string spec_source(const tilek::Program& P, bool bulk, int g) {
     return s;
 }
 
-int get(const tilek::Program& P, bool bulk, int g, int dyn_max, CUfunction* out) {
+int get(const tilek::Program& P, const Form& f, int dyn_max, CUfunction* out) {
     *out = nullptr;
     const int m = mode();
     if (m == 0) return 0;
@@ -256,7 +260,7 @@ int get(const tilek::Program& P, bool bulk, int g, int dyn_max, CUfunction* out)
     int dev = -1;
     int rc = sg::cuda_status(cudaGetDevice(&dev), "cudaGetDevice");
     if (rc) return rc;
-    const std::string src = spec_source(P, bulk, g);
+    const std::string src = spec_source(P, f);
     const std::string key = std::to_string(dev) + "|" + src;
     std::lock_guard<std::mutex> lk(g_mu);
     auto it = g_cache.find(key);
@@ -280,11 +284,19 @@ int get(const tilek::Program& P, bool bulk, int g, int dyn_max, CUfunction* out)
     return 0;
 }
 
-int compile_only(const tilek::Program& P, bool bulk, int g) {
+bool available() {
+    if (mode() == 0) return false;
+    std::call_once(g_rtc_once, open_nvrtc);
+    std::call_once(g_drv_once, open_driver);
+    // Mode 2 reports true so that get() fails with the reason.
+    return mode() == 2 || (g_rtc.ok && g_drv.ok);
+}
+
+int compile_only(const tilek::Program& P, const Form& f) {
     std::call_once(g_rtc_once, open_nvrtc);
     if (!g_rtc.ok) return sg::fail(SIMTGO_EDEVICE, "tile: %s", g_rtc.why.c_str());
     std::string cubin;
-    return compile_source(spec_source(P, bulk, g), &cubin);
+    return compile_source(spec_source(P, f), &cubin);
 }
 
 int occupancy(CUfunction fn, size_t smem, int* blocks) {

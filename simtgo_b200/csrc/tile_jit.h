@@ -10,15 +10,29 @@
 
 namespace tilejit {
 
+// The form of a specialised kernel besides its program: input addressing
+// (bulk copies or direct loads), float4 groups per thread, and where the
+// temporaries live (registers, tmp_regs, or shared memory at temps4).
+struct Form {
+    bool bulk;
+    int g;
+    bool tmp_regs;
+    int temps4, n_tmp;
+};
+
 // The source of the specialised kernel for program P (instructions and
 // window descriptors as constants; inputs, taps and SCALE factors stay in
 // the parameter block).
-std::string spec_source(const tilek::Program& P, bool bulk, int g);
+std::string spec_source(const tilek::Program& P, const Form& f);
 
 // The compiled kernel for P on the current device (compiled and cached on
 // first use, its dynamic shared memory limit set to dyn_max), or nullptr
 // with 0 when specialisation is off or (mode 1) NVRTC is unavailable.
-int get(const tilek::Program& P, bool bulk, int g, int dyn_max, CUfunction* out);
+int get(const tilek::Program& P, const Form& f, int dyn_max, CUfunction* out);
+
+// Whether launches use specialised kernels (mode != 0 and NVRTC and the
+// driver's module entry points are there; always true in mode 2).
+bool available();
 
 // Resident blocks per SM of fn at kThreads threads and smem bytes.
 int occupancy(CUfunction fn, size_t smem, int* blocks);
@@ -27,6 +41,6 @@ int occupancy(CUfunction fn, size_t smem, int* blocks);
 int launch(CUfunction fn, int blocks, size_t smem, cudaStream_t s, void** args);
 
 // Compiles the specialised source of P without loading it (no GPU needed).
-int compile_only(const tilek::Program& P, bool bulk, int g);
+int compile_only(const tilek::Program& P, const Form& f);
 
 }  // namespace tilejit

@@ -292,7 +292,9 @@ __device__ __forceinline__ float4 mask_outside(float4 v, int64_t p, const Ctx& c
 // operation, temporary, window tile, output). The hooks give what depends
 // on where the program lives: hk.win(in, c, r, A) accumulates the window
 // the instruction names (OP_FIRACC), hk.tile_of(in, c) is the float4
-// offset of the tile it stages (F_STAGE), hk.imm(in) the SCALE factor. The
+// offset of the tile it stages (F_STAGE), hk.imm(in) the SCALE factor, and
+// hk.tmp_reg(x) says whether the temporary at x lives in registers
+// (hk.tmp_get / tmp_set) instead of shared memory. The
 // interpreter's hooks read the program in shared memory, a graph's
 // specialised kernel's are compile-time constants and its parameter block.
 // In DIRECT mode (BULK false) an input operand is read from HBM at the
@@ -304,6 +306,7 @@ __device__ __forceinline__ bool exec(const Insn& in, const Hooks& hk, const Ctx&
     auto operand = [&](int x, bool input, int k) -> float4 {
         if (!FULL && !((r.gm >> k) & 1)) return A[k];
         if (!BULK && input) return gload4(c.in[x], r.p0 + 4 * (t + kThreads * k), c);
+        if (!input && hk.tmp_reg(x)) return hk.tmp_get(x, k);
         return c.S[x + (input ? r.sh_in : 0) + t + kThreads * k];
     };
     if (in.flags & F_LOADA) {
@@ -349,7 +352,12 @@ __device__ __forceinline__ bool exec(const Insn& in, const Hooks& hk, const Ctx&
         if (in.flags & F_STA) {
 #pragma unroll
             for (int k = 0; k < G; k++)
-                if (FULL || ((r.gm >> k) & 1)) c.S[in.d + t + kThreads * k] = A[k];
+                if (FULL || ((r.gm >> k) & 1)) {
+                    if (hk.tmp_reg(in.d))
+                        hk.tmp_set(in.d, k, A[k]);
+                    else
+                        c.S[in.d + t + kThreads * k] = A[k];
+                }
         }
         if (in.flags & F_STAGE) {
             float4* dst = c.S + hk.tile_of(in, c) + r.sh_st + t;
@@ -393,6 +401,9 @@ struct InterpHooks {
     __device__ __forceinline__ int tile_of(const Insn& in, const Ctx& c) const {
         return c.fir[in.d].w;
     }
+    __device__ __forceinline__ bool tmp_reg(int) const { return false; }
+    __device__ __forceinline__ float4 tmp_get(int, int) const { return float4{}; }
+    __device__ __forceinline__ void tmp_set(int, int, float4) const {}
 };
 
 // Runs the program from pc until an instruction with F_END, leaving the
@@ -425,6 +436,8 @@ __device__ __forceinline__ void interpret(const Insn* code, int pc, const Ctx& c
 //                                       factors come from the parameter block)
 //   static constexpr FirC fir[];        per window (at least one entry)
 //   static constexpr int n_fir, main_start, reduce;
+//   static constexpr int temps4, n_tmp;  the temporaries' float4 offset and count
+//   static constexpr bool tmp_regs;      temporaries in registers, not shared memory
 // and exec() runs each instruction with its operation, flags and
 // addresses folded, so nothing is decoded or dispatched at run time, and a
 // window's taps are parameter-bank operands of its FMAs. The arithmetic is
@@ -434,28 +447,39 @@ struct FirC {
     int32_t start, taps, head, tile4;  // as FirDesc (taps | kSyncAfter)
 };
 
-template <int G, int PC, int TAPS, int WTILE, int DTILE>
+template <class S, int G, int PC, int TAPS, int WTILE, int DTILE>
 struct StaticHooks {
     const Program& P;
+    float4 (&T)[kMaxTmp][G];  // the temporaries, when S::tmp_regs
     __device__ __forceinline__ float imm(const Insn&) const { return P.code[PC].imm; }
     __device__ __forceinline__ void win(const Insn& in, const Ctx& c, const Run& r,
                                         float4 (&A)[G]) const {
         fir_acc_static<G, TAPS>(A, c.S + WTILE + threadIdx.x + r.woff4, P.fir[in.b].h);
     }
     __device__ __forceinline__ int tile_of(const Insn&, const Ctx&) const { return DTILE; }
+    // A temporary's float4 offset x names slot (x - temps4) / (chunk / 4).
+    __device__ __forceinline__ bool tmp_reg(int x) const {
+        return S::tmp_regs && x >= S::temps4 && x < S::temps4 + S::n_tmp * (chunk_of(G) / 4);
+    }
+    __device__ __forceinline__ float4 tmp_get(int x, int k) const {
+        return T[(x - S::temps4) / (chunk_of(G) / 4)][k];
+    }
+    __device__ __forceinline__ void tmp_set(int x, int k, float4 v) const {
+        T[(x - S::temps4) / (chunk_of(G) / 4)][k] = v;
+    }
 };
 
 template <class S, int PC, bool BULK, bool FULL, int G>
 __device__ __forceinline__ void interpret_s(const Program& P, const Ctx& c, const Run& r,
-                                            float4 (&A)[G]) {
+                                            float4 (&A)[G], float4 (&T)[kMaxTmp][G]) {
     constexpr Insn in = S::code[PC];
     constexpr int FW = in.op == OP_FIRACC ? in.b : 0;
     constexpr int TAPS = S::fir[FW].taps & (kSyncAfter - 1);
     constexpr int WTILE = S::fir[FW].tile4 + S::fir[FW].head / 4;
     constexpr int DTILE = (in.flags & F_STAGE) ? S::fir[in.d].tile4 : 0;
-    (void)exec<BULK, FULL, G>(in, StaticHooks<G, PC, TAPS, WTILE, DTILE>{P}, c, r, A,
+    (void)exec<BULK, FULL, G>(in, StaticHooks<S, G, PC, TAPS, WTILE, DTILE>{P, T}, c, r, A,
                               (int)threadIdx.x);
-    if constexpr (!(in.flags & F_END)) interpret_s<S, PC + 1, BULK, FULL, G>(P, c, r, A);
+    if constexpr (!(in.flags & F_END)) interpret_s<S, PC + 1, BULK, FULL, G>(P, c, r, A, T);
 }
 
 // ---- reductions ---------------------------------------------------------------
@@ -1029,16 +1053,17 @@ struct is_interp<Interp> {
 // constant.
 template <class S, int PC, bool BULK, bool FULL, int G>
 __device__ __forceinline__ void run_s(const Program& P, const Ctx& c, const Run& r,
-                                      float4 (&A)[G]) {
+                                      float4 (&A)[G], float4 (&T)[kMaxTmp][G]) {
     if (!FULL) {
 #pragma unroll
         for (int k = 0; k < G; k++) A[k] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    interpret_s<S, PC, BULK, FULL, G>(P, c, r, A);
+    interpret_s<S, PC, BULK, FULL, G>(P, c, r, A, T);
 }
 template <class S, int J, bool BULK, int G>
 __device__ __forceinline__ void jobs_s(const Program& P, const Ctx& cx, int32_t in4, int32_t hs,
-                                       int64_t cb, bool first, bool edge, float4 (&A)[G]) {
+                                       int64_t cb, bool first, bool edge, float4 (&A)[G],
+                                       float4 (&T)[kMaxTmp][G]) {
     constexpr int NF = S::n_fir;
     const int tid = threadIdx.x;
     Run r;
@@ -1052,7 +1077,7 @@ __device__ __forceinline__ void jobs_s(const Program& P, const Ctx& cx, int32_t 
             r.woff4 = -head4;
             r.gm = first && tid < head4 ? 1u : 0u;
             r.p0 = cb - fd.head;
-            if (r.gm) run_s<S, fd.start, BULK, false, G>(P, cx, r, A);
+            if (r.gm) run_s<S, fd.start, BULK, false, G>(P, cx, r, A, T);
         } else {
             if (!first && tid >= kThreads - head4) {
                 float4* tile = cx.S + fd.tile4;
@@ -1064,17 +1089,17 @@ __device__ __forceinline__ void jobs_s(const Program& P, const Ctx& cx, int32_t 
             r.woff4 = 0;
             r.gm = (1u << G) - 1;
             r.p0 = cb;
-            run_s<S, fd.start, BULK, true, G>(P, cx, r, A);
+            run_s<S, fd.start, BULK, true, G>(P, cx, r, A, T);
             if constexpr (J + 1 == 2 * NF || (fd.taps & kSyncAfter)) __syncthreads();
         }
-        jobs_s<S, J + 1, BULK, G>(P, cx, in4, hs, cb, first, edge, A);
+        jobs_s<S, J + 1, BULK, G>(P, cx, in4, hs, cb, first, edge, A, T);
     } else {
         r.sh_in = in4 + hs / 4;
         r.sh_st = 0;
         r.woff4 = 0;
         r.gm = (1u << G) - 1;
         r.p0 = cb;
-        run_s<S, S::main_start, BULK, true, G>(P, cx, r, A);
+        run_s<S, S::main_start, BULK, true, G>(P, cx, r, A, T);
     }
 }
 
@@ -1162,6 +1187,7 @@ __device__ __forceinline__ void tile_body(const Program& P, float* __restrict__ 
     };
     const bool free_run = nf == 0;
     float4 A[G];  // the last run's values (the main program's, for a reduction)
+    float4 T[kMaxTmp][G];  // a specialised kernel's temporaries (S::tmp_regs)
     int s = 0;           // this chunk's stage
     uint32_t phase = 0;  // the parity its mbarrier completes next
     for (int64_t c = c0; c < c1; c++) {
@@ -1196,7 +1222,7 @@ __device__ __forceinline__ void tile_body(const Program& P, float* __restrict__ 
         }
         const int32_t in4 = stages4 + s * (stage_floats / 4);
         if constexpr (SPEC) {
-            jobs_s<S, 0, BULK, G>(P, cx, in4, hs, cb, first, edge, A);
+            jobs_s<S, 0, BULK, G>(P, cx, in4, hs, cb, first, edge, A, T);
         } else {
             // Jobs 2f and 2f+1 stage window f: its head (first chunk only) and
             // the chunk itself; job 2 nf is the main program over the chunk. One
