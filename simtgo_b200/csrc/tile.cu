@@ -1,11 +1,14 @@
 // tile.cu -- the tile track (package tile): graph recording (tile/tile.go),
 // lowering to one fused program (tile/codegen.go) and running it
-// (tile/run.go), with no run-time compiler.
+// (tile/run.go).
 //
 // The reference renders each graph as CUDA C and compiles it with NVRTC per
 // distinct graph (tile/run.go:40). Here the graph is lowered on the host to a
 // short program for an accumulator machine that travels in the kernel's
-// parameter block, and ONE precompiled sm_100a kernel interprets it:
+// parameter block. A precompiled sm_100a kernel interprets it, and by
+// default the program runs instead in its own specialised kernel
+// (tile_jit.cu): the same kernel body with the program compiled in as
+// constants. The machine:
 //  * a block works on chunks of 2048 elements; a thread owns 2 float4 groups
 //    of each chunk (groups t and t + 256, so a warp's 16-byte shared-memory
 //    accesses are consecutive and conflict-free) held in an accumulator of
