@@ -703,7 +703,7 @@ def bench_tile(args, torch, np, L, dev, sp, rank, world, barrier, max_over_ranks
     # The first run of the graph compiles its specialised kernel (NVRTC);
     # its wall time, compile included, is reported, and the timed steps
     # that follow launch the cached kernel.
-    mode, nvrtc, _, launches0 = tile.JITInfo()
+    mode, nvrtc, _, launches0, _ = tile.JITInfo()
     t0 = time.perf_counter()
     step()
     torch.cuda.synchronize()

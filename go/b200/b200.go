@@ -132,7 +132,7 @@ var (
 	TileProgramSize           func(g uintptr, t int32, nInstructions *int32, nInputs *int32, nWindows *int32) int32
 	TileSource                func(g uintptr, t int32, buf unsafe.Pointer, capacity int32) int32
 	TileSetJIT                func(mode int32) int32
-	TileJITInfo               func(mode *int32, available *int32, compiled *int64, launches *int64) int32
+	TileJITInfo               func(mode *int32, available *int32, compiled *int64, launches *int64, cacheHits *int64) int32
 	TileJITSource             func(g uintptr, t int32, reduce int32, groups int32, bulk int32, compile int32, buf unsafe.Pointer, capacity int32) int32
 	TileMaterialize           func(g uintptr, t int32, hostOut unsafe.Pointer, outLen int32) int32
 	TileMaterializeStepwise   func(g uintptr, t int32, hostOut unsafe.Pointer, outLen int32, launches *int32) int32

@@ -328,11 +328,15 @@ int32_t simtgo_tile_source(simtgo_tile_graph* g, simtgo_tensor t, char* buf, int
  * of a new program compiles (about a second) before it enqueues, so make it
  * before any stream capture. */
 int simtgo_tile_set_jit(int32_t mode);
-/* The mode, whether libnvrtc could be opened, and how many programs were
- * compiled and specialised launches made in this process. Any pointer may
- * be NULL. */
+/* The mode, whether libnvrtc could be opened, how many programs were
+ * compiled and specialised launches made in this process, and how many
+ * kernels came from the on-disk cache instead of a compilation (compiled
+ * cubins are kept in $SIMTGO_B200_CACHE, else $XDG_CACHE_HOME/simtgo_b200,
+ * else ~/.cache/simtgo_b200; SIMTGO_B200_CACHE=off disables it; an entry is
+ * served only when its stored identity -- source, headers, options, NVRTC
+ * version -- matches byte for byte). Any pointer may be NULL. */
 int simtgo_tile_jit_info(int32_t* mode, int32_t* available, int64_t* compiled,
-                         int64_t* launches);
+                         int64_t* launches, int64_t* cache_hits);
 /* The specialised kernel's source for t (reduce: -1 or a SIMTGO_TILE_*
  * reduction) with `groups` (2 or 4) float4 groups per thread and bulk-copied
  * (bulk != 0) or directly read inputs, written like simtgo_tile_source; with

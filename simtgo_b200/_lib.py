@@ -85,7 +85,7 @@ _SIGS = {
     "simtgo_tile_source": [_vp, _i32, C.c_char_p, _i32],
     "simtgo_tile_set_jit": [_i32],
     "simtgo_tile_jit_info": [C.POINTER(_i32), C.POINTER(_i32), C.POINTER(C.c_int64),
-                             C.POINTER(C.c_int64)],
+                             C.POINTER(C.c_int64), C.POINTER(C.c_int64)],
     "simtgo_tile_jit_source": [_vp, _i32, _i32, _i32, _i32, _i32, C.c_char_p, _i32],
     "simtgo_tile_materialize": [_vp, _i32, _vp, _i32],
     "simtgo_tile_materialize_stepwise": [_vp, _i32, _vp, _i32, C.POINTER(_i32)],

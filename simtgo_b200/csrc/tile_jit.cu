@@ -20,12 +20,24 @@
 // every program, falling back to the interpreter when NVRTC cannot be opened;
 // 2 = specialise or fail. A program whose compilation fails is an error in
 // modes 1 and 2 (it is a bug, not a missing dependency).
+//
+// Compiled cubins are also kept on disk (internal/jit/diskcache.go keeps the
+// reference's PTX the same way), so a new process does not compile again:
+// in $SIMTGO_B200_CACHE, else $XDG_CACHE_HOME/simtgo_b200, else
+// ~/.cache/simtgo_b200 ("off" disables it). An entry is named by a hash of
+// everything that can change its bytes -- the source with the embedded
+// headers, the compile options and NVRTC's version -- and holds that whole
+// identity before the cubin, so a read serves the cubin only when the
+// identity matches byte for byte: a hash collision is a miss, never a wrong
+// kernel. Every failure to read or write is a miss.
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <dlfcn.h>
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
+#include <sys/stat.h>
+#include <unistd.h>
 
 #include <atomic>
 #include <mutex>
@@ -53,6 +65,7 @@ struct Nvrtc {
     nvrtcResult_t (*cubin)(nvrtcProgram_t, char*);
     nvrtcResult_t (*destroy)(nvrtcProgram_t*);
     const char* (*err)(nvrtcResult_t);
+    nvrtcResult_t (*version)(int*, int*);
     bool ok = false;
     std::string why;
 };
@@ -82,6 +95,7 @@ void open_nvrtc() {
     g_rtc.cubin = (decltype(g_rtc.cubin))sym("nvrtcGetCUBIN");
     g_rtc.destroy = (decltype(g_rtc.destroy))sym("nvrtcDestroyProgram");
     g_rtc.err = (decltype(g_rtc.err))sym("nvrtcGetErrorString");
+    g_rtc.version = (decltype(g_rtc.version))sym("nvrtcVersion");
     if (!all) {
         g_rtc.why = "libnvrtc.so.12 lacks an entry point this library needs";
         return;
@@ -133,7 +147,7 @@ int drv_status(CUresult r, const char* what) {
 
 // ---- mode and counters --------------------------------------------------------
 std::atomic<int> g_mode{-1};
-std::atomic<int64_t> g_compiled{0}, g_launches{0};
+std::atomic<int64_t> g_compiled{0}, g_launches{0}, g_disk_hits{0};
 
 int mode() {
     int m = g_mode.load();
@@ -169,13 +183,98 @@ struct Entry {
 std::mutex g_mu;
 std::unordered_map<std::string, Entry> g_cache;  // key: device | source
 
+const char* const kOptArch = "-arch=sm_100a";
+
+// ---- the persistent cubin cache -------------------------------------------------
+std::string cache_dir() {
+    const char* e = getenv("SIMTGO_B200_CACHE");
+    if (e && *e) return strcmp(e, "off") == 0 ? std::string() : std::string(e);
+    if ((e = getenv("XDG_CACHE_HOME")) && *e) return std::string(e) + "/simtgo_b200";
+    if ((e = getenv("HOME")) && *e) return std::string(e) + "/.cache/simtgo_b200";
+    return std::string();
+}
+
+// What determines a cubin's bytes: options, NVRTC's version, the embedded
+// headers and the source.
+std::string identity(const std::string& src) {
+    int major = 0, minor = 0;
+    if (g_rtc.version) g_rtc.version(&major, &minor);
+    std::string id = std::string(kOptArch) + " -std=c++17 --fmad=false taps=" +
+                     std::to_string(SIMTGO_TILE_MAX_TAPS) + " nvrtc " + std::to_string(major) +
+                     "." + std::to_string(minor) + "\n";
+    for (int i = 0; i < kRtcHeaderCount; i++) {
+        id += kRtcHeaderNames[i];
+        id += '\0';
+        id += std::to_string(strlen(kRtcHeaderSources[i]));
+        id += '\0';
+        id += kRtcHeaderSources[i];
+    }
+    id += src;
+    return id;
+}
+
+// 128 bits of FNV-1a (two 64-bit passes, different offset bases) as hex.
+std::string name_of(const std::string& id) {
+    uint64_t a = 0xcbf29ce484222325ull, b = 0x84222325cbf29ce4ull;
+    for (unsigned char ch : id) {
+        a = (a ^ ch) * 0x100000001b3ull;
+        b = (b ^ ch) * 0x100000001b3ull;
+    }
+    char buf[40];
+    snprintf(buf, sizeof buf, "%016llx%016llx", (unsigned long long)a, (unsigned long long)b);
+    return buf;
+}
+
+bool read_all(const std::string& path, std::string* out) {
+    FILE* f = fopen(path.c_str(), "rb");
+    if (!f) return false;
+    out->clear();
+    char buf[1 << 16];
+    size_t n;
+    while ((n = fread(buf, 1, sizeof buf, f)) > 0) out->append(buf, n);
+    const bool ok = !ferror(f);
+    fclose(f);
+    return ok;
+}
+
+// The cached cubin of `id`, if an entry with exactly this identity exists.
+bool disk_read(const std::string& id, std::string* cubin) {
+    const std::string dir = cache_dir();
+    if (dir.empty()) return false;
+    std::string file;
+    if (!read_all(dir + "/" + name_of(id) + ".cubin", &file)) return false;
+    const uint64_t n = id.size();
+    if (file.size() <= 8 + n) return false;
+    uint64_t stored = 0;
+    memcpy(&stored, file.data(), 8);
+    if (stored != n || file.compare(8, n, id) != 0) return false;
+    cubin->assign(file, 8 + n, std::string::npos);
+    return true;
+}
+
+void disk_write(const std::string& id, const std::string& cubin) {
+    std::string dir = cache_dir();
+    if (dir.empty() || cubin.empty()) return;
+    for (size_t i = 1; i <= dir.size(); i++)  // mkdir -p
+        if (i == dir.size() || dir[i] == '/') mkdir(dir.substr(0, i).c_str(), 0755);
+    const std::string path = dir + "/" + name_of(id) + ".cubin";
+    const std::string tmp = path + ".tmp" + std::to_string((long)getpid());
+    FILE* f = fopen(tmp.c_str(), "wb");
+    if (!f) return;
+    const uint64_t n = id.size();
+    bool ok = fwrite(&n, 8, 1, f) == 1 && fwrite(id.data(), 1, n, f) == n &&
+              fwrite(cubin.data(), 1, cubin.size(), f) == cubin.size();
+    ok = fclose(f) == 0 && ok;
+    if (!ok || rename(tmp.c_str(), path.c_str()) != 0) unlink(tmp.c_str());
+}
+
 int compile_source(const std::string& src, std::string* cubin) {
     nvrtcProgram_t prog = nullptr;
     nvrtcResult_t r = g_rtc.create(&prog, src.c_str(), "tile_spec.cu", kRtcHeaderCount,
                                    kRtcHeaderSources, kRtcHeaderNames);
     if (r) return sg::fail(SIMTGO_EDEVICE, "tile: nvrtcCreateProgram: %s", g_rtc.err(r));
     const std::string taps = "-DSIMTGO_TILE_MAX_TAPS=" + std::to_string(SIMTGO_TILE_MAX_TAPS);
-    const char* opts[] = {"-arch=sm_100a", "-std=c++17", "--fmad=false", taps.c_str()};
+    const char* opts[] = {kOptArch, "-std=c++17", "--fmad=false", taps.c_str()};
     r = g_rtc.compile(prog, 4, opts);
     if (r) {
         size_t n = 0;
@@ -269,7 +368,14 @@ int get(const tilek::Program& P, const Form& f, int dyn_max, CUfunction* out) {
         return 0;
     }
     std::string cubin;
-    if ((rc = compile_source(src, &cubin))) return rc;
+    const std::string id = identity(src);
+    if (disk_read(id, &cubin)) {
+        g_disk_hits.fetch_add(1);
+    } else {
+        if ((rc = compile_source(src, &cubin))) return rc;
+        g_compiled.fetch_add(1);
+        disk_write(id, cubin);
+    }
     Entry e;
     if ((rc = drv_status(g_drv.load(&e.mod, cubin.data()), "cuModuleLoadData"))) return rc;
     if ((rc = drv_status(g_drv.get_fn(&e.fn, e.mod, "k_tile_spec"), "cuModuleGetFunction")))
@@ -279,7 +385,6 @@ int get(const tilek::Program& P, const Form& f, int dyn_max, CUfunction* out) {
              "cuFuncSetAttribute")))
         return rc;
     g_cache.emplace(key, e);
-    g_compiled.fetch_add(1);
     *out = e.fn;
     return 0;
 }
@@ -295,8 +400,16 @@ bool available() {
 int compile_only(const tilek::Program& P, const Form& f) {
     std::call_once(g_rtc_once, open_nvrtc);
     if (!g_rtc.ok) return sg::fail(SIMTGO_EDEVICE, "tile: %s", g_rtc.why.c_str());
+    const std::string src = spec_source(P, f), id = identity(src);
     std::string cubin;
-    return compile_source(spec_source(P, f), &cubin);
+    if (disk_read(id, &cubin)) {
+        g_disk_hits.fetch_add(1);
+        return 0;
+    }
+    if (int rc = compile_source(src, &cubin)) return rc;
+    g_compiled.fetch_add(1);
+    disk_write(id, cubin);
+    return 0;
 }
 
 int occupancy(CUfunction fn, size_t smem, int* blocks) {
@@ -324,13 +437,15 @@ int simtgo_tile_set_jit(int32_t m) {
     return 0;
 }
 
-int simtgo_tile_jit_info(int32_t* m, int32_t* available, int64_t* compiled, int64_t* launches) {
+int simtgo_tile_jit_info(int32_t* m, int32_t* available, int64_t* compiled, int64_t* launches,
+                         int64_t* cache_hits) {
     sg::clear_error();
     std::call_once(g_rtc_once, open_nvrtc);
     if (m) *m = mode();
     if (available) *available = g_rtc.ok ? 1 : 0;
     if (compiled) *compiled = g_compiled.load();
     if (launches) *launches = g_launches.load();
+    if (cache_hits) *cache_hits = g_disk_hits.load();
     return 0;
 }
 

@@ -203,11 +203,13 @@ def SetJIT(mode: int) -> None:
 
 
 def JITInfo():
-    """(mode, NVRTC available, programs compiled, specialised launches)."""
+    """(mode, NVRTC available, programs compiled, specialised launches,
+    kernels served by the on-disk cache) of this process."""
     m, a = C.c_int32(), C.c_int32()
-    c, n = C.c_int64(), C.c_int64()
-    check(_lib.load().simtgo_tile_jit_info(C.byref(m), C.byref(a), C.byref(c), C.byref(n)))
-    return m.value, bool(a.value), c.value, n.value
+    c, n, h = C.c_int64(), C.c_int64(), C.c_int64()
+    check(_lib.load().simtgo_tile_jit_info(C.byref(m), C.byref(a), C.byref(c), C.byref(n),
+                                           C.byref(h)))
+    return m.value, bool(a.value), c.value, n.value, h.value
 
 
 def ShardRange(n_total: int, nranks: int, rank: int):

@@ -43,7 +43,7 @@ def bits(x):
 
 
 def test_nvrtc_is_there():
-    mode, available, _, _ = tile.JITInfo()
+    mode, available, _, _, _ = tile.JITInfo()
     assert available, "libnvrtc could not be opened: tile programs would run interpreted"
 
 
@@ -152,3 +152,35 @@ def test_reductions_both_modes(kind):
 
     interp, spec = both(run)
     assert interp[0] == spec[0] and bits(interp[1]) == bits(spec[1]), (kind, interp, spec)
+
+
+def test_kernel_from_disk_cache_runs(tmp_path):
+    """A second process loads the first one's compiled kernel from the
+    on-disk cache (no compilation) and computes the same bits."""
+    import os
+    import subprocess
+    import sys
+
+    prog = (
+        "import sys, numpy as np\n"
+        "from simtgo_b200 import tile\n"
+        "tile.SetJIT(2)\n"
+        "rng = np.random.default_rng(3)\n"
+        "g = tile.New()\n"
+        "a, b = (g.Input(rng.uniform(-4, 4, 100003).astype(np.float32)) for _ in range(2))\n"
+        "t = tile.Hypot(tile.FIR(tile.Scale(a, 0.5), np.full(9, 1 / 9, np.float32)), b)\n"
+        "out = t.Materialize()\n"
+        "np.save(sys.argv[1], out)\n"
+        "print(tile.JITInfo()[2], tile.JITInfo()[4])\n")
+    env = dict(os.environ, SIMTGO_B200_CACHE=str(tmp_path / "cache"))
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+    def run(name):
+        out = subprocess.run([sys.executable, "-c", prog, str(tmp_path / name)], env=env,
+                             cwd=root, check=True, capture_output=True, text=True).stdout.split()
+        return int(out[0]), int(out[1]), np.load(tmp_path / (name + ".npy"))
+
+    c1, h1, y1 = run("first")
+    c2, h2, y2 = run("second")
+    assert (c1, h1) == (1, 0) and (c2, h2) == (0, 1)
+    assert np.array_equal(bits(y1), bits(y2))

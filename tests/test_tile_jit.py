@@ -86,3 +86,40 @@ def test_random_graphs_compile(seed):
 def test_chained_windows_compile():
     root, _ = _chained_graph(1, 3001, 0)
     root.JITSource(groups=2, bulk=True, compile=True)
+
+
+@needs_nvrtc
+def test_disk_cache_across_processes(tmp_path):
+    """A compiled kernel is kept on disk and a new process takes it from
+    there instead of compiling; a corrupted entry is a miss, not a crash."""
+    import os
+    import subprocess
+    import sys
+
+    prog = (
+        "import numpy as np\n"
+        "from simtgo_b200 import tile\n"
+        "g = tile.New()\n"
+        "a = g.Input(np.ones(3001, np.float32))\n"
+        "t = tile.Add(tile.Scale(a, 2.0), tile.FIR(a, np.full(5, 0.2, np.float32)))\n"
+        "t.JITSource(groups=2, bulk=True, compile=True)\n"
+        "print(tile.JITInfo()[2], tile.JITInfo()[4])\n")
+    env = dict(os.environ, SIMTGO_B200_CACHE=str(tmp_path / "cache"))
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+    def run():
+        out = subprocess.run([sys.executable, "-c", prog], env=env, cwd=root, check=True,
+                             capture_output=True, text=True).stdout.split()
+        return int(out[0]), int(out[1])
+
+    assert run() == (1, 0)          # compiled, written
+    files = list((tmp_path / "cache").glob("*.cubin"))
+    assert len(files) == 1
+    assert run() == (0, 1)          # read back
+    data = bytearray(files[0].read_bytes())
+    data[20] ^= 0xFF                 # the stored identity no longer matches
+    files[0].write_bytes(bytes(data))
+    assert run() == (1, 0)          # a miss: compiled again and rewritten
+    assert run() == (0, 1)
+    env["SIMTGO_B200_CACHE"] = "off"
+    assert run() == (1, 0)
