@@ -340,7 +340,10 @@ int simtgo_tile_jit_info(int32_t* mode, int32_t* available, int64_t* compiled,
 /* The specialised kernel's source for t (reduce: -1 or a SIMTGO_TILE_*
  * reduction) with `groups` (2 or 4) float4 groups per thread and bulk-copied
  * (bulk != 0) or directly read inputs, written like simtgo_tile_source; with
- * compile != 0 it is compiled too (no GPU needed) and a failure returned. */
+ * compile != 0 it is compiled too (no GPU needed) and a failure returned.
+ * groups 0 (with a reduction of a chain of Scale, Sqrt, Abs, x+x, x*x steps
+ * on one input) gives the streaming reduction's kernel for that chain
+ * instead, the steps compiled in as constants; bulk is then ignored. */
 int32_t simtgo_tile_jit_source(simtgo_tile_graph* g, simtgo_tensor t, int32_t reduce,
                                int32_t groups, int32_t bulk, int32_t compile, char* buf,
                                int32_t cap);

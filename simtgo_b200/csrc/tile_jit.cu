@@ -66,6 +66,8 @@ struct Nvrtc {
     nvrtcResult_t (*destroy)(nvrtcProgram_t*);
     const char* (*err)(nvrtcResult_t);
     nvrtcResult_t (*version)(int*, int*);
+    nvrtcResult_t (*add_name)(nvrtcProgram_t, const char*);
+    nvrtcResult_t (*lowered)(nvrtcProgram_t, const char*, const char**);
     bool ok = false;
     std::string why;
 };
@@ -96,6 +98,8 @@ void open_nvrtc() {
     g_rtc.destroy = (decltype(g_rtc.destroy))sym("nvrtcDestroyProgram");
     g_rtc.err = (decltype(g_rtc.err))sym("nvrtcGetErrorString");
     g_rtc.version = (decltype(g_rtc.version))sym("nvrtcVersion");
+    g_rtc.add_name = (decltype(g_rtc.add_name))sym("nvrtcAddNameExpression");
+    g_rtc.lowered = (decltype(g_rtc.lowered))sym("nvrtcGetLoweredName");
     if (!all) {
         g_rtc.why = "libnvrtc.so.12 lacks an entry point this library needs";
         return;
@@ -199,7 +203,7 @@ std::string cache_dir() {
 std::string identity(const std::string& src) {
     int major = 0, minor = 0;
     if (g_rtc.version) g_rtc.version(&major, &minor);
-    std::string id = std::string(kOptArch) + " -std=c++17 --fmad=false taps=" +
+    std::string id = std::string("entry v2 ") + kOptArch + " -std=c++17 --fmad=false taps=" +
                      std::to_string(SIMTGO_TILE_MAX_TAPS) + " nvrtc " + std::to_string(major) +
                      "." + std::to_string(minor) + "\n";
     for (int i = 0; i < kRtcHeaderCount; i++) {
@@ -237,22 +241,32 @@ bool read_all(const std::string& path, std::string* out) {
     return ok;
 }
 
-// The cached cubin of `id`, if an entry with exactly this identity exists.
-bool disk_read(const std::string& id, std::string* cubin) {
+// A compiled entry: the cubin and its kernel's (lowered) name.
+struct Compiled {
+    std::string cubin, name;
+};
+
+// The cached entry of `id`, if one with exactly this identity exists. An
+// entry is [u64 |id|][id][u64 |name|][name][cubin].
+bool disk_read(const std::string& id, Compiled* c) {
     const std::string dir = cache_dir();
     if (dir.empty()) return false;
     std::string file;
     if (!read_all(dir + "/" + name_of(id) + ".cubin", &file)) return false;
     const uint64_t n = id.size();
-    if (file.size() <= 8 + n) return false;
-    uint64_t stored = 0;
+    if (file.size() < 16 + n) return false;
+    uint64_t stored = 0, nl = 0;
     memcpy(&stored, file.data(), 8);
     if (stored != n || file.compare(8, n, id) != 0) return false;
-    cubin->assign(file, 8 + n, std::string::npos);
+    memcpy(&nl, file.data() + 8 + n, 8);
+    if (nl == 0 || file.size() <= 16 + n + nl) return false;
+    c->name.assign(file, 16 + n, nl);
+    c->cubin.assign(file, 16 + n + nl, std::string::npos);
     return true;
 }
 
-void disk_write(const std::string& id, const std::string& cubin) {
+void disk_write(const std::string& id, const Compiled& c) {
+    const std::string& cubin = c.cubin;
     std::string dir = cache_dir();
     if (dir.empty() || cubin.empty()) return;
     for (size_t i = 1; i <= dir.size(); i++)  // mkdir -p
@@ -261,18 +275,26 @@ void disk_write(const std::string& id, const std::string& cubin) {
     const std::string tmp = path + ".tmp" + std::to_string((long)getpid());
     FILE* f = fopen(tmp.c_str(), "wb");
     if (!f) return;
-    const uint64_t n = id.size();
+    const uint64_t n = id.size(), nl = c.name.size();
     bool ok = fwrite(&n, 8, 1, f) == 1 && fwrite(id.data(), 1, n, f) == n &&
+              fwrite(&nl, 8, 1, f) == 1 && fwrite(c.name.data(), 1, nl, f) == nl &&
               fwrite(cubin.data(), 1, cubin.size(), f) == cubin.size();
     ok = fclose(f) == 0 && ok;
     if (!ok || rename(tmp.c_str(), path.c_str()) != 0) unlink(tmp.c_str());
 }
 
-int compile_source(const std::string& src, std::string* cubin) {
+// Compiles src; its kernel is the extern "C" function `name`, or, with
+// expr, the template instance the name expression expr denotes.
+int compile_source(const std::string& src, const char* name, const char* expr, Compiled* out) {
+    std::string* cubin = &out->cubin;
     nvrtcProgram_t prog = nullptr;
     nvrtcResult_t r = g_rtc.create(&prog, src.c_str(), "tile_spec.cu", kRtcHeaderCount,
                                    kRtcHeaderSources, kRtcHeaderNames);
     if (r) return sg::fail(SIMTGO_EDEVICE, "tile: nvrtcCreateProgram: %s", g_rtc.err(r));
+    if (expr && (r = g_rtc.add_name(prog, expr))) {
+        g_rtc.destroy(&prog);
+        return sg::fail(SIMTGO_EDEVICE, "tile: nvrtcAddNameExpression: %s", g_rtc.err(r));
+    }
     const std::string taps = "-DSIMTGO_TILE_MAX_TAPS=" + std::to_string(SIMTGO_TILE_MAX_TAPS);
     const char* opts[] = {kOptArch, "-std=c++17", "--fmad=false", taps.c_str()};
     r = g_rtc.compile(prog, 4, opts);
@@ -287,11 +309,73 @@ int compile_source(const std::string& src, std::string* cubin) {
                                         "%s\n%s",
                         g_rtc.err(r), log.c_str());
     }
+    out->name = name ? name : "";
+    if (expr) {
+        const char* lowered = nullptr;
+        if ((r = g_rtc.lowered(prog, expr, &lowered)) || !lowered) {
+            g_rtc.destroy(&prog);
+            return sg::fail(SIMTGO_EDEVICE, "tile: nvrtcGetLoweredName: %s", g_rtc.err(r));
+        }
+        out->name = lowered;
+    }
     size_t n = 0;
     g_rtc.cubin_size(prog, &n);
     cubin->assign(n, '\0');
     if (n) g_rtc.cubin(prog, &(*cubin)[0]);
     g_rtc.destroy(&prog);
+    return 0;
+}
+
+// The compiled entry for src (memory cache per device, then the disk cache,
+// then NVRTC), loaded on the current device with its dynamic shared memory
+// limit set to dyn_max. Returns nullptr with 0 when specialisation is off
+// or (mode 1) NVRTC is unavailable.
+int get_kernel(const std::string& src, const char* name, const char* expr, int dyn_max,
+               CUfunction* out);
+
+int get_kernel(const std::string& src, const char* name, const char* expr, int dyn_max,
+               CUfunction* out) {
+    *out = nullptr;
+    const int m = mode();
+    if (m == 0) return 0;
+    std::call_once(g_rtc_once, open_nvrtc);
+    std::call_once(g_drv_once, open_driver);
+    if (!g_rtc.ok || !g_drv.ok) {
+        if (m == 1) return 0;
+        return sg::fail(SIMTGO_EDEVICE, "tile: specialised kernels are required but %s",
+                        !g_rtc.ok ? g_rtc.why.c_str()
+                                  : "the driver's module entry points are not available");
+    }
+    int dev = -1;
+    int rc = sg::cuda_status(cudaGetDevice(&dev), "cudaGetDevice");
+    if (rc) return rc;
+    const std::string key = std::to_string(dev) + "|" + src;
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto it = g_cache.find(key);
+    if (it != g_cache.end()) {
+        *out = it->second.fn;
+        return 0;
+    }
+    Compiled c;
+    const std::string id = identity(src);
+    if (disk_read(id, &c)) {
+        g_disk_hits.fetch_add(1);
+    } else {
+        if ((rc = compile_source(src, name, expr, &c))) return rc;
+        g_compiled.fetch_add(1);
+        disk_write(id, c);
+    }
+    Entry e;
+    if ((rc = drv_status(g_drv.load(&e.mod, c.cubin.data()), "cuModuleLoadData"))) return rc;
+    if ((rc = drv_status(g_drv.get_fn(&e.fn, e.mod, c.name.c_str()), "cuModuleGetFunction")))
+        return rc;
+    if (dyn_max > 0 &&
+        (rc = drv_status(
+             g_drv.set_attr(e.fn, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, dyn_max),
+             "cuFuncSetAttribute")))
+        return rc;
+    g_cache.emplace(key, e);
+    *out = e.fn;
     return 0;
 }
 
@@ -345,47 +429,47 @@ std::string spec_source(const tilek::Program& P, const Form& f) {
 }
 
 int get(const tilek::Program& P, const Form& f, int dyn_max, CUfunction* out) {
-    *out = nullptr;
-    const int m = mode();
-    if (m == 0) return 0;
+    return get_kernel(spec_source(P, f), "k_tile_spec", nullptr, dyn_max, out);
+}
+
+// A streaming reduction's specialised kernel: k_red_direct<kind,
+// StaticChain<Steps>> with the chain's steps as constants (the factors stay
+// in the parameter block).
+std::string chain_source(int kind, const tilek::Chain& ch, std::string* expr_out) {
+    std::string src = kPrelude;
+    src += "#include \"tile_kernel.cuh\"\nstruct Steps {\n  static constexpr int n = " +
+           std::to_string(ch.n) + ";\n  static constexpr int op[] = {";
+    for (int i = 0; i < std::max(ch.n, 1); i++)
+        src += (i ? ", " : "") + std::to_string(i < ch.n ? ch.op[i] : 0);
+    src += "};\n};\n";
+    const std::string expr =
+        "tilek::k_red_direct<" + std::to_string(kind) + ", tilek::StaticChain<Steps>>";
+    src += "template __global__ void " + expr +
+           "(const float* __restrict__, int64_t, int64_t, const tilek::Chain, float* "
+           "__restrict__, int64_t* __restrict__, int64_t, int64_t);\n";
+    *expr_out = expr;
+    return src;
+}
+
+int get_chain(int kind, const tilek::Chain& ch, CUfunction* out) {
+    std::string expr;
+    const std::string src = chain_source(kind, ch, &expr);
+    return get_kernel(src, nullptr, expr.c_str(), 0, out);
+}
+
+int compile_chain_only(int kind, const tilek::Chain& ch) {
     std::call_once(g_rtc_once, open_nvrtc);
-    std::call_once(g_drv_once, open_driver);
-    if (!g_rtc.ok || !g_drv.ok) {
-        if (m == 1) return 0;
-        return sg::fail(SIMTGO_EDEVICE, "tile: specialised kernels are required but %s",
-                        !g_rtc.ok ? g_rtc.why.c_str()
-                                  : "the driver's module entry points are not available");
-    }
-    int dev = -1;
-    int rc = sg::cuda_status(cudaGetDevice(&dev), "cudaGetDevice");
-    if (rc) return rc;
-    const std::string src = spec_source(P, f);
-    const std::string key = std::to_string(dev) + "|" + src;
-    std::lock_guard<std::mutex> lk(g_mu);
-    auto it = g_cache.find(key);
-    if (it != g_cache.end()) {
-        *out = it->second.fn;
+    if (!g_rtc.ok) return sg::fail(SIMTGO_EDEVICE, "tile: %s", g_rtc.why.c_str());
+    std::string expr;
+    const std::string src = chain_source(kind, ch, &expr), id = identity(src);
+    Compiled c;
+    if (disk_read(id, &c)) {
+        g_disk_hits.fetch_add(1);
         return 0;
     }
-    std::string cubin;
-    const std::string id = identity(src);
-    if (disk_read(id, &cubin)) {
-        g_disk_hits.fetch_add(1);
-    } else {
-        if ((rc = compile_source(src, &cubin))) return rc;
-        g_compiled.fetch_add(1);
-        disk_write(id, cubin);
-    }
-    Entry e;
-    if ((rc = drv_status(g_drv.load(&e.mod, cubin.data()), "cuModuleLoadData"))) return rc;
-    if ((rc = drv_status(g_drv.get_fn(&e.fn, e.mod, "k_tile_spec"), "cuModuleGetFunction")))
-        return rc;
-    if ((rc = drv_status(
-             g_drv.set_attr(e.fn, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, dyn_max),
-             "cuFuncSetAttribute")))
-        return rc;
-    g_cache.emplace(key, e);
-    *out = e.fn;
+    if (int rc = compile_source(src, nullptr, expr.c_str(), &c)) return rc;
+    g_compiled.fetch_add(1);
+    disk_write(id, c);
     return 0;
 }
 
@@ -401,14 +485,14 @@ int compile_only(const tilek::Program& P, const Form& f) {
     std::call_once(g_rtc_once, open_nvrtc);
     if (!g_rtc.ok) return sg::fail(SIMTGO_EDEVICE, "tile: %s", g_rtc.why.c_str());
     const std::string src = spec_source(P, f), id = identity(src);
-    std::string cubin;
-    if (disk_read(id, &cubin)) {
+    Compiled c;
+    if (disk_read(id, &c)) {
         g_disk_hits.fetch_add(1);
         return 0;
     }
-    if (int rc = compile_source(src, &cubin)) return rc;
+    if (int rc = compile_source(src, "k_tile_spec", nullptr, &c)) return rc;
     g_compiled.fetch_add(1);
-    disk_write(id, cubin);
+    disk_write(id, c);
     return 0;
 }
 

@@ -30,6 +30,15 @@ std::string spec_source(const tilek::Program& P, const Form& f);
 // with 0 when specialisation is off or (mode 1) NVRTC is unavailable.
 int get(const tilek::Program& P, const Form& f, int dyn_max, CUfunction* out);
 
+// The streaming reduction k_red_direct<kind> with the chain ch's steps as
+// constants (compiled and cached like get); nullptr with 0 when
+// specialisation is off or unavailable.
+int get_chain(int kind, const tilek::Chain& ch, CUfunction* out);
+// Its source (and the kernel's name expression), and a compile without
+// loading (no GPU needed).
+std::string chain_source(int kind, const tilek::Chain& ch, std::string* expr);
+int compile_chain_only(int kind, const tilek::Chain& ch);
+
 // Whether launches use specialised kernels (mode != 0 and NVRTC and the
 // driver's module entry points are there; always true in mode 2).
 bool available();

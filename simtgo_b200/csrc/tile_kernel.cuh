@@ -891,8 +891,49 @@ __device__ __forceinline__ void row_argmax(const float4 (&V)[2], int w, int lane
 // out_i[b] = idx_base + the position) receive the chunk partials. Rows
 // stream through a ring of four register slots, three rows ahead of the
 // one being reduced.
-template <int KIND>
-__global__ void __launch_bounds__(kThreads) k_red_direct(const float* __restrict__ x, int64_t n,
+// The chain's steps applied to a row: RunChain reads them from the
+// parameter block at run time (one uniform branch per step); StaticChain<S>
+// has them as compile-time constants (S::n steps, S::op[i]; a reduction's
+// specialised kernel, compiled at run time), so a row's steps are
+// straight-line code. Both take Scale's factor from the parameter block.
+struct RunChain {
+    static constexpr int kMinBlocks = 0;  // no minimum: the compiler's own register choice
+    __device__ __forceinline__ static void apply(const Chain& ch, float4 (&A)[2]) {
+        apply_chain<2>(ch, A);
+    }
+};
+template <class S, int I>
+__device__ __forceinline__ void apply_static(const Chain& ch, float4 (&A)[2]) {
+    if constexpr (I < S::n) {
+        constexpr int op = S::op[I];
+#pragma unroll
+        for (int j = 0; j < 2; j++) {
+            if constexpr (op == OP_SCALE)
+                A[j] = f4_scale(ch.imm[I], A[j]);
+            else if constexpr (op == OP_SQRT)
+                A[j] = f4_sqrt(A[j]);
+            else if constexpr (op == OP_ABS)
+                A[j] = f4_abs(A[j]);
+            else if constexpr (op == OP_ADD)
+                A[j] = f4_add(A[j], A[j]);
+            else
+                A[j] = f4_mul(A[j], A[j]);
+        }
+        apply_static<S, I + 1>(ch, A);
+    }
+}
+template <class S>
+struct StaticChain {
+    // Unrolled steps raise the register count; three blocks per SM keep
+    // the rows in flight.
+    static constexpr int kMinBlocks = 3;
+    __device__ __forceinline__ static void apply(const Chain& ch, float4 (&A)[2]) {
+        apply_static<S, 0>(ch, A);
+    }
+};
+
+template <int KIND, class CH = RunChain>
+__global__ void __launch_bounds__(kThreads, CH::kMinBlocks) k_red_direct(const float* __restrict__ x, int64_t n,
                                                          int64_t idx_base, const Chain ch,
                                                          float* __restrict__ out,
                                                          int64_t* __restrict__ out_i,
@@ -921,7 +962,7 @@ __global__ void __launch_bounds__(kThreads) k_red_direct(const float* __restrict
             else if (b + 1 < b1)
                 load_row(x, n, b + 1, w + 3 - 8, lane, R[(w + 3) & 3]);
             float4 (&cur)[2] = R[w & 3];
-            apply_chain<2>(ch, cur);
+            CH::apply(ch, cur);
             if constexpr (KIND == RED_ARGMAX) {
                 uint32_t K;
                 int32_t O;

@@ -107,7 +107,8 @@ class Tensor:
         program as compile-time constants, tile_jit.cu) for `groups` float4
         groups per thread and bulk-copied or directly read inputs; with
         compile=True NVRTC also compiles it (no GPU needed) and a failure
-        raises."""
+        raises. groups=0 with a reduction of a chain of steps on one input:
+        the streaming reduction's kernel for that chain."""
         L, g = self.g._L, self.g._h
         need = L.simtgo_tile_jit_source(g, self.node, reduce, groups, int(bulk), int(compile),
                                         None, 0)

@@ -184,3 +184,35 @@ def test_kernel_from_disk_cache_runs(tmp_path):
     c2, h2, y2 = run("second")
     assert (c1, h1) == (1, 0) and (c2, h2) == (0, 1)
     assert np.array_equal(bits(y1), bits(y2))
+
+
+@pytest.mark.parametrize("kind", list(KINDS))
+def test_streaming_chains_both_modes(kind):
+    """Reductions of a chain of steps on one aligned device input (the
+    streaming path), with a NaN, a -0 and an infinity among the values: the
+    chain compiled in as constants against the run-time chain, bit for bit
+    (value and index). The oracle's tree pins the run-time chain in
+    test_gpu_tile_reduce.py."""
+    n = (1 << 21) + 1234
+    rng = np.random.default_rng(7)
+    xs = rng.uniform(-4, 4, n).astype(np.float32)
+    xs[[5, 77777, n - 3]] = [np.nan, -0.0, np.inf]
+    g = tile.New()
+    keep = torch.from_numpy(xs).cuda()
+    a = g.InputDevice(keep)
+    chains = {
+        "abs_scale": tile.Abs(tile.Scale(a, -2.0)),
+        "sqrt_abs": tile.Sqrt(tile.Abs(a)),
+        "mul_add": tile.Mul(tile.Add(a, a), tile.Add(a, a)),
+        "scale_abs_scale": tile.Scale(tile.Abs(tile.Scale(a, 0.75)), -3.0),
+    }
+    for name, t in chains.items():
+        def run():
+            v = torch.empty(1, device="cuda")
+            i = torch.empty(1, dtype=torch.int64, device="cuda")
+            KINDS[kind](t).Run(v, i)
+            torch.cuda.synchronize()
+            return (int(i.item()) if kind == "argmax" else None), v.cpu().numpy()[0]
+
+        interp, spec = both(run)
+        assert interp[0] == spec[0] and bits(interp[1]) == bits(spec[1]), (kind, name)

@@ -123,3 +123,24 @@ def test_disk_cache_across_processes(tmp_path):
     assert run() == (0, 1)
     env["SIMTGO_B200_CACHE"] = "off"
     assert run() == (1, 0)
+
+
+@needs_nvrtc
+@pytest.mark.parametrize("reduce", [0, 1, 2, 3])
+def test_streaming_chain_compiles(reduce):
+    """The streaming reduction's kernel for a chain on one input: the steps
+    in order as constants, the kernel named by its template instance."""
+    g = tile.New()
+    a = g.Input(np.ones(5000, f32))
+    t = tile.Mul(tile.Sqrt(tile.Abs(tile.Scale(a, -2.0))), tile.Sqrt(tile.Abs(tile.Scale(a, -2.0))))
+    # Mul of two different nodes is not a chain; a chain is x op x:
+    s = tile.Sqrt(tile.Abs(tile.Scale(a, -2.0)))
+    c = tile.Add(s, s)
+    src = c.JITSource(reduce=reduce, groups=0, compile=True)
+    assert "static constexpr int n = 4;" in src
+    assert "op[] = {6, 8, 7, 3}" in src                     # Scale, Abs, Sqrt, Add
+    assert f"k_red_direct<{reduce}, tilek::StaticChain<Steps>>" in src
+    with pytest.raises(SimtgoError):
+        t.JITSource(reduce=reduce, groups=0)                 # not a chain
+    with pytest.raises(SimtgoError):
+        c.JITSource(reduce=-1, groups=0)                     # not a reduction
