@@ -788,14 +788,18 @@ def bench_tile_reduce(args, torch, L, dev, rank, world, barrier, max_over_ranks,
     peak = measured_peaks()[0]["hbm_gbs"]
     res = {"elements_total": total, "scaling": "strong", "bytes_per_element": 4,
            "split": "whole blocks of 2048 per rank (tile.ShardRange)"}
-    for name, red in (("sum_of_squares", tile.Sum(tile.Mul(a, a))), ("argmax", tile.ArgMax(a))):
+    # argmax_abs: the peak of |k x| (a chain of two steps, which runs in
+    # its own specialised streaming kernel).
+    for name, red in (("sum_of_squares", tile.Sum(tile.Mul(a, a))), ("argmax", tile.ArgMax(a)),
+                      ("argmax_abs", tile.ArgMax(tile.Abs(tile.Scale(a, -2.0))))):
         barrier()
         ms = max_over_ranks(timed(lambda: red.RunShard(comm, total, v, i, stream=stream),
                                   args.steps, args.warmup, stream, events))
         gbs = 4.0 * total / (ms * 1e-3) / 1e9
         res[name] = {"ms": round(ms, 4), "gbs": round(gbs, 1),
                      "frac_hbm_per_gpu": round(gbs / world / peak, 4),
-                     "value": float(v.item()), "index": int(i.item()) if name == "argmax" else None}
+                     "value": float(v.item()),
+                     "index": int(i.item()) if name.startswith("argmax") else None}
     barrier()
     _lib.check(L.simtgo_comm_destroy(comm))
     return res
