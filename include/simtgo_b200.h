@@ -72,8 +72,10 @@ int simtgo_device_info(int32_t* sm_count, int32_t* cc_major, int32_t* cc_minor);
 /* cudaStreamSynchronize(stream); the synchronous tail of simt.Kernel.Launch. */
 int simtgo_stream_sync(void* stream);
 /* Frees the library's private device resources: the buffers, streams and
- * events of simtgo_FIR_shard_host on every device that used it, and the
- * freed scratch the tile reductions' memory pool keeps mapped. Call with no
+ * events of simtgo_FIR_shard_host on every device that used it, the freed
+ * scratch the tile reductions' memory pool keeps mapped, and the modules of
+ * the specialised tile kernels (a later launch loads them again, from the
+ * on-disk cache when it has them). Call with no
  * library work in flight (e.g. before the process or the Go context ends);
  * later calls allocate afresh. Caller-owned buffers and communicators
  * (simtgo_comm_destroy) are not touched; the fixed 16 MiB scratch of

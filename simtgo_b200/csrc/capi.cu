@@ -163,7 +163,8 @@ int simtgo_shutdown(void) {
     sg::clear_error();
     const int rc = sg::fir_host_release();
     const int rc2 = sg::tile_pool_release();
-    return rc ? rc : rc2;
+    const int rc3 = sg::tile_jit_release();
+    return rc ? rc : rc2 ? rc2 : rc3;
 }
 
 int simtgo_device_info(int32_t* sm_count, int32_t* cc_major, int32_t* cc_minor) {

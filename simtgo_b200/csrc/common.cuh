@@ -50,6 +50,7 @@ int watchdog_check_and_clear(uint32_t* bits);
 // Private resources released by simtgo_shutdown (fir.cu).
 int fir_host_release();
 int tile_pool_release();  // trims the tile reductions' scratch pools (simtgo_shutdown)
+int tile_jit_release();   // unloads the specialised tile kernels' modules (simtgo_shutdown)
 
 // ---- launch-contract checks (simt/kernel.go:293-369, :488-514) -------------
 // The covered thread extent of a 1-D launch, or a status code. Refuses what

@@ -116,6 +116,7 @@ struct Drv {
                        unsigned, CUstream, void**, void**);
     CUresult (*occupancy)(int*, CUfunction, int, size_t);
     CUresult (*err)(CUresult, const char**);
+    CUresult (*unload)(CUmodule);
     bool ok = false;
 };
 Drv g_drv;
@@ -138,6 +139,7 @@ void open_driver() {
     g_drv.launch = (decltype(g_drv.launch))ep("cuLaunchKernel");
     g_drv.occupancy = (decltype(g_drv.occupancy))ep("cuOccupancyMaxActiveBlocksPerMultiprocessor");
     g_drv.err = (decltype(g_drv.err))ep("cuGetErrorString");
+    g_drv.unload = (decltype(g_drv.unload))ep("cuModuleUnload");
     g_drv.ok = all;
 }
 
@@ -186,6 +188,7 @@ struct Entry {
 };
 std::mutex g_mu;
 std::unordered_map<std::string, Entry> g_cache;  // key: device | source
+std::unordered_map<std::string, int> g_cache_dev;  // key -> its device
 
 const char* const kOptArch = "-arch=sm_100a";
 
@@ -375,6 +378,7 @@ int get_kernel(const std::string& src, const char* name, const char* expr, int d
              "cuFuncSetAttribute")))
         return rc;
     g_cache.emplace(key, e);
+    g_cache_dev.emplace(key, dev);
     *out = e.fn;
     return 0;
 }
@@ -509,6 +513,26 @@ int launch(CUfunction fn, int blocks, size_t smem, cudaStream_t s, void** args) 
 }
 
 }  // namespace tilejit
+
+namespace sg {
+// Unloads every specialised kernel's module (simtgo_shutdown), each with its
+// device current; later launches compile or load them again.
+int tile_jit_release() {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (g_cache.empty()) return 0;
+    int prev = 0, rc = 0;
+    cudaGetDevice(&prev);
+    for (auto& kv : g_cache) {
+        int r = cuda_status(cudaSetDevice(g_cache_dev[kv.first]), "cudaSetDevice");
+        if (!r && g_drv.unload) r = drv_status(g_drv.unload(kv.second.mod), "cuModuleUnload");
+        if (r && !rc) rc = r;
+    }
+    g_cache.clear();
+    g_cache_dev.clear();
+    cudaSetDevice(prev);
+    return rc;
+}
+}  // namespace sg
 
 extern "C" {
 

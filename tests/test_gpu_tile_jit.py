@@ -216,3 +216,23 @@ def test_streaming_chains_both_modes(kind):
 
         interp, spec = both(run)
         assert interp[0] == spec[0] and bits(interp[1]) == bits(spec[1]), (kind, name)
+
+
+def test_shutdown_unloads_and_relaunch_reloads():
+    """simtgo_shutdown unloads the specialised kernels' modules; the next
+    launch of the same graph loads its kernel again (from the on-disk cache,
+    not a compilation) and computes the same bits."""
+    from simtgo_b200 import _lib
+
+    rng = np.random.default_rng(21)
+    g = tile.New()
+    a, b = (g.Input(rng.uniform(-4, 4, 70001).astype(np.float32)) for _ in range(2))
+    t = tile.Add(tile.Hypot(a, b), tile.FIR(tile.Abs(a), np.full(13, 1 / 13, np.float32)))
+    tile.SetJIT(2)
+    y1 = t.Materialize()
+    _, _, compiled, _, hits = tile.JITInfo()
+    _lib.check(_lib.load().simtgo_shutdown())
+    y2 = t.Materialize()
+    _, _, compiled2, _, hits2 = tile.JITInfo()
+    assert compiled2 == compiled and hits2 == hits + 1
+    assert np.array_equal(bits(y1), bits(y2))
