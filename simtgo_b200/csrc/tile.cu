@@ -1056,15 +1056,18 @@ int launch_partials(const simtgo_tile_graph* g, int root, int kind, int64_t n, i
             if ((rc = sg::current_device(&d))) return rc;
             // One wave of resident blocks; each warp takes a contiguous
             // range of chunks.
-            // A chain of steps runs in the reduction's specialised kernel
-            // (the steps compiled in as constants: straight-line code per
-            // row) when run-time compilation is on: measured at 2^28,
-            // ArgMax(Abs(Scale(a, k))) 0.54 -> 0.205 ms, Max(Abs(a)) 0.250 ->
-            // 0.195, Sum(Sqrt(Abs(a))) 0.390 -> 0.216, Sum(a*a) 0.176 ->
-            // 0.170 (the run-time chain's branch per step and row held the
-            // rows' loads back).
+            // A chain with steps, and any ArgMax, runs in the reduction's
+            // specialised kernel (the steps compiled in as constants:
+            // straight-line code per row) when run-time compilation is on:
+            // measured at 2^28, ArgMax(Abs(Scale(a, k))) 0.54 -> 0.205 ms,
+            // Max(Abs(a)) 0.250 -> 0.195, Sum(Sqrt(Abs(a))) 0.390 -> 0.216,
+            // Sum(a*a) 0.176 -> 0.170, ArgMax(a) 0.212 -> 0.183 (the run-time
+            // chain's branch per step and row held the rows' loads back);
+            // Sum(a) and Max(a), with no step, stay on the precompiled
+            // kernel (0.170 and 0.185 there, 0.175 and 0.197 specialised).
             CUfunction spec = nullptr;
-            if (ch.n > 0 && tilejit::available() && (rc = tilejit::get_chain(kind, ch, &spec)))
+            if ((ch.n > 0 || kind == tilek::RED_ARGMAX) && tilejit::available() &&
+                (rc = tilejit::get_chain(kind, ch, &spec)))
                 return rc;
             int ps;
             if (spec)
