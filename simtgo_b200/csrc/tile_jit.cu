@@ -75,12 +75,21 @@ struct Nvrtc {
 Nvrtc g_rtc;
 std::once_flag g_rtc_once;
 
+// SIMTGO_NVRTC_LIB names the library to open instead of libnvrtc.so.12
+// (a path, or a name the loader searches for).
 void open_nvrtc() {
-    void* h = dlopen("libnvrtc.so.12", RTLD_NOW | RTLD_LOCAL);
-    if (!h) h = dlopen("libnvrtc.so", RTLD_NOW | RTLD_LOCAL);
+    const char* want = getenv("SIMTGO_NVRTC_LIB");
+    void* h = nullptr;
+    if (want && *want) {
+        h = dlopen(want, RTLD_NOW | RTLD_LOCAL);
+    } else {
+        h = dlopen("libnvrtc.so.12", RTLD_NOW | RTLD_LOCAL);
+        if (!h) h = dlopen("libnvrtc.so", RTLD_NOW | RTLD_LOCAL);
+    }
     if (!h) {
         const char* e = dlerror();
-        g_rtc.why = std::string("libnvrtc.so.12 could not be opened: ") + (e ? e : "?");
+        g_rtc.why = std::string(want && *want ? want : "libnvrtc.so.12") +
+                    " could not be opened: " + (e ? e : "?");
         return;
     }
     bool all = true;

@@ -236,3 +236,41 @@ def test_shutdown_unloads_and_relaunch_reloads():
     _, _, compiled2, _, hits2 = tile.JITInfo()
     assert compiled2 == compiled and hits2 == hits + 1
     assert np.array_equal(bits(y1), bits(y2))
+
+
+def test_without_nvrtc_falls_back_or_fails(tmp_path):
+    """With libnvrtc unavailable, mode 1 runs the graph on the interpreter
+    (no specialised launch, the same bits) and mode 2 refuses with an
+    error; nothing crashes."""
+    import os
+    import subprocess
+    import sys
+
+    prog = (
+        "import sys, numpy as np\n"
+        "from simtgo_b200 import tile\n"
+        "from simtgo_b200._lib import SimtgoError\n"
+        "rng = np.random.default_rng(5)\n"
+        "g = tile.New()\n"
+        "a, b = (g.Input(rng.uniform(-4, 4, 50001).astype(np.float32)) for _ in range(2))\n"
+        "t = tile.Mul(tile.FIR(a, np.full(7, 1 / 7, np.float32)), tile.Sqrt(tile.Abs(b)))\n"
+        "np.save(sys.argv[1], t.Materialize())\n"
+        "launches = tile.JITInfo()[3]\n"
+        "tile.SetJIT(2)\n"
+        "try:\n"
+        "    t.Materialize()\n"
+        "    refused = False\n"
+        "except SimtgoError:\n"
+        "    refused = True\n"
+        "print(launches, refused)\n")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    base = dict(os.environ, SIMTGO_B200_CACHE="off")
+    bad = dict(base, SIMTGO_NVRTC_LIB=str(tmp_path / "no_such_libnvrtc.so"))
+    out = subprocess.run([sys.executable, "-c", prog, str(tmp_path / "interp")], env=bad,
+                         cwd=root, check=True, capture_output=True, text=True).stdout.split()
+    assert out == ["0", "True"]
+    out = subprocess.run([sys.executable, "-c", prog, str(tmp_path / "spec")], env=base,
+                         cwd=root, check=True, capture_output=True, text=True).stdout.split()
+    assert out[0] != "0" and out[1] == "False"
+    assert np.array_equal(bits(np.load(tmp_path / "interp.npy")),
+                          bits(np.load(tmp_path / "spec.npy")))

@@ -144,3 +144,32 @@ def test_streaming_chain_compiles(reduce):
         t.JITSource(reduce=reduce, groups=0)                 # not a chain
     with pytest.raises(SimtgoError):
         c.JITSource(reduce=-1, groups=0)                     # not a reduction
+
+
+def test_without_nvrtc(tmp_path):
+    """Where libnvrtc cannot be opened, mode 1 reports it unavailable (and
+    launches would use the interpreter), and compiling a specialised source
+    fails with a message instead of crashing."""
+    import os
+    import subprocess
+    import sys
+
+    prog = (
+        "import numpy as np\n"
+        "from simtgo_b200 import tile\n"
+        "from simtgo_b200._lib import SimtgoError\n"
+        "m, avail, _, _, _ = tile.JITInfo()\n"
+        "g = tile.New()\n"
+        "a = g.Input(np.ones(100, np.float32))\n"
+        "t = tile.Scale(a, 2.0)\n"
+        "src = t.JITSource(groups=4)\n"
+        "try:\n"
+        "    t.JITSource(groups=4, compile=True)\n"
+        "    print(m, avail, 'compiled')\n"
+        "except SimtgoError as e:\n"
+        "    print(m, avail, 'refused', 'could not be opened' in str(e))\n")
+    env = dict(os.environ, SIMTGO_NVRTC_LIB=str(tmp_path / "no_such_libnvrtc.so"))
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    out = subprocess.run([sys.executable, "-c", prog], env=env, cwd=root, check=True,
+                         capture_output=True, text=True).stdout.split()
+    assert out == ["1", "False", "refused", "True"]
