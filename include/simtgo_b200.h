@@ -326,7 +326,8 @@ int32_t simtgo_tile_source(simtgo_tile_graph* g, simtgo_tensor t, char* buf, int
  * computing the same bits as the interpreter it replaces. Mode 0: the
  * interpreter only; 1 (the default, or SIMTGO_TILE_JIT=1 in the environment
  * before the first tile launch): specialise, or interpret when libnvrtc
- * cannot be opened; 2: specialise or fail with SIMTGO_EDEVICE. A first launch
+ * cannot be opened (libnvrtc.so.12, or the library SIMTGO_NVRTC_LIB names);
+ * 2: specialise or fail with SIMTGO_EDEVICE. A first launch
  * of a new program compiles (about a second) before it enqueues, so make it
  * before any stream capture. */
 int simtgo_tile_set_jit(int32_t mode);
