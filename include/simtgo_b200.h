@@ -319,11 +319,14 @@ int32_t simtgo_tile_source(simtgo_tile_graph* g, simtgo_tensor t, char* buf, int
 
 /* Specialised kernels (tile/run.go:38 run -> internal/jit/jit.go Load: the
  * reference compiles each distinct graph with NVRTC and caches the result).
- * Every launch of a fused program (materialise, run, shards, reductions,
- * stepwise steps) runs the program's own specialised kernel: the lowered
+ * Every launch of a fused program of up to 32 device instructions
+ * (simtgo_tile_program_size) -- materialise, run, shards, reductions,
+ * stepwise steps -- runs the program's own specialised kernel: the lowered
  * program compiled in as constants (NVRTC, sm_100a, on first use of each
  * distinct program per device, then cached for the life of the process),
- * computing the same bits as the interpreter it replaces. Mode 0: the
+ * computing the same bits as the interpreter it replaces. Longer programs
+ * run on the interpreter in every mode (their compile time grows faster
+ * than their length, while their dispatch is spread over more work). Mode 0: the
  * interpreter only; 1 (the default, or SIMTGO_TILE_JIT=1 in the environment
  * before the first tile launch): specialise, or interpret when libnvrtc
  * cannot be opened (libnvrtc.so.12, or the library SIMTGO_NVRTC_LIB names);

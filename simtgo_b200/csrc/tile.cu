@@ -526,6 +526,13 @@ struct Layout {
 // (registers); programs with more keep them in shared memory.
 constexpr int kTmpRegFloats = 32;
 
+// Device instructions up to which a program gets a specialised kernel;
+// longer ones run on the interpreter (whose dispatch cost they amortise over
+// more work). Compile time grows faster than the length: measured 0.7 s at
+// 9 instructions, 1.3 s at 18, 2.6 s at 30, 4.8 s at 42, 14 s at 75, and
+// from a few hundred on NVRTC refuses the template recursion.
+constexpr int kMaxSpecCode = 32;
+
 // The float4 offsets of the layout's parts for Y.g groups per thread; hs
 // is the samples a chunk's windows reach below it.
 void set_offsets(const Lowered& L, int32_t hs, Layout& Y) {
@@ -632,7 +639,7 @@ int launch_program(const simtgo_tile_graph* g, const Lowered& L,
     // A specialised kernel keeps the program's temporaries in registers
     // when they take at most kTmpRegFloats per thread (each is the thread's
     // G float4 groups), and then reserves no shared memory for them.
-    const bool jit_on = jit_ok && tilejit::available();
+    const bool jit_on = jit_ok && (int)L.code.size() <= kMaxSpecCode && tilejit::available();
     auto tmp_regs = [&](int g) {
         return jit_on && L.n_tmp > 0 && L.n_tmp * g * 4 <= kTmpRegFloats;
     };

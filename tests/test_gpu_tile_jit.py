@@ -274,3 +274,23 @@ def test_without_nvrtc_falls_back_or_fails(tmp_path):
     assert out[0] != "0" and out[1] == "False"
     assert np.array_equal(bits(np.load(tmp_path / "interp.npy")),
                           bits(np.load(tmp_path / "spec.npy")))
+
+
+def test_long_program_runs_on_the_interpreter():
+    """A program of more than 32 device instructions runs on the
+    interpreter in every mode (its compile would outgrow its run): no
+    specialised launch, and the interpreter's bits."""
+    rng = np.random.default_rng(9)
+    g = tile.New()
+    a, b = (g.Input(rng.uniform(-1, 1, 30001).astype(np.float32)) for _ in range(2))
+    t = a
+    for i in range(30):
+        t = tile.Add(tile.Mul(t, b), a) if i % 2 else tile.Scale(t, 0.5)
+    assert t.ProgramSize()[0] > 32
+    tile.SetJIT(0)
+    y0 = t.Materialize()
+    tile.SetJIT(2)
+    before = tile.JITInfo()[3]
+    y2 = t.Materialize()
+    assert tile.JITInfo()[3] == before
+    assert np.array_equal(bits(y0), bits(y2))
