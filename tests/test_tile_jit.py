@@ -76,16 +76,21 @@ def test_reduction_compiles(reduce):
 
 
 @needs_nvrtc
-@pytest.mark.parametrize("seed", [0, 1, 2])
+@pytest.mark.parametrize("seed", range(8))
 def test_random_graphs_compile(seed):
+    """Every form the launcher can pick compiles for random graphs (shared
+    values, x-op-x nodes, windows, reductions), one form per seed."""
     root, _ = _random_graph(seed, 3001, 0)
-    root.JITSource(groups=4 if seed % 2 else 2, bulk=seed != 2, compile=True)
+    reduce = (-1, 0, 3, -1)[seed % 4]
+    root.JITSource(reduce=reduce, groups=4 if seed % 2 else 2, bulk=seed % 3 != 2,
+                   compile=True)
 
 
 @needs_nvrtc
-def test_chained_windows_compile():
-    root, _ = _chained_graph(1, 3001, 0)
-    root.JITSource(groups=2, bulk=True, compile=True)
+@pytest.mark.parametrize("seed", [1, 2, 5])
+def test_chained_windows_compile(seed):
+    root, _ = _chained_graph(seed, 3001, 0)
+    root.JITSource(groups=2, bulk=seed != 2, compile=True)
 
 
 @needs_nvrtc
@@ -120,6 +125,9 @@ def test_disk_cache_across_processes(tmp_path):
     data[20] ^= 0xFF                 # the stored identity no longer matches
     files[0].write_bytes(bytes(data))
     assert run() == (1, 0)          # a miss: compiled again and rewritten
+    assert run() == (0, 1)
+    files[0].write_bytes(files[0].read_bytes()[:100])  # truncated mid-identity
+    assert run() == (1, 0)
     assert run() == (0, 1)
     env["SIMTGO_B200_CACHE"] = "off"
     assert run() == (1, 0)
