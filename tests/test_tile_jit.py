@@ -181,3 +181,39 @@ def test_without_nvrtc(tmp_path):
     out = subprocess.run([sys.executable, "-c", prog], env=env, cwd=root, check=True,
                          capture_output=True, text=True).stdout.split()
     assert out == ["1", "False", "refused", "True"]
+
+
+_OPS = {3: "add", 4: "mul", 5: "hypot", 6: "scale", 7: "sqrt", 8: "abs", 9: "firacc"}
+
+
+def _steps_of(op, flags):
+    """The listing's step kinds of one device instruction, decoded from its
+    op and flags the way the kernel runs them: load, operation, temporary,
+    window tile, output, end."""
+    steps = []
+    if flags & 1:
+        steps.append("lda")
+    if op in _OPS:
+        steps.append(_OPS[op])
+    for bit, name in ((16, "sta"), (32, "stage"), (64, "store"), (128, "end")):
+        if flags & bit:
+            steps.append(name)
+    return steps
+
+
+@pytest.mark.parametrize("seed", range(6))
+def test_source_is_the_listed_program(seed):
+    """The specialised source's constant program is the lowered program the
+    listing (Tensor.Source) shows, instruction by instruction; main_start and
+    the windows' start points agree too."""
+    root, _ = _random_graph(seed, 3001, 0)
+    listing = [ln for ln in root.Source().splitlines() if ln[:1].isdigit()]
+    want = [[st.split()[0] for st in ln.split(" ", 1)[1].split(" | ")] for ln in listing]
+    src = root.JITSource(groups=2, bulk=True)
+    code = src.split("code[] = {", 1)[1].split("};", 1)[0]
+    got = [_steps_of(int(m[0]), int(m[1]))
+           for m in re.findall(r"\{(\d+), (\d+), \d+, \d+, \d+, 0\.0f, 0u\}", code)]
+    assert got == want
+    main = int(re.search(r"main_start = (\d+)", src).group(1))
+    text = root.Source()
+    assert text.splitlines()[text.splitlines().index("main") + 1].startswith(f"{main} ")
