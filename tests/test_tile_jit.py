@@ -214,6 +214,13 @@ def test_source_is_the_listed_program(seed):
     got = [_steps_of(int(m[0]), int(m[1]))
            for m in re.findall(r"\{(\d+), (\d+), \d+, \d+, \d+, 0\.0f, 0u\}", code)]
     assert got == want
+    lines = root.Source().splitlines()
     main = int(re.search(r"main_start = (\d+)", src).group(1))
-    text = root.Source()
-    assert text.splitlines()[text.splitlines().index("main") + 1].startswith(f"{main} ")
+    assert lines[lines.index("main") + 1].startswith(f"{main} ")
+    fir = src.split("fir[] = {", 1)[1].split("};", 1)[0]
+    starts = [int(m) for m in re.findall(r"\{(\d+), \d+, \d+, \d+\}", fir)]
+    heads = [i for i, ln in enumerate(lines) if ln.startswith("window ")]
+    if heads:
+        assert [int(lines[i + 1].split()[0]) for i in heads] == starts
+        assert [int(lines[i].split()[3]) for i in heads] == [
+            int(m) & 0xFF for m in re.findall(r"\{\d+, (\d+), \d+, \d+\}", fir)]
