@@ -157,7 +157,7 @@ extern "C" {
 
 const char* simtgo_last_error(void) { return t_msg; }
 
-const char* simtgo_version(void) { return "simtgo_b200 0.1.0 (sm_100a)"; }
+const char* simtgo_version(void) { return "simtgo_b200 0.2.0 (sm_100a; tile programs specialised by NVRTC)"; }
 
 int simtgo_shutdown(void) {
     sg::clear_error();
