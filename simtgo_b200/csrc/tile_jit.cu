@@ -15,11 +15,17 @@
 // module loaded through the runtime's driver entry points, so the library
 // links against neither.
 //
+// A streaming reduction (k_red_direct) is specialised the same way: its
+// chain of steps compiled in as constants (get_chain), the kernel named by
+// its template instance (an NVRTC name expression).
+//
 // Modes (simtgo_tile_set_jit, or SIMTGO_TILE_JIT in the environment at the
 // first tile launch): 0 = the interpreter only; 1 (default) = specialise
-// every program, falling back to the interpreter when NVRTC cannot be opened;
-// 2 = specialise or fail. A program whose compilation fails is an error in
-// modes 1 and 2 (it is a bug, not a missing dependency).
+// every program tile.cu routes here (up to 32 instructions), falling back to
+// the interpreter when NVRTC cannot be opened (libnvrtc.so.12, or the
+// library SIMTGO_NVRTC_LIB names); 2 = specialise or fail. A program whose
+// compilation fails is an error in modes 1 and 2 (it is a bug, not a
+// missing dependency).
 //
 // Compiled cubins are also kept on disk (internal/jit/diskcache.go keeps the
 // reference's PTX the same way), so a new process does not compile again:
