@@ -200,10 +200,10 @@ const char* kPrelude =
 struct Entry {
     CUmodule mod = nullptr;
     CUfunction fn = nullptr;
+    int dev = -1;
 };
 std::mutex g_mu;
 std::unordered_map<std::string, Entry> g_cache;  // key: device | source
-std::unordered_map<std::string, int> g_cache_dev;  // key -> its device
 
 const char* const kOptArch = "-arch=sm_100a";
 
@@ -290,7 +290,11 @@ void disk_write(const std::string& id, const Compiled& c) {
     for (size_t i = 1; i <= dir.size(); i++)  // mkdir -p
         if (i == dir.size() || dir[i] == '/') mkdir(dir.substr(0, i).c_str(), 0755);
     const std::string path = dir + "/" + name_of(id) + ".cubin";
-    const std::string tmp = path + ".tmp" + std::to_string((long)getpid());
+    // A temporary name of this writer's own (process and a per-process
+    // count: threads of one process may write the same entry at once).
+    static std::atomic<uint64_t> seq{0};
+    const std::string tmp = path + ".tmp" + std::to_string((long)getpid()) + "." +
+                            std::to_string(seq.fetch_add(1));
     FILE* f = fopen(tmp.c_str(), "wb");
     if (!f) return;
     const uint64_t n = id.size(), nl = c.name.size();
@@ -349,9 +353,6 @@ int compile_source(const std::string& src, const char* name, const char* expr, C
 // limit set to dyn_max. Returns nullptr with 0 when specialisation is off
 // or (mode 1) NVRTC is unavailable.
 int get_kernel(const std::string& src, const char* name, const char* expr, int dyn_max,
-               CUfunction* out);
-
-int get_kernel(const std::string& src, const char* name, const char* expr, int dyn_max,
                CUfunction* out) {
     *out = nullptr;
     const int m = mode();
@@ -368,12 +369,18 @@ int get_kernel(const std::string& src, const char* name, const char* expr, int d
     int rc = sg::cuda_status(cudaGetDevice(&dev), "cudaGetDevice");
     if (rc) return rc;
     const std::string key = std::to_string(dev) + "|" + src;
-    std::lock_guard<std::mutex> lk(g_mu);
-    auto it = g_cache.find(key);
-    if (it != g_cache.end()) {
-        *out = it->second.fn;
-        return 0;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        auto it = g_cache.find(key);
+        if (it != g_cache.end()) {
+            *out = it->second.fn;
+            return 0;
+        }
     }
+    // Not cached: read or compile, and load, without holding the lock, so
+    // that launches of kernels already loaded do not wait for a compile. Two
+    // threads that miss on the same program both build it; the first to
+    // finish keeps its module and the other unloads its own.
     Compiled c;
     const std::string id = identity(src);
     if (disk_read(id, &c)) {
@@ -384,17 +391,20 @@ int get_kernel(const std::string& src, const char* name, const char* expr, int d
         disk_write(id, c);
     }
     Entry e;
+    e.dev = dev;
     if ((rc = drv_status(g_drv.load(&e.mod, c.cubin.data()), "cuModuleLoadData"))) return rc;
-    if ((rc = drv_status(g_drv.get_fn(&e.fn, e.mod, c.name.c_str()), "cuModuleGetFunction")))
+    if ((rc = drv_status(g_drv.get_fn(&e.fn, e.mod, c.name.c_str()), "cuModuleGetFunction")) ||
+        (dyn_max > 0 &&
+         (rc = drv_status(
+              g_drv.set_attr(e.fn, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, dyn_max),
+              "cuFuncSetAttribute")))) {
+        if (g_drv.unload) g_drv.unload(e.mod);
         return rc;
-    if (dyn_max > 0 &&
-        (rc = drv_status(
-             g_drv.set_attr(e.fn, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, dyn_max),
-             "cuFuncSetAttribute")))
-        return rc;
-    g_cache.emplace(key, e);
-    g_cache_dev.emplace(key, dev);
-    *out = e.fn;
+    }
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto ins = g_cache.emplace(key, e);
+    if (!ins.second && g_drv.unload) g_drv.unload(e.mod);  // another thread's came first
+    *out = ins.first->second.fn;
     return 0;
 }
 
@@ -538,12 +548,11 @@ int tile_jit_release() {
     int prev = 0, rc = 0;
     cudaGetDevice(&prev);
     for (auto& kv : g_cache) {
-        int r = cuda_status(cudaSetDevice(g_cache_dev[kv.first]), "cudaSetDevice");
+        int r = cuda_status(cudaSetDevice(kv.second.dev), "cudaSetDevice");
         if (!r && g_drv.unload) r = drv_status(g_drv.unload(kv.second.mod), "cuModuleUnload");
         if (r && !rc) rc = r;
     }
     g_cache.clear();
-    g_cache_dev.clear();
     cudaSetDevice(prev);
     return rc;
 }

@@ -224,3 +224,37 @@ def test_source_is_the_listed_program(seed):
         assert [int(lines[i + 1].split()[0]) for i in heads] == starts
         assert [int(lines[i].split()[3]) for i in heads] == [
             int(m) & 0xFF for m in re.findall(r"\{\d+, (\d+), \d+, \d+\}", fir)]
+
+
+@needs_nvrtc
+def test_concurrent_writers_leave_a_valid_entry(tmp_path):
+    """Threads of one process compiling the same program at once each write
+    through a temporary file of their own; the entry left behind is whole
+    (a later process reads it instead of compiling)."""
+    import os
+    import subprocess
+    import sys
+
+    prog = (
+        "import sys, threading, numpy as np\n"
+        "from simtgo_b200 import tile\n"
+        "def work():\n"
+        "    g = tile.New()\n"
+        "    a = g.Input(np.ones(1000, np.float32))\n"
+        "    tile.Sqrt(tile.Add(tile.Abs(a), tile.Scale(a, 3.0))).JITSource(groups=2, compile=True)\n"
+        "ts = [threading.Thread(target=work) for _ in range(int(sys.argv[1]))]\n"
+        "[t.start() for t in ts]\n"
+        "[t.join() for t in ts]\n"
+        "print(tile.JITInfo()[2], tile.JITInfo()[4])\n")
+    env = dict(os.environ, SIMTGO_B200_CACHE=str(tmp_path / "cache"))
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+    def run(threads):
+        out = subprocess.run([sys.executable, "-c", prog, str(threads)], env=env, cwd=root,
+                             check=True, capture_output=True, text=True).stdout.split()
+        return int(out[0]), int(out[1])
+
+    compiled, hits = run(4)
+    assert compiled + hits == 4 and compiled >= 1
+    assert run(1) == (0, 1)
+    assert not list((tmp_path / "cache").glob("*.tmp*"))
